@@ -1,0 +1,105 @@
+// pi0.5 action-expert denoise megakernel: parameters and work plan shared by host and device.
+//
+// Reference semantics: src/pi05/mk6.cu:112-519 (loop body), src/pi05/hybrid_model.py:76-133
+// (weight layout, modulations). Architecture constants are those of the Gemma-300M expert.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+namespace fa {
+namespace pi05 {
+
+constexpr int D = 1024;     // width
+constexpr int H = 8;        // query heads (one shared KV head)
+constexpr int HD = 256;     // head dim
+constexpr int QD = H * HD;  // 2048
+constexpr int F = 4096;     // GeGLU hidden
+constexpr int QKV_ROWS = QD + 2 * HD;  // 2560
+constexpr int MOD = 3 * D;  // scale|shift|gate
+constexpr int TPAD = 64;    // action tokens padded per (observation, head) for attention tiles
+constexpr int KCH = 128;    // prefix keys per attention chunk
+constexpr int MAX_CH = 32;  // prefix chunks per observation (max_prefix <= 4096)
+
+constexpr int kThreads = 192;  // warp 0 producer, warp 1 MMA, warps 2-5 epilogue / vector work
+constexpr int kAtomBytes = 128 * 64 * 2;  // one 128-row x 64-col bf16 SW128 atom
+constexpr int kSmemUse = 224 * 1024;
+constexpr int kSmemDyn = kSmemUse + 1024;  // + alignment slack
+constexpr int kMaxRing = 12;
+constexpr int kBSlots = 4;
+constexpr int kAttnWork = 160 * 1024;  // Q 64K | K/V 64K | P 32K
+
+enum Mat : int { MAT_QKV = 0, MAT_O = 1, MAT_GU = 2, MAT_DN = 3 };
+enum Map : int {
+  MAP_W_QKV = 0, MAP_W_O, MAP_W_GU, MAP_W_DN,  // weights, box {64, 128}
+  MAP_XN, MAP_ATTN, MAP_H,                     // activations, box {64, NTILE}
+  MAP_Q, MAP_K, MAP_VT, MAP_SK, MAP_SVT,       // attention operands
+  NUM_MAPS
+};
+enum Stage : int {
+  ST_NORM1 = 0, ST_QKV, ST_ATTN, ST_MERGE, ST_O, ST_NORM2, ST_GU, ST_DN, ST_FINAL, NUM_STAGES
+};
+
+struct GemmUnit {
+  uint16_t mtile;   // 128-row tile of the packed weight
+  uint16_t katom0;  // first 64-wide K atom
+  uint16_t natoms;  // K atoms in this unit
+  uint16_t split;   // index of the fp32 partial slice it writes (K-split stages)
+};
+struct AttnUnit {
+  uint16_t b, hp, chunk, is_suffix;  // observation, head pair, key chunk
+};
+struct CtaPlan {
+  int g_off[4], g_cnt[4];  // GEMM units of this CTA per matrix, same for every layer
+  int a_off, a_cnt;        // attention units of this CTA
+  int ring_slots;          // weight-ring depth (attention CTAs keep room for Q/K/V/P)
+};
+
+struct Params {
+  CUtensorMap maps[NUM_MAPS];
+  // geometry
+  int L, T, B, NT, NPAD, NTILE, TG, ngroups, nsteps, LPAD, AD;
+  int split_o, split_dn;
+  float dt;
+  // plan
+  const GemmUnit* gunits;
+  const AttnUnit* aunits;
+  const CtaPlan* plans;
+  const int* valid_len;  // [B]
+  const int* nchunks;    // [B] prefix chunks (ceil(valid_len/128))
+  // conditioning
+  const float* mods;       // [S][L][2][3072]
+  const float* mod_final;  // [S][3072]
+  const float* rope_cos;   // [B][T][128]
+  const float* rope_sin;
+  const float* w_ain;   // [1024][AD]
+  const float* b_ain;   // [1024]
+  const float* w_aout;  // [AD][1024]
+  const float* b_aout;  // [AD]
+  // state / scratch
+  float* x_t;      // [NT][AD]
+  float* x;        // [NPAD][1024] residual stream
+  float* part;     // [8][NPAD][1024] K-split partials
+  __nv_bfloat16* xn;    // [NPAD][1024]
+  __nv_bfloat16* attn;  // [NPAD][2048]
+  __nv_bfloat16* hbuf;  // [NPAD][4096]
+  __nv_bfloat16* q;     // [B][8][64][256]
+  __nv_bfloat16* sk;    // [B][64][256] this layer's action-token keys (RoPE applied)
+  __nv_bfloat16* svt;   // [B][256][64] this layer's action-token values, transposed
+  float* opart;  // [B][4][MAX_CH+1][128][256] per-chunk normalised attention output
+  float* oml;    // [B][4][MAX_CH+1][128][2] per-chunk (max, sum)
+  // control
+  unsigned int* bar;             // grid-barrier counter, zeroed before each launch
+  int* err;                      // 0 = ok; otherwise the first failure code
+  unsigned long long* stage_ns;  // [NUM_STAGES] or null
+  // host-side fault injection for tests: CTA 0 skips arriving at grid barrier number
+  // `inject_barrier` (-1 = off); every grid-barrier spin gives up after `spin_limit` polls.
+  int inject_barrier;
+  unsigned int spin_limit;
+};
+
+// Error codes written to *err by the kernel.
+enum KernelError : int { KERR_BARRIER = 1, KERR_PRODUCER = 2, KERR_MMA = 3, KERR_EPI = 4, KERR_ATTN = 5 };
+
+}  // namespace pi05
+}  // namespace fa

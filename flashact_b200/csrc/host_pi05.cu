@@ -1,0 +1,702 @@
+// Host side of the C ABI (include/flashact.h) for the pi0.5 engine: device buffers, on-device
+// weight packing and conditioning, prefix-KV bind, work planning, TMA descriptors, launch.
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/flashact.h"
+#include "fa_pi05.cuh"
+
+using namespace fa::pi05;
+using bf16 = __nv_bfloat16;
+
+namespace fa {
+namespace pi05 {
+__global__ void pi05_denoise_kernel(const __grid_constant__ Params p);
+}
+}  // namespace fa
+
+// ------------------------------------------------------------------ handle
+struct fa_handle {
+  fa_model_kind kind;
+  fa_config cfg;
+  int device = 0;
+  int num_sms = 0;
+  std::string err;
+  bool weights_ready = false, kv_ready = false, timing = false;
+  int last_launches = 0;
+  int split_o = 4, split_dn = 8, attn_penalty = 8;
+  // bound batch
+  int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LPAD = 0;
+  std::vector<int> valid_len;
+  // device memory
+  std::vector<void*> allocs;
+  bf16 *w_qkv = nullptr, *w_o = nullptr, *w_gu = nullptr, *w_dn = nullptr;
+  float *mods = nullptr, *mod_final = nullptr;
+  float *w_ain = nullptr, *b_ain = nullptr, *w_aout = nullptr, *b_aout = nullptr;
+  float *x_t = nullptr, *x = nullptr, *part = nullptr, *opart = nullptr, *oml = nullptr;
+  bf16 *xn = nullptr, *attn = nullptr, *hbuf = nullptr, *q = nullptr, *sk = nullptr, *svt = nullptr;
+  bf16 *kcache = nullptr, *vtcache = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  int *d_valid = nullptr, *d_nchunks = nullptr;
+  unsigned int* ctrl = nullptr;  // [0] barrier counter, [1] error word
+  unsigned long long* stage_ns = nullptr;
+  GemmUnit* d_gunits = nullptr;
+  AttnUnit* d_aunits = nullptr;
+  CtaPlan* d_plans = nullptr;
+  size_t n_gunits_cap = 0, n_aunits_cap = 0;
+  Params params;
+};
+
+static thread_local std::string g_create_err;
+
+static fa_status fail(fa_handle* h, fa_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (h) h->err = buf; else g_create_err = buf;
+  return st;
+}
+#define FA_CUDA(h, call)                                                                        \
+  do {                                                                                          \
+    cudaError_t e_ = (call);                                                                    \
+    if (e_ != cudaSuccess) return fail(h, FA_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                       __FILE__, __LINE__);                                     \
+  } while (0)
+
+template <class T>
+static fa_status dalloc(fa_handle* h, T** out, size_t count) {
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, count * sizeof(T) + 16);
+  if (e != cudaSuccess) return fail(h, FA_ERR_OOM, "cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
+  e = cudaMemset(p, 0, count * sizeof(T) + 16);
+  if (e != cudaSuccess) return fail(h, FA_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(e));
+  h->allocs.push_back(p);
+  *out = reinterpret_cast<T*>(p);
+  return FA_OK;
+}
+
+static bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+static size_t dtype_size(fa_dtype t) { return t == FA_DT_F32 ? 4 : 2; }
+
+__device__ __forceinline__ float load_as_float(const void* p, size_t i, int dt) {
+  if (dt == FA_DT_F32) return reinterpret_cast<const float*>(p)[i];
+  if (dt == FA_DT_BF16) return __bfloat162float(reinterpret_cast<const bf16*>(p)[i]);
+  return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+// ------------------------------------------------------------------ device helper kernels
+// Row-gather pack: dst[l][r][k] = bf16(src_{sel(r)}[l][row(r)][k]). rowmap[r] = (source id, row).
+struct PackSrc {
+  const void* ptr[3];
+  int dtype[3];
+  int rows[3];  // rows per layer of each source
+};
+__global__ void pack_rows_kernel(PackSrc s, const int2* rowmap, bf16* dst, int R, int K, int L) {
+  const size_t total = (size_t)L * R * K;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int k = (int)(i % K);
+    const size_t lr = i / K;
+    const int r = (int)(lr % R), l = (int)(lr / R);
+    const int2 m = rowmap[r];
+    const size_t si = ((size_t)l * s.rows[m.x] + m.y) * K + k;
+    dst[i] = __float2bfloat16(load_as_float(s.ptr[m.x], si, s.dtype[m.x]));
+  }
+}
+__global__ void to_f32_kernel(const void* src, int dt, float* dst, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = load_as_float(src, i, dt);
+}
+// openpi create_sinusoidal_pos_embedding(t, 1024, min_period=4e-3, max_period=4.0):
+// period_i = min * (max/min)^(i/511); emb = [sin(2 pi t / period) | cos(2 pi t / period)].
+// Computed in double like the reference's float64 path, stored fp32. t_s = 1 - s/N.
+__global__ void time_embed_kernel(float* emb, int S, int dim) {
+  const int half = dim / 2;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < S * half; i += gridDim.x * blockDim.x) {
+    const int s = i / half, j = i % half;
+    const double frac = half > 1 ? (double)j / (double)(half - 1) : 0.0;
+    const double period = 4e-3 * pow(4.0 / 4e-3, frac);
+    const double t = 1.0 - (double)s / (double)S;
+    const double arg = (2.0 * 3.14159265358979323846 / period) * (double)(float)t;
+    emb[(size_t)s * dim + j] = (float)sin(arg);
+    emb[(size_t)s * dim + half + j] = (float)cos(arg);
+  }
+}
+// out[s][o] = act(b[o] + sum_i W[o][i] in[s][i]) for s < S; warp per output row; fp32 math.
+// act: 0 none, 1 silu. out row s is at out + s * out_stride.
+__global__ void linear_f32_kernel(const void* W, int wdt, const void* b, int bdt, const float* in, int S, int IN,
+                                  int OUT, float* out, size_t out_stride, int act) {
+  extern __shared__ float xs[];  // [S][IN]
+  for (int i = threadIdx.x; i < S * IN; i += blockDim.x) xs[i] = in[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  for (int o = blockIdx.x * warps + (threadIdx.x >> 5); o < OUT; o += gridDim.x * warps) {
+    float acc[16];
+    for (int s0 = 0; s0 < S; s0 += 16) {
+      const int ns = min(16, S - s0);
+#pragma unroll
+      for (int s = 0; s < 16; ++s) acc[s] = 0.f;
+      for (int i = lane; i < IN; i += 32) {
+        const float w = load_as_float(W, (size_t)o * IN + i, wdt);
+#pragma unroll
+        for (int s = 0; s < 16; ++s)
+          if (s < ns) acc[s] = fmaf(w, xs[(s0 + s) * IN + i], acc[s]);
+      }
+#pragma unroll
+      for (int s = 0; s < 16; ++s) {
+        float v = acc[s];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0 && s < ns) {
+          v += load_as_float(b, o, bdt);
+          if (act == 1) v = v / (1.f + expf(-v));
+          out[(size_t)(s0 + s) * out_stride + o] = v;
+        }
+      }
+    }
+  }
+}
+// Prefix KV bind: K -> kcache[b][l][LPAD][256] (split-half RoPE order), V -> vtcache[b][l][256][LPAD]
+// (transposed), rows >= valid_len zero. Interleaved sources (FlashRT) have rotary pairs at
+// (2d, 2d+1): d -> d, d+1 -> d+128 (src/pi05/mk6.cu:258-277 does the same de-interleave).
+__global__ void bind_k_kernel(const bf16* k, int src_rows, const int* valid, int L, int LPAD, int interleaved,
+                              bf16* kc) {
+  const int b = blockIdx.z, l = blockIdx.y;
+  const int vl = valid[b];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < LPAD * HD; i += gridDim.x * blockDim.x) {
+    const int r = i / HD, d = i % HD;
+    bf16 v = __float2bfloat16(0.f);
+    if (r < vl) {
+      int sd = d;
+      if (interleaved) sd = d < 128 ? 2 * d : 2 * (d - 128) + 1;
+      v = k[(((size_t)b * L + l) * src_rows + r) * HD + sd];
+    }
+    kc[(((size_t)b * L + l) * LPAD + r) * HD + d] = v;
+  }
+}
+__global__ void bind_vt_kernel(const bf16* v, int src_rows, const int* valid, int L, int LPAD, bf16* vt) {
+  __shared__ bf16 tile[32][33];
+  const int b = blockIdx.z / L, l = blockIdx.z % L;
+  const int vl = valid[b];
+  const int r0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, d = d0 + threadIdx.x;
+    tile[i][threadIdx.x] = r < vl ? v[(((size_t)b * L + l) * src_rows + r) * HD + d] : __float2bfloat16(0.f);
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int d = d0 + i, r = r0 + threadIdx.x;
+    vt[(((size_t)b * L + l) * HD + d) * LPAD + r] = tile[threadIdx.x][i];
+  }
+}
+// RoPE tables for the action tokens: pos = valid_len[b] + t, inv_freq_i = 10000^(-2i/256)
+// (src/pi05/pack_weights.py:54-58), angle = fp32(pos) * fp32(inv_freq) as in the fp32 reference.
+__global__ void rope_kernel(const int* valid, int B, int T, float* cs, float* sn) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * T * 128; i += gridDim.x * blockDim.x) {
+    const int j = i % 128, t = (i / 128) % T, b = i / (128 * T);
+    const float inv = (float)(1.0 / pow(10000.0, (double)(2 * j) / 256.0));
+    const float ang = (float)(valid[b] + t) * inv;
+    cs[i] = (float)cos((double)ang);
+    sn[i] = (float)sin((double)ang);
+  }
+}
+
+// ------------------------------------------------------------------ create / destroy
+static int round_up(int a, int b) { return (a + b - 1) / b * b; }
+
+extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int device, fa_handle** out) {
+  if (!cfg || !out) return fail(nullptr, FA_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (kind != FA_MODEL_PI05) return fail(nullptr, FA_ERR_UNSUPPORTED, "model kind %d not built into this library", (int)kind);
+  const fa_config& c = *cfg;
+  if (c.width != D || c.num_heads != H || c.num_kv_heads != 1 || c.head_dim != HD || c.mlp_dim != F)
+    return fail(nullptr, FA_ERR_INVALID, "pi0.5 expert geometry must be width 1024, 8 heads, 1 kv head, head_dim 256, mlp 4096");
+  if (c.num_layers < 1 || c.num_layers > 64 || c.horizon < 1 || c.horizon > TPAD || c.action_dim < 1 || c.action_dim > 32 ||
+      c.max_prefix < 0 || c.max_prefix > MAX_CH * KCH || c.max_batch < 1 || c.max_batch > 1024 || c.num_steps < 1 ||
+      c.num_steps > 50)
+    return fail(nullptr, FA_ERR_INVALID,
+                "config out of range (layers 1..64, horizon 1..64, action_dim 1..32, max_prefix 0..4096, batch 1..1024, steps 1..50)");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    return fail(nullptr, FA_ERR_INVALID, "device %d not available", device);
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return fail(nullptr, FA_ERR_CUDA, "cudaGetDeviceProperties failed");
+  if (prop.major != 10 || prop.minor != 0)
+    return fail(nullptr, FA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a (B200)", device, prop.major, prop.minor);
+  if (!prop.cooperativeLaunch) return fail(nullptr, FA_ERR_UNSUPPORTED, "device lacks cooperative launch");
+
+  fa_handle* h = new fa_handle();
+  h->kind = kind;
+  h->cfg = c;
+  h->device = device;
+  h->num_sms = prop.multiProcessorCount;
+  if (const char* e = getenv("FA_SPLIT_O")) h->split_o = std::max(1, std::min(8, atoi(e)));
+  if (const char* e = getenv("FA_SPLIT_DN")) h->split_dn = std::max(1, std::min(8, atoi(e)));
+  if (const char* e = getenv("FA_ATTN_PENALTY")) h->attn_penalty = std::max(0, atoi(e));
+  auto bad = [&](fa_status st) { g_create_err = h->err; fa_destroy(h); return st; };
+  if (cudaSetDevice(device) != cudaSuccess) return bad(fail(h, FA_ERR_CUDA, "cudaSetDevice(%d) failed", device));
+
+  const int L = c.num_layers, T = c.horizon, S = c.num_steps, MB = c.max_batch;
+  const int NPADm = round_up(MB * T, 128);
+  const int LPADm = std::max(KCH, round_up(c.max_prefix, KCH));
+  fa_status st = FA_OK;
+#define ALLOC(ptr, n) if ((st = dalloc(h, &h->ptr, (size_t)(n))) != FA_OK) return bad(st)
+  ALLOC(w_qkv, (size_t)L * QKV_ROWS * D);
+  ALLOC(w_o, (size_t)L * D * QD);
+  ALLOC(w_gu, (size_t)L * 2 * F * D);
+  ALLOC(w_dn, (size_t)L * D * F);
+  ALLOC(mods, (size_t)S * L * 2 * MOD);
+  ALLOC(mod_final, (size_t)S * MOD);
+  ALLOC(w_ain, (size_t)D * c.action_dim);
+  ALLOC(b_ain, D);
+  ALLOC(w_aout, (size_t)c.action_dim * D);
+  ALLOC(b_aout, c.action_dim);
+  ALLOC(x_t, (size_t)NPADm * c.action_dim);
+  ALLOC(x, (size_t)NPADm * D);
+  ALLOC(part, (size_t)8 * NPADm * D);
+  ALLOC(xn, (size_t)NPADm * D);
+  ALLOC(attn, (size_t)NPADm * QD);
+  ALLOC(hbuf, (size_t)NPADm * F);
+  ALLOC(q, (size_t)MB * H * TPAD * HD);
+  ALLOC(sk, (size_t)MB * TPAD * HD);
+  ALLOC(svt, (size_t)MB * HD * TPAD);
+  ALLOC(opart, (size_t)MB * 4 * (MAX_CH + 1) * 128 * HD);
+  ALLOC(oml, (size_t)MB * 4 * (MAX_CH + 1) * 128 * 2);
+  ALLOC(kcache, (size_t)MB * L * LPADm * HD);
+  ALLOC(vtcache, (size_t)MB * L * HD * LPADm);
+  ALLOC(rope_cos, (size_t)MB * T * 128);
+  ALLOC(rope_sin, (size_t)MB * T * 128);
+  ALLOC(d_valid, MB);
+  ALLOC(d_nchunks, MB);
+  ALLOC(ctrl, 2);
+  ALLOC(stage_ns, NUM_STAGES);
+  ALLOC(d_plans, h->num_sms);
+#undef ALLOC
+  if (cudaFuncSetAttribute(fa::pi05::pi05_denoise_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDyn) != cudaSuccess)
+    return bad(fail(h, FA_ERR_CUDA, "cannot reserve %d bytes of shared memory", kSmemDyn));
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fa::pi05::pi05_denoise_kernel, kThreads, kSmemDyn) != cudaSuccess ||
+      occ < 1)
+    return bad(fail(h, FA_ERR_UNSUPPORTED, "megakernel does not fit on an SM (occupancy %d)", occ));
+  *out = h;
+  return FA_OK;
+}
+
+extern "C" void fa_destroy(fa_handle* h) {
+  if (!h) return;
+  cudaSetDevice(h->device);
+  for (void* p : h->allocs) cudaFree(p);
+  delete h;
+}
+
+extern "C" const char* fa_last_error(fa_handle* h) { return h ? h->err.c_str() : g_create_err.c_str(); }
+extern "C" int fa_last_launch_count(fa_handle* h) { return h ? h->last_launches : 0; }
+
+// ------------------------------------------------------------------ weights
+// Returns a device pointer holding `t` (staging host data into `tmp` when needed).
+static fa_status stage_tensor(fa_handle* h, const fa_tensor& t, size_t count, const char* name, const void** dptr,
+                              std::vector<void*>& tmp) {
+  if (!t.ptr) return fail(h, FA_ERR_INVALID, "weight '%s' is null", name);
+  if (t.dtype != FA_DT_F32 && t.dtype != FA_DT_BF16 && t.dtype != FA_DT_F16)
+    return fail(h, FA_ERR_INVALID, "weight '%s' has unsupported dtype %d", name, (int)t.dtype);
+  if (is_device_ptr(t.ptr)) { *dptr = t.ptr; return FA_OK; }
+  void* d = nullptr;
+  const size_t bytes = count * dtype_size(t.dtype);
+  if (cudaMalloc(&d, bytes) != cudaSuccess) return fail(h, FA_ERR_OOM, "staging '%s' (%zu bytes)", name, bytes);
+  tmp.push_back(d);
+  FA_CUDA(h, cudaMemcpy(d, t.ptr, bytes, cudaMemcpyHostToDevice));
+  *dptr = d;
+  return FA_OK;
+}
+
+static fa_status pack_matrix(fa_handle* h, const std::vector<int2>& rowmap, PackSrc src, bf16* dst, int K,
+                             std::vector<void*>& tmp) {
+  int2* d_map = nullptr;
+  FA_CUDA(h, cudaMalloc(&d_map, rowmap.size() * sizeof(int2)));
+  tmp.push_back(d_map);
+  FA_CUDA(h, cudaMemcpy(d_map, rowmap.data(), rowmap.size() * sizeof(int2), cudaMemcpyHostToDevice));
+  pack_rows_kernel<<<h->num_sms * 8, 256>>>(src, d_map, dst, (int)rowmap.size(), K, h->cfg.num_layers);
+  FA_CUDA(h, cudaGetLastError());
+  return FA_OK;
+}
+
+static fa_status run_linear(fa_handle* h, const void* W, fa_dtype wdt, const void* b, fa_dtype bdt, const float* in, int S,
+                            int IN, int OUT, float* out, size_t out_stride, int act) {
+  const size_t smem = (size_t)S * IN * sizeof(float);
+  if (smem > 48 * 1024) FA_CUDA(h, cudaFuncSetAttribute(linear_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  linear_f32_kernel<<<h->num_sms * 2, 256, smem>>>(W, wdt, b, bdt, in, S, IN, OUT, out, out_stride, act);
+  FA_CUDA(h, cudaGetLastError());
+  return FA_OK;
+}
+
+extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt) {
+  if (!h || !w) return fail(h, FA_ERR_INVALID, "null argument");
+  if (fmt != FA_WFMT_BF16) return fail(h, FA_ERR_UNSUPPORTED, "weight format %d not available yet (bf16 only)", (int)fmt);
+  FA_CUDA(h, cudaSetDevice(h->device));
+  const int L = h->cfg.num_layers, AD = h->cfg.action_dim, S = h->cfg.num_steps;
+  std::vector<void*> tmp;
+  struct Cleanup {
+    std::vector<void*>& t;
+    ~Cleanup() { for (void* p : t) cudaFree(p); }
+  } cleanup{tmp};
+  fa_status st;
+  const void *wq, *wk, *wv, *wo, *wg, *wu, *wd, *lniw, *lnib, *lnpw, *lnpb, *nw, *nb, *tiw, *tib, *tow, *tob, *aiw, *aib, *aow, *aob;
+#define STAGE(var, field, count) \
+  if ((st = stage_tensor(h, w->field, (size_t)(count), #field, &var, tmp)) != FA_OK) return st
+  STAGE(wq, wq, (size_t)L * QD * D);
+  STAGE(wk, wk, (size_t)L * HD * D);
+  STAGE(wv, wv, (size_t)L * HD * D);
+  STAGE(wo, wo, (size_t)L * D * QD);
+  STAGE(wg, w_gate, (size_t)L * F * D);
+  STAGE(wu, w_up, (size_t)L * F * D);
+  STAGE(wd, w_down, (size_t)L * D * F);
+  STAGE(lniw, ln_in_w, (size_t)L * MOD * D);
+  STAGE(lnib, ln_in_b, (size_t)L * MOD);
+  STAGE(lnpw, ln_post_w, (size_t)L * MOD * D);
+  STAGE(lnpb, ln_post_b, (size_t)L * MOD);
+  STAGE(nw, norm_w, (size_t)MOD * D);
+  STAGE(nb, norm_b, MOD);
+  STAGE(tiw, time_in_w, (size_t)D * D);
+  STAGE(tib, time_in_b, D);
+  STAGE(tow, time_out_w, (size_t)D * D);
+  STAGE(tob, time_out_b, D);
+  STAGE(aiw, ain_w, (size_t)D * AD);
+  STAGE(aib, ain_b, D);
+  STAGE(aow, aout_w, (size_t)AD * D);
+  STAGE(aob, aout_b, AD);
+#undef STAGE
+
+  // QKV rows: Q head h / K in 128-row tiles where row 32*q + lane holds rotary pair
+  // p = 64*pb + 16*q + (lane & 15), dim p + 128*(lane >> 4); V rows in natural order.
+  std::vector<int2> m1(QKV_ROWS);
+  for (int mt = 0; mt < 20; ++mt)
+    for (int r = 0; r < 128; ++r) {
+      const int qd = r >> 5, lane = r & 31;
+      if (mt < 18) {
+        const int pb = mt < 16 ? (mt & 1) : mt - 16;
+        const int dim = 64 * pb + 16 * qd + (lane & 15) + 128 * (lane >> 4);
+        m1[mt * 128 + r] = mt < 16 ? make_int2(0, (mt >> 1) * HD + dim) : make_int2(1, dim);
+      } else {
+        m1[mt * 128 + r] = make_int2(2, (mt - 18) * 128 + r);
+      }
+    }
+  PackSrc s1 = {{wq, wk, wv}, {w->wq.dtype, w->wk.dtype, w->wv.dtype}, {QD, HD, HD}};
+  if ((st = pack_matrix(h, m1, s1, h->w_qkv, D, tmp)) != FA_OK) return st;
+  std::vector<int2> mo(D);
+  for (int r = 0; r < D; ++r) mo[r] = make_int2(0, r);
+  PackSrc so = {{wo, wo, wo}, {w->wo.dtype, w->wo.dtype, w->wo.dtype}, {D, D, D}};
+  if ((st = pack_matrix(h, mo, so, h->w_o, QD, tmp)) != FA_OK) return st;
+  // gate/up rows: tile mt, row 32*q + lane -> feature 64*mt + 16*q + (lane & 15); lanes < 16 gate.
+  std::vector<int2> m2(2 * F);
+  for (int mt = 0; mt < 64; ++mt)
+    for (int r = 0; r < 128; ++r) {
+      const int qd = r >> 5, lane = r & 31;
+      m2[mt * 128 + r] = make_int2(lane < 16 ? 0 : 1, 64 * mt + 16 * qd + (lane & 15));
+    }
+  PackSrc s2 = {{wg, wu, wu}, {w->w_gate.dtype, w->w_up.dtype, w->w_up.dtype}, {F, F, F}};
+  if ((st = pack_matrix(h, m2, s2, h->w_gu, D, tmp)) != FA_OK) return st;
+  PackSrc s3 = {{wd, wd, wd}, {w->w_down.dtype, w->w_down.dtype, w->w_down.dtype}, {D, D, D}};
+  if ((st = pack_matrix(h, mo, s3, h->w_dn, F, tmp)) != FA_OK) return st;
+
+  to_f32_kernel<<<64, 256>>>(aiw, w->ain_w.dtype, h->w_ain, (size_t)D * AD);
+  to_f32_kernel<<<4, 256>>>(aib, w->ain_b.dtype, h->b_ain, D);
+  to_f32_kernel<<<64, 256>>>(aow, w->aout_w.dtype, h->w_aout, (size_t)AD * D);
+  to_f32_kernel<<<1, 64>>>(aob, w->aout_b.dtype, h->b_aout, AD);
+  FA_CUDA(h, cudaGetLastError());
+
+  // Conditioning for the fixed schedule t_s = 1 - s/N (src/pi05/hybrid_model.py:111-128):
+  // cond = silu(W_out silu(W_in emb + b_in) + b_out); mods = Dense_{in,post}(cond); final = Dense_norm(cond).
+  float *emb = nullptr, *h1 = nullptr, *cond = nullptr;
+  FA_CUDA(h, cudaMalloc(&emb, (size_t)S * D * 4));
+  tmp.push_back(emb);
+  FA_CUDA(h, cudaMalloc(&h1, (size_t)S * D * 4));
+  tmp.push_back(h1);
+  FA_CUDA(h, cudaMalloc(&cond, (size_t)S * D * 4));
+  tmp.push_back(cond);
+  time_embed_kernel<<<8, 256>>>(emb, S, D);
+  FA_CUDA(h, cudaGetLastError());
+  if ((st = run_linear(h, tiw, w->time_in_w.dtype, tib, w->time_in_b.dtype, emb, S, D, D, h1, D, 1)) != FA_OK) return st;
+  if ((st = run_linear(h, tow, w->time_out_w.dtype, tob, w->time_out_b.dtype, h1, S, D, D, cond, D, 1)) != FA_OK) return st;
+  const size_t sstride = (size_t)L * 2 * MOD;
+  for (int l = 0; l < L; ++l) {
+    const size_t wo_ = (size_t)l * MOD * D * dtype_size(w->ln_in_w.dtype);
+    const size_t bo_ = (size_t)l * MOD * dtype_size(w->ln_in_b.dtype);
+    if ((st = run_linear(h, (const char*)lniw + wo_, w->ln_in_w.dtype, (const char*)lnib + bo_, w->ln_in_b.dtype, cond, S, D,
+                         MOD, h->mods + (size_t)l * 2 * MOD, sstride, 0)) != FA_OK)
+      return st;
+    const size_t wp_ = (size_t)l * MOD * D * dtype_size(w->ln_post_w.dtype);
+    const size_t bp_ = (size_t)l * MOD * dtype_size(w->ln_post_b.dtype);
+    if ((st = run_linear(h, (const char*)lnpw + wp_, w->ln_post_w.dtype, (const char*)lnpb + bp_, w->ln_post_b.dtype, cond, S,
+                         D, MOD, h->mods + (size_t)l * 2 * MOD + MOD, sstride, 0)) != FA_OK)
+      return st;
+  }
+  if ((st = run_linear(h, nw, w->norm_w.dtype, nb, w->norm_b.dtype, cond, S, D, MOD, h->mod_final, MOD, 0)) != FA_OK) return st;
+  FA_CUDA(h, cudaDeviceSynchronize());
+  h->weights_ready = true;
+  return FA_OK;
+}
+
+extern "C" fa_status fa_set_modulation(fa_handle* h, const float* mods, const float* mod_final) {
+  if (!h || !mods || !mod_final) return fail(h, FA_ERR_INVALID, "null argument");
+  FA_CUDA(h, cudaSetDevice(h->device));
+  const size_t n = (size_t)h->cfg.num_steps * h->cfg.num_layers * 2 * MOD;
+  FA_CUDA(h, cudaMemcpy(h->mods, mods, n * 4, cudaMemcpyDefault));
+  FA_CUDA(h, cudaMemcpy(h->mod_final, mod_final, (size_t)h->cfg.num_steps * MOD * 4, cudaMemcpyDefault));
+  return FA_OK;
+}
+
+// ------------------------------------------------------------------ TMA descriptors
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+// 2D bf16 map over a row-major [outer][inner] array, 128-byte swizzle, box {box_inner, box_outer}.
+static fa_status make_map(fa_handle* h, CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+                          uint32_t box_inner, uint32_t box_outer) {
+  auto enc = get_encode();
+  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FA_OK;
+}
+
+// ------------------------------------------------------------------ work plan
+// GEMM units per layer: QKV 20 x 128-row tiles (full K), O 8 tiles x split_o K-slices,
+// gate/up 64 tiles (full K), down 8 tiles x split_dn K-slices. Attention units: per
+// observation, 4 head pairs x (prefix chunks + 1 suffix chunk). Attention units go to the first
+// CTAs in contiguous runs (same head pair -> Q reuse); each GEMM stage is then spread so that
+// no CTA holds two units of one stage before all CTAs hold one, ties broken by total bytes.
+static fa_status build_plan(fa_handle* h) {
+  const int nblk = h->num_sms;
+  std::vector<AttnUnit> au;
+  for (int b = 0; b < h->B; ++b) {
+    const int npc = (h->valid_len[b] + KCH - 1) / KCH;
+    for (int hp = 0; hp < 4; ++hp) {
+      for (int c = 0; c < npc; ++c) au.push_back({(uint16_t)b, (uint16_t)hp, (uint16_t)c, 0});
+      au.push_back({(uint16_t)b, (uint16_t)hp, 0, 1});
+    }
+  }
+  std::vector<CtaPlan> plans(nblk);
+  std::vector<long> load(nblk, 0);
+  const int na = (int)au.size();
+  const int acta = std::min(na, nblk);
+  for (int i = 0; i < nblk; ++i) {
+    const int lo = i < acta ? (int)((long)na * i / acta) : 0, hi = i < acta ? (int)((long)na * (i + 1) / acta) : 0;
+    plans[i].a_off = lo;
+    plans[i].a_cnt = hi - lo;
+    load[i] = (long)plans[i].a_cnt * h->attn_penalty;
+  }
+  struct Spec { int mtiles, katoms, split; };
+  const Spec spec[4] = {{20, D / 64, 1}, {8, QD / 64, h->split_o}, {64, D / 64, 1}, {8, F / 64, h->split_dn}};
+  std::vector<std::vector<GemmUnit>> per(nblk * 4);
+  const int order[4] = {MAT_QKV, MAT_GU, MAT_DN, MAT_O};
+  for (int oi = 0; oi < 4; ++oi) {
+    const int m = order[oi];
+    const Spec& s = spec[m];
+    const int per_split = s.katoms / s.split;
+    std::vector<int> cnt(nblk, 0);
+    for (int mt = 0; mt < s.mtiles; ++mt)
+      for (int sp = 0; sp < s.split; ++sp) {
+        int best = 0;
+        for (int i = 1; i < nblk; ++i)
+          if (cnt[i] < cnt[best] || (cnt[i] == cnt[best] && load[i] < load[best])) best = i;
+        per[best * 4 + m].push_back({(uint16_t)mt, (uint16_t)(sp * per_split), (uint16_t)per_split, (uint16_t)sp});
+        cnt[best]++;
+        load[best] += per_split;
+      }
+  }
+  std::vector<GemmUnit> gu;
+  for (int i = 0; i < nblk; ++i) {
+    const int R = (kSmemUse - (plans[i].a_cnt > 0 ? kAttnWork : kBSlots * h->NTILE * 128)) / kAtomBytes;
+    plans[i].ring_slots = std::min(kMaxRing, R);
+    for (int m = 0; m < 4; ++m) {
+      plans[i].g_off[m] = (int)gu.size();
+      plans[i].g_cnt[m] = (int)per[i * 4 + m].size();
+      gu.insert(gu.end(), per[i * 4 + m].begin(), per[i * 4 + m].end());
+    }
+  }
+  if (gu.size() > h->n_gunits_cap) {
+    if (h->d_gunits) cudaFree(h->d_gunits);
+    FA_CUDA(h, cudaMalloc(&h->d_gunits, gu.size() * sizeof(GemmUnit)));
+    h->n_gunits_cap = gu.size();
+  }
+  if (au.size() > h->n_aunits_cap) {
+    if (h->d_aunits) cudaFree(h->d_aunits);
+    FA_CUDA(h, cudaMalloc(&h->d_aunits, au.size() * sizeof(AttnUnit)));
+    h->n_aunits_cap = au.size();
+  }
+  FA_CUDA(h, cudaMemcpy(h->d_gunits, gu.data(), gu.size() * sizeof(GemmUnit), cudaMemcpyHostToDevice));
+  FA_CUDA(h, cudaMemcpy(h->d_aunits, au.data(), au.size() * sizeof(AttnUnit), cudaMemcpyHostToDevice));
+  FA_CUDA(h, cudaMemcpy(h->d_plans, plans.data(), plans.size() * sizeof(CtaPlan), cudaMemcpyHostToDevice));
+  return FA_OK;
+}
+
+static fa_status build_params(fa_handle* h) {
+  Params& p = h->params;
+  memset(&p, 0, sizeof(p));
+  const int L = h->cfg.num_layers, B = h->B;
+  fa_status st;
+#define MAP(i, base, inner, outer, bi, bo) if ((st = make_map(h, &p.maps[i], base, inner, outer, bi, bo)) != FA_OK) return st
+  MAP(MAP_W_QKV, h->w_qkv, D, (uint64_t)L * QKV_ROWS, 64, 128);
+  MAP(MAP_W_O, h->w_o, QD, (uint64_t)L * D, 64, 128);
+  MAP(MAP_W_GU, h->w_gu, D, (uint64_t)L * 2 * F, 64, 128);
+  MAP(MAP_W_DN, h->w_dn, F, (uint64_t)L * D, 64, 128);
+  MAP(MAP_XN, h->xn, D, h->NPAD, 64, h->NTILE);
+  MAP(MAP_ATTN, h->attn, QD, h->NPAD, 64, h->NTILE);
+  MAP(MAP_H, h->hbuf, F, h->NPAD, 64, h->NTILE);
+  MAP(MAP_Q, h->q, HD, (uint64_t)B * H * TPAD, 64, 128);
+  MAP(MAP_K, h->kcache, HD, (uint64_t)B * L * h->LPAD, 64, 128);
+  MAP(MAP_VT, h->vtcache, h->LPAD, (uint64_t)B * L * HD, 64, 128);
+  MAP(MAP_SK, h->sk, HD, (uint64_t)B * TPAD, 64, 64);
+  MAP(MAP_SVT, h->svt, TPAD, (uint64_t)B * HD, 64, 128);
+#undef MAP
+  p.L = L; p.T = h->cfg.horizon; p.B = B; p.NT = h->NT; p.NPAD = h->NPAD; p.NTILE = h->NTILE; p.TG = h->TG;
+  p.ngroups = h->ngroups; p.nsteps = h->cfg.num_steps; p.LPAD = h->LPAD; p.AD = h->cfg.action_dim;
+  p.split_o = h->split_o; p.split_dn = h->split_dn;
+  p.dt = -1.0f / (float)h->cfg.num_steps;
+  p.gunits = h->d_gunits; p.aunits = h->d_aunits; p.plans = h->d_plans;
+  p.valid_len = h->d_valid; p.nchunks = h->d_nchunks;
+  p.mods = h->mods; p.mod_final = h->mod_final; p.rope_cos = h->rope_cos; p.rope_sin = h->rope_sin;
+  p.w_ain = h->w_ain; p.b_ain = h->b_ain; p.w_aout = h->w_aout; p.b_aout = h->b_aout;
+  p.x_t = h->x_t; p.x = h->x; p.part = h->part; p.xn = h->xn; p.attn = h->attn; p.hbuf = h->hbuf;
+  p.q = h->q; p.sk = h->sk; p.svt = h->svt; p.opart = h->opart; p.oml = h->oml;
+  p.bar = h->ctrl; p.err = reinterpret_cast<int*>(h->ctrl + 1);
+  p.stage_ns = nullptr;
+  p.inject_barrier = -1;
+  p.spin_limit = 1u << 24;
+  return FA_OK;
+}
+
+extern "C" fa_status fa_bind_prefix_kv(fa_handle* h, int batch, const void* k, const void* v, int src_rows,
+                                       const int* valid_len, fa_kv_layout layout, fa_stream stream) {
+  if (!h) return fail(h, FA_ERR_INVALID, "null handle");
+  if (batch < 1 || batch > h->cfg.max_batch) return fail(h, FA_ERR_INVALID, "batch %d outside 1..%d", batch, h->cfg.max_batch);
+  if (!valid_len) return fail(h, FA_ERR_INVALID, "valid_len is null");
+  if (layout != FA_KV_COMPACT_SPLIT_HALF && layout != FA_KV_FLASHRT_INTERLEAVED) return fail(h, FA_ERR_INVALID, "unknown kv layout");
+  int maxvl = 0;
+  for (int b = 0; b < batch; ++b) {
+    if (valid_len[b] < 0 || valid_len[b] > src_rows || valid_len[b] > h->cfg.max_prefix)
+      return fail(h, FA_ERR_INVALID, "valid_len[%d]=%d outside 0..min(src_rows=%d, max_prefix=%d)", b, valid_len[b], src_rows,
+                  h->cfg.max_prefix);
+    maxvl = std::max(maxvl, valid_len[b]);
+  }
+  if (maxvl > 0 && (!k || !v)) return fail(h, FA_ERR_INVALID, "k/v pointers are null");
+  if (maxvl > 0 && (!is_device_ptr(k) || !is_device_ptr(v))) return fail(h, FA_ERR_INVALID, "k/v must be device pointers");
+  FA_CUDA(h, cudaSetDevice(h->device));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  FA_CUDA(h, cudaStreamSynchronize(s));  // previous launches may still read the cache and plan
+  const int T = h->cfg.horizon, L = h->cfg.num_layers;
+  h->B = batch;
+  h->NT = batch * T;
+  h->NTILE = h->NT <= 64 ? 64 : 128;
+  h->NPAD = round_up(h->NT, h->NTILE);
+  h->TG = 256 / h->NTILE;
+  h->ngroups = (h->NPAD / h->NTILE + h->TG - 1) / h->TG;
+  h->LPAD = std::max(KCH, round_up(h->cfg.max_prefix, KCH));
+  h->valid_len.assign(valid_len, valid_len + batch);
+  std::vector<int> nch(batch);
+  for (int b = 0; b < batch; ++b) nch[b] = (valid_len[b] + KCH - 1) / KCH;
+  FA_CUDA(h, cudaMemcpy(h->d_valid, valid_len, batch * sizeof(int), cudaMemcpyHostToDevice));
+  FA_CUDA(h, cudaMemcpy(h->d_nchunks, nch.data(), batch * sizeof(int), cudaMemcpyHostToDevice));
+  fa_status st;
+  if ((st = build_plan(h)) != FA_OK) return st;
+  if ((st = build_params(h)) != FA_OK) return st;
+  const int sr = std::max(src_rows, 1);
+  bind_k_kernel<<<dim3(std::max(1, h->LPAD * HD / 256 / 4), L, batch), 256, 0, s>>>(
+      (const bf16*)k, sr, h->d_valid, L, h->LPAD, layout == FA_KV_FLASHRT_INTERLEAVED, h->kcache);
+  FA_CUDA(h, cudaGetLastError());
+  bind_vt_kernel<<<dim3(h->LPAD / 32, HD / 32, batch * L), dim3(32, 8), 0, s>>>((const bf16*)v, sr, h->d_valid, L, h->LPAD,
+                                                                              h->vtcache);
+  FA_CUDA(h, cudaGetLastError());
+  rope_kernel<<<64, 256, 0, s>>>(h->d_valid, batch, T, h->rope_cos, h->rope_sin);
+  FA_CUDA(h, cudaGetLastError());
+  FA_CUDA(h, cudaStreamSynchronize(s));
+  h->kv_ready = true;
+  return FA_OK;
+}
+
+extern "C" fa_status fa_set_stage_timing(fa_handle* h, int enable) {
+  if (!h) return FA_ERR_INVALID;
+  h->timing = enable != 0;
+  return FA_OK;
+}
+
+extern "C" fa_status fa_get_stage_cycles(fa_handle* h, uint64_t* out, int n) {
+  if (!h || !out) return fail(h, FA_ERR_INVALID, "null argument");
+  FA_CUDA(h, cudaSetDevice(h->device));
+  unsigned long long tmp[NUM_STAGES];
+  FA_CUDA(h, cudaMemcpy(tmp, h->stage_ns, sizeof(tmp), cudaMemcpyDeviceToHost));
+  for (int i = 0; i < n; ++i) out[i] = i < NUM_STAGES ? tmp[i] : 0;
+  return FA_OK;
+}
+
+extern "C" fa_status fa_sample_actions(fa_handle* h, int batch, const float* noise, float* actions_out, fa_stream stream) {
+  if (!h || !noise || !actions_out) return fail(h, FA_ERR_INVALID, "null argument");
+  if (!h->weights_ready) return fail(h, FA_ERR_STATE, "weights not loaded");
+  if (!h->kv_ready) return fail(h, FA_ERR_STATE, "prefix KV not bound");
+  if (batch != h->B) return fail(h, FA_ERR_INVALID, "batch %d differs from the bound batch %d", batch, h->B);
+  FA_CUDA(h, cudaSetDevice(h->device));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t bytes = (size_t)h->NT * h->cfg.action_dim * sizeof(float);
+  Params& p = h->params;
+  p.stage_ns = h->timing ? h->stage_ns : nullptr;
+  FA_CUDA(h, cudaMemsetAsync(h->ctrl, 0, 2 * sizeof(unsigned int), s));
+  if (h->timing) FA_CUDA(h, cudaMemsetAsync(h->stage_ns, 0, NUM_STAGES * sizeof(unsigned long long), s));
+  FA_CUDA(h, cudaMemcpyAsync(h->x_t, noise, bytes, cudaMemcpyDefault, s));
+  void* args[] = {&p};
+  FA_CUDA(h, cudaLaunchCooperativeKernel((const void*)fa::pi05::pi05_denoise_kernel, dim3(h->num_sms), dim3(kThreads), args,
+                                         kSmemDyn, s));
+  FA_CUDA(h, cudaMemcpyAsync(actions_out, h->x_t, bytes, cudaMemcpyDefault, s));
+  h->last_launches = 1;
+  return FA_OK;
+}
+
+extern "C" fa_status fa_sync(fa_handle* h, fa_stream stream) {
+  if (!h) return FA_ERR_INVALID;
+  FA_CUDA(h, cudaSetDevice(h->device));
+  FA_CUDA(h, cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+  unsigned int ctrl[2];
+  FA_CUDA(h, cudaMemcpy(ctrl, h->ctrl, sizeof(ctrl), cudaMemcpyDeviceToHost));
+  if (ctrl[1] != 0) return fail(h, FA_ERR_TIMEOUT, "in-kernel wait ran out (code %u)", ctrl[1]);
+  return FA_OK;
+}
+
+extern "C" fa_status fa_set_fault_injection(fa_handle* h, int barrier_index, unsigned int spin_limit) {
+  if (!h) return FA_ERR_INVALID;
+  h->params.inject_barrier = barrier_index;
+  h->params.spin_limit = spin_limit ? spin_limit : (1u << 24);
+  return FA_OK;
+}

@@ -1,0 +1,112 @@
+"""pi0.5 action-expert denoise engine: Python host mirror of the reference's deployment path.
+
+The reference's caller (src/pi05/hybrid_model.py: HybridPi05._pack_weights :76-133, the KV
+handoff + launch in predict :188-222) maps onto three calls here: construct (weight load +
+on-device conditioning), bind_prefix_kv, sample_actions. Everything runs through the C ABI of
+libflashact.so; torch is only used to hold device memory and name the current stream. There is
+no CPU fallback: without the library or an sm_100 GPU the constructor raises.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _capi as C
+
+_DT = {torch.float32: C.FA_DT_F32, torch.bfloat16: C.FA_DT_BF16, torch.float16: C.FA_DT_F16}
+
+
+def _stream_ptr(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+class Pi05ActionExpert:
+    """Owns one fa_handle on one device. Weights: dict with the keys of
+    flashact_b200._capi.PI05_WEIGHT_FIELDS, [out][in] row-major, stacked over layers."""
+
+    def __init__(self, weights: dict, *, num_layers=18, horizon=50, action_dim=32, max_prefix=968, max_batch=1,
+                 num_steps=10, device: int = 0, mods=None, mod_final=None):
+        self.lib = C.load_library()
+        self.device = device
+        self.cfg = C.FaConfig(num_layers, 1024, 8, 1, 256, 4096, horizon, action_dim, max_prefix, max_batch,
+                              num_steps)
+        self.horizon, self.action_dim, self.max_batch = horizon, action_dim, max_batch
+        h = ctypes.c_void_p()
+        st = self.lib.fa_create(C.FA_MODEL_PI05, ctypes.byref(self.cfg), device, ctypes.byref(h))
+        C.check(self.lib, None, st)
+        self.h = h
+        self._kv_keep = None
+        self.batch = 0
+        keep = []
+        w = C.FaPi05Weights()
+        for name in C.PI05_WEIGHT_FIELDS:
+            t = weights[name]
+            if t.dtype not in _DT:
+                t = t.float()
+            t = t.contiguous()
+            keep.append(t)
+            setattr(w, name, C.FaTensor(t.data_ptr(), _DT[t.dtype]))
+        self._check(self.lib.fa_pi05_load_weights(self.h, ctypes.byref(w), C.FA_WFMT_BF16))
+        if mods is not None:
+            m = mods.float().contiguous()
+            mf = mod_final.float().contiguous()
+            self._check(self.lib.fa_set_modulation(self.h, m.data_ptr(), mf.data_ptr()))
+
+    def _check(self, st):
+        C.check(self.lib, self.h, st)
+
+    def bind_prefix_kv(self, k: torch.Tensor, v: torch.Tensor, valid_len, layout: str = "compact", stream=None):
+        """k, v: [B][L][rows][256] bf16 on this device (other dtypes converted)."""
+        k = k.to(device=f"cuda:{self.device}", dtype=torch.bfloat16).contiguous()
+        v = v.to(device=f"cuda:{self.device}", dtype=torch.bfloat16).contiguous()
+        B, rows = k.shape[0], k.shape[2]
+        vl = (ctypes.c_int * B)(*[int(x) for x in valid_len])
+        lay = C.FA_KV_FLASHRT_INTERLEAVED if layout == "flashrt" else C.FA_KV_COMPACT_SPLIT_HALF
+        self._check(self.lib.fa_bind_prefix_kv(self.h, B, k.data_ptr(), v.data_ptr(), rows, vl, lay,
+                                               _stream_ptr(stream)))
+        self.batch = B
+
+    def sample_actions(self, noise: torch.Tensor, out: torch.Tensor | None = None, stream=None,
+                       sync: bool = True) -> torch.Tensor:
+        """noise [B][T][AD] fp32 (host or device). Returns actions, same shape, on noise's device
+        unless `out` is given. sync=True waits and reports in-kernel timeouts."""
+        noise = noise.float().contiguous()
+        if out is None:
+            out = torch.empty_like(noise)
+        self._check(self.lib.fa_sample_actions(self.h, self.batch, noise.data_ptr(), out.data_ptr(),
+                                               _stream_ptr(stream)))
+        if sync:
+            self.sync(stream)
+        return out
+
+    def sync(self, stream=None):
+        self._check(self.lib.fa_sync(self.h, _stream_ptr(stream)))
+
+    def set_stage_timing(self, enable=True):
+        self._check(self.lib.fa_set_stage_timing(self.h, int(enable)))
+
+    STAGES = ["embed/norm1", "qkv", "attention", "merge", "o_proj", "norm2", "gate_up", "down", "final"]
+
+    def stage_times_ns(self):
+        arr = (ctypes.c_uint64 * 9)()
+        self._check(self.lib.fa_get_stage_cycles(self.h, arr, 9))
+        return dict(zip(self.STAGES, list(arr)))
+
+    def launch_count(self) -> int:
+        return int(self.lib.fa_last_launch_count(self.h))
+
+    def inject_fault(self, barrier_index: int, spin_limit: int = 0):
+        self._check(self.lib.fa_set_fault_injection(self.h, barrier_index, spin_limit))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.fa_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

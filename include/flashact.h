@@ -1,0 +1,158 @@
+/*
+ * flashact.h — C ABI of the B200 (sm_100a) flow-matching action-expert denoise engine.
+ *
+ * The reference (GautamSharda/FlashAct) exposes its denoise loop as one pybind11 function per
+ * model, `launch(...)`, that takes pre-packed torch tensors plus caller-owned scratch:
+ *   - pi0.5:     src/pi05/binding.cpp:28-68      (kernel src/pi05/mk6.cu:112)
+ *   - MolmoAct2: src/molmoact2/binding.cpp:28-83 (kernel src/molmoact2/mk_ma2.cu:103)
+ * Its three implicit steps — weight packing (src/pi05/hybrid_model.py:76-133), prefix-KV bind
+ * (src/pi05/pack_weights.py:60-70 + hybrid_model.py:202-208) and sample = launch + x_t readback
+ * (hybrid_model.py:215-222) — are explicit entry points here. Everything takes plain pointers and
+ * sizes; no torch types cross this boundary. Every function returns a status and never throws.
+ *
+ * Threading: one handle belongs to one device. Calls on different handles may run concurrently
+ * from different host threads; calls on one handle must be serialised by the caller.
+ */
+#ifndef FLASHACT_H_
+#define FLASHACT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FA_API __attribute__((visibility("default")))
+#else
+#define FA_API
+#endif
+
+typedef struct fa_handle fa_handle;
+typedef struct CUstream_st* fa_stream; /* a cudaStream_t; NULL = legacy default stream */
+
+typedef enum {
+  FA_OK = 0,
+  FA_ERR_INVALID = 1,     /* bad argument: shape, pointer, dtype, batch > capacity ...          */
+  FA_ERR_CUDA = 2,        /* a CUDA runtime call failed (message in fa_last_error)             */
+  FA_ERR_TIMEOUT = 3,     /* a bounded in-kernel wait (grid barrier, mbarrier) ran out          */
+  FA_ERR_STATE = 4,       /* call order: sample before weights / KV were bound                  */
+  FA_ERR_UNSUPPORTED = 5, /* feature or device not supported (e.g. not an sm_100 GPU)           */
+  FA_ERR_OOM = 6
+} fa_status;
+
+typedef enum { FA_MODEL_PI05 = 0, FA_MODEL_MOLMOACT2 = 1 } fa_model_kind;
+typedef enum { FA_WFMT_BF16 = 0, FA_WFMT_FP8 = 1, FA_WFMT_NVFP4 = 2 } fa_wfmt;
+typedef enum { FA_DT_F32 = 0, FA_DT_BF16 = 1, FA_DT_F16 = 2 } fa_dtype;
+
+/* Prefix-KV source layouts accepted by fa_bind_prefix_kv.
+ * COMPACT_SPLIT_HALF: K and V as [B][L][src_rows][256], RoPE already applied to K in the
+ *   split-half convention (pairs d, d+128), rows 0..valid_len-1 valid. This is the layout
+ *   `compact_kv` produces (src/pi05/pack_weights.py:60-70).
+ * FLASHRT_INTERLEAVED: same shape, but K's rotary pairs are interleaved (2d, 2d+1), as in the
+ *   FlashRT encoder cache the reference ingests in its prologue (src/pi05/mk6.cu:258-277). */
+typedef enum { FA_KV_COMPACT_SPLIT_HALF = 0, FA_KV_FLASHRT_INTERLEAVED = 1 } fa_kv_layout;
+
+/* Model geometry. pi0.5: width 1024, 8 query heads, 1 KV head, head_dim 256, mlp 4096 are
+ * fixed by the architecture; num_layers (18), horizon (50), action_dim (32), max_prefix,
+ * max_batch and num_steps (10) are free. */
+typedef struct fa_config {
+  int num_layers;
+  int width;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int mlp_dim;
+  int horizon;    /* action tokens per observation (T)                  */
+  int action_dim; /* AD                                                 */
+  int max_prefix; /* capacity of the bound prefix KV per observation     */
+  int max_batch;  /* observations per fa_sample_actions call             */
+  int num_steps;  /* Euler steps N; pi0.5 integrates t = 1 -> 0, dt=-1/N */
+} fa_config;
+
+/* One weight tensor. ptr may be host or device memory (CUDA unified addressing decides). */
+typedef struct fa_tensor {
+  const void* ptr;
+  fa_dtype dtype;
+} fa_tensor;
+
+/* pi0.5 action-expert weights, each stacked over layers where it is per layer, in the
+ * [out][in] row-major layout of torch.nn.Linear. Names mirror the openpi keys the reference
+ * reads in src/pi05/hybrid_model.py:94-133:
+ *   layers.{i}.self_attn.{q,k,v,o}_proj.weight, mlp.{gate,up,down}_proj.weight,
+ *   input_layernorm.dense.{weight,bias}, post_attention_layernorm.dense.{weight,bias},
+ *   model.norm.dense.{weight,bias}, time_mlp_{in,out}.{weight,bias},
+ *   action_{in,out}_proj.{weight,bias}. */
+typedef struct fa_pi05_weights {
+  fa_tensor wq, wk, wv, wo;         /* [L][2048][1024], [L][256][1024] x2, [L][1024][2048] */
+  fa_tensor w_gate, w_up, w_down;   /* [L][4096][1024] x2, [L][1024][4096]                 */
+  fa_tensor ln_in_w, ln_in_b;       /* [L][3072][1024], [L][3072]                          */
+  fa_tensor ln_post_w, ln_post_b;   /* [L][3072][1024], [L][3072]                          */
+  fa_tensor norm_w, norm_b;         /* [3072][1024], [3072]                                */
+  fa_tensor time_in_w, time_in_b;   /* [1024][1024], [1024]                                */
+  fa_tensor time_out_w, time_out_b; /* [1024][1024], [1024]                                */
+  fa_tensor ain_w, ain_b;           /* [1024][AD], [1024]                                  */
+  fa_tensor aout_w, aout_b;         /* [AD][1024], [AD]                                    */
+} fa_pi05_weights;
+
+/* Creates a handle on `device`. Fails with FA_ERR_UNSUPPORTED on a GPU that is not sm_100. */
+FA_API fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int device, fa_handle** out);
+
+/* Packs the weights into the engine's streaming layout on the device and computes, on the
+ * device, the time embedding -> conditioning MLP -> per-layer adaRMS modulations for the
+ * configured fixed schedule (reference: host-side in src/pi05/hybrid_model.py:111-128).
+ * Synchronous. Replaces HybridPi05._pack_weights. */
+FA_API fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt);
+
+/* Overrides the modulations with precomputed ones: mods [num_steps][L][2][3072] fp32 (input /
+ * post-attention adaRMS; each scale|shift|gate) and mod_final [num_steps][3072] (scale|shift
+ * used). Device or host pointers. This is the form the reference's launch() receives
+ * (src/pi05/binding.cpp:31, `mods`, `mod_final`). */
+FA_API fa_status fa_set_modulation(fa_handle* h, const float* mods, const float* mod_final);
+
+/* Binds the cached VLM prefix KV of `batch` observations (device pointers, bf16). K and V are
+ * [batch][L][src_rows][256]; valid_len (host array, batch entries) gives each observation's
+ * number of valid (compacted) prefix tokens, <= src_rows <= max_prefix. The action tokens'
+ * RoPE positions start at valid_len (src/pi05/pack_weights.py:54-58). The copy / transpose /
+ * de-interleave runs on `stream`. Replaces compact_kv + the kcache/vtcache fill. */
+FA_API fa_status fa_bind_prefix_kv(fa_handle* h, int batch, const void* k, const void* v, int src_rows,
+                            const int* valid_len, fa_kv_layout layout, fa_stream stream);
+
+/* Runs the whole N-step x L-layer Euler denoise loop as one cooperative megakernel.
+ * noise: [batch][T][AD] fp32 initial x_1; actions_out: [batch][T][AD] fp32 final x_0. Either
+ * may be host or device memory; host buffers are copied on `stream` inside the call. batch
+ * must equal the batch of the last fa_bind_prefix_kv. Asynchronous w.r.t. the host when both
+ * pointers are device (or pinned) memory; a barrier timeout is reported by the NEXT call that
+ * synchronises (fa_sync) as FA_ERR_TIMEOUT. */
+FA_API fa_status fa_sample_actions(fa_handle* h, int batch, const float* noise, float* actions_out,
+                            fa_stream stream);
+
+/* Waits for the handle's last launch and reports an in-kernel timeout / error flag. */
+FA_API fa_status fa_sync(fa_handle* h, fa_stream stream);
+
+/* Per-stage time of the last launch, in nanoseconds summed over the loop (block 0's view):
+ * [0] embed/norm1 [1] qkv [2] attention [3] merge [4] o_proj [5] norm2 [6] gate/up [7] down
+ * [8] final+euler. Enable with fa_set_stage_timing(h, 1) before sampling. n = array length. */
+FA_API fa_status fa_set_stage_timing(fa_handle* h, int enable);
+FA_API fa_status fa_get_stage_cycles(fa_handle* h, uint64_t* out, int n);
+
+/* Number of kernel launches the last fa_sample_actions issued on the device (the megakernel
+ * and any copies-by-kernel), for launch accounting. */
+FA_API int fa_last_launch_count(fa_handle* h);
+
+/* Test hook (host-side fault injection, no GPU fault): block 0 skips arriving at grid barrier
+ * number `barrier_index` of the next launches (-1 = off) and every grid-barrier wait gives up
+ * after `spin_limit` polls (0 = default). The launch then ends early with its error word set and
+ * fa_sync reports FA_ERR_TIMEOUT; the context stays usable. Reset by fa_bind_prefix_kv. */
+FA_API fa_status fa_set_fault_injection(fa_handle* h, int barrier_index, unsigned int spin_limit);
+
+/* Last error message of the handle (or of the thread's last failed fa_create when h is NULL). */
+FA_API const char* fa_last_error(fa_handle* h);
+
+FA_API void fa_destroy(fa_handle* h);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLASHACT_H_ */

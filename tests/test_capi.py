@@ -1,0 +1,44 @@
+"""CPU checks of the C-ABI boundary: the library builds/loads and exports every declared symbol."""
+import ctypes
+import os
+import re
+
+from flashact_b200 import _capi
+from flashact_b200.build import build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "flashact.h")).read()
+    return sorted(set(re.findall(r"^FA_API\s+[\w\s\*]+?\b(fa_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_header_lists_match_binding():
+    assert declared_functions() == sorted(_capi.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(build())
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_create_without_gpu_fails_cleanly():
+    """On a box without an sm_100 GPU fa_create returns an error status, never crashes."""
+    import torch
+    if torch.cuda.is_available():
+        return
+    lib = _capi.load_library(build())
+    cfg = _capi.FaConfig(18, 1024, 8, 1, 256, 4096, 50, 32, 968, 1, 10)
+    h = ctypes.c_void_p()
+    st = lib.fa_create(_capi.FA_MODEL_PI05, ctypes.byref(cfg), 0, ctypes.byref(h))
+    assert st in (_capi.FA_ERR_INVALID, _capi.FA_ERR_CUDA, _capi.FA_ERR_UNSUPPORTED)
+    assert not h.value
+    assert len(lib.fa_last_error(None)) > 0
+
+
+def test_struct_layouts():
+    assert ctypes.sizeof(_capi.FaConfig) == 11 * 4
+    assert ctypes.sizeof(_capi.FaTensor) == 16
+    assert ctypes.sizeof(_capi.FaPi05Weights) == 21 * 16

@@ -1,0 +1,77 @@
+"""GPU parity of the pi0.5 megakernel (through the C ABI) against the CPU fp32 oracle.
+
+Tolerance (north_star): bf16 weights/activations vs the fp32 reference, max-abs 2e-2 on the
+action chunk."""
+import pytest
+import torch
+
+from oracle import pi05_oracle as O
+from tests.pi05_util import engine_for, err, oracle_bf16_kv, run_engine
+
+TOL = 2e-2
+pytestmark = pytest.mark.gpu
+
+
+def test_small_single(require_gpu):
+    c = O.make_case(seed=3, L=2, T=50, Lp=300, B=1, num_steps=2)
+    out, _ = run_engine(c)
+    ref = oracle_bf16_kv(c)
+    mx, cos = err(out, ref)
+    assert torch.isfinite(out).all()
+    assert mx < TOL and cos > 0.9999, (mx, cos)
+
+
+def test_small_batch_ragged_prefix(require_gpu):
+    """Observations with different valid prefix lengths (incl. a partial chunk and an empty
+    prefix): each uses its own RoPE positions and key mask."""
+    c = O.make_case(seed=4, L=2, T=50, Lp=300, B=3, num_steps=2, valid_len=[300, 77, 0])
+    out, _ = run_engine(c)
+    ref = oracle_bf16_kv(c)
+    mx, cos = err(out, ref)
+    assert mx < TOL and cos > 0.9999, (mx, cos)
+
+
+def test_short_horizon(require_gpu):
+    c = O.make_case(seed=5, L=1, T=10, AD=7, Lp=128, B=1, num_steps=3)
+    out, _ = run_engine(c)
+    mx, cos = err(out, oracle_bf16_kv(c))
+    assert mx < TOL, (mx, cos)
+
+
+def test_flashrt_interleaved_kv(require_gpu):
+    c = O.make_case(seed=6, L=2, T=50, Lp=200, B=1, num_steps=2)
+    out, _ = run_engine(c, layout="flashrt")
+    mx, cos = err(out, oracle_bf16_kv(c))
+    assert mx < TOL, (mx, cos)
+
+
+def test_deterministic_repeat(require_gpu):
+    c = O.make_case(seed=7, L=2, T=50, Lp=256, B=1, num_steps=2)
+    a, eng = run_engine(c)
+    b = eng.sample_actions(c.noise.cuda()).cpu()
+    assert torch.equal(a, b)
+
+
+def test_baseline_config_bs1(require_gpu):
+    """18 layers, T=50, Lp=968, N=10, bs=1, vs the fp32 oracle (C0)."""
+    c = O.make_case(seed=0)
+    out, _ = run_engine(c)
+    ref = O.denoise(c)  # fp32 KV and weights: the C0 reference actions
+    mx, cos = err(out, ref)
+    print(f"baseline bs=1 max_abs={mx:.4g} cos={cos:.7f}")
+    assert mx < TOL and cos > 0.999, (mx, cos)
+
+
+def test_barrier_timeout_reported(require_gpu):
+    """Host-side fault injection: block 0 skips a grid barrier; every wait is bounded, the launch
+    ends with its error word set, fa_sync reports FA_ERR_TIMEOUT and the context stays usable."""
+    from flashact_b200 import FlashActError
+    c = O.make_case(seed=8, L=1, T=50, Lp=128, B=1, num_steps=1)
+    good, eng = run_engine(c)
+    eng.inject_fault(barrier_index=3, spin_limit=20000)
+    with pytest.raises(FlashActError) as ei:
+        eng.sample_actions(c.noise.cuda())
+    assert "FA_ERR_TIMEOUT" in str(ei.value)
+    eng.inject_fault(-1, 0)
+    again = eng.sample_actions(c.noise.cuda()).cpu()
+    assert torch.equal(good, again)
