@@ -53,6 +53,8 @@ struct fa_handle {
   AttnUnit* d_aunits = nullptr;
   CtaPlan* d_plans = nullptr;
   size_t n_gunits_cap = 0, n_aunits_cap = 0;
+  unsigned long long* trace = nullptr;
+  int trace_step = -1, trace_layer = -1;
   Params params;
 };
 
@@ -233,7 +235,7 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
       c.max_prefix < 0 || c.max_prefix > MAX_CH * KCH || c.max_batch < 1 || c.max_batch > 1024 || c.num_steps < 1 ||
       c.num_steps > 50)
     return fail(nullptr, FA_ERR_INVALID,
-                "config out of range (layers 1..64, horizon 1..64, action_dim 1..32, max_prefix 0..4096, batch 1..1024, steps 1..50)");
+                "config out of range (layers 1..64, horizon 1..64, action_dim 1..32, max_prefix 0..3968, batch 1..1024, steps 1..50)");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
     cudaGetLastError();
@@ -539,9 +541,21 @@ static fa_status build_plan(fa_handle* h) {
       }
   }
   std::vector<GemmUnit> gu;
+  const int tile = h->NTILE * 128;
   for (int i = 0; i < nblk; ++i) {
-    const int R = (kSmemUse - (plans[i].a_cnt > 0 ? kAttnWork : kBSlots * h->NTILE * 128)) / kAtomBytes;
-    plans[i].ring_slots = std::min(kMaxRing, R);
+    // Activation area: the largest (unit, token group) K-range of this CTA, whole if it fits.
+    int bb = tile, ng = 0;
+    for (int m = 0; m < 4; ++m) {
+      ng += (int)per[i * 4 + m].size();
+      for (const GemmUnit& x : per[i * 4 + m]) bb = std::max(bb, (int)x.natoms * h->TG * tile);
+    }
+    if (ng > kMaxGU || plans[i].a_cnt > kMaxAU)
+      return fail(h, FA_ERR_INVALID, "batch too large for the per-CTA work lists (%d GEMM, %d attention units)", ng,
+                  plans[i].a_cnt);
+    bb = std::min(bb, std::min(kMaxBBytes, kMaxBAtoms * tile));
+    const int work = plans[i].a_cnt > 0 ? std::max(kAttnWork, bb) : bb;
+    plans[i].b_bytes = plans[i].a_cnt > 0 ? std::min(work, kMaxBBytes) : bb;
+    plans[i].ring_slots = std::min(kMaxRing, (kSmemUse - work) / kAtomBytes);
     for (int m = 0; m < 4; ++m) {
       plans[i].g_off[m] = (int)gu.size();
       plans[i].g_cnt[m] = (int)per[i * 4 + m].size();
@@ -587,6 +601,7 @@ static fa_status build_params(fa_handle* h) {
   p.ngroups = h->ngroups; p.nsteps = h->cfg.num_steps; p.LPAD = h->LPAD; p.AD = h->cfg.action_dim;
   p.split_o = h->split_o; p.split_dn = h->split_dn;
   p.dt = -1.0f / (float)h->cfg.num_steps;
+  p.invT = 1.0f / (float)h->cfg.horizon;
   p.gunits = h->d_gunits; p.aunits = h->d_aunits; p.plans = h->d_plans;
   p.valid_len = h->d_valid; p.nchunks = h->d_nchunks;
   p.mods = h->mods; p.mod_final = h->mod_final; p.rope_cos = h->rope_cos; p.rope_sin = h->rope_sin;
@@ -596,6 +611,9 @@ static fa_status build_params(fa_handle* h) {
   p.bar = h->ctrl; p.err = reinterpret_cast<int*>(h->ctrl + 1);
   p.stage_ns = nullptr;
   p.inject_barrier = -1;
+  p.trace = h->trace;
+  p.trace_step = h->trace_step;
+  p.trace_layer = h->trace_layer;
   p.spin_limit = 1u << 24;
   return FA_OK;
 }
@@ -691,6 +709,27 @@ extern "C" fa_status fa_sync(fa_handle* h, fa_stream stream) {
   unsigned int ctrl[2];
   FA_CUDA(h, cudaMemcpy(ctrl, h->ctrl, sizeof(ctrl), cudaMemcpyDeviceToHost));
   if (ctrl[1] != 0) return fail(h, FA_ERR_TIMEOUT, "in-kernel wait ran out (code %u)", ctrl[1]);
+  return FA_OK;
+}
+
+// Diagnostics: arm (step >= 0) or read back (step < 0) a clock64 trace of one (step, layer).
+extern "C" fa_status fa_debug_trace(fa_handle* h, int step, int layer, unsigned long long* host_out, int n) {
+  if (!h) return FA_ERR_INVALID;
+  const size_t need = (size_t)NUM_STAGES * h->num_sms * kTrStride;
+  FA_CUDA(h, cudaSetDevice(h->device));
+  if (step < 0) {
+    if (!h->trace) return fail(h, FA_ERR_STATE, "trace not armed");
+    FA_CUDA(h, cudaMemcpy(host_out, h->trace, std::min((size_t)std::max(n, 0), need) * 8, cudaMemcpyDeviceToHost));
+    return FA_OK;
+  }
+  if (!h->trace) {
+    fa_status st = dalloc(h, &h->trace, need);
+    if (st != FA_OK) return st;
+  }
+  FA_CUDA(h, cudaMemset(h->trace, 0, need * 8));
+  h->trace_step = h->params.trace_step = step;
+  h->trace_layer = h->params.trace_layer = layer;
+  h->params.trace = h->trace;
   return FA_OK;
 }
 

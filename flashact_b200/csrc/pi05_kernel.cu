@@ -47,6 +47,19 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// Observation index of packed token n = b * T + t without an integer division: exact for
+// n < 2^16 because (n + 0.5) / T stays at least 0.5 / T away from an integer.
+__device__ __forceinline__ int tok_b(const Params& p, int n) { return (int)(((float)n + 0.5f) * p.invT); }
+
+// Stage tracing (diagnostics): g_trp points at this CTA's stamps for the current stage (null
+// when the stage is not traced); g_t0 is the stage's start clock. Set by the barrier thread.
+__shared__ unsigned long long* g_trp;
+__shared__ unsigned long long g_t0;
+__device__ __forceinline__ void trace_mark(int slot) {
+  unsigned long long* tr = g_trp;
+  if (tr) tr[slot] = clock64() - g_t0;
+}
+
 // gelu with the tanh approximation (src/pi05/mk6.cu:79-82).
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;
@@ -56,10 +69,11 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 // Grid barrier among warps 1-5 of every CTA. `gen` counts barriers passed by this launch; the
 // counter only grows, so barrier k completes when it reaches (k+1) * gridDim.x. Bounded: on
 // timeout (or when another CTA already failed) it raises *err and returns false.
-__device__ bool grid_barrier(const Params& p, uint32_t& gen) {
+__device__ __noinline__ bool grid_barrier(const Params& p, uint32_t gen, unsigned long long* next_tr) {
   __shared__ int s_ok;
   sync_main();
   if (threadIdx.x == 32) {
+    trace_mark(kTrBarArrive);
     int ok = 1;
     __threadfence();
     fence_proxy_async_global();
@@ -77,9 +91,11 @@ __device__ bool grid_barrier(const Params& p, uint32_t& gen) {
     __threadfence();
     fence_proxy_async_global();
     s_ok = ok;
+    g_t0 = clock64();
+    g_trp = next_tr;
+    if (next_tr) next_tr[kTrStart] = g_t0;
   }
   sync_main();
-  ++gen;
   return s_ok != 0;
 }
 
@@ -99,6 +115,12 @@ __device__ __forceinline__ float epi_sum(float v, float* red) {
 // xn = x * rsqrt(mean(x^2) + 1e-6) * (1 + scale) + shift, stored as bf16 (src/pi05/mk6.cu:139-164).
 __device__ __forceinline__ void rms_store(const Params& p, int n, const float v[8], const float* mod, float* red) {
   const int e = threadIdx.x - 64;
+  float4 scs[2], shs[2];
+#pragma unroll
+  for (int hlf = 0; hlf < 2; ++hlf) {  // issue the modulation reads before the reduction
+    scs[hlf] = __ldg(reinterpret_cast<const float4*>(mod + hlf * 512 + e * 4));
+    shs[hlf] = __ldg(reinterpret_cast<const float4*>(mod + D + hlf * 512 + e * 4));
+  }
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
@@ -107,8 +129,8 @@ __device__ __forceinline__ void rms_store(const Params& p, int n, const float v[
 #pragma unroll
   for (int hlf = 0; hlf < 2; ++hlf) {
     const int d = hlf * 512 + e * 4;
-    const float4 sc = *reinterpret_cast<const float4*>(mod + d);
-    const float4 sh = *reinterpret_cast<const float4*>(mod + D + d);
+    const float4 sc = scs[hlf];
+    const float4 sh = shs[hlf];
     const float* w = v + hlf * 4;
     __nv_bfloat162 a = __floats2bfloat162_rn(w[0] * r * (1.f + sc.x) + sh.x, w[1] * r * (1.f + sc.y) + sh.y);
     __nv_bfloat162 b = __floats2bfloat162_rn(w[2] * r * (1.f + sc.z) + sh.z, w[3] * r * (1.f + sc.w) + sh.w);
@@ -121,23 +143,42 @@ __device__ __forceinline__ void rms_store(const Params& p, int n, const float v[
 
 // Loads x[n] and folds in `nsplit` fp32 partials scaled by `gate`: x += gate * sum_s part[s]
 // (the gated residual of the previous sub-block, summed in a fixed order: deterministic).
+// All loads are issued before any use so the row costs one memory round trip.
 __device__ __forceinline__ void load_residual(const Params& p, int n, const float* gate, int nsplit, float v[8]) {
   const int e = threadIdx.x - 64;
+  float4 x[2], acc[2], g[2];
 #pragma unroll
   for (int hlf = 0; hlf < 2; ++hlf) {
     const int d = hlf * 512 + e * 4;
-    float4 x = __ldcg(reinterpret_cast<const float4*>(p.x + (size_t)n * D + d));
-    if (nsplit > 0) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s = 0; s < nsplit; ++s) {
-        float4 q = __ldcg(reinterpret_cast<const float4*>(p.part + ((size_t)s * p.NPAD + n) * D + d));
-        acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
-      }
-      const float4 g = *reinterpret_cast<const float4*>(gate + d);
-      x.x += g.x * acc.x; x.y += g.y * acc.y; x.z += g.z * acc.z; x.w += g.w * acc.w;
-      *reinterpret_cast<float4*>(p.x + (size_t)n * D + d) = x;
+    x[hlf] = __ldcg(reinterpret_cast<const float4*>(p.x + (size_t)n * D + d));
+    acc[hlf] = make_float4(0.f, 0.f, 0.f, 0.f);
+    g[hlf] = nsplit > 0 ? __ldg(reinterpret_cast<const float4*>(gate + d)) : acc[hlf];
+  }
+  if (nsplit > 0) {
+    float4 q[8][2];
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+#pragma unroll
+      for (int hlf = 0; hlf < 2; ++hlf)
+        if (s < nsplit)
+          q[s][hlf] = __ldcg(reinterpret_cast<const float4*>(p.part + ((size_t)s * p.NPAD + n) * D + hlf * 512 + e * 4));
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+#pragma unroll
+      for (int hlf = 0; hlf < 2; ++hlf)
+        if (s < nsplit) {
+          acc[hlf].x += q[s][hlf].x; acc[hlf].y += q[s][hlf].y; acc[hlf].z += q[s][hlf].z; acc[hlf].w += q[s][hlf].w;
+        }
+#pragma unroll
+    for (int hlf = 0; hlf < 2; ++hlf) {
+      x[hlf].x += g[hlf].x * acc[hlf].x; x[hlf].y += g[hlf].y * acc[hlf].y;
+      x[hlf].z += g[hlf].z * acc[hlf].z; x[hlf].w += g[hlf].w * acc[hlf].w;
+      *reinterpret_cast<float4*>(p.x + (size_t)n * D + hlf * 512 + e * 4) = x[hlf];
     }
-    v[hlf * 4 + 0] = x.x; v[hlf * 4 + 1] = x.y; v[hlf * 4 + 2] = x.z; v[hlf * 4 + 3] = x.w;
+  }
+#pragma unroll
+  for (int hlf = 0; hlf < 2; ++hlf) {
+    v[hlf * 4 + 0] = x[hlf].x; v[hlf * 4 + 1] = x[hlf].y; v[hlf * 4 + 2] = x[hlf].z; v[hlf * 4 + 3] = x[hlf].w;
   }
 }
 
@@ -146,7 +187,7 @@ __device__ __forceinline__ const float* mod_ptr(const Params& p, int step, int l
 }
 
 // norm stage: x += gate * sum(partials); xn = adaRMS(x; mod). One token per CTA iteration.
-__device__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
+__device__ __noinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     float v[8];
     load_residual(p, n, gate, nsplit, v);
@@ -176,7 +217,7 @@ __device__ void embed_norm_token(const Params& p, int n, int step, const float* 
   rms_store(p, n, v, mod_ptr(p, step, 0, 0), red);
 }
 
-__device__ void stage_embed(const Params& p, float* xt_s, float* red) {
+__device__ __noinline__ void stage_embed(const Params& p, float* xt_s, float* red) {
   const int e = threadIdx.x - 64;
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     if (e < p.AD) xt_s[e] = p.x_t[(size_t)n * p.AD + e];
@@ -188,7 +229,7 @@ __device__ void stage_embed(const Params& p, float* xt_s, float* red) {
 
 // Final adaRMS (mod_final scale|shift), velocity head v = W_aout xn + b, Euler update
 // x_t += dt * v (src/pi05/mk6.cu:503-515), then the next step's embed + norm1.
-__device__ void stage_final(const Params& p, int step, float* xf, float* xt_s, float* red) {
+__device__ __noinline__ void stage_final(const Params& p, int step, float* xf, float* xt_s, float* red) {
   const int e = threadIdx.x - 64, lane = e & 31, w = e >> 5;
   const float* gate = mod_ptr(p, step, p.L - 1, 1) + 2 * D;
   const float* modf = p.mod_final + (size_t)step * MOD;
@@ -224,56 +265,72 @@ __device__ void stage_final(const Params& p, int step, float* xf, float* xt_s, f
 }
 
 // Merge the per-chunk attention partials (flash-decoding combine): for each (token, head),
-// out = sum_c w_c O_c / sum_c w_c with w_c = exp(m_c - M) l_c.
-__device__ void stage_merge(const Params& p) {
-  const int e = threadIdx.x - 64;
-  const int total = p.NT * H * (HD / 4);
-  for (int idx = blockIdx.x * 128 + e; idx < total; idx += gridDim.x * 128) {
-    const int n = idx / (H * (HD / 4));
-    const int h = (idx / (HD / 4)) % H;
-    const int d = (idx % (HD / 4)) * 4;
-    const int b = n / p.T, t = n % p.T, hp = h >> 1, r = (h & 1) * TPAD + t;
+// out = sum_c w_c O_c / sum_c w_c with w_c = 2^(m_c - M) l_c (maxima kept in log2 units).
+// One warp per (token, head); lane c reads chunk c's (max, sum), lanes own 8 dims each.
+__device__ __noinline__ void stage_merge(const Params& p) {
+  const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
+  const int total = p.NT * H;
+  for (int item = blockIdx.x * 4 + wq; item < total; item += gridDim.x * 4) {
+    const int n = item / H, h = item % H;
+    const int b = tok_b(p, n), t = n - b * p.T, hp = h >> 1, r = (h & 1) * TPAD + t;
     const int npc = p.nchunks[b];
     const size_t base = (size_t)(b * 4 + hp) * (MAX_CH + 1);
-    float M = -INFINITY;
-    for (int c = 0; c <= npc; ++c) {
-      const int cc = c < npc ? c : MAX_CH;
-      M = fmaxf(M, __ldcg(p.oml + ((base + cc) * 128 + r) * 2));
+    const int nc = npc + 1;  // prefix chunks + the action-token chunk (stored at MAX_CH); <= 32
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (lane < nc) {
+      const int cc = lane < npc ? lane : MAX_CH;
+      ml = __ldcg(reinterpret_cast<const float2*>(p.oml + ((base + cc) * 128 + r) * 2));
     }
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float wsum = 0.f;
-    for (int c = 0; c <= npc; ++c) {
+    const float M = warp_max(ml.x);
+    const float wgt_own = (lane < nc && ml.y > 0.f) ? exp2f(ml.x - M) * ml.y : 0.f;
+    const float wsum = warp_sum(wgt_own);
+    float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+    for (int c = 0; c < nc; ++c) {
+      const float wgt = __shfl_sync(0xffffffffu, wgt_own, c);
       const int cc = c < npc ? c : MAX_CH;
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.oml + ((base + cc) * 128 + r) * 2));
-      const float wgt = exp2f(ml.x - M) * ml.y;  // max kept in log2 units
-      const float4 o = __ldcg(reinterpret_cast<const float4*>(p.opart + ((base + cc) * 128 + r) * HD + d));
-      acc.x += wgt * o.x; acc.y += wgt * o.y; acc.z += wgt * o.z; acc.w += wgt * o.w;
-      wsum += wgt;
+      const float* src = p.opart + ((base + cc) * 128 + r) * HD + lane * 8;
+      const float4 o0 = __ldcg(reinterpret_cast<const float4*>(src));
+      const float4 o1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
+      acc0.x += wgt * o0.x; acc0.y += wgt * o0.y; acc0.z += wgt * o0.z; acc0.w += wgt * o0.w;
+      acc1.x += wgt * o1.x; acc1.y += wgt * o1.y; acc1.z += wgt * o1.z; acc1.w += wgt * o1.w;
     }
     const float inv = 1.f / wsum;
-    __nv_bfloat162 a = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-    __nv_bfloat162 bb = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
-    uint2 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&a);
-    pk.y = *reinterpret_cast<uint32_t*>(&bb);
-    *reinterpret_cast<uint2*>(p.attn + (size_t)n * QD + h * HD + d) = pk;
+    __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0.x * inv, acc0.y * inv);
+    __nv_bfloat162 b1 = __floats2bfloat162_rn(acc0.z * inv, acc0.w * inv);
+    __nv_bfloat162 b2 = __floats2bfloat162_rn(acc1.x * inv, acc1.y * inv);
+    __nv_bfloat162 b3 = __floats2bfloat162_rn(acc1.z * inv, acc1.w * inv);
+    *reinterpret_cast<uint4*>(p.attn + (size_t)n * QD + h * HD + lane * 8) =
+        make_uint4(*reinterpret_cast<uint32_t*>(&b0), *reinterpret_cast<uint32_t*>(&b1),
+                   *reinterpret_cast<uint32_t*>(&b2), *reinterpret_cast<uint32_t*>(&b3));
   }
 }
+
+// The producer and MMA roles run as whole warps (uniform control flow, every lane waits on
+// the same barriers) and only lane 0 issues TMA / tcgen05 / commit instructions.
+__device__ __forceinline__ bool leader() { return (threadIdx.x & 31) == 0; }
+#define FA_ONE(stmt)      \
+  do {                    \
+    if (leader()) { stmt; } \
+  } while (0)
 
 // ------------------------------------------------------------------ CTA context
 struct Bars {
   uint64_t wfull[kMaxRing], wempty[kMaxRing];
-  uint64_t bfull[kBSlots], bempty[kBSlots];
+  uint64_t bfull, bempty;  // activation batch loaded / consumed
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
 };
 struct Ctx {
-  uint8_t* ring;   // ring_slots x 16 KB
-  uint8_t* work;   // B slots (GEMM) or Q | K/V | P (attention)
+  uint8_t* ring;  // ring_slots x 16 KB
+  uint8_t* work;  // activation atoms (GEMM) or Q | K/V | P (attention)
   Bars* bars;
   uint32_t tmem;
   int ring_slots;
-  const CtaPlan* plan;
+  int batoms;               // activation atoms that fit in the work area at once
+  const GemmUnit* gu[4];    // this CTA's units per matrix (shared-memory copy of the plan)
+  int gcnt[4];
+  const AttnUnit* au;
+  int acnt;
 };
 
 __host__ __device__ constexpr int mat_rows(int m) {
@@ -291,107 +348,157 @@ __device__ __forceinline__ int group_tiles(const Params& p, int g) {
 // ------------------------------------------------------------------ warp 0: weight producer
 // Walks (step, layer, GEMM matrix, unit, token group, K atom) — the exact order the MMA lane
 // consumes — and keeps the ring full. It never waits on activations.
-__device__ void run_producer(const Params& p, Ctx& c) {
+__device__ __noinline__ void run_producer(const Params& p, const Ctx& c) {
+  // Every field is read once into registers: the inline-asm memory clobbers would otherwise
+  // force a reload through the generic Params/Ctx references after each TMA / mbarrier op.
   const uint64_t pol = policy_evict_first();
-  const int R = c.ring_slots;
+  const int R = c.ring_slots, nsteps = p.nsteps, L = p.L, ngroups = p.ngroups;
+  uint8_t* const ring = c.ring;
+  Bars* const bars = c.bars;
+  int* const err = p.err;
+  const CUtensorMap* const wmaps = &p.maps[MAP_W_QKV];
+  unsigned long long* const trace = p.trace;
+  const int tstep = p.trace_step, tlayer = p.trace_layer;
+  const GemmUnit* gul[4];
+  int gcnt[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) { gul[m] = c.gu[m]; gcnt[m] = c.gcnt[m]; }
   uint32_t it = 0;
   bool ok = true;
-  for (int step = 0; ok && step < p.nsteps; ++step)
-    for (int l = 0; ok && l < p.L; ++l)
+  for (int step = 0; ok && step < nsteps; ++step)
+    for (int l = 0; ok && l < L; ++l)
       for (int m = 0; ok && m < 4; ++m) {
         const int rows = mat_rows(m);
-        for (int u = 0; ok && u < c.plan->g_cnt[m]; ++u) {
-          const GemmUnit gu = p.gunits[c.plan->g_off[m] + u];
-          for (int g = 0; ok && g < p.ngroups; ++g)
+        for (int u = 0; ok && u < gcnt[m]; ++u) {
+          const GemmUnit gu = gul[m][u];
+          for (int g = 0; ok && g < ngroups; ++g)
             for (int j = 0; j < gu.natoms; ++j, ++it) {
               const int slot = it % R, round = it / R;
-              if (round > 0 && !mbar_wait(&c.bars->wempty[slot], (round - 1) & 1, p.err, KERR_PRODUCER)) {
+              if (round > 0 && !mbar_wait(&bars->wempty[slot], (round - 1) & 1, err, KERR_PRODUCER)) {
                 ok = false;
                 break;
               }
-              mbar_expect_tx(&c.bars->wfull[slot], kAtomBytes);
-              tma_load_2d(c.ring + (size_t)slot * kAtomBytes, &p.maps[MAP_W_QKV + m], &c.bars->wfull[slot],
-                          (gu.katom0 + j) * 64, l * rows + gu.mtile * 128, pol);
+              if (leader()) {
+                if (trace && u == 0 && g == 0 && j == 0 && step == tstep && l == tlayer) {
+                  const int stg = m == MAT_QKV ? ST_QKV : m == MAT_O ? ST_O : m == MAT_GU ? ST_GU : ST_DN;
+                  trace[((size_t)stg * gridDim.x + blockIdx.x) * kTrStride + kTrProdIssue] = clock64();
+                }
+                mbar_expect_tx(&bars->wfull[slot], kAtomBytes);
+                tma_load_2d(ring + (size_t)slot * kAtomBytes, wmaps + m, &bars->wfull[slot], (gu.katom0 + j) * 64,
+                            l * rows + gu.mtile * 128, pol);
+              }
+              __syncwarp();
             }
         }
       }
   // Drain: never leave a TMA write into shared memory in flight at exit.
   const uint32_t first = it > (uint32_t)R ? it - R : 0;
-  for (uint32_t k = first; k < it; ++k) mbar_wait(&c.bars->wfull[k % R], (k / R) & 1, p.err, KERR_PRODUCER);
+  for (uint32_t k = first; k < it; ++k) mbar_wait(&bars->wfull[k % R], (k / R) & 1, err, KERR_PRODUCER);
 }
 
 // ------------------------------------------------------------------ warp 1 lane 0: GEMM MMAs
+// MMA-lane state; lives in shared memory (one instance per CTA, touched by one thread).
 struct MmaState {
-  uint32_t wit = 0;       // weight-ring items consumed
-  uint32_t bis = 0, bcs = 0;  // activation items issued / consumed
-  uint32_t acc = 0;       // accumulator buffers used
-  uint32_t nq = 0, nu = 0;  // attention: Q loads, units
-  int last_q = -1;
+  uint32_t wit;          // weight-ring items consumed
+  uint32_t bload;        // activation batches loaded (phase of bfull)
+  uint32_t bfree;        // activation batches released (phase of bempty)
+  uint32_t acc;          // accumulator buffers used
+  uint32_t nq, nu;       // attention: Q loads, units
+  int last_q;
 };
 
-__device__ __forceinline__ void issue_b(const Params& p, Ctx& c, MmaState& st, int mapi, int x, int y) {
-  const int slot = st.bis % kBSlots, round = st.bis / kBSlots;
-  if (round > 0) mbar_wait(&c.bars->bempty[slot], (round - 1) & 1, p.err, KERR_MMA);
-  const uint32_t bytes = p.NTILE * 128;
-  mbar_expect_tx(&c.bars->bfull[slot], bytes);
-  tma_load_2d(c.work + (size_t)slot * (p.NTILE * 128), &p.maps[mapi], &c.bars->bfull[slot], x, y,
-              policy_evict_last());
-  ++st.bis;
+// Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
+// on ONE barrier so the MMA lane pays a single wait per batch. Item (j, i) sits at
+// work + ((j - j0) * nt + i) * tile bytes.
+// Register copy of what the GEMM MMA loop needs (see run_producer for why).
+struct MmaCtx {
+  uint8_t* ring;
+  uint8_t* work;
+  Bars* bars;
+  int* err;
+  const CUtensorMap* amap;
+  uint32_t tmem;
+  int R, batoms, NTILE, TG, ngroups, tiles;
+};
+
+// Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
+// on ONE barrier so the MMA lane pays a single wait per batch. Item (j, i) sits at
+// work + ((j - j0) * nt + i) * tile bytes.
+__device__ __forceinline__ void load_b_batch(const MmaCtx& k, const GemmUnit& gu, int g, int nt, int j0, int j1) {
+  if (!leader()) return;
+  const uint32_t tile = k.NTILE * 128;
+  mbar_expect_tx(&k.bars->bfull, (uint32_t)((j1 - j0) * nt) * tile);
+  const uint64_t pol = policy_evict_last();
+  const int y0 = g * k.TG * k.NTILE;
+  for (int j = j0; j < j1; ++j)
+    for (int i = 0; i < nt; ++i)
+      tma_load_2d(k.work + (size_t)((j - j0) * nt + i) * tile, k.amap, &k.bars->bfull, (gu.katom0 + j) * 64,
+                  y0 + i * k.NTILE, pol);
 }
 
-__device__ bool mma_gemm(const Params& p, Ctx& c, MmaState& st, int m) {
-  const int R = c.ring_slots;
-  const uint32_t idesc = idesc_bf16(128, p.NTILE);
-  const int mapi = act_map(m);
-  for (int u = 0; u < c.plan->g_cnt[m]; ++u) {
-    const GemmUnit gu = p.gunits[c.plan->g_off[m] + u];
-    for (int g = 0; g < p.ngroups; ++g) {
-      const int nt = group_tiles(p, g);
-      const int Q = gu.natoms * nt;
-      const uint32_t bbase = st.bcs;
-      auto item_xy = [&](int k, int& x, int& y) {
-        x = (gu.katom0 + k / nt) * 64;
-        y = g * p.TG * p.NTILE + (k % nt) * p.NTILE;
-      };
-      for (int k = 0; k < Q && k < kBSlots - 1; ++k) {
-        int x, y;
-        item_xy(k, x, y);
-        issue_b(p, c, st, mapi, x, y);
-      }
+__device__ __noinline__ bool mma_gemm(const Params& p, const Ctx& c, MmaState& st_shared, int m) {
+  MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
+  MmaCtx k;
+  k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[act_map(m)];
+  k.tmem = c.tmem; k.R = c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG; k.ngroups = p.ngroups;
+  k.tiles = p.NPAD / p.NTILE;
+  const GemmUnit* const units = c.gu[m];
+  const int nunits = c.gcnt[m];
+  const uint32_t idesc = idesc_bf16(128, k.NTILE);
+  const uint32_t tile = k.NTILE * 128;
+  Bars* const bars = k.bars;
+  for (int u = 0; u < nunits; ++u) {
+    const GemmUnit gu = units[u];
+    for (int g = 0; g < k.ngroups; ++g) {
+      const int nt = min(k.TG, k.tiles - g * k.TG);
+      const int per_batch = max(1, k.batoms / nt);  // K atoms per activation batch
+      int j1 = min((int)gu.natoms, per_batch);
+      load_b_batch(k, gu, g, nt, 0, j1);
+      if (u == 0 && g == 0) FA_ONE(trace_mark(kTrMmaPre));
       const int a = st.acc & 1;
-      if (st.acc >= 2 && !mbar_wait(&c.bars->acc_empty[a], ((st.acc >> 1) - 1) & 1, p.err, KERR_MMA)) return false;
+      if (st.acc >= 2 && !mbar_wait(&bars->acc_empty[a], ((st.acc >> 1) - 1) & 1, k.err, KERR_MMA)) return false;
       tc_fence_after();
-      const uint32_t tacc = c.tmem + a * 256;
-      for (int j = 0; j < gu.natoms; ++j) {
-        const int wslot = st.wit % R;
-        if (!mbar_wait(&c.bars->wfull[wslot], (st.wit / R) & 1, p.err, KERR_MMA)) return false;
-        tc_fence_after();
-        const uint64_t da = sdesc_sw128(c.ring + (size_t)wslot * kAtomBytes);
-        for (int i = 0; i < nt; ++i) {
-          const int k = j * nt + i;
-          const uint32_t bq = bbase + k;
-          const int bslot = bq % kBSlots;
-          if (!mbar_wait(&c.bars->bfull[bslot], (bq / kBSlots) & 1, p.err, KERR_MMA)) return false;
-          tc_fence_after();
-          const uint64_t db = sdesc_sw128(c.work + (size_t)bslot * (p.NTILE * 128));
+      const uint32_t tacc = k.tmem + a * 256;
+      for (int j0 = 0; j0 < gu.natoms;) {
+        if (!mbar_wait(&bars->bfull, st.bload & 1, k.err, KERR_MMA)) return false;
+        ++st.bload;
+        if (u == 0 && g == 0 && j0 == 0) FA_ONE(trace_mark(kTrMmaB0));
+        for (int j = j0; j < j1; ++j) {
+          const int wslot = st.wit % k.R;
+          if (!mbar_wait(&bars->wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
+          if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(kTrMmaW0));
+          const uint64_t da = sdesc_sw128(k.ring + (size_t)wslot * kAtomBytes);
+          if (leader()) {
+            for (int i = 0; i < nt; ++i) {
+              const uint64_t db = sdesc_sw128(k.work + (size_t)((j - j0) * nt + i) * tile);
 #pragma unroll
-          for (int s = 0; s < 4; ++s)
-            tc_mma_bf16(tacc + i * p.NTILE, da + 2 * s, db + 2 * s, idesc, (j | s) != 0);
-          tc_commit(&c.bars->bempty[bslot]);
-          if (k + kBSlots - 1 < Q) {
-            int x, y;
-            item_xy(k + kBSlots - 1, x, y);
-            issue_b(p, c, st, mapi, x, y);
+              for (int s = 0; s < 4; ++s) tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, (j | s) != 0);
+            }
+            tc_commit(&bars->wempty[wslot]);
           }
+          __syncwarp();
+          ++st.wit;
         }
-        tc_commit(&c.bars->wempty[wslot]);
-        ++st.wit;
+        j0 = j1;
+        if (j0 < gu.natoms) {  // reuse the activation area: wait for this batch's MMAs first
+          FA_ONE(tc_commit(&bars->bempty));
+          if (!mbar_wait(&bars->bempty, st.bfree & 1, k.err, KERR_MMA)) return false;
+          ++st.bfree;
+          j1 = min((int)gu.natoms, j0 + per_batch);
+          load_b_batch(k, gu, g, nt, j0, j1);
+        }
       }
-      st.bcs += Q;
-      tc_commit(&c.bars->acc_full[a]);
+      FA_ONE(tc_commit(&bars->acc_full[a]));
       ++st.acc;
     }
   }
+  // The next stage overwrites the activation area: its TMA loads must follow these MMAs.
+  FA_ONE(tc_commit(&bars->bempty));
+  if (!mbar_wait(&bars->bempty, st.bfree & 1, k.err, KERR_MMA)) return false;
+  ++st.bfree;
+  FA_ONE(trace_mark(kTrMmaDone));
+  if (leader()) st_shared = st;
+  __syncwarp();
   return true;
 }
 
@@ -399,68 +506,96 @@ __device__ bool mma_gemm(const Params& p, Ctx& c, MmaState& st, int m) {
 // TMEM lane = packed weight row (32 * quadrant + lane), columns = tokens of the tile.
 // Packed row orders (host packer) put rotary partners and gate/up partners 16 lanes apart in
 // the same warp, so the fused epilogues need one shuffle and no shared memory.
-__device__ bool epi_gemm(const Params& p, Ctx& c, uint32_t& ecnt, int m) {
+// Fused epilogue for 16 consecutive tokens (nb..nb+15) of one accumulator row.
+__device__ __forceinline__ void epi_tile(const Params& p, const GemmUnit& gu, int m, int qd, int lane, int row, int nb,
+                                         const float* v) {
+  if (m == MAT_QKV) {
+    const int mt = gu.mtile;
+    if (mt < 18) {  // Q heads (mtile 0..15) or K (16, 17): split-half RoPE epilogue
+      const int pb = mt < 16 ? (mt & 1) : mt - 16;
+      const int pr = 64 * pb + 16 * qd + (lane & 15);
+      const int hi = lane >> 4;
+      const int dim = pr + 128 * hi;
+      float cs[16], sn[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {  // batch the table reads before any use
+        const int n = min(nb + k, p.NT - 1);
+        cs[k] = __ldg(p.rope_cos + (size_t)n * 128 + pr);
+        sn[k] = __ldg(p.rope_sin + (size_t)n * 128 + pr);
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float x = v[k];
+        const float partner = __shfl_xor_sync(0xffffffffu, x, 16);
+        const int n = nb + k;
+        if (n < p.NT) {
+          const int b = tok_b(p, n), t = n - b * p.T;
+          const float o = hi ? fmaf(x, cs[k], partner * sn[k]) : fmaf(x, cs[k], -partner * sn[k]);
+          __nv_bfloat16* dst = mt < 16 ? p.q + ((size_t)(b * H + (mt >> 1)) * TPAD + t) * HD + dim
+                                       : p.sk + ((size_t)b * TPAD + t) * HD + dim;
+          *dst = __float2bfloat16(o);
+        }
+      }
+    } else {  // V: natural order, stored transposed [dim][token]: 8 tokens per 16-byte store
+      const int dim = (mt - 18) * 128 + row;
+#pragma unroll
+      for (int g8 = 0; g8 < 16; g8 += 8) {
+        const int n0 = nb + g8;
+        const int b0 = tok_b(p, n0), t0 = n0 - b0 * p.T;
+        if (n0 + 7 < p.NT && t0 + 7 < p.T && (t0 & 7) == 0) {
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(v[g8 + 2 * k], v[g8 + 2 * k + 1]);
+            w[k] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          *reinterpret_cast<uint4*>(p.svt + ((size_t)b0 * HD + dim) * TPAD + t0) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int n = n0 + k;
+            if (n < p.NT) {
+              const int b = tok_b(p, n), t = n - b * p.T;
+              p.svt[((size_t)b * HD + dim) * TPAD + t] = __float2bfloat16(v[g8 + k]);
+            }
+          }
+        }
+      }
+    }
+  } else if (m == MAT_GU) {  // GeGLU: lanes 0-15 gate rows, 16-31 up rows of one feature
+    const int f = 64 * gu.mtile + 16 * qd + (lane & 15);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float up = __shfl_xor_sync(0xffffffffu, v[k], 16);
+      const int n = nb + k;
+      if (lane < 16 && n < p.NT) p.hbuf[(size_t)n * F + f] = __float2bfloat16(gelu_tanh(v[k]) * up);
+    }
+  } else {  // O / down: fp32 K-split partial, each warp store covers 32 consecutive rows
+    float* dst = p.part + ((size_t)gu.split * p.NPAD + nb) * D + gu.mtile * 128 + row;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) dst[(size_t)k * D] = v[k];
+  }
+}
+
+__device__ __noinline__ uint32_t epi_gemm(const Params& p, const Ctx& c, uint32_t ecnt, int m) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int row = qd * 32 + lane;
   const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
-  for (int u = 0; u < c.plan->g_cnt[m]; ++u) {
-    const GemmUnit gu = p.gunits[c.plan->g_off[m] + u];
+  for (int u = 0; u < c.gcnt[m]; ++u) {
+    const GemmUnit gu = c.gu[m][u];
     for (int g = 0; g < p.ngroups; ++g) {
       const int nt = group_tiles(p, g);
       const int a = ecnt & 1;
-      if (!mbar_wait(&c.bars->acc_full[a], (ecnt >> 1) & 1, p.err, KERR_EPI)) return false;
+      if (!mbar_wait(&c.bars->acc_full[a], (ecnt >> 1) & 1, p.err, KERR_EPI)) return ecnt;
+      if (u == 0 && g == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
       tc_fence_after();
       for (int i = 0; i < nt; ++i) {
+#pragma unroll 1
         for (int cc = 0; cc < p.NTILE; cc += 16) {
           float v[16];
           tmem_ld16(c.tmem + lane_addr + a * 256 + i * p.NTILE + cc, v);
           tc_wait_ld();
-          const int n0 = g * p.TG * p.NTILE + i * p.NTILE + cc;
-          if (m == MAT_QKV) {
-            const int mt = gu.mtile;
-            if (mt < 18) {  // Q heads (mtile 0..15) or K (16, 17): split-half RoPE epilogue
-              const int pb = mt < 16 ? (mt & 1) : mt - 16;
-              const int pr = 64 * pb + 16 * qd + (lane & 15);
-              const int hi = lane >> 4;
-#pragma unroll
-              for (int k = 0; k < 16; ++k) {
-                const float partner = __shfl_xor_sync(0xffffffffu, v[k], 16);
-                const int n = n0 + k;
-                if (n < p.NT) {
-                  const int b = n / p.T, t = n - b * p.T;
-                  const float cs = p.rope_cos[(size_t)n * 128 + pr], sn = p.rope_sin[(size_t)n * 128 + pr];
-                  const float o = hi ? fmaf(v[k], cs, partner * sn) : fmaf(v[k], cs, -partner * sn);
-                  const int dim = pr + 128 * hi;
-                  if (mt < 16)
-                    p.q[((size_t)(b * H + (mt >> 1)) * TPAD + t) * HD + dim] = __float2bfloat16(o);
-                  else
-                    p.sk[((size_t)b * TPAD + t) * HD + dim] = __float2bfloat16(o);
-                }
-              }
-            } else {  // V: natural order, stored transposed [dim][token]
-              const int dim = (mt - 18) * 128 + row;
-#pragma unroll
-              for (int k = 0; k < 16; ++k) {
-                const int n = n0 + k;
-                if (n < p.NT) {
-                  const int b = n / p.T, t = n - b * p.T;
-                  p.svt[((size_t)b * HD + dim) * TPAD + t] = __float2bfloat16(v[k]);
-                }
-              }
-            }
-          } else if (m == MAT_GU) {  // GeGLU: lanes 0-15 gate rows, 16-31 up rows of one feature
-            const int f = 64 * gu.mtile + 16 * qd + (lane & 15);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              const float up = __shfl_xor_sync(0xffffffffu, v[k], 16);
-              const int n = n0 + k;
-              if (lane < 16 && n < p.NT) p.hbuf[(size_t)n * F + f] = __float2bfloat16(gelu_tanh(v[k]) * up);
-            }
-          } else {  // O / down: fp32 K-split partial
-            float* dst = p.part + ((size_t)gu.split * p.NPAD + n0) * D + gu.mtile * 128 + row;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) dst[(size_t)k * D] = v[k];
-          }
+          epi_tile(p, gu, m, qd, lane, row, g * p.TG * p.NTILE + i * p.NTILE + cc, v);
         }
       }
       tc_fence_before();
@@ -468,7 +603,7 @@ __device__ bool epi_gemm(const Params& p, Ctx& c, uint32_t& ecnt, int m) {
       ++ecnt;
     }
   }
-  return true;
+  return ecnt;
 }
 
 // ------------------------------------------------------------------ attention (split-KV)
@@ -479,30 +614,31 @@ __device__ bool epi_gemm(const Params& p, Ctx& c, uint32_t& ecnt, int m) {
 // (TMEM cols 128..383) -> normalised partial + (max, sum) to global, merged by stage_merge.
 constexpr int kQOff = 0, kKVOff = 64 * 1024, kPOff = 128 * 1024;
 
-__device__ bool mma_attn(const Params& p, Ctx& c, MmaState& st, int l) {
+__device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& st_shared, int l) {
+  MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
   const uint64_t pol_kv = policy_evict_last();
   Bars* br = c.bars;
-  for (int u = 0; u < c.plan->a_cnt; ++u) {
-    const AttnUnit au = p.aunits[c.plan->a_off + u];
+  for (int u = 0; u < c.acnt; ++u) {
+    const AttnUnit au = c.au[u];
     const int nk = au.is_suffix ? TPAD : KCH;
     const int qkey = au.b * 4 + au.hp;
     if (qkey != st.last_q) {  // previous unit's S MMAs completed (kv_free waited), Q is free
-      mbar_expect_tx(&br->q_full, 4 * kAtomBytes);
+      FA_ONE(mbar_expect_tx(&br->q_full, 4 * kAtomBytes));
       for (int a = 0; a < 4; ++a)
-        tma_load_2d(c.work + kQOff + a * kAtomBytes, &p.maps[MAP_Q], &br->q_full, a * 64,
-                    (au.b * H + 2 * au.hp) * TPAD, pol_kv);
+        FA_ONE(tma_load_2d(c.work + kQOff + a * kAtomBytes, &p.maps[MAP_Q], &br->q_full, a * 64,
+                    (au.b * H + 2 * au.hp) * TPAD, pol_kv));
       if (!mbar_wait(&br->q_full, st.nq & 1, p.err, KERR_ATTN)) return false;
       ++st.nq;
       st.last_q = qkey;
     }
     if (st.nu > 0 && !mbar_wait(&br->v_free, (st.nu - 1) & 1, p.err, KERR_ATTN)) return false;
-    mbar_expect_tx(&br->k_full, 4 * nk * 128);
+    FA_ONE(mbar_expect_tx(&br->k_full, 4 * nk * 128));
     for (int a = 0; a < 4; ++a) {
       if (au.is_suffix)
-        tma_load_2d(c.work + kKVOff + a * kAtomBytes, &p.maps[MAP_SK], &br->k_full, a * 64, au.b * TPAD, pol_kv);
+        FA_ONE(tma_load_2d(c.work + kKVOff + a * kAtomBytes, &p.maps[MAP_SK], &br->k_full, a * 64, au.b * TPAD, pol_kv));
       else
-        tma_load_2d(c.work + kKVOff + a * kAtomBytes, &p.maps[MAP_K], &br->k_full, a * 64,
-                    (au.b * p.L + l) * p.LPAD + au.chunk * KCH, pol_kv);
+        FA_ONE(tma_load_2d(c.work + kKVOff + a * kAtomBytes, &p.maps[MAP_K], &br->k_full, a * 64,
+                    (au.b * p.L + l) * p.LPAD + au.chunk * KCH, pol_kv));
     }
     if (!mbar_wait(&br->k_full, st.nu & 1, p.err, KERR_ATTN)) return false;
     tc_fence_after();
@@ -511,21 +647,21 @@ __device__ bool mma_attn(const Params& p, Ctx& c, MmaState& st, int l) {
       const uint64_t dq = sdesc_sw128(c.work + kQOff + a * kAtomBytes);
       const uint64_t dk = sdesc_sw128(c.work + kKVOff + a * kAtomBytes);
 #pragma unroll
-      for (int s = 0; s < 4; ++s) tc_mma_bf16(c.tmem, dq + 2 * s, dk + 2 * s, id_s, (a | s) != 0);
+      for (int s = 0; s < 4; ++s) FA_ONE(tc_mma_bf16(c.tmem, dq + 2 * s, dk + 2 * s, id_s, (a | s) != 0));
     }
-    tc_commit(&br->s_full);
-    tc_commit(&br->kv_free);
+    FA_ONE(tc_commit(&br->s_full));
+    FA_ONE(tc_commit(&br->kv_free));
     if (!mbar_wait(&br->kv_free, st.nu & 1, p.err, KERR_ATTN)) return false;
     const int nka = nk / 64;  // 64-key atoms
-    mbar_expect_tx(&br->v_full, nka * 2 * kAtomBytes);
+    FA_ONE(mbar_expect_tx(&br->v_full, nka * 2 * kAtomBytes));
     for (int kk = 0; kk < nka; ++kk)
       for (int hh = 0; hh < 2; ++hh) {
         uint8_t* dst = c.work + kKVOff + (kk * 2 + hh) * kAtomBytes;
         if (au.is_suffix)
-          tma_load_2d(dst, &p.maps[MAP_SVT], &br->v_full, 0, au.b * HD + 128 * hh, pol_kv);
+          FA_ONE(tma_load_2d(dst, &p.maps[MAP_SVT], &br->v_full, 0, au.b * HD + 128 * hh, pol_kv));
         else
-          tma_load_2d(dst, &p.maps[MAP_VT], &br->v_full, au.chunk * KCH + 64 * kk, (au.b * p.L + l) * HD + 128 * hh,
-                      pol_kv);
+          FA_ONE(tma_load_2d(dst, &p.maps[MAP_VT], &br->v_full, au.chunk * KCH + 64 * kk, (au.b * p.L + l) * HD + 128 * hh,
+                      pol_kv));
       }
     if (!mbar_wait(&br->v_full, st.nu & 1, p.err, KERR_ATTN)) return false;
     if (!mbar_wait(&br->p_full, st.nu & 1, p.err, KERR_ATTN)) return false;
@@ -537,27 +673,29 @@ __device__ bool mma_attn(const Params& p, Ctx& c, MmaState& st, int l) {
       for (int hh = 0; hh < 2; ++hh) {
         const uint64_t dv = sdesc_sw128(c.work + kKVOff + (kk * 2 + hh) * kAtomBytes);
 #pragma unroll
-        for (int s = 0; s < 4; ++s) tc_mma_bf16(c.tmem + 128 + 128 * hh, dp + 2 * s, dv + 2 * s, id_o, (kk | s) != 0);
+        for (int s = 0; s < 4; ++s) FA_ONE(tc_mma_bf16(c.tmem + 128 + 128 * hh, dp + 2 * s, dv + 2 * s, id_o, (kk | s) != 0));
       }
     }
-    tc_commit(&br->o_full);
-    tc_commit(&br->v_free);
+    FA_ONE(tc_commit(&br->o_full));
+    FA_ONE(tc_commit(&br->v_free));
     ++st.nu;
   }
+  if (leader()) st_shared = st;
+  __syncwarp();
   return true;
 }
 
-__device__ bool epi_attn(const Params& p, Ctx& c, uint32_t& anu) {
+__device__ __noinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint32_t anu) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int r = qd * 32 + lane;
   const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
   const float sl2 = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256) in log2 units
   Bars* br = c.bars;
-  for (int u = 0; u < c.plan->a_cnt; ++u) {
-    const AttnUnit au = p.aunits[c.plan->a_off + u];
+  for (int u = 0; u < c.acnt; ++u) {
+    const AttnUnit au = c.au[u];
     const int nk = au.is_suffix ? TPAD : KCH;
     const int nvalid = au.is_suffix ? p.T : min(KCH, p.valid_len[au.b] - au.chunk * KCH);
-    if (!mbar_wait(&br->s_full, anu & 1, p.err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->s_full, anu & 1, p.err, KERR_ATTN)) return anu;
     tc_fence_after();
     float mx = -INFINITY;
     for (int cc = 0; cc < nk; cc += 16) {
@@ -591,7 +729,7 @@ __device__ bool epi_attn(const Params& p, Ctx& c, uint32_t& anu) {
     fence_proxy_async_shared();
     tc_fence_before();
     mbar_arrive(&br->p_full);
-    if (!mbar_wait(&br->o_full, anu & 1, p.err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->o_full, anu & 1, p.err, KERR_ATTN)) return anu;
     tc_fence_after();
     const int cidx = au.is_suffix ? MAX_CH : au.chunk;
     const size_t slot = ((size_t)(au.b * 4 + au.hp) * (MAX_CH + 1) + cidx) * 128 + r;
@@ -610,7 +748,7 @@ __device__ bool epi_attn(const Params& p, Ctx& c, uint32_t& anu) {
     mbar_arrive(&br->o_free);
     ++anu;
   }
-  return true;
+  return anu;
 }
 
 // ------------------------------------------------------------------ kernel
@@ -620,18 +758,46 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   __shared__ uint32_t s_tmem;
   __shared__ float s_red[8];
   __shared__ float s_xt[32];
+  __shared__ CtaPlan s_plan;
+  __shared__ GemmUnit s_gu[kMaxGU];
+  __shared__ AttnUnit s_au[kMaxAU];
 
+  __shared__ Ctx s_c;        // per-CTA constants, shared so that no role keeps them on its stack
+  __shared__ MmaState s_st;  // MMA-lane state
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  Ctx c;
-  c.plan = p.plans + blockIdx.x;
-  c.ring_slots = c.plan->ring_slots;
+  Ctx& c = s_c;
+  if (threadIdx.x == 0) {
+    s_plan = p.plans[blockIdx.x];
+    g_trp = nullptr;
+    s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = 0;
+    s_st.last_q = -1;
+  }
+  __syncthreads();
+  {  // this CTA's work lists, read once from global memory
+    int ng = 0;
+    for (int m = 0; m < 4; ++m) ng += s_plan.g_cnt[m];
+    for (int i = threadIdx.x; i < ng; i += blockDim.x) s_gu[i] = p.gunits[s_plan.g_off[0] + i];
+    for (int i = threadIdx.x; i < s_plan.a_cnt; i += blockDim.x) s_au[i] = p.aunits[s_plan.a_off + i];
+  }
+  if (threadIdx.x == 0) {
+  for (int m = 0, off = 0; m < 4; ++m) {
+    c.gu[m] = s_gu + off;
+    c.gcnt[m] = s_plan.g_cnt[m];
+    off += s_plan.g_cnt[m];
+  }
+  c.au = s_au;
+  c.acnt = s_plan.a_cnt;
+  c.batoms = min(kMaxBAtoms, s_plan.b_bytes / (p.NTILE * 128));
+  c.ring_slots = s_plan.ring_slots;
   c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   c.work = c.ring + (size_t)c.ring_slots * kAtomBytes;
   c.bars = &bars;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], 1); }
-    for (int i = 0; i < kBSlots; ++i) { mbar_init(&bars.bfull[i], 1); mbar_init(&bars.bempty[i], 1); }
+    mbar_init(&bars.bfull, 1);
+    mbar_init(&bars.bempty, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&bars.acc_full[i], 1); mbar_init(&bars.acc_empty[i], 128); }
     mbar_init(&bars.q_full, 1); mbar_init(&bars.k_full, 1); mbar_init(&bars.v_full, 1);
     mbar_init(&bars.kv_free, 1); mbar_init(&bars.v_free, 1); mbar_init(&bars.s_full, 1);
@@ -647,15 +813,16 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  c.tmem = s_tmem;
+  if (threadIdx.x == 0) c.tmem = s_tmem;
+  __syncthreads();
 
   if (warp == 0) {
-    if (lane == 0) run_producer(p, c);
+    run_producer(p, c);
     __syncwarp();
   } else {
-    const bool is_mma = (threadIdx.x == 32);
+    const bool is_mma = (warp == 1);
     const bool is_epi = warp >= 2;
-    MmaState st;
+    MmaState& st = s_st;
     uint32_t ecnt = 0, anu = 0, gen = 0;
     uint64_t t_prev = globaltimer();
     const bool timing = p.stage_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 32;
@@ -668,53 +835,70 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
     };
     // Each stage: role work, then a grid barrier. *err is the single failure signal.
     bool ok = true;
+    auto tr = [&](int stage, int step, int l) -> unsigned long long* {
+      if (!p.trace || step != p.trace_step || l != p.trace_layer) return nullptr;
+      return p.trace + ((size_t)stage * gridDim.x + blockIdx.x) * kTrStride;
+    };
+    auto epi_done = [&]() {
+      if (threadIdx.x == 64) trace_mark(kTrEpiDone);
+    };
     if (is_epi) stage_embed(p, s_xt, s_red);
-    ok = grid_barrier(p, gen);
+    ok = grid_barrier(p, gen++, tr(ST_QKV, 0, 0));
     mark(ST_NORM1);
     for (int step = 0; ok && step < p.nsteps; ++step) {
       for (int l = 0; ok && l < p.L; ++l) {
         const float* mod_in = mod_ptr(p, step, l, 0);
         const float* mod_post = mod_ptr(p, step, l, 1);
         if (is_mma) mma_gemm(p, c, st, MAT_QKV);
-        if (is_epi) epi_gemm(p, c, ecnt, MAT_QKV);
-        if (!(ok = grid_barrier(p, gen))) break;
+        if (is_epi) ecnt = epi_gemm(p, c, ecnt, MAT_QKV);
+        epi_done();
+        if (!(ok = grid_barrier(p, gen++, tr(ST_ATTN, step, l)))) break;
         mark(ST_QKV);
-        st.last_q = -1;
+        if (is_mma && leader()) st.last_q = -1;
+        __syncwarp();
         if (is_mma) mma_attn(p, c, st, l);
-        if (is_epi) epi_attn(p, c, anu);
-        if (!(ok = grid_barrier(p, gen))) break;
+        if (is_epi) anu = epi_attn(p, c, anu);
+        epi_done();
+        if (!(ok = grid_barrier(p, gen++, tr(ST_MERGE, step, l)))) break;
         mark(ST_ATTN);
         if (is_epi) stage_merge(p);
-        if (!(ok = grid_barrier(p, gen))) break;
+        epi_done();
+        if (!(ok = grid_barrier(p, gen++, tr(ST_O, step, l)))) break;
         mark(ST_MERGE);
         if (is_mma) mma_gemm(p, c, st, MAT_O);
-        if (is_epi) epi_gemm(p, c, ecnt, MAT_O);
-        if (!(ok = grid_barrier(p, gen))) break;
+        if (is_epi) ecnt = epi_gemm(p, c, ecnt, MAT_O);
+        epi_done();
+        if (!(ok = grid_barrier(p, gen++, tr(ST_NORM2, step, l)))) break;
         mark(ST_O);
         if (is_epi) stage_norm(p, mod_in + 2 * D, p.split_o, mod_post, s_red);
-        if (!(ok = grid_barrier(p, gen))) break;
+        epi_done();
+        if (!(ok = grid_barrier(p, gen++, tr(ST_GU, step, l)))) break;
         mark(ST_NORM2);
         if (is_mma) mma_gemm(p, c, st, MAT_GU);
-        if (is_epi) epi_gemm(p, c, ecnt, MAT_GU);
-        if (!(ok = grid_barrier(p, gen))) break;
+        if (is_epi) ecnt = epi_gemm(p, c, ecnt, MAT_GU);
+        epi_done();
+        if (!(ok = grid_barrier(p, gen++, tr(ST_DN, step, l)))) break;
         mark(ST_GU);
         if (is_mma) mma_gemm(p, c, st, MAT_DN);
-        if (is_epi) epi_gemm(p, c, ecnt, MAT_DN);
-        if (!(ok = grid_barrier(p, gen))) break;
+        if (is_epi) ecnt = epi_gemm(p, c, ecnt, MAT_DN);
+        epi_done();
+        if (!(ok = grid_barrier(p, gen++, tr(l + 1 < p.L ? ST_NORM1 : ST_FINAL, step, l)))) break;
         mark(ST_DN);
         if (l + 1 < p.L) {
           if (is_epi) stage_norm(p, mod_post + 2 * D, p.split_dn, mod_ptr(p, step, l + 1, 0), s_red);
-          if (!(ok = grid_barrier(p, gen))) break;
+          epi_done();
+          if (!(ok = grid_barrier(p, gen++, tr(ST_QKV, step, l + 1)))) break;
           mark(ST_NORM1);
         } else {
           if (is_epi) stage_final(p, step, reinterpret_cast<float*>(c.work), s_xt, s_red);  // work area idle here
-          if (!(ok = grid_barrier(p, gen))) break;
+          epi_done();
+          if (!(ok = grid_barrier(p, gen++, tr(ST_QKV, step + 1, 0)))) break;
           mark(ST_FINAL);
         }
       }
     }
-    if (is_mma) {  // retire every MMA this thread issued before TMEM is released
-      tc_commit(&bars.drain);
+    if (is_mma) {  // retire every MMA this warp issued before TMEM is released
+      FA_ONE(tc_commit(&bars.drain));
       mbar_wait(&bars.drain, 0, p.err, KERR_MMA);
     }
     __syncwarp();
