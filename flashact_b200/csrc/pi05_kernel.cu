@@ -49,7 +49,8 @@ __device__ __forceinline__ uint64_t globaltimer() {
 
 // Observation index of packed token n = b * T + t without an integer division: exact for
 // n < 2^16 because (n + 0.5) / T stays at least 0.5 / T away from an integer.
-__device__ __forceinline__ int tok_b(const Params& p, int n) { return (int)(((float)n + 0.5f) * p.invT); }
+__device__ __forceinline__ int tok_bi(float invT, int n) { return (int)(((float)n + 0.5f) * invT); }
+__device__ __forceinline__ int tok_b(const Params& p, int n) { return tok_bi(p.invT, n); }
 
 // Stage tracing (diagnostics): g_trp points at this CTA's stamps for the current stage (null
 // when the stage is not traced); g_t0 is the stage's start clock. Set by the barrier thread.
@@ -268,18 +269,26 @@ __device__ __noinline__ void stage_final(const Params& p, int step, float* xf, f
 // out = sum_c w_c O_c / sum_c w_c with w_c = 2^(m_c - M) l_c (maxima kept in log2 units).
 // One warp per (token, head); lane c reads chunk c's (max, sum), lanes own 8 dims each.
 __device__ __noinline__ void stage_merge(const Params& p) {
+  // register copies: the asm memory clobbers would force reloads through the references
+  const int p_NT = p.NT;
+  const int p_T = p.T;
+  __nv_bfloat16* const p_attn = p.attn;
+  const int* const p_nchunks = p.nchunks;
+  float* const p_oml = p.oml;
+  float* const p_opart = p.opart;
+  const float p_invT = p.invT;
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
-  const int total = p.NT * H;
+  const int total = p_NT * H;
   for (int item = blockIdx.x * 4 + wq; item < total; item += gridDim.x * 4) {
     const int n = item / H, h = item % H;
-    const int b = tok_b(p, n), t = n - b * p.T, hp = h >> 1, r = (h & 1) * TPAD + t;
-    const int npc = p.nchunks[b];
+    const int b = tok_bi(p_invT, n), t = n - b * p_T, hp = h >> 1, r = (h & 1) * TPAD + t;
+    const int npc = p_nchunks[b];
     const size_t base = (size_t)(b * 4 + hp) * (MAX_CH + 1);
     const int nc = npc + 1;  // prefix chunks + the action-token chunk (stored at MAX_CH); <= 32
     float2 ml = make_float2(-INFINITY, 0.f);
     if (lane < nc) {
       const int cc = lane < npc ? lane : MAX_CH;
-      ml = __ldcg(reinterpret_cast<const float2*>(p.oml + ((base + cc) * 128 + r) * 2));
+      ml = __ldcg(reinterpret_cast<const float2*>(p_oml + ((base + cc) * 128 + r) * 2));
     }
     const float M = warp_max(ml.x);
     const float wgt_own = (lane < nc && ml.y > 0.f) ? exp2f(ml.x - M) * ml.y : 0.f;
@@ -288,7 +297,7 @@ __device__ __noinline__ void stage_merge(const Params& p) {
     for (int c = 0; c < nc; ++c) {
       const float wgt = __shfl_sync(0xffffffffu, wgt_own, c);
       const int cc = c < npc ? c : MAX_CH;
-      const float* src = p.opart + ((base + cc) * 128 + r) * HD + lane * 8;
+      const float* src = p_opart + ((base + cc) * 128 + r) * HD + lane * 8;
       const float4 o0 = __ldcg(reinterpret_cast<const float4*>(src));
       const float4 o1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
       acc0.x += wgt * o0.x; acc0.y += wgt * o0.y; acc0.z += wgt * o0.z; acc0.w += wgt * o0.w;
@@ -299,7 +308,7 @@ __device__ __noinline__ void stage_merge(const Params& p) {
     __nv_bfloat162 b1 = __floats2bfloat162_rn(acc0.z * inv, acc0.w * inv);
     __nv_bfloat162 b2 = __floats2bfloat162_rn(acc1.x * inv, acc1.y * inv);
     __nv_bfloat162 b3 = __floats2bfloat162_rn(acc1.z * inv, acc1.w * inv);
-    *reinterpret_cast<uint4*>(p.attn + (size_t)n * QD + h * HD + lane * 8) =
+    *reinterpret_cast<uint4*>(p_attn + (size_t)n * QD + h * HD + lane * 8) =
         make_uint4(*reinterpret_cast<uint32_t*>(&b0), *reinterpret_cast<uint32_t*>(&b1),
                    *reinterpret_cast<uint32_t*>(&b2), *reinterpret_cast<uint32_t*>(&b3));
   }
@@ -507,7 +516,20 @@ __device__ __noinline__ bool mma_gemm(const Params& p, const Ctx& c, MmaState& s
 // Packed row orders (host packer) put rotary partners and gate/up partners 16 lanes apart in
 // the same warp, so the fused epilogues need one shuffle and no shared memory.
 // Fused epilogue for 16 consecutive tokens (nb..nb+15) of one accumulator row.
-__device__ __forceinline__ void epi_tile(const Params& p, const GemmUnit& gu, int m, int qd, int lane, int row, int nb,
+// Register copy of the fields the GEMM epilogues touch (see run_producer for why).
+struct EpiCtx {
+  int NT, T, NPAD;
+  float invT;
+  const float* rope_cos;
+  const float* rope_sin;
+  __nv_bfloat16* q;
+  __nv_bfloat16* sk;
+  __nv_bfloat16* svt;
+  __nv_bfloat16* hbuf;
+  float* part;
+};
+
+__device__ __forceinline__ void epi_tile(const EpiCtx& p, const GemmUnit& gu, int m, int qd, int lane, int row, int nb,
                                          const float* v) {
   if (m == MAT_QKV) {
     const int mt = gu.mtile;
@@ -529,7 +551,7 @@ __device__ __forceinline__ void epi_tile(const Params& p, const GemmUnit& gu, in
         const float partner = __shfl_xor_sync(0xffffffffu, x, 16);
         const int n = nb + k;
         if (n < p.NT) {
-          const int b = tok_b(p, n), t = n - b * p.T;
+          const int b = tok_bi(p.invT, n), t = n - b * p.T;
           const float o = hi ? fmaf(x, cs[k], partner * sn[k]) : fmaf(x, cs[k], -partner * sn[k]);
           __nv_bfloat16* dst = mt < 16 ? p.q + ((size_t)(b * H + (mt >> 1)) * TPAD + t) * HD + dim
                                        : p.sk + ((size_t)b * TPAD + t) * HD + dim;
@@ -541,7 +563,7 @@ __device__ __forceinline__ void epi_tile(const Params& p, const GemmUnit& gu, in
 #pragma unroll
       for (int g8 = 0; g8 < 16; g8 += 8) {
         const int n0 = nb + g8;
-        const int b0 = tok_b(p, n0), t0 = n0 - b0 * p.T;
+        const int b0 = tok_bi(p.invT, n0), t0 = n0 - b0 * p.T;
         if (n0 + 7 < p.NT && t0 + 7 < p.T && (t0 & 7) == 0) {
           uint32_t w[4];
 #pragma unroll
@@ -555,7 +577,7 @@ __device__ __forceinline__ void epi_tile(const Params& p, const GemmUnit& gu, in
           for (int k = 0; k < 8; ++k) {
             const int n = n0 + k;
             if (n < p.NT) {
-              const int b = tok_b(p, n), t = n - b * p.T;
+              const int b = tok_bi(p.invT, n), t = n - b * p.T;
               p.svt[((size_t)b * HD + dim) * TPAD + t] = __float2bfloat16(v[g8 + k]);
             }
           }
@@ -580,26 +602,34 @@ __device__ __forceinline__ void epi_tile(const Params& p, const GemmUnit& gu, in
 __device__ __noinline__ uint32_t epi_gemm(const Params& p, const Ctx& c, uint32_t ecnt, int m) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int row = qd * 32 + lane;
-  const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
-  for (int u = 0; u < c.gcnt[m]; ++u) {
-    const GemmUnit gu = c.gu[m][u];
-    for (int g = 0; g < p.ngroups; ++g) {
-      const int nt = group_tiles(p, g);
+  EpiCtx e;
+  e.NT = p.NT; e.T = p.T; e.NPAD = p.NPAD; e.invT = p.invT; e.rope_cos = p.rope_cos; e.rope_sin = p.rope_sin;
+  e.q = p.q; e.sk = p.sk; e.svt = p.svt; e.hbuf = p.hbuf; e.part = p.part;
+  const int NTILE = p.NTILE, TG = p.TG, ngroups = p.ngroups, tiles = p.NPAD / p.NTILE;
+  int* const err = p.err;
+  Bars* const bars = c.bars;
+  const uint32_t taddr = c.tmem + ((uint32_t)(qd * 32) << 16);
+  const GemmUnit* const units = c.gu[m];
+  const int nunits = c.gcnt[m];
+  for (int u = 0; u < nunits; ++u) {
+    const GemmUnit gu = units[u];
+    for (int g = 0; g < ngroups; ++g) {
+      const int nt = min(TG, tiles - g * TG);
       const int a = ecnt & 1;
-      if (!mbar_wait(&c.bars->acc_full[a], (ecnt >> 1) & 1, p.err, KERR_EPI)) return ecnt;
+      if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;
       if (u == 0 && g == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
       tc_fence_after();
       for (int i = 0; i < nt; ++i) {
 #pragma unroll 1
-        for (int cc = 0; cc < p.NTILE; cc += 16) {
+        for (int cc = 0; cc < NTILE; cc += 16) {
           float v[16];
-          tmem_ld16(c.tmem + lane_addr + a * 256 + i * p.NTILE + cc, v);
+          tmem_ld16(taddr + a * 256 + i * NTILE + cc, v);
           tc_wait_ld();
-          epi_tile(p, gu, m, qd, lane, row, g * p.TG * p.NTILE + i * p.NTILE + cc, v);
+          epi_tile(e, gu, m, qd, lane, row, g * TG * NTILE + i * NTILE + cc, v);
         }
       }
       tc_fence_before();
-      mbar_arrive(&c.bars->acc_empty[a]);
+      mbar_arrive(&bars->acc_empty[a]);
       ++ecnt;
     }
   }
@@ -615,65 +645,75 @@ __device__ __noinline__ uint32_t epi_gemm(const Params& p, const Ctx& c, uint32_
 constexpr int kQOff = 0, kKVOff = 64 * 1024, kPOff = 128 * 1024;
 
 __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& st_shared, int l) {
+  // register copies: the asm memory clobbers would force reloads through the references
+  const int c_acnt = c.acnt;
+  const AttnUnit* const c_au = c.au;
+  Bars* const c_bars = c.bars;
+  const uint32_t c_tmem = c.tmem;
+  uint8_t* const c_work = c.work;
+  const int p_L = p.L;
+  const int p_LPAD = p.LPAD;
+  int* const p_err = p.err;
+  const CUtensorMap* const p_maps = p.maps;
   MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
   const uint64_t pol_kv = policy_evict_last();
-  Bars* br = c.bars;
-  for (int u = 0; u < c.acnt; ++u) {
-    const AttnUnit au = c.au[u];
+  Bars* br = c_bars;
+  for (int u = 0; u < c_acnt; ++u) {
+    const AttnUnit au = c_au[u];
     const int nk = au.is_suffix ? TPAD : KCH;
     const int qkey = au.b * 4 + au.hp;
     if (qkey != st.last_q) {  // previous unit's S MMAs completed (kv_free waited), Q is free
       FA_ONE(mbar_expect_tx(&br->q_full, 4 * kAtomBytes));
       for (int a = 0; a < 4; ++a)
-        FA_ONE(tma_load_2d(c.work + kQOff + a * kAtomBytes, &p.maps[MAP_Q], &br->q_full, a * 64,
+        FA_ONE(tma_load_2d(c_work + kQOff + a * kAtomBytes, &p_maps[MAP_Q], &br->q_full, a * 64,
                     (au.b * H + 2 * au.hp) * TPAD, pol_kv));
-      if (!mbar_wait(&br->q_full, st.nq & 1, p.err, KERR_ATTN)) return false;
+      if (!mbar_wait(&br->q_full, st.nq & 1, p_err, KERR_ATTN)) return false;
       ++st.nq;
       st.last_q = qkey;
     }
-    if (st.nu > 0 && !mbar_wait(&br->v_free, (st.nu - 1) & 1, p.err, KERR_ATTN)) return false;
+    if (st.nu > 0 && !mbar_wait(&br->v_free, (st.nu - 1) & 1, p_err, KERR_ATTN)) return false;
     FA_ONE(mbar_expect_tx(&br->k_full, 4 * nk * 128));
     for (int a = 0; a < 4; ++a) {
       if (au.is_suffix)
-        FA_ONE(tma_load_2d(c.work + kKVOff + a * kAtomBytes, &p.maps[MAP_SK], &br->k_full, a * 64, au.b * TPAD, pol_kv));
+        FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_SK], &br->k_full, a * 64, au.b * TPAD, pol_kv));
       else
-        FA_ONE(tma_load_2d(c.work + kKVOff + a * kAtomBytes, &p.maps[MAP_K], &br->k_full, a * 64,
-                    (au.b * p.L + l) * p.LPAD + au.chunk * KCH, pol_kv));
+        FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_K], &br->k_full, a * 64,
+                    (au.b * p_L + l) * p_LPAD + au.chunk * KCH, pol_kv));
     }
-    if (!mbar_wait(&br->k_full, st.nu & 1, p.err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->k_full, st.nu & 1, p_err, KERR_ATTN)) return false;
     tc_fence_after();
     const uint32_t id_s = idesc_bf16(128, nk);
     for (int a = 0; a < 4; ++a) {
-      const uint64_t dq = sdesc_sw128(c.work + kQOff + a * kAtomBytes);
-      const uint64_t dk = sdesc_sw128(c.work + kKVOff + a * kAtomBytes);
+      const uint64_t dq = sdesc_sw128(c_work + kQOff + a * kAtomBytes);
+      const uint64_t dk = sdesc_sw128(c_work + kKVOff + a * kAtomBytes);
 #pragma unroll
-      for (int s = 0; s < 4; ++s) FA_ONE(tc_mma_bf16(c.tmem, dq + 2 * s, dk + 2 * s, id_s, (a | s) != 0));
+      for (int s = 0; s < 4; ++s) FA_ONE(tc_mma_bf16(c_tmem, dq + 2 * s, dk + 2 * s, id_s, (a | s) != 0));
     }
     FA_ONE(tc_commit(&br->s_full));
     FA_ONE(tc_commit(&br->kv_free));
-    if (!mbar_wait(&br->kv_free, st.nu & 1, p.err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->kv_free, st.nu & 1, p_err, KERR_ATTN)) return false;
     const int nka = nk / 64;  // 64-key atoms
     FA_ONE(mbar_expect_tx(&br->v_full, nka * 2 * kAtomBytes));
     for (int kk = 0; kk < nka; ++kk)
       for (int hh = 0; hh < 2; ++hh) {
-        uint8_t* dst = c.work + kKVOff + (kk * 2 + hh) * kAtomBytes;
+        uint8_t* dst = c_work + kKVOff + (kk * 2 + hh) * kAtomBytes;
         if (au.is_suffix)
-          FA_ONE(tma_load_2d(dst, &p.maps[MAP_SVT], &br->v_full, 0, au.b * HD + 128 * hh, pol_kv));
+          FA_ONE(tma_load_2d(dst, &p_maps[MAP_SVT], &br->v_full, 0, au.b * HD + 128 * hh, pol_kv));
         else
-          FA_ONE(tma_load_2d(dst, &p.maps[MAP_VT], &br->v_full, au.chunk * KCH + 64 * kk, (au.b * p.L + l) * HD + 128 * hh,
+          FA_ONE(tma_load_2d(dst, &p_maps[MAP_VT], &br->v_full, au.chunk * KCH + 64 * kk, (au.b * p_L + l) * HD + 128 * hh,
                       pol_kv));
       }
-    if (!mbar_wait(&br->v_full, st.nu & 1, p.err, KERR_ATTN)) return false;
-    if (!mbar_wait(&br->p_full, st.nu & 1, p.err, KERR_ATTN)) return false;
-    if (st.nu > 0 && !mbar_wait(&br->o_free, (st.nu - 1) & 1, p.err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->v_full, st.nu & 1, p_err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->p_full, st.nu & 1, p_err, KERR_ATTN)) return false;
+    if (st.nu > 0 && !mbar_wait(&br->o_free, (st.nu - 1) & 1, p_err, KERR_ATTN)) return false;
     tc_fence_after();
     const uint32_t id_o = idesc_bf16(128, 128);
     for (int kk = 0; kk < nka; ++kk) {
-      const uint64_t dp = sdesc_sw128(c.work + kPOff + kk * kAtomBytes);
+      const uint64_t dp = sdesc_sw128(c_work + kPOff + kk * kAtomBytes);
       for (int hh = 0; hh < 2; ++hh) {
-        const uint64_t dv = sdesc_sw128(c.work + kKVOff + (kk * 2 + hh) * kAtomBytes);
+        const uint64_t dv = sdesc_sw128(c_work + kKVOff + (kk * 2 + hh) * kAtomBytes);
 #pragma unroll
-        for (int s = 0; s < 4; ++s) FA_ONE(tc_mma_bf16(c.tmem + 128 + 128 * hh, dp + 2 * s, dv + 2 * s, id_o, (kk | s) != 0));
+        for (int s = 0; s < 4; ++s) FA_ONE(tc_mma_bf16(c_tmem + 128 + 128 * hh, dp + 2 * s, dv + 2 * s, id_o, (kk | s) != 0));
       }
     }
     FA_ONE(tc_commit(&br->o_full));
@@ -686,31 +726,42 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
 }
 
 __device__ __noinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint32_t anu) {
+  // register copies: the asm memory clobbers would force reloads through the references
+  const int c_acnt = c.acnt;
+  const AttnUnit* const c_au = c.au;
+  Bars* const c_bars = c.bars;
+  const uint32_t c_tmem = c.tmem;
+  uint8_t* const c_work = c.work;
+  const int p_T = p.T;
+  int* const p_err = p.err;
+  float* const p_oml = p.oml;
+  float* const p_opart = p.opart;
+  const int* const p_valid_len = p.valid_len;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int r = qd * 32 + lane;
   const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
   const float sl2 = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256) in log2 units
-  Bars* br = c.bars;
-  for (int u = 0; u < c.acnt; ++u) {
-    const AttnUnit au = c.au[u];
+  Bars* br = c_bars;
+  for (int u = 0; u < c_acnt; ++u) {
+    const AttnUnit au = c_au[u];
     const int nk = au.is_suffix ? TPAD : KCH;
-    const int nvalid = au.is_suffix ? p.T : min(KCH, p.valid_len[au.b] - au.chunk * KCH);
-    if (!mbar_wait(&br->s_full, anu & 1, p.err, KERR_ATTN)) return anu;
+    const int nvalid = au.is_suffix ? p_T : min(KCH, p_valid_len[au.b] - au.chunk * KCH);
+    if (!mbar_wait(&br->s_full, anu & 1, p_err, KERR_ATTN)) return anu;
     tc_fence_after();
     float mx = -INFINITY;
     for (int cc = 0; cc < nk; cc += 16) {
       float v[16];
-      tmem_ld16(c.tmem + lane_addr + cc, v);
+      tmem_ld16(c_tmem + lane_addr + cc, v);
       tc_wait_ld();
 #pragma unroll
       for (int k = 0; k < 16; ++k)
         if (cc + k < nvalid) mx = fmaxf(mx, v[k] * sl2);
     }
     float sum = 0.f;
-    uint8_t* prow = c.work + kPOff + (r >> 3) * 1024 + (r & 7) * 128;
+    uint8_t* prow = c_work + kPOff + (r >> 3) * 1024 + (r & 7) * 128;
     for (int cc = 0; cc < nk; cc += 16) {
       float v[16];
-      tmem_ld16(c.tmem + lane_addr + cc, v);
+      tmem_ld16(c_tmem + lane_addr + cc, v);
       tc_wait_ld();
       uint32_t pk[8];
 #pragma unroll
@@ -729,21 +780,21 @@ __device__ __noinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint32_
     fence_proxy_async_shared();
     tc_fence_before();
     mbar_arrive(&br->p_full);
-    if (!mbar_wait(&br->o_full, anu & 1, p.err, KERR_ATTN)) return anu;
+    if (!mbar_wait(&br->o_full, anu & 1, p_err, KERR_ATTN)) return anu;
     tc_fence_after();
     const int cidx = au.is_suffix ? MAX_CH : au.chunk;
     const size_t slot = ((size_t)(au.b * 4 + au.hp) * (MAX_CH + 1) + cidx) * 128 + r;
     const float inv = sum > 0.f ? 1.f / sum : 0.f;
-    float* orow = p.opart + slot * HD;
+    float* orow = p_opart + slot * HD;
     for (int cc = 0; cc < HD; cc += 16) {
       float v[16];
-      tmem_ld16(c.tmem + lane_addr + 128 + cc, v);
+      tmem_ld16(c_tmem + lane_addr + 128 + cc, v);
       tc_wait_ld();
 #pragma unroll
       for (int k = 0; k < 16; k += 4)
         *reinterpret_cast<float4*>(orow + cc + k) = make_float4(v[k] * inv, v[k + 1] * inv, v[k + 2] * inv, v[k + 3] * inv);
     }
-    *reinterpret_cast<float2*>(p.oml + slot * 2) = make_float2(sum > 0.f ? mx : -INFINITY, sum);
+    *reinterpret_cast<float2*>(p_oml + slot * 2) = make_float2(sum > 0.f ? mx : -INFINITY, sum);
     tc_fence_before();
     mbar_arrive(&br->o_free);
     ++anu;
