@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -737,5 +738,92 @@ extern "C" fa_status fa_set_fault_injection(fa_handle* h, int barrier_index, uns
   if (!h) return FA_ERR_INVALID;
   h->params.inject_barrier = barrier_index;
   h->params.spin_limit = spin_limit ? spin_limit : (1u << 24);
+  return FA_OK;
+}
+
+// ------------------------------------------------------------------ allocation-free conditioning
+// Some callers cannot allocate device memory when they need the adaRMS modulations: a robot
+// control process that pins its memory budget after start-up, or a host that owns a fixed pool
+// and forbids cudaMalloc outside it. For them, fa_pi05_modulations_noalloc computes the same
+// time embedding -> conditioning MLP -> per-layer modulations as fa_pi05_load_weights, but its
+// scratch (embedding, MLP hidden and conditioning vectors) lives in this file-scope array,
+// sized for at most kNoAllocMaxSteps Euler steps of width 1024 (3 x 50 x 1024 floats = 600 KB,
+// held by every GPU that loads this library until the process exits).
+constexpr int kNoAllocMaxSteps = 50;
+static __device__ __align__(256) float g_cond_scratch[3 * kNoAllocMaxSteps * D];
+
+// Device address of g_cond_scratch, looked up once per device (the host-side symbol is only a
+// stand-in and must never be handed to a kernel).
+static float* g_cond_scratch_dev[64];
+static std::mutex g_cond_scratch_mu;
+
+static fa_status cond_scratch_address(int device, float** out) {
+  std::lock_guard<std::mutex> lock(g_cond_scratch_mu);
+  if (device < 0 || device >= 64) return fail(nullptr, FA_ERR_INVALID, "device %d out of range", device);
+  if (!g_cond_scratch_dev[device]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_cond_scratch);
+    if (e != cudaSuccess)
+      return fail(nullptr, FA_ERR_CUDA, "cudaGetSymbolAddress(g_cond_scratch): %s", cudaGetErrorString(e));
+    g_cond_scratch_dev[device] = reinterpret_cast<float*>(ptr);
+  }
+  *out = g_cond_scratch_dev[device];
+  return FA_OK;
+}
+
+extern "C" fa_status fa_pi05_modulations_noalloc(const fa_pi05_weights* w, int num_layers, int num_steps,
+                                                 float* mods_out, float* mod_final_out, fa_stream stream) {
+  if (!w || !mods_out || !mod_final_out) return fail(nullptr, FA_ERR_INVALID, "null argument");
+  if (num_steps < 1 || num_steps > kNoAllocMaxSteps)
+    return fail(nullptr, FA_ERR_INVALID, "num_steps %d outside 1..%d (the static scratch holds %d steps)", num_steps,
+                kNoAllocMaxSteps, kNoAllocMaxSteps);
+  if (num_layers < 1 || num_layers > 64) return fail(nullptr, FA_ERR_INVALID, "num_layers %d outside 1..64", num_layers);
+  const fa_tensor* need[] = {&w->ln_in_w, &w->ln_in_b, &w->ln_post_w, &w->ln_post_b, &w->norm_w,
+                             &w->norm_b, &w->time_in_w, &w->time_in_b, &w->time_out_w, &w->time_out_b};
+  for (const fa_tensor* t : need) {
+    if (!t->ptr || !is_device_ptr(t->ptr))
+      return fail(nullptr, FA_ERR_INVALID, "every conditioning weight must be a device pointer (none is staged here)");
+    if (t->dtype != FA_DT_F32 && t->dtype != FA_DT_BF16 && t->dtype != FA_DT_F16)
+      return fail(nullptr, FA_ERR_INVALID, "unsupported weight dtype %d", (int)t->dtype);
+  }
+  if (!is_device_ptr(mods_out) || !is_device_ptr(mod_final_out))
+    return fail(nullptr, FA_ERR_INVALID, "mods_out / mod_final_out must be device pointers");
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return fail(nullptr, FA_ERR_CUDA, "cudaGetDevice failed");
+  float* scratch = nullptr;
+  fa_status st = cond_scratch_address(device, &scratch);
+  if (st != FA_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int S = num_steps, L = num_layers;
+  float* emb = scratch;                   // [S][1024]; every element is written before it is read,
+  float* h1 = scratch + (size_t)S * D;    // so nothing from an earlier call needs clearing
+  float* cond = scratch + (size_t)2 * S * D;
+  const size_t smem = (size_t)S * D * sizeof(float);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(linear_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return fail(nullptr, FA_ERR_CUDA, "cannot reserve %zu bytes of shared memory", smem);
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const int grid = std::max(1, sms * 2);
+  time_embed_kernel<<<8, 256, 0, s>>>(emb, S, D);
+  linear_f32_kernel<<<grid, 256, smem, s>>>(w->time_in_w.ptr, w->time_in_w.dtype, w->time_in_b.ptr, w->time_in_b.dtype,
+                                            emb, S, D, D, h1, D, 1);
+  linear_f32_kernel<<<grid, 256, smem, s>>>(w->time_out_w.ptr, w->time_out_w.dtype, w->time_out_b.ptr,
+                                            w->time_out_b.dtype, h1, S, D, D, cond, D, 1);
+  const size_t sstride = (size_t)L * 2 * MOD;
+  for (int l = 0; l < L; ++l) {
+    linear_f32_kernel<<<grid, 256, smem, s>>>(
+        (const char*)w->ln_in_w.ptr + (size_t)l * MOD * D * dtype_size(w->ln_in_w.dtype), w->ln_in_w.dtype,
+        (const char*)w->ln_in_b.ptr + (size_t)l * MOD * dtype_size(w->ln_in_b.dtype), w->ln_in_b.dtype, cond, S, D, MOD,
+        mods_out + (size_t)l * 2 * MOD, sstride, 0);
+    linear_f32_kernel<<<grid, 256, smem, s>>>(
+        (const char*)w->ln_post_w.ptr + (size_t)l * MOD * D * dtype_size(w->ln_post_w.dtype), w->ln_post_w.dtype,
+        (const char*)w->ln_post_b.ptr + (size_t)l * MOD * dtype_size(w->ln_post_b.dtype), w->ln_post_b.dtype, cond, S, D,
+        MOD, mods_out + (size_t)l * 2 * MOD + MOD, sstride, 0);
+  }
+  linear_f32_kernel<<<grid, 256, smem, s>>>(w->norm_w.ptr, w->norm_w.dtype, w->norm_b.ptr, w->norm_b.dtype, cond, S, D,
+                                            MOD, mod_final_out, MOD, 0);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(nullptr, FA_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
   return FA_OK;
 }

@@ -155,6 +155,22 @@ FA_API fa_status fa_set_fault_injection(fa_handle* h, int barrier_index, unsigne
  * the activation loads were issued. */
 FA_API fa_status fa_debug_trace(fa_handle* h, int step, int layer, unsigned long long* host_out, int n);
 
+/* Allocation-free variant of the conditioning step of fa_pi05_load_weights; it has no
+ * counterpart in the reference. For callers that cannot allocate device memory at the point
+ * where they need the modulations (a control process whose memory budget is fixed after start-up,
+ * a host that hands out memory only from its own pool). It computes the time embedding ->
+ * conditioning MLP -> adaRMS modulations for the fixed schedule t_s = 1 - s/num_steps, writing
+ * mods_out [num_steps][num_layers][2][3072] and mod_final_out [num_steps][3072] (device fp32,
+ * the layout fa_set_modulation takes) on `stream`, asynchronously. Only the conditioning fields of
+ * `w` are read (ln_*, norm_*, time_*), and they must already be in device memory.
+ * Scratch: a static 600 KB device array inside the library (at most 50 steps), held by every GPU
+ * that loads the library until exit; the call allocates nothing. The first call on each device
+ * looks the array up (cudaGetSymbolAddress) with that device current, so make that first call
+ * before any stream capture. All calls share the array: calls that overlap on the GPU race. The
+ * last error message is read with fa_last_error(NULL). Rejects num_steps > 50. */
+FA_API fa_status fa_pi05_modulations_noalloc(const fa_pi05_weights* w, int num_layers, int num_steps,
+                                             float* mods_out, float* mod_final_out, fa_stream stream);
+
 /* Last error message of the handle (or of the thread's last failed fa_create when h is NULL). */
 FA_API const char* fa_last_error(fa_handle* h);
 
