@@ -91,7 +91,7 @@ struct Params {
   __nv_bfloat16* q;     // [B][8][64][256]
   __nv_bfloat16* sk;    // [B][64][256] this layer's action-token keys (RoPE applied)
   __nv_bfloat16* svt;   // [B][256][64] this layer's action-token values, transposed
-  float* opart;  // [B][4][MAX_CH+1][128][256] per-chunk normalised attention output
+  __nv_bfloat16* opart;  // [B][4][MAX_CH+1][128][256] per-chunk normalised attention output (bf16)
   float* oml;    // [B][4][MAX_CH+1][128][2] per-chunk (max, sum)
   // control
   unsigned int* bar;             // grid-barrier counter, zeroed before each launch

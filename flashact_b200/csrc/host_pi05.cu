@@ -43,7 +43,8 @@ struct fa_handle {
   bf16 *w_qkv = nullptr, *w_o = nullptr, *w_gu = nullptr, *w_dn = nullptr;
   float *mods = nullptr, *mod_final = nullptr;
   float *w_ain = nullptr, *b_ain = nullptr, *w_aout = nullptr, *b_aout = nullptr;
-  float *x_t = nullptr, *x = nullptr, *part = nullptr, *opart = nullptr, *oml = nullptr;
+  float *x_t = nullptr, *x = nullptr, *part = nullptr, *oml = nullptr;
+  bf16* opart = nullptr;
   bf16 *xn = nullptr, *attn = nullptr, *hbuf = nullptr, *q = nullptr, *sk = nullptr, *svt = nullptr;
   bf16 *kcache = nullptr, *vtcache = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
@@ -554,8 +555,10 @@ static fa_status build_plan(fa_handle* h) {
       return fail(h, FA_ERR_INVALID, "batch too large for the per-CTA work lists (%d GEMM, %d attention units)", ng,
                   plans[i].a_cnt);
     bb = std::min(bb, std::min(kMaxBBytes, kMaxBAtoms * tile));
-    const int work = plans[i].a_cnt > 0 ? std::max(kAttnWork, bb) : bb;
-    plans[i].b_bytes = plans[i].a_cnt > 0 ? std::min(work, kMaxBBytes) : bb;
+    const int work = plans[i].a_cnt > 0 ? kAttnWork : bb + 16 * 1024;  // + epilogue staging
+    // Attention CTAs keep their activation area inside the Q region (first 64 KB) so that the
+    // prefix-K prefetch into the K/V area survives the GEMM stages in between.
+    plans[i].b_bytes = plans[i].a_cnt > 0 ? std::max(tile, std::min(bb, 64 * 1024)) : bb;
     plans[i].ring_slots = std::min(kMaxRing, (kSmemUse - work) / kAtomBytes);
     for (int m = 0; m < 4; ++m) {
       plans[i].g_off[m] = (int)gu.size();

@@ -62,9 +62,13 @@ __device__ __forceinline__ void trace_mark(int slot) {
 }
 
 // gelu with the tanh approximation (src/pi05/mk6.cu:79-82).
+// tanh by the hardware approximation (tanh.approx.f32, max relative error ~2^-11: below the
+// bf16 rounding the result gets next).
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + 0.044715f * x * x * x)));
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(k0 * (x + 0.044715f * x * x * x)));
+  return 0.5f * x * (1.0f + t);
 }
 
 // Grid barrier among warps 1-5 of every CTA. `gen` counts barriers passed by this launch; the
@@ -275,7 +279,7 @@ __device__ __noinline__ void stage_merge(const Params& p) {
   __nv_bfloat16* const p_attn = p.attn;
   const int* const p_nchunks = p.nchunks;
   float* const p_oml = p.oml;
-  float* const p_opart = p.opart;
+  __nv_bfloat16* const p_opart = p.opart;
   const float p_invT = p.invT;
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   const int total = p_NT * H;
@@ -297,9 +301,12 @@ __device__ __noinline__ void stage_merge(const Params& p) {
     for (int c = 0; c < nc; ++c) {
       const float wgt = __shfl_sync(0xffffffffu, wgt_own, c);
       const int cc = c < npc ? c : MAX_CH;
-      const float* src = p_opart + ((base + cc) * 128 + r) * HD + lane * 8;
-      const float4 o0 = __ldcg(reinterpret_cast<const float4*>(src));
-      const float4 o1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
+      const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base + cc) * 128 + r) * HD + lane * 8));
+      const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+      const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+      const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.z));
+      const float2 f3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.w));
+      const float4 o0 = make_float4(f0.x, f0.y, f1.x, f1.y), o1 = make_float4(f2.x, f2.y, f3.x, f3.y);
       acc0.x += wgt * o0.x; acc0.y += wgt * o0.y; acc0.z += wgt * o0.z; acc0.w += wgt * o0.w;
       acc1.x += wgt * o1.x; acc1.y += wgt * o1.y; acc1.z += wgt * o1.z; acc1.w += wgt * o1.w;
     }
@@ -336,6 +343,7 @@ struct Ctx {
   uint32_t tmem;
   int ring_slots;
   int batoms;               // activation atoms that fit in the work area at once
+  uint8_t* stage;           // 16 KB epilogue staging area (coalesced bf16 output writes)
   const GemmUnit* gu[4];    // this CTA's units per matrix (shared-memory copy of the plan)
   int gcnt[4];
   const AttnUnit* au;
@@ -414,6 +422,7 @@ struct MmaState {
   uint32_t acc;          // accumulator buffers used
   uint32_t nq, nu;       // attention: Q loads, units
   int last_q;
+  int k_pre;             // the next attention unit's prefix K is already loading (prefetched)
 };
 
 // Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
@@ -446,6 +455,7 @@ __device__ __forceinline__ void load_b_batch(const MmaCtx& k, const GemmUnit& gu
 }
 
 __device__ __noinline__ bool mma_gemm(const Params& p, const Ctx& c, MmaState& st_shared, int m) {
+  FA_ONE(trace_mark(12));
   MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
   MmaCtx k;
   k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[act_map(m)];
@@ -462,6 +472,7 @@ __device__ __noinline__ bool mma_gemm(const Params& p, const Ctx& c, MmaState& s
       const int nt = min(k.TG, k.tiles - g * k.TG);
       const int per_batch = max(1, k.batoms / nt);  // K atoms per activation batch
       int j1 = min((int)gu.natoms, per_batch);
+      if (u == 0 && g == 0) FA_ONE(trace_mark(13));
       load_b_batch(k, gu, g, nt, 0, j1);
       if (u == 0 && g == 0) FA_ONE(trace_mark(kTrMmaPre));
       const int a = st.acc & 1;
@@ -527,17 +538,17 @@ struct EpiCtx {
   __nv_bfloat16* svt;
   __nv_bfloat16* hbuf;
   float* part;
+  uint8_t* stage;
 };
 
 __device__ __forceinline__ void epi_tile(const EpiCtx& p, const GemmUnit& gu, int m, int qd, int lane, int row, int nb,
-                                         const float* v) {
+                                         int nb0, const float* v) {
   if (m == MAT_QKV) {
     const int mt = gu.mtile;
     if (mt < 18) {  // Q heads (mtile 0..15) or K (16, 17): split-half RoPE epilogue
       const int pb = mt < 16 ? (mt & 1) : mt - 16;
       const int pr = 64 * pb + 16 * qd + (lane & 15);
       const int hi = lane >> 4;
-      const int dim = pr + 128 * hi;
       float cs[16], sn[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) {  // batch the table reads before any use
@@ -545,18 +556,15 @@ __device__ __forceinline__ void epi_tile(const EpiCtx& p, const GemmUnit& gu, in
         cs[k] = __ldg(p.rope_cos + (size_t)n * 128 + pr);
         sn[k] = __ldg(p.rope_sin + (size_t)n * 128 + pr);
       }
+      float partner[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) partner[k] = __shfl_xor_sync(0xffffffffu, v[k], 16);  // exchanges first
+      __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(p.stage) + (nb - nb0) * 128 + (lane & 15) + 16 * qd + 64 * hi;
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
-        const float x = v[k];
-        const float partner = __shfl_xor_sync(0xffffffffu, x, 16);
-        const int n = nb + k;
-        if (n < p.NT) {
-          const int b = tok_bi(p.invT, n), t = n - b * p.T;
-          const float o = hi ? fmaf(x, cs[k], partner * sn[k]) : fmaf(x, cs[k], -partner * sn[k]);
-          __nv_bfloat16* dst = mt < 16 ? p.q + ((size_t)(b * H + (mt >> 1)) * TPAD + t) * HD + dim
-                                       : p.sk + ((size_t)b * TPAD + t) * HD + dim;
-          *dst = __float2bfloat16(o);
-        }
+        // staging row = token within the 64-token sub-tile, 128 dims: (lane & 15) + 16 qd + 64 hi
+        const float o = hi ? fmaf(v[k], cs[k], partner[k] * sn[k]) : fmaf(v[k], cs[k], -partner[k] * sn[k]);
+        st[k * 128] = __float2bfloat16(o);
       }
     } else {  // V: natural order, stored transposed [dim][token]: 8 tokens per 16-byte store
       const int dim = (mt - 18) * 128 + row;
@@ -585,12 +593,15 @@ __device__ __forceinline__ void epi_tile(const EpiCtx& p, const GemmUnit& gu, in
       }
     }
   } else if (m == MAT_GU) {  // GeGLU: lanes 0-15 gate rows, 16-31 up rows of one feature
-    const int f = 64 * gu.mtile + 16 * qd + (lane & 15);
+    float up[16], h[16];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float up = __shfl_xor_sync(0xffffffffu, v[k], 16);
-      const int n = nb + k;
-      if (lane < 16 && n < p.NT) p.hbuf[(size_t)n * F + f] = __float2bfloat16(gelu_tanh(v[k]) * up);
+    for (int k = 0; k < 16; ++k) up[k] = __shfl_xor_sync(0xffffffffu, v[k], 16);  // all exchanges first
+#pragma unroll
+    for (int k = 0; k < 16; ++k) h[k] = gelu_tanh(v[k]) * up[k];  // 16 independent chains
+    if (lane < 16) {  // staging row = token within the sub-tile, 64 features
+      __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(p.stage) + (nb - nb0) * 64 + 16 * qd + lane;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) st[k * 64] = __float2bfloat16(h[k]);
     }
   } else {  // O / down: fp32 K-split partial, each warp store covers 32 consecutive rows
     float* dst = p.part + ((size_t)gu.split * p.NPAD + nb) * D + gu.mtile * 128 + row;
@@ -599,12 +610,37 @@ __device__ __forceinline__ void epi_tile(const EpiCtx& p, const GemmUnit& gu, in
   }
 }
 
+// Coalesced copy of a staged 64-token sub-tile to its destination (16-byte stores).
+__device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu, int m, int nb0) {
+  const int e = threadIdx.x - 64;
+  if (m == MAT_GU) {  // 64 rows (tokens) x 128 B: 8 threads per row
+    for (int it = e; it < 64 * 8; it += 128) {
+      const int t = it >> 3, seg = it & 7, n = nb0 + t;
+      if (n >= p.NT) continue;
+      const uint4 val = *reinterpret_cast<const uint4*>(p.stage + t * 128 + seg * 16);
+      *reinterpret_cast<uint4*>(p.hbuf + (size_t)n * F + 64 * gu.mtile + seg * 8) = val;
+    }
+  } else {  // Q / K: 64 rows x 256 B, dims [0, 64) -> 64 pb + ..., dims [64, 128) -> 128 + 64 pb + ...
+    const int mt = gu.mtile;
+    const int pb = mt < 16 ? (mt & 1) : mt - 16;
+    for (int it = e; it < 64 * 16; it += 128) {
+      const int t = it >> 4, seg = it & 15, n = nb0 + t;
+      if (n >= p.NT) continue;
+      const int b = tok_bi(p.invT, n), tt = n - b * p.T;
+      const int dim = 64 * pb + (seg & 7) * 8 + (seg >> 3) * 128;
+      __nv_bfloat16* dst = mt < 16 ? p.q + ((size_t)(b * H + (mt >> 1)) * TPAD + tt) * HD + dim
+                                   : p.sk + ((size_t)b * TPAD + tt) * HD + dim;
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(p.stage + t * 256 + seg * 16);
+    }
+  }
+}
+
 __device__ __noinline__ uint32_t epi_gemm(const Params& p, const Ctx& c, uint32_t ecnt, int m) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int row = qd * 32 + lane;
   EpiCtx e;
   e.NT = p.NT; e.T = p.T; e.NPAD = p.NPAD; e.invT = p.invT; e.rope_cos = p.rope_cos; e.rope_sin = p.rope_sin;
-  e.q = p.q; e.sk = p.sk; e.svt = p.svt; e.hbuf = p.hbuf; e.part = p.part;
+  e.q = p.q; e.sk = p.sk; e.svt = p.svt; e.hbuf = p.hbuf; e.part = p.part; e.stage = c.stage;
   const int NTILE = p.NTILE, TG = p.TG, ngroups = p.ngroups, tiles = p.NPAD / p.NTILE;
   int* const err = p.err;
   Bars* const bars = c.bars;
@@ -619,13 +655,25 @@ __device__ __noinline__ uint32_t epi_gemm(const Params& p, const Ctx& c, uint32_
       if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;
       if (u == 0 && g == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
       tc_fence_after();
+      const bool staged = (m == MAT_GU) || (m == MAT_QKV && gu.mtile < 18);
       for (int i = 0; i < nt; ++i) {
 #pragma unroll 1
-        for (int cc = 0; cc < NTILE; cc += 16) {
-          float v[16];
-          tmem_ld16(taddr + a * 256 + i * NTILE + cc, v);
-          tc_wait_ld();
-          epi_tile(e, gu, m, qd, lane, row, g * TG * NTILE + i * NTILE + cc, v);
+        for (int c64 = 0; c64 < NTILE; c64 += 64) {
+          const int nb0 = g * TG * NTILE + i * NTILE + c64;
+#pragma unroll 1
+          for (int cc = 0; cc < 64; cc += 16) {
+            float v[16];
+            tmem_ld16(taddr + a * 256 + i * NTILE + c64 + cc, v);
+            tc_wait_ld();
+            if (u == 0 && g == 0 && i == 0 && c64 + cc == 0 && threadIdx.x == 64) trace_mark(14);
+            epi_tile(e, gu, m, qd, lane, row, nb0 + cc, nb0, v);
+            if (u == 0 && g == 0 && i == 0 && c64 + cc == 0 && threadIdx.x == 64) trace_mark(15);
+          }
+          if (staged) {
+            sync_epi();
+            epi_copy_out(e, gu, m, nb0);
+            sync_epi();
+          }
         }
       }
       tc_fence_before();
@@ -644,7 +692,7 @@ __device__ __noinline__ uint32_t epi_gemm(const Params& p, const Ctx& c, uint32_
 // (TMEM cols 128..383) -> normalised partial + (max, sum) to global, merged by stage_merge.
 constexpr int kQOff = 0, kKVOff = 64 * 1024, kPOff = 128 * 1024;
 
-__device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& st_shared, int l) {
+__device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& st_shared, int l, bool last) {
   // register copies: the asm memory clobbers would force reloads through the references
   const int c_acnt = c.acnt;
   const AttnUnit* const c_au = c.au;
@@ -662,25 +710,35 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
     const AttnUnit au = c_au[u];
     const int nk = au.is_suffix ? TPAD : KCH;
     const int qkey = au.b * 4 + au.hp;
-    if (qkey != st.last_q) {  // previous unit's S MMAs completed (kv_free waited), Q is free
+    // The epilogue stages the previous unit's output in the K/V + P area and then arrives on
+    // o_free; nothing may land there (or in TMEM) before that.
+    if (st.nu > 0 && !mbar_wait(&br->o_free, (st.nu - 1) & 1, p_err, KERR_ATTN)) return false;
+    const bool load_q = qkey != st.last_q;  // Q stays resident across units of one head pair
+    if (load_q) {
       FA_ONE(mbar_expect_tx(&br->q_full, 4 * kAtomBytes));
       for (int a = 0; a < 4; ++a)
         FA_ONE(tma_load_2d(c_work + kQOff + a * kAtomBytes, &p_maps[MAP_Q], &br->q_full, a * 64,
-                    (au.b * H + 2 * au.hp) * TPAD, pol_kv));
+                           (au.b * H + 2 * au.hp) * TPAD, pol_kv));
+    }
+    if (st.k_pre) {  // issued at the end of the previous attention stage
+      st.k_pre = 0;
+    } else {
+      FA_ONE(mbar_expect_tx(&br->k_full, 4 * nk * 128));
+      for (int a = 0; a < 4; ++a) {
+        if (au.is_suffix)
+          FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_SK], &br->k_full, a * 64, au.b * TPAD, pol_kv));
+        else
+          FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_K], &br->k_full, a * 64,
+                             (au.b * p_L + l) * p_LPAD + au.chunk * KCH, pol_kv));
+      }
+    }
+    if (load_q) {
       if (!mbar_wait(&br->q_full, st.nq & 1, p_err, KERR_ATTN)) return false;
       ++st.nq;
       st.last_q = qkey;
     }
-    if (st.nu > 0 && !mbar_wait(&br->v_free, (st.nu - 1) & 1, p_err, KERR_ATTN)) return false;
-    FA_ONE(mbar_expect_tx(&br->k_full, 4 * nk * 128));
-    for (int a = 0; a < 4; ++a) {
-      if (au.is_suffix)
-        FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_SK], &br->k_full, a * 64, au.b * TPAD, pol_kv));
-      else
-        FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_K], &br->k_full, a * 64,
-                    (au.b * p_L + l) * p_LPAD + au.chunk * KCH, pol_kv));
-    }
     if (!mbar_wait(&br->k_full, st.nu & 1, p_err, KERR_ATTN)) return false;
+    if (u == 0) FA_ONE(trace_mark(kTrMmaW0));  // Q and K in shared memory
     tc_fence_after();
     const uint32_t id_s = idesc_bf16(128, nk);
     for (int a = 0; a < 4; ++a) {
@@ -704,8 +762,9 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
                       pol_kv));
       }
     if (!mbar_wait(&br->v_full, st.nu & 1, p_err, KERR_ATTN)) return false;
+    if (u == 0) FA_ONE(trace_mark(kTrMmaB0));  // V in shared memory
     if (!mbar_wait(&br->p_full, st.nu & 1, p_err, KERR_ATTN)) return false;
-    if (st.nu > 0 && !mbar_wait(&br->o_free, (st.nu - 1) & 1, p_err, KERR_ATTN)) return false;
+    if (u == 0) FA_ONE(trace_mark(10));  // P written by the softmax warps
     tc_fence_after();
     const uint32_t id_o = idesc_bf16(128, 128);
     for (int kk = 0; kk < nka; ++kk) {
@@ -717,84 +776,139 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
       }
     }
     FA_ONE(tc_commit(&br->o_full));
-    FA_ONE(tc_commit(&br->v_free));
     ++st.nu;
   }
+  // Prefix keys do not change during the loop: once the epilogue has released the K/V area
+  // (o_free of the last unit), start loading the first unit's chunk for the next attention stage
+  // (layer l + 1, or layer 0 of the next Euler step) so that it is resident when that stage begins.
+  if (!last && c_acnt > 0 && !c_au[0].is_suffix) {
+    if (!mbar_wait(&br->o_free, (st.nu - 1) & 1, p_err, KERR_ATTN)) return false;
+    const AttnUnit au = c_au[0];
+    const int ln = (l + 1) % p_L;
+    FA_ONE(mbar_expect_tx(&br->k_full, 4 * KCH * 128));
+    for (int a = 0; a < 4; ++a)
+      FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_K], &br->k_full, a * 64,
+                         (au.b * p_L + ln) * p_LPAD + au.chunk * KCH, pol_kv));
+    st.k_pre = 1;
+  }
+  FA_ONE(trace_mark(kTrMmaDone));
   if (leader()) st_shared = st;
   __syncwarp();
   return true;
 }
 
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Softmax of one 128-query-row tile over NK keys, all in one TMEM round trip: thread r owns
+// row r (its NK scores in registers), writes the bf16 probabilities as the A operand of O = P V
+// (128-byte-swizzled K-major atoms of 64 keys) and returns (max in log2 units, sum).
+template <int NK>
+__device__ __forceinline__ float2 softmax_row(uint32_t taddr, int nvalid, uint8_t* prow, int r) {
+  constexpr float sl2 = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2 units
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+  for (int cc = 0; cc < NK; cc += 32) {  // pass 1: row max, 4 independent chains
+    float v[32];
+    tmem_ld16(taddr + cc, v);
+    tmem_ld16(taddr + cc + 16, v + 16);
+    tc_wait_ld();
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      if (cc + k < nvalid) m4[k & 3] = fmaxf(m4[k & 3], v[k]);
+  }
+  const float mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+  const float mx = mraw * sl2;
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int cc = 0; cc < NK; cc += 32) {  // pass 2: probabilities -> bf16 P atoms
+    float v[32];
+    tmem_ld16(taddr + cc, v);
+    tmem_ld16(taddr + cc + 16, v + 16);
+    tc_wait_ld();
+    uint32_t pk[16];
+#pragma unroll
+    for (int k = 0; k < 32; k += 2) {
+      const float p0 = cc + k < nvalid ? fast_exp2(fmaf(v[k], sl2, -mx)) : 0.f;
+      const float p1 = cc + k + 1 < nvalid ? fast_exp2(fmaf(v[k + 1], sl2, -mx)) : 0.f;
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+      s4[(k >> 1) & 3] += __low2float(b2) + __high2float(b2);  // normalise with the stored values
+      pk[k >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    uint8_t* base = prow + (cc >> 6) * kAtomBytes;
+    const int ch0 = (cc & 63) >> 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(base + (((ch0 + q) ^ (r & 7)) << 4)) =
+          make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+  }
+  return make_float2(mx, (s4[0] + s4[1]) + (s4[2] + s4[3]));
+}
+
+constexpr int kOPitch = HD * 2 + 16;  // staged bf16 output row, padded against bank conflicts
+
 __device__ __noinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint32_t anu) {
   // register copies: the asm memory clobbers would force reloads through the references
-  const int c_acnt = c.acnt;
-  const AttnUnit* const c_au = c.au;
-  Bars* const c_bars = c.bars;
-  const uint32_t c_tmem = c.tmem;
-  uint8_t* const c_work = c.work;
-  const int p_T = p.T;
-  int* const p_err = p.err;
-  float* const p_oml = p.oml;
-  float* const p_opart = p.opart;
-  const int* const p_valid_len = p.valid_len;
+  const int nunits = c.acnt;
+  const AttnUnit* const units = c.au;
+  Bars* const br = c.bars;
+  const uint32_t tmem = c.tmem;
+  uint8_t* const work = c.work;
+  const int T = p.T;
+  int* const err = p.err;
+  float* const oml = p.oml;
+  __nv_bfloat16* const opart = p.opart;
+  const int* const valid_len = p.valid_len;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int r = qd * 32 + lane;
   const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
-  const float sl2 = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256) in log2 units
-  Bars* br = c_bars;
-  for (int u = 0; u < c_acnt; ++u) {
-    const AttnUnit au = c_au[u];
-    const int nk = au.is_suffix ? TPAD : KCH;
-    const int nvalid = au.is_suffix ? p_T : min(KCH, p_valid_len[au.b] - au.chunk * KCH);
-    if (!mbar_wait(&br->s_full, anu & 1, p_err, KERR_ATTN)) return anu;
+  uint8_t* const stage = work + kKVOff;  // K/V + P area, free once O is in TMEM
+  for (int u = 0; u < nunits; ++u) {
+    const AttnUnit au = units[u];
+    const int nvalid = au.is_suffix ? T : min(KCH, valid_len[au.b] - au.chunk * KCH);
+    if (!mbar_wait(&br->s_full, anu & 1, err, KERR_ATTN)) return anu;
     tc_fence_after();
-    float mx = -INFINITY;
-    for (int cc = 0; cc < nk; cc += 16) {
-      float v[16];
-      tmem_ld16(c_tmem + lane_addr + cc, v);
-      tc_wait_ld();
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (cc + k < nvalid) mx = fmaxf(mx, v[k] * sl2);
-    }
-    float sum = 0.f;
-    uint8_t* prow = c_work + kPOff + (r >> 3) * 1024 + (r & 7) * 128;
-    for (int cc = 0; cc < nk; cc += 16) {
-      float v[16];
-      tmem_ld16(c_tmem + lane_addr + cc, v);
-      tc_wait_ld();
-      uint32_t pk[8];
-#pragma unroll
-      for (int k = 0; k < 16; k += 2) {
-        const float p0 = (cc + k < nvalid) ? exp2f(v[k] * sl2 - mx) : 0.f;
-        const float p1 = (cc + k + 1 < nvalid) ? exp2f(v[k + 1] * sl2 - mx) : 0.f;
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-        sum += __low2float(b2) + __high2float(b2);  // normalise with the probabilities actually used
-        pk[k >> 1] = *reinterpret_cast<uint32_t*>(&b2);
-      }
-      const int atom = cc >> 6, ch = (cc & 63) >> 3;  // two 16-byte chunks of this row
-      uint8_t* base = prow + atom * kAtomBytes;
-      *reinterpret_cast<uint4*>(base + (((ch) ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      *reinterpret_cast<uint4*>(base + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-    }
+    if (u == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);  // S in TMEM
+    uint8_t* prow = work + kPOff + (r >> 3) * 1024 + (r & 7) * 128;
+    const float2 ms = au.is_suffix ? softmax_row<TPAD>(tmem + lane_addr, nvalid, prow, r)
+                                   : softmax_row<KCH>(tmem + lane_addr, nvalid, prow, r);
     fence_proxy_async_shared();
     tc_fence_before();
     mbar_arrive(&br->p_full);
-    if (!mbar_wait(&br->o_full, anu & 1, p_err, KERR_ATTN)) return anu;
+    if (!mbar_wait(&br->o_full, anu & 1, err, KERR_ATTN)) return anu;
+    if (u == 0 && threadIdx.x == 64) trace_mark(11);  // O in TMEM
     tc_fence_after();
-    const int cidx = au.is_suffix ? MAX_CH : au.chunk;
-    const size_t slot = ((size_t)(au.b * 4 + au.hp) * (MAX_CH + 1) + cidx) * 128 + r;
-    const float inv = sum > 0.f ? 1.f / sum : 0.f;
-    float* orow = p_opart + slot * HD;
-    for (int cc = 0; cc < HD; cc += 16) {
-      float v[16];
-      tmem_ld16(c_tmem + lane_addr + 128 + cc, v);
+    const float inv = ms.y > 0.f ? 1.f / ms.y : 0.f;
+    uint8_t* srow = stage + r * kOPitch;
+#pragma unroll 1
+    for (int cc = 0; cc < HD; cc += 32) {  // normalised O row -> bf16 -> padded staging row
+      float v[32];
+      tmem_ld16(tmem + lane_addr + 128 + cc, v);
+      tmem_ld16(tmem + lane_addr + 128 + cc + 16, v + 16);
       tc_wait_ld();
 #pragma unroll
-      for (int k = 0; k < 16; k += 4)
-        *reinterpret_cast<float4*>(orow + cc + k) = make_float4(v[k] * inv, v[k + 1] * inv, v[k + 2] * inv, v[k + 3] * inv);
+      for (int k = 0; k < 32; k += 8) {
+        uint32_t w4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(v[k + 2 * q] * inv, v[k + 2 * q + 1] * inv);
+          w4[q] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(srow + (cc + k) * 2) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
     }
-    *reinterpret_cast<float2*>(p_oml + slot * 2) = make_float2(sum > 0.f ? mx : -INFINITY, sum);
+    const int cidx = au.is_suffix ? MAX_CH : au.chunk;
+    const size_t slot0 = ((size_t)(au.b * 4 + au.hp) * (MAX_CH + 1) + cidx) * 128;
+    *reinterpret_cast<float2*>(oml + (slot0 + r) * 2) = make_float2(ms.y > 0.f ? ms.x : -INFINITY, ms.y);
+    sync_epi();
+    // coalesced copy-out: one 512-byte row per warp instruction
+    for (int rr = warp & 3; rr < 128; rr += 4) {
+      const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * kOPitch + lane * 16);
+      *reinterpret_cast<uint4*>(opart + (slot0 + rr) * HD + lane * 8) = val;
+    }
     tc_fence_before();
     mbar_arrive(&br->o_free);
     ++anu;
@@ -822,6 +936,7 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
     g_trp = nullptr;
     s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = 0;
     s_st.last_q = -1;
+    s_st.k_pre = 0;
   }
   __syncthreads();
   {  // this CTA's work lists, read once from global memory
@@ -842,6 +957,9 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   c.ring_slots = s_plan.ring_slots;
   c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   c.work = c.ring + (size_t)c.ring_slots * kAtomBytes;
+  // epilogue staging: the P area on attention CTAs (idle outside the attention stage), else the
+  // 16 KB after the activation area
+  c.stage = s_plan.a_cnt > 0 ? c.work + kPOff : c.work + s_plan.b_bytes;
   c.bars = &bars;
   }
 
@@ -907,7 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
         mark(ST_QKV);
         if (is_mma && leader()) st.last_q = -1;
         __syncwarp();
-        if (is_mma) mma_attn(p, c, st, l);
+        if (is_mma) mma_attn(p, c, st, l, step + 1 == p.nsteps && l + 1 == p.L);
         if (is_epi) anu = epi_attn(p, c, anu);
         epi_done();
         if (!(ok = grid_barrier(p, gen++, tr(ST_MERGE, step, l)))) break;
@@ -951,6 +1069,7 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
     if (is_mma) {  // retire every MMA this warp issued before TMEM is released
       FA_ONE(tc_commit(&bars.drain));
       mbar_wait(&bars.drain, 0, p.err, KERR_MMA);
+      if (s_st.k_pre) mbar_wait(&bars.k_full, s_st.nu & 1, p.err, KERR_ATTN);  // no TMA left in flight
     }
     __syncwarp();
   }
