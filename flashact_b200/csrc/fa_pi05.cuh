@@ -35,8 +35,8 @@ constexpr int kAttnWork = 160 * 1024;  // Q 64K | K/V 64K | P 32K
 enum Mat : int { MAT_QKV = 0, MAT_O = 1, MAT_GU = 2, MAT_DN = 3 };
 enum Map : int {
   MAP_W_QKV = 0, MAP_W_O, MAP_W_GU, MAP_W_DN,  // weights, box {64, 128}
-  MAP_XN, MAP_ATTN, MAP_H,                     // activations, box {64, NTILE}
-  MAP_Q, MAP_K, MAP_VT, MAP_SK, MAP_SVT,       // attention operands
+  MAP_XN, MAP_ATTN, MAP_H,                     // activations, 3D box {64, NTILE, box_atoms}
+  MAP_Q, MAP_K, MAP_VT, MAP_SK, MAP_SVT,       // attention operands, 3D boxes of whole tiles
   NUM_MAPS
 };
 enum Stage : int {
@@ -64,6 +64,7 @@ struct Params {
   // geometry
   int L, T, B, NT, NPAD, NTILE, TG, ngroups, nsteps, LPAD, AD;
   int split_o, split_dn;
+  int box_atoms;  // K atoms per activation TMA load (3D box)
   float dt;
   float invT;  // 1 / T
   // plan

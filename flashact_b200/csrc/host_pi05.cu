@@ -254,8 +254,10 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   h->cfg = c;
   h->device = device;
   h->num_sms = prop.multiProcessorCount;
-  if (const char* e = getenv("FA_SPLIT_O")) h->split_o = std::max(1, std::min(8, atoi(e)));
-  if (const char* e = getenv("FA_SPLIT_DN")) h->split_dn = std::max(1, std::min(8, atoi(e)));
+  // K-split factors (tuning knobs): powers of two, so that every unit covers a multiple of 4 atoms
+  auto pow2 = [](int v) { int r = 1; while (r * 2 <= v) r *= 2; return r; };
+  if (const char* e = getenv("FA_SPLIT_O")) h->split_o = pow2(std::max(1, std::min(8, atoi(e))));
+  if (const char* e = getenv("FA_SPLIT_DN")) h->split_dn = pow2(std::max(1, std::min(8, atoi(e))));
   if (const char* e = getenv("FA_ATTN_PENALTY")) h->attn_penalty = std::max(0, atoi(e));
   auto bad = [&](fa_status st) { g_create_err = h->err; fa_destroy(h); return st; };
   if (cudaSetDevice(device) != cudaSuccess) return bad(fail(h, FA_ERR_CUDA, "cudaSetDevice(%d) failed", device));
@@ -497,6 +499,23 @@ static fa_status make_map(fa_handle* h, CUtensorMap* m, const void* base, uint64
   return FA_OK;
 }
 
+// 3D bf16 map viewing a row-major [rows][K] array as [K/64 atoms][rows][64]: one box
+// {64, box_rows, box_atoms} lands in shared memory as box_atoms consecutive 128B-swizzled atoms.
+static fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
+                           uint32_t box_rows, uint32_t box_atoms) {
+  auto enc = get_encode();
+  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {64, rows, K / 64};
+  cuuint64_t strides[2] = {K * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, box_atoms};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled (3D) failed (%d)", (int)r);
+  return FA_OK;
+}
+
 // ------------------------------------------------------------------ work plan
 // GEMM units per layer: QKV 20 x 128-row tiles (full K), O 8 tiles x split_o K-slices,
 // gate/up 64 tiles (full K), down 8 tiles x split_dn K-slices. Attention units: per
@@ -592,15 +611,19 @@ static fa_status build_params(fa_handle* h) {
   MAP(MAP_W_O, h->w_o, QD, (uint64_t)L * D, 64, 128);
   MAP(MAP_W_GU, h->w_gu, D, (uint64_t)L * 2 * F, 64, 128);
   MAP(MAP_W_DN, h->w_dn, F, (uint64_t)L * D, 64, 128);
-  MAP(MAP_XN, h->xn, D, h->NPAD, 64, h->NTILE);
-  MAP(MAP_ATTN, h->attn, QD, h->NPAD, 64, h->NTILE);
-  MAP(MAP_H, h->hbuf, F, h->NPAD, 64, h->NTILE);
-  MAP(MAP_Q, h->q, HD, (uint64_t)B * H * TPAD, 64, 128);
-  MAP(MAP_K, h->kcache, HD, (uint64_t)B * L * h->LPAD, 64, 128);
-  MAP(MAP_VT, h->vtcache, h->LPAD, (uint64_t)B * L * HD, 64, 128);
-  MAP(MAP_SK, h->sk, HD, (uint64_t)B * TPAD, 64, 64);
-  MAP(MAP_SVT, h->svt, TPAD, (uint64_t)B * HD, 64, 128);
 #undef MAP
+  const uint32_t ba = h->NTILE == 64 ? 4 : 2;  // 32 KB per activation TMA load
+#define MAP3(i, base, K, rows, br, bat) if ((st = make_map3(h, &p.maps[i], base, K, rows, br, bat)) != FA_OK) return st
+  MAP3(MAP_XN, h->xn, D, h->NPAD, h->NTILE, ba);
+  MAP3(MAP_ATTN, h->attn, QD, h->NPAD, h->NTILE, ba);
+  MAP3(MAP_H, h->hbuf, F, h->NPAD, h->NTILE, ba);
+  MAP3(MAP_Q, h->q, HD, (uint64_t)B * H * TPAD, 128, 4);
+  MAP3(MAP_K, h->kcache, HD, (uint64_t)B * L * h->LPAD, 128, 4);
+  MAP3(MAP_VT, h->vtcache, h->LPAD, (uint64_t)B * L * HD, 128, 2);
+  MAP3(MAP_SK, h->sk, HD, (uint64_t)B * TPAD, 64, 4);
+  MAP3(MAP_SVT, h->svt, TPAD, (uint64_t)B * HD, 128, 1);
+#undef MAP3
+  p.box_atoms = (int)ba;
   p.L = L; p.T = h->cfg.horizon; p.B = B; p.NT = h->NT; p.NPAD = h->NPAD; p.NTILE = h->NTILE; p.TG = h->TG;
   p.ngroups = h->ngroups; p.nsteps = h->cfg.num_steps; p.LPAD = h->LPAD; p.AD = h->cfg.action_dim;
   p.split_o = h->split_o; p.split_dn = h->split_dn;

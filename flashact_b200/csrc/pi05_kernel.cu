@@ -436,7 +436,7 @@ struct MmaCtx {
   int* err;
   const CUtensorMap* amap;
   uint32_t tmem;
-  int R, batoms, NTILE, TG, ngroups, tiles;
+  int R, batoms, NTILE, TG, ngroups, tiles, box_atoms;
 };
 
 // Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
@@ -448,10 +448,11 @@ __device__ __forceinline__ void load_b_batch(const MmaCtx& k, const GemmUnit& gu
   mbar_expect_tx(&k.bars->bfull, (uint32_t)((j1 - j0) * nt) * tile);
   const uint64_t pol = policy_evict_last();
   const int y0 = g * k.TG * k.NTILE;
-  for (int j = j0; j < j1; ++j)
-    for (int i = 0; i < nt; ++i)
-      tma_load_2d(k.work + (size_t)((j - j0) * nt + i) * tile, k.amap, &k.bars->bfull, (gu.katom0 + j) * 64,
-                  y0 + i * k.NTILE, pol);
+  // tile-major: item (j, i) at work + (i * (j1 - j0) + (j - j0)) * tile; one 3D box = box_atoms atoms
+  for (int i = 0; i < nt; ++i)
+    for (int j = j0; j < j1; j += k.box_atoms)
+      tma_load_3d(k.work + (size_t)(i * (j1 - j0) + (j - j0)) * tile, k.amap, &k.bars->bfull, 0, y0 + i * k.NTILE,
+                  gu.katom0 + j, pol);
 }
 
 __device__ __noinline__ bool mma_gemm(const Params& p, const Ctx& c, MmaState& st_shared, int m) {
@@ -461,6 +462,7 @@ __device__ __noinline__ bool mma_gemm(const Params& p, const Ctx& c, MmaState& s
   k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[act_map(m)];
   k.tmem = c.tmem; k.R = c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG; k.ngroups = p.ngroups;
   k.tiles = p.NPAD / p.NTILE;
+  k.box_atoms = p.box_atoms;
   const GemmUnit* const units = c.gu[m];
   const int nunits = c.gcnt[m];
   const uint32_t idesc = idesc_bf16(128, k.NTILE);
@@ -490,7 +492,7 @@ __device__ __noinline__ bool mma_gemm(const Params& p, const Ctx& c, MmaState& s
           const uint64_t da = sdesc_sw128(k.ring + (size_t)wslot * kAtomBytes);
           if (leader()) {
             for (int i = 0; i < nt; ++i) {
-              const uint64_t db = sdesc_sw128(k.work + (size_t)((j - j0) * nt + i) * tile);
+              const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j - j0)) * tile);
 #pragma unroll
               for (int s = 0; s < 4; ++s) tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, (j | s) != 0);
             }
@@ -716,21 +718,17 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
     const bool load_q = qkey != st.last_q;  // Q stays resident across units of one head pair
     if (load_q) {
       FA_ONE(mbar_expect_tx(&br->q_full, 4 * kAtomBytes));
-      for (int a = 0; a < 4; ++a)
-        FA_ONE(tma_load_2d(c_work + kQOff + a * kAtomBytes, &p_maps[MAP_Q], &br->q_full, a * 64,
-                           (au.b * H + 2 * au.hp) * TPAD, pol_kv));
+      FA_ONE(tma_load_3d(c_work + kQOff, &p_maps[MAP_Q], &br->q_full, 0, (au.b * H + 2 * au.hp) * TPAD, 0, pol_kv));
     }
     if (st.k_pre) {  // issued at the end of the previous attention stage
       st.k_pre = 0;
     } else {
       FA_ONE(mbar_expect_tx(&br->k_full, 4 * nk * 128));
-      for (int a = 0; a < 4; ++a) {
-        if (au.is_suffix)
-          FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_SK], &br->k_full, a * 64, au.b * TPAD, pol_kv));
-        else
-          FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_K], &br->k_full, a * 64,
-                             (au.b * p_L + l) * p_LPAD + au.chunk * KCH, pol_kv));
-      }
+      if (au.is_suffix)  // atom a of the action-token keys at KV + a * 8 KB
+        FA_ONE(tma_load_3d(c_work + kKVOff, &p_maps[MAP_SK], &br->k_full, 0, au.b * TPAD, 0, pol_kv));
+      else
+        FA_ONE(tma_load_3d(c_work + kKVOff, &p_maps[MAP_K], &br->k_full, 0, (au.b * p_L + l) * p_LPAD + au.chunk * KCH,
+                           0, pol_kv));
     }
     if (load_q) {
       if (!mbar_wait(&br->q_full, st.nq & 1, p_err, KERR_ATTN)) return false;
@@ -743,7 +741,7 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
     const uint32_t id_s = idesc_bf16(128, nk);
     for (int a = 0; a < 4; ++a) {
       const uint64_t dq = sdesc_sw128(c_work + kQOff + a * kAtomBytes);
-      const uint64_t dk = sdesc_sw128(c_work + kKVOff + a * kAtomBytes);
+      const uint64_t dk = sdesc_sw128(c_work + kKVOff + a * nk * 128);
 #pragma unroll
       for (int s = 0; s < 4; ++s) FA_ONE(tc_mma_bf16(c_tmem, dq + 2 * s, dk + 2 * s, id_s, (a | s) != 0));
     }
@@ -752,15 +750,13 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
     if (!mbar_wait(&br->kv_free, st.nu & 1, p_err, KERR_ATTN)) return false;
     const int nka = nk / 64;  // 64-key atoms
     FA_ONE(mbar_expect_tx(&br->v_full, nka * 2 * kAtomBytes));
-    for (int kk = 0; kk < nka; ++kk)
-      for (int hh = 0; hh < 2; ++hh) {
-        uint8_t* dst = c_work + kKVOff + (kk * 2 + hh) * kAtomBytes;
-        if (au.is_suffix)
-          FA_ONE(tma_load_2d(dst, &p_maps[MAP_SVT], &br->v_full, 0, au.b * HD + 128 * hh, pol_kv));
-        else
-          FA_ONE(tma_load_2d(dst, &p_maps[MAP_VT], &br->v_full, au.chunk * KCH + 64 * kk, (au.b * p_L + l) * HD + 128 * hh,
-                      pol_kv));
-      }
+    for (int hh = 0; hh < 2; ++hh) {  // V^T atom (dim half hh, key atom kk) at KV + (hh * nka + kk) * 16 KB
+      uint8_t* dst = c_work + kKVOff + hh * nka * kAtomBytes;
+      if (au.is_suffix)
+        FA_ONE(tma_load_3d(dst, &p_maps[MAP_SVT], &br->v_full, 0, au.b * HD + 128 * hh, 0, pol_kv));
+      else
+        FA_ONE(tma_load_3d(dst, &p_maps[MAP_VT], &br->v_full, 0, (au.b * p_L + l) * HD + 128 * hh, au.chunk * 2, pol_kv));
+    }
     if (!mbar_wait(&br->v_full, st.nu & 1, p_err, KERR_ATTN)) return false;
     if (u == 0) FA_ONE(trace_mark(kTrMmaB0));  // V in shared memory
     if (!mbar_wait(&br->p_full, st.nu & 1, p_err, KERR_ATTN)) return false;
@@ -770,7 +766,7 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
     for (int kk = 0; kk < nka; ++kk) {
       const uint64_t dp = sdesc_sw128(c_work + kPOff + kk * kAtomBytes);
       for (int hh = 0; hh < 2; ++hh) {
-        const uint64_t dv = sdesc_sw128(c_work + kKVOff + (kk * 2 + hh) * kAtomBytes);
+        const uint64_t dv = sdesc_sw128(c_work + kKVOff + (hh * nka + kk) * kAtomBytes);
 #pragma unroll
         for (int s = 0; s < 4; ++s) FA_ONE(tc_mma_bf16(c_tmem + 128 + 128 * hh, dp + 2 * s, dv + 2 * s, id_o, (kk | s) != 0));
       }
@@ -786,9 +782,8 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
     const AttnUnit au = c_au[0];
     const int ln = (l + 1) % p_L;
     FA_ONE(mbar_expect_tx(&br->k_full, 4 * KCH * 128));
-    for (int a = 0; a < 4; ++a)
-      FA_ONE(tma_load_2d(c_work + kKVOff + a * kAtomBytes, &p_maps[MAP_K], &br->k_full, a * 64,
-                         (au.b * p_L + ln) * p_LPAD + au.chunk * KCH, pol_kv));
+    FA_ONE(tma_load_3d(c_work + kKVOff, &p_maps[MAP_K], &br->k_full, 0, (au.b * p_L + ln) * p_LPAD + au.chunk * KCH, 0,
+                       pol_kv));
     st.k_pre = 1;
   }
   FA_ONE(trace_mark(kTrMmaDone));
