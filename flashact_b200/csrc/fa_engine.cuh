@@ -1,0 +1,373 @@
+// Model-independent engine of the denoise megakernels (sm_100a): warp / CTA helpers, the
+// bounded grid barrier, stage tracing, and the three GEMM roles — weight producer (warp 0),
+// tcgen05 MMA issuer (warp 1) and epilogue driver (warps 2-5). The roles are templates over a
+// model-traits type that supplies the per-layer matrices (row counts, tensor maps, activation
+// operand) and the fused epilogue; see pi05_kernel.cu and ma2_kernel.cu.
+//
+// Roles run as whole warps with uniform control flow; lane 0 alone issues TMA / tcgen05 /
+// commit instructions. Every field a role needs is copied into registers at entry: the inline
+// asm "memory" clobbers would otherwise force a reload through the generic Params / Ctx
+// references after every TMA or mbarrier operation.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "fa_engine_types.cuh"
+#include "fa_ptx.cuh"
+
+namespace fa {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// Named barriers: 1 = warps 1-5 (stage sequencing), 2 = warps 2-5 (epilogue group).
+// barrier.sync (non-.aligned): warp 1 reaches it with lane 0 arriving after the other lanes.
+__device__ __forceinline__ void sync_main() {
+  __syncwarp();
+  asm volatile("barrier.sync 1, 160;" ::: "memory");
+}
+__device__ __forceinline__ void sync_epi() {
+  __syncwarp();
+  asm volatile("barrier.sync 2, 128;" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Observation index of packed token n = b * T + t without an integer division: exact for
+// n < 2^16 because (n + 0.5) / T stays at least 0.5 / T away from an integer.
+__device__ __forceinline__ int tok_bi(float invT, int n) { return (int)(((float)n + 0.5f) * invT); }
+
+// Stage tracing (diagnostics): g_trp points at this CTA's stamps for the current stage (null
+// when the stage is not traced); g_t0 is the stage's start clock. Set by the barrier thread.
+__shared__ unsigned long long* g_trp;
+__shared__ unsigned long long g_t0;
+__device__ __forceinline__ void trace_mark(int slot) {
+  unsigned long long* tr = g_trp;
+  if (tr) tr[slot] = clock64() - g_t0;
+}
+
+// gelu with the tanh approximation (src/pi05/mk6.cu:79-82).
+// tanh by the hardware approximation (tanh.approx.f32, max relative error ~2^-11: below the
+// bf16 rounding the result gets next).
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(k0 * (x + 0.044715f * x * x * x)));
+  return 0.5f * x * (1.0f + t);
+}
+
+// Grid barrier among warps 1-5 of every CTA. `gen` counts barriers passed by this launch; the
+// counter only grows, so barrier k completes when it reaches (k+1) * gridDim.x. Bounded: on
+// timeout (or when another CTA already failed) it raises *err and returns false.
+template <class P>
+__device__ __noinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned long long* next_tr) {
+  __shared__ int s_ok;
+  sync_main();
+  if (threadIdx.x == 32) {
+    trace_mark(kTrBarArrive);
+    int ok = 1;
+    __threadfence();
+    fence_proxy_async_global();
+    if (!(blockIdx.x == 0 && (int)gen == p.inject_barrier)) atomicAdd(p.bar, 1u);
+    const uint32_t target = (gen + 1) * gridDim.x;
+    uint32_t i = 0;
+    for (;; ++i) {
+      uint32_t v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.bar) : "memory");
+      if (v >= target) break;
+      if (*(volatile int*)p.err) { ok = 0; break; }
+      if (i > p.spin_limit) { atomicCAS(p.err, 0, KERR_BARRIER); ok = 0; break; }
+      if (i > 64) __nanosleep(32);
+    }
+    __threadfence();
+    fence_proxy_async_global();
+    s_ok = ok;
+    g_t0 = clock64();
+    g_trp = next_tr;
+    if (next_tr) next_tr[kTrStart] = g_t0;
+  }
+  sync_main();
+  return s_ok != 0;
+}
+
+// Block-wide sum over the 128 epilogue threads.
+__device__ __forceinline__ float epi_sum(float v, float* red) {
+  const int e = threadIdx.x - 64;
+  v = warp_sum(v);
+  if ((e & 31) == 0) red[e >> 5] = v;
+  sync_epi();
+  float s = red[0] + red[1] + red[2] + red[3];
+  sync_epi();
+  return s;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The producer and MMA roles run as whole warps (uniform control flow, every lane waits on
+// the same barriers) and only lane 0 issues TMA / tcgen05 / commit instructions.
+__device__ __forceinline__ bool leader() { return (threadIdx.x & 31) == 0; }
+#define FA_ONE(stmt)      \
+  do {                    \
+    if (leader()) { stmt; } \
+  } while (0)
+
+// ------------------------------------------------------------------ CTA context
+struct Bars {
+  uint64_t wfull[kMaxRing], wempty[kMaxRing];
+  uint64_t bfull, bempty;  // activation batch loaded / consumed
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
+};
+struct Ctx {
+  uint8_t* ring;  // ring_slots x 16 KB
+  uint8_t* work;  // activation atoms (GEMM) or Q | K/V | P (attention)
+  Bars* bars;
+  uint32_t tmem;
+  int ring_slots;
+  int batoms;               // activation atoms that fit in the work area at once
+  uint8_t* stage;           // 16 KB epilogue staging area (coalesced bf16 output writes)
+  const GemmUnit* gu[kMaxMats];  // this CTA's units per matrix (shared-memory copy of the plan)
+  int gcnt[kMaxMats];
+  const AttnUnit* au;
+  int acnt;
+};
+
+template <class P>
+__device__ __forceinline__ int group_tiles(const P& p, int g) {
+  const int tiles = p.NPAD / p.NTILE;
+  const int rem = tiles - g * p.TG;
+  return rem < p.TG ? rem : p.TG;
+}
+
+// ------------------------------------------------------------------ warp 0: weight producer
+// Walks (step, layer, GEMM matrix, unit, token group, K atom) — the exact order the MMA lane
+// consumes — and keeps the ring full. It never waits on activations.
+template <class Model>
+__device__ __noinline__ void run_producer(const typename Model::Params& p, const Ctx& c) {
+  // Every field is read once into registers: the inline-asm memory clobbers would otherwise
+  // force a reload through the generic Params/Ctx references after each TMA / mbarrier op.
+  const uint64_t pol = policy_evict_first();
+  const int R = c.ring_slots, nsteps = p.nsteps, L = p.L, ngroups = p.ngroups;
+  uint8_t* const ring = c.ring;
+  Bars* const bars = c.bars;
+  int* const err = p.err;
+  const CUtensorMap* const maps = p.maps;
+  unsigned long long* const trace = p.trace;
+  const int tstep = p.trace_step, tlayer = p.trace_layer;
+  const GemmUnit* gul[Model::kMats];
+  int gcnt[Model::kMats];
+#pragma unroll
+  for (int m = 0; m < Model::kMats; ++m) { gul[m] = c.gu[m]; gcnt[m] = c.gcnt[m]; }
+  uint32_t it = 0;
+  bool ok = true;
+  for (int step = 0; ok && step < nsteps; ++step)
+    for (int l = 0; ok && l < L; ++l)
+      for (int m = 0; ok && m < Model::kMats; ++m) {
+        const int rows = Model::rows(m);
+        for (int u = 0; ok && u < gcnt[m]; ++u) {
+          const GemmUnit gu = gul[m][u];
+          for (int g = 0; ok && g < ngroups; ++g)
+            for (int j = 0; j < gu.natoms; ++j, ++it) {
+              const int slot = it % R, round = it / R;
+              if (round > 0 && !mbar_wait(&bars->wempty[slot], (round - 1) & 1, err, KERR_PRODUCER)) {
+                ok = false;
+                break;
+              }
+              if (leader()) {
+                if (trace && u == 0 && g == 0 && j == 0 && step == tstep && l == tlayer) {
+                  const int stg = Model::trace_stage(m);
+                  trace[((size_t)stg * gridDim.x + blockIdx.x) * kTrStride + kTrProdIssue] = clock64();
+                }
+                mbar_expect_tx(&bars->wfull[slot], kAtomBytes);
+                tma_load_2d(ring + (size_t)slot * kAtomBytes, maps + Model::wmap(m), &bars->wfull[slot], (gu.katom0 + j) * 64,
+                            l * rows + gu.mtile * 128, pol);
+              }
+              __syncwarp();
+            }
+        }
+      }
+  // Drain: never leave a TMA write into shared memory in flight at exit.
+  const uint32_t first = it > (uint32_t)R ? it - R : 0;
+  for (uint32_t k = first; k < it; ++k) mbar_wait(&bars->wfull[k % R], (k / R) & 1, err, KERR_PRODUCER);
+}
+
+// ------------------------------------------------------------------ warp 1 lane 0: GEMM MMAs
+// MMA-lane state; lives in shared memory (one instance per CTA, touched by one thread).
+struct MmaState {
+  uint32_t wit;          // weight-ring items consumed
+  uint32_t bload;        // activation batches loaded (phase of bfull)
+  uint32_t bfree;        // activation batches released (phase of bempty)
+  uint32_t acc;          // accumulator buffers used
+  uint32_t nq, nu;       // attention: Q loads, units
+  int last_q;
+  int k_pre;             // the next attention unit's prefix K is already loading (prefetched)
+};
+
+// Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
+// on ONE barrier so the MMA lane pays a single wait per batch. Item (j, i) sits at
+// work + ((j - j0) * nt + i) * tile bytes.
+// Register copy of what the GEMM MMA loop needs (see run_producer for why).
+struct MmaCtx {
+  uint8_t* ring;
+  uint8_t* work;
+  Bars* bars;
+  int* err;
+  const CUtensorMap* amap;
+  uint32_t tmem;
+  int R, batoms, NTILE, TG, ngroups, tiles, box_atoms;
+};
+
+// Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
+// on ONE barrier so the MMA lane pays a single wait per batch. Item (j, i) sits at
+// work + ((j - j0) * nt + i) * tile bytes.
+__device__ __forceinline__ void load_b_batch(const MmaCtx& k, const GemmUnit& gu, int g, int nt, int j0, int j1) {
+  if (!leader()) return;
+  const uint32_t tile = k.NTILE * 128;
+  mbar_expect_tx(&k.bars->bfull, (uint32_t)((j1 - j0) * nt) * tile);
+  const uint64_t pol = policy_evict_last();
+  const int y0 = g * k.TG * k.NTILE;
+  // tile-major: item (j, i) at work + (i * (j1 - j0) + (j - j0)) * tile; one 3D box = box_atoms atoms
+  for (int i = 0; i < nt; ++i)
+    for (int j = j0; j < j1; j += k.box_atoms)
+      tma_load_3d(k.work + (size_t)(i * (j1 - j0) + (j - j0)) * tile, k.amap, &k.bars->bfull, 0, y0 + i * k.NTILE,
+                  gu.katom0 + j, pol);
+}
+
+template <class Model>
+__device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
+  FA_ONE(trace_mark(12));
+  MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
+  MmaCtx k;
+  k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[Model::act_map(m)];
+  k.tmem = c.tmem; k.R = c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG; k.ngroups = p.ngroups;
+  k.tiles = p.NPAD / p.NTILE;
+  k.box_atoms = p.box_atoms;
+  const GemmUnit* const units = c.gu[m];
+  const int nunits = c.gcnt[m];
+  const uint32_t idesc = idesc_bf16(128, k.NTILE);
+  const uint32_t tile = k.NTILE * 128;
+  Bars* const bars = k.bars;
+  for (int u = 0; u < nunits; ++u) {
+    const GemmUnit gu = units[u];
+    for (int g = 0; g < k.ngroups; ++g) {
+      const int nt = min(k.TG, k.tiles - g * k.TG);
+      const int per_batch = max(1, k.batoms / nt);  // K atoms per activation batch
+      int j1 = min((int)gu.natoms, per_batch);
+      if (u == 0 && g == 0) FA_ONE(trace_mark(13));
+      load_b_batch(k, gu, g, nt, 0, j1);
+      if (u == 0 && g == 0) FA_ONE(trace_mark(kTrMmaPre));
+      const int a = st.acc & 1;
+      if (st.acc >= 2 && !mbar_wait(&bars->acc_empty[a], ((st.acc >> 1) - 1) & 1, k.err, KERR_MMA)) return false;
+      tc_fence_after();
+      const uint32_t tacc = k.tmem + a * 256;
+      for (int j0 = 0; j0 < gu.natoms;) {
+        if (!mbar_wait(&bars->bfull, st.bload & 1, k.err, KERR_MMA)) return false;
+        ++st.bload;
+        if (u == 0 && g == 0 && j0 == 0) FA_ONE(trace_mark(kTrMmaB0));
+        for (int j = j0; j < j1; ++j) {
+          const int wslot = st.wit % k.R;
+          if (!mbar_wait(&bars->wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
+          if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(kTrMmaW0));
+          const uint64_t da = sdesc_sw128(k.ring + (size_t)wslot * kAtomBytes);
+          if (leader()) {
+            for (int i = 0; i < nt; ++i) {
+              const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j - j0)) * tile);
+#pragma unroll
+              for (int s = 0; s < 4; ++s) tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, (j | s) != 0);
+            }
+            tc_commit(&bars->wempty[wslot]);
+          }
+          __syncwarp();
+          ++st.wit;
+        }
+        j0 = j1;
+        if (j0 < gu.natoms) {  // reuse the activation area: wait for this batch's MMAs first
+          FA_ONE(tc_commit(&bars->bempty));
+          if (!mbar_wait(&bars->bempty, st.bfree & 1, k.err, KERR_MMA)) return false;
+          ++st.bfree;
+          j1 = min((int)gu.natoms, j0 + per_batch);
+          load_b_batch(k, gu, g, nt, j0, j1);
+        }
+      }
+      FA_ONE(tc_commit(&bars->acc_full[a]));
+      ++st.acc;
+    }
+  }
+  // The next stage overwrites the activation area: its TMA loads must follow these MMAs.
+  FA_ONE(tc_commit(&bars->bempty));
+  if (!mbar_wait(&bars->bempty, st.bfree & 1, k.err, KERR_MMA)) return false;
+  ++st.bfree;
+  FA_ONE(trace_mark(kTrMmaDone));
+  if (leader()) st_shared = st;
+  __syncwarp();
+  return true;
+}
+
+// GEMM epilogue driver (warps 2-5): waits for each accumulator, walks it in 16-token chunks
+// through Model::epi_tile and, for staged outputs, copies each 64-token sub-tile out with
+// Model::epi_copy_out.
+template <class Model>
+__device__ __noinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
+  const int row = qd * 32 + lane;
+  typename Model::Epi e;
+  Model::epi_load(e, p, c, l);
+  const int NTILE = p.NTILE, TG = p.TG, ngroups = p.ngroups, tiles = p.NPAD / p.NTILE;
+  int* const err = p.err;
+  Bars* const bars = c.bars;
+  const uint32_t taddr = c.tmem + ((uint32_t)(qd * 32) << 16);
+  const GemmUnit* const units = c.gu[m];
+  const int nunits = c.gcnt[m];
+  for (int u = 0; u < nunits; ++u) {
+    const GemmUnit gu = units[u];
+    for (int g = 0; g < ngroups; ++g) {
+      const int nt = min(TG, tiles - g * TG);
+      const int a = ecnt & 1;
+      if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;
+      if (u == 0 && g == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
+      tc_fence_after();
+      const bool staged = Model::staged(m, gu);
+      for (int i = 0; i < nt; ++i) {
+#pragma unroll 1
+        for (int c64 = 0; c64 < NTILE; c64 += 64) {
+          const int nb0 = g * TG * NTILE + i * NTILE + c64;
+#pragma unroll 1
+          for (int cc = 0; cc < 64; cc += 16) {
+            float v[16];
+            tmem_ld16(taddr + a * 256 + i * NTILE + c64 + cc, v);
+            tc_wait_ld();
+            if (u == 0 && g == 0 && i == 0 && c64 + cc == 0 && threadIdx.x == 64) trace_mark(14);
+            Model::epi_tile(e, gu, m, qd, lane, row, nb0 + cc, nb0, v);
+            if (u == 0 && g == 0 && i == 0 && c64 + cc == 0 && threadIdx.x == 64) trace_mark(15);
+          }
+          if (staged) {
+            sync_epi();
+            Model::epi_copy_out(e, gu, m, nb0);
+            sync_epi();
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty[a]);
+      ++ecnt;
+    }
+  }
+  return ecnt;
+}
+
+}  // namespace fa

@@ -1,0 +1,54 @@
+// Types and constants shared by host and device code of every denoise megakernel in this
+// library (pi0.5 and MolmoAct2): the per-CTA work plan, shared-memory budget, trace slots and
+// in-kernel error codes.
+#pragma once
+#include <cstdint>
+
+namespace fa {
+
+constexpr int kThreads = 192;              // warp 0 producer, warp 1 MMA, warps 2-5 epilogue / vector work
+constexpr int kAtomBytes = 128 * 64 * 2;   // one 128-row x 64-col bf16 atom, 128-byte swizzle
+constexpr int kSmemUse = 224 * 1024;       // dynamic shared memory used (ring + work area)
+constexpr int kSmemDyn = kSmemUse + 1024;  // + alignment slack
+constexpr int kMaxRing = 12;               // weight-ring slots
+constexpr int kMaxBBytes = 128 * 1024;     // activation (B operand) area of a GEMM CTA, upper bound
+constexpr int kMaxBAtoms = 16;             // activation atoms resident at once
+constexpr int kMaxGU = 48;                 // GEMM units per CTA per layer (all matrices)
+constexpr int kMaxAU = 64;                 // attention units per CTA per layer
+constexpr int kMaxMats = 6;                // GEMM matrices per layer
+constexpr int kStageBytes = 16 * 1024;     // epilogue staging area
+constexpr int kMaxStages = 16;             // traced stage kinds
+
+struct GemmUnit {
+  uint16_t mtile;   // 128-row tile of the packed weight
+  uint16_t katom0;  // first 64-wide K atom
+  uint16_t natoms;  // K atoms in this unit
+  uint16_t split;   // index of the fp32 partial slice it writes (K-split stages)
+};
+struct AttnUnit {
+  uint16_t b, hp, chunk, is_suffix;  // observation, head (pair), key chunk, action-token chunk flag
+};
+struct CtaPlan {
+  int g_off[kMaxMats], g_cnt[kMaxMats];  // GEMM units of this CTA per matrix, same for every layer
+  int a_off, a_cnt;                      // attention units of this CTA
+  int ring_slots;                        // weight-ring depth
+  int b_bytes;                           // activation area of this CTA
+};
+
+enum TraceSlot : int {
+  kTrStart = 0,      // absolute clock64 at stage start (after the barrier); others are offsets
+  kTrMmaW0 = 1,      // MMA lane: first weight atom ready / attention: Q and K ready
+  kTrMmaB0 = 2,      // MMA lane: activation atoms ready / attention: V ready
+  kTrMmaDone = 3,    // MMA lane: last accumulator committed
+  kTrEpiAcc0 = 4,    // epilogue: first accumulator ready
+  kTrEpiDone = 5,    // epilogue: stage work done
+  kTrBarArrive = 6,  // barrier thread: arrived
+  kTrProdIssue = 7,  // producer: ABSOLUTE clock64 when it issued this stage's first weight atom
+  kTrMmaPre = 8,     // MMA lane: activation loads issued
+  kTrStride = 16
+};
+
+// Error codes written to the launch's error word.
+enum KernelError : int { KERR_BARRIER = 1, KERR_PRODUCER = 2, KERR_MMA = 3, KERR_EPI = 4, KERR_ATTN = 5 };
+
+}  // namespace fa

@@ -7,6 +7,8 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include "fa_engine_types.cuh"
+
 namespace fa {
 namespace pi05 {
 
@@ -21,15 +23,6 @@ constexpr int TPAD = 64;    // action tokens padded per (observation, head) for 
 constexpr int KCH = 128;    // prefix keys per attention chunk
 constexpr int MAX_CH = 31;  // prefix chunks per observation (max_prefix <= 3968); index MAX_CH = action chunk
 
-constexpr int kThreads = 192;  // warp 0 producer, warp 1 MMA, warps 2-5 epilogue / vector work
-constexpr int kAtomBytes = 128 * 64 * 2;  // one 128-row x 64-col bf16 SW128 atom
-constexpr int kSmemUse = 224 * 1024;
-constexpr int kSmemDyn = kSmemUse + 1024;  // + alignment slack
-constexpr int kMaxRing = 12;
-constexpr int kMaxBBytes = 128 * 1024;  // activation (B operand) area of a GEMM CTA, upper bound
-constexpr int kMaxBAtoms = 16;          // activation atoms resident at once
-constexpr int kMaxGU = 48;              // GEMM units per CTA per layer (all matrices)
-constexpr int kMaxAU = 64;              // attention units per CTA per layer
 constexpr int kAttnWork = 160 * 1024;  // Q 64K | K/V 64K | P 32K
 
 enum Mat : int { MAT_QKV = 0, MAT_O = 1, MAT_GU = 2, MAT_DN = 3 };
@@ -41,22 +34,6 @@ enum Map : int {
 };
 enum Stage : int {
   ST_NORM1 = 0, ST_QKV, ST_ATTN, ST_MERGE, ST_O, ST_NORM2, ST_GU, ST_DN, ST_FINAL, NUM_STAGES
-};
-
-struct GemmUnit {
-  uint16_t mtile;   // 128-row tile of the packed weight
-  uint16_t katom0;  // first 64-wide K atom
-  uint16_t natoms;  // K atoms in this unit
-  uint16_t split;   // index of the fp32 partial slice it writes (K-split stages)
-};
-struct AttnUnit {
-  uint16_t b, hp, chunk, is_suffix;  // observation, head pair, key chunk
-};
-struct CtaPlan {
-  int g_off[4], g_cnt[4];  // GEMM units of this CTA per matrix, same for every layer
-  int a_off, a_cnt;        // attention units of this CTA
-  int ring_slots;          // weight-ring depth (attention CTAs keep room for Q/K/V/P)
-  int b_bytes;             // activation area of this CTA (the rest of shared memory is ring)
 };
 
 struct Params {
@@ -107,21 +84,5 @@ struct Params {
   unsigned long long* trace;
   int trace_step, trace_layer;
 };
-enum TraceSlot : int {
-  kTrStart = 0,      // absolute clock64 at stage start (after the barrier); others are offsets
-  kTrMmaW0 = 1,      // MMA lane: first weight atom ready
-  kTrMmaB0 = 2,      // MMA lane: activation atoms ready
-  kTrMmaDone = 3,    // MMA lane: last accumulator committed
-  kTrEpiAcc0 = 4,    // epilogue: first accumulator ready
-  kTrEpiDone = 5,    // epilogue: stage work done
-  kTrBarArrive = 6,  // barrier thread: arrived
-  kTrProdIssue = 7,  // producer: ABSOLUTE clock64 when it issued this stage's first weight atom
-  kTrMmaPre = 8,     // MMA lane: activation loads issued
-  kTrStride = 16
-};
-
-// Error codes written to *err by the kernel.
-enum KernelError : int { KERR_BARRIER = 1, KERR_PRODUCER = 2, KERR_MMA = 3, KERR_EPI = 4, KERR_ATTN = 5 };
-
 }  // namespace pi05
 }  // namespace fa

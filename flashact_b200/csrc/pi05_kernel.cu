@@ -14,108 +14,13 @@
 //   warps 2-5 epilogue + vector work: TMEM -> registers (tcgen05.ld) -> fused epilogues
 //           (RoPE, GeGLU, split-K partials), softmax, adaRMSNorm, merge, final projection.
 // Stages of a layer are separated by a bounded grid barrier (a counter in global memory).
+#include "fa_engine.cuh"
 #include "fa_pi05.cuh"
-#include "fa_ptx.cuh"
 
 namespace fa {
 namespace pi05 {
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-// Named barriers: 1 = warps 1-5 (stage sequencing), 2 = warps 2-5 (epilogue group).
-// barrier.sync (non-.aligned): warp 1 reaches it with lane 0 arriving after the other lanes.
-__device__ __forceinline__ void sync_main() {
-  __syncwarp();
-  asm volatile("barrier.sync 1, 160;" ::: "memory");
-}
-__device__ __forceinline__ void sync_epi() {
-  __syncwarp();
-  asm volatile("barrier.sync 2, 128;" ::: "memory");
-}
-
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Observation index of packed token n = b * T + t without an integer division: exact for
-// n < 2^16 because (n + 0.5) / T stays at least 0.5 / T away from an integer.
-__device__ __forceinline__ int tok_bi(float invT, int n) { return (int)(((float)n + 0.5f) * invT); }
-__device__ __forceinline__ int tok_b(const Params& p, int n) { return tok_bi(p.invT, n); }
-
-// Stage tracing (diagnostics): g_trp points at this CTA's stamps for the current stage (null
-// when the stage is not traced); g_t0 is the stage's start clock. Set by the barrier thread.
-__shared__ unsigned long long* g_trp;
-__shared__ unsigned long long g_t0;
-__device__ __forceinline__ void trace_mark(int slot) {
-  unsigned long long* tr = g_trp;
-  if (tr) tr[slot] = clock64() - g_t0;
-}
-
-// gelu with the tanh approximation (src/pi05/mk6.cu:79-82).
-// tanh by the hardware approximation (tanh.approx.f32, max relative error ~2^-11: below the
-// bf16 rounding the result gets next).
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(k0 * (x + 0.044715f * x * x * x)));
-  return 0.5f * x * (1.0f + t);
-}
-
-// Grid barrier among warps 1-5 of every CTA. `gen` counts barriers passed by this launch; the
-// counter only grows, so barrier k completes when it reaches (k+1) * gridDim.x. Bounded: on
-// timeout (or when another CTA already failed) it raises *err and returns false.
-__device__ __noinline__ bool grid_barrier(const Params& p, uint32_t gen, unsigned long long* next_tr) {
-  __shared__ int s_ok;
-  sync_main();
-  if (threadIdx.x == 32) {
-    trace_mark(kTrBarArrive);
-    int ok = 1;
-    __threadfence();
-    fence_proxy_async_global();
-    if (!(blockIdx.x == 0 && (int)gen == p.inject_barrier)) atomicAdd(p.bar, 1u);
-    const uint32_t target = (gen + 1) * gridDim.x;
-    uint32_t i = 0;
-    for (;; ++i) {
-      uint32_t v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.bar) : "memory");
-      if (v >= target) break;
-      if (*(volatile int*)p.err) { ok = 0; break; }
-      if (i > p.spin_limit) { atomicCAS(p.err, 0, KERR_BARRIER); ok = 0; break; }
-      if (i > 64) __nanosleep(32);
-    }
-    __threadfence();
-    fence_proxy_async_global();
-    s_ok = ok;
-    g_t0 = clock64();
-    g_trp = next_tr;
-    if (next_tr) next_tr[kTrStart] = g_t0;
-  }
-  sync_main();
-  return s_ok != 0;
-}
-
 // ------------------------------------------------------------------ vector stages (warps 2-5)
-// Block-wide sum over the 128 epilogue threads.
-__device__ __forceinline__ float epi_sum(float v, float* red) {
-  const int e = threadIdx.x - 64;
-  v = warp_sum(v);
-  if ((e & 31) == 0) red[e >> 5] = v;
-  sync_epi();
-  float s = red[0] + red[1] + red[2] + red[3];
-  sync_epi();
-  return s;
-}
-
 // adaRMSNorm of one token row already held as 8 values per thread (dims e*4.. and 512+e*4..):
 // xn = x * rsqrt(mean(x^2) + 1e-6) * (1 + scale) + shift, stored as bf16 (src/pi05/mk6.cu:139-164).
 __device__ __forceinline__ void rms_store(const Params& p, int n, const float v[8], const float* mod, float* red) {
@@ -186,6 +91,8 @@ __device__ __forceinline__ void load_residual(const Params& p, int n, const floa
     v[hlf * 4 + 0] = x[hlf].x; v[hlf * 4 + 1] = x[hlf].y; v[hlf * 4 + 2] = x[hlf].z; v[hlf * 4 + 3] = x[hlf].w;
   }
 }
+
+__device__ __forceinline__ int tok_b(const Params& p, int n) { return tok_bi(p.invT, n); }
 
 __device__ __forceinline__ const float* mod_ptr(const Params& p, int step, int l, int which) {
   return p.mods + ((size_t)(step * p.L + l) * 2 + which) * MOD;
@@ -321,209 +228,6 @@ __device__ __noinline__ void stage_merge(const Params& p) {
   }
 }
 
-// The producer and MMA roles run as whole warps (uniform control flow, every lane waits on
-// the same barriers) and only lane 0 issues TMA / tcgen05 / commit instructions.
-__device__ __forceinline__ bool leader() { return (threadIdx.x & 31) == 0; }
-#define FA_ONE(stmt)      \
-  do {                    \
-    if (leader()) { stmt; } \
-  } while (0)
-
-// ------------------------------------------------------------------ CTA context
-struct Bars {
-  uint64_t wfull[kMaxRing], wempty[kMaxRing];
-  uint64_t bfull, bempty;  // activation batch loaded / consumed
-  uint64_t acc_full[2], acc_empty[2];
-  uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
-};
-struct Ctx {
-  uint8_t* ring;  // ring_slots x 16 KB
-  uint8_t* work;  // activation atoms (GEMM) or Q | K/V | P (attention)
-  Bars* bars;
-  uint32_t tmem;
-  int ring_slots;
-  int batoms;               // activation atoms that fit in the work area at once
-  uint8_t* stage;           // 16 KB epilogue staging area (coalesced bf16 output writes)
-  const GemmUnit* gu[4];    // this CTA's units per matrix (shared-memory copy of the plan)
-  int gcnt[4];
-  const AttnUnit* au;
-  int acnt;
-};
-
-__host__ __device__ constexpr int mat_rows(int m) {
-  return m == MAT_QKV ? QKV_ROWS : (m == MAT_GU ? 2 * F : D);
-}
-__device__ __forceinline__ int act_map(int m) {
-  return m == MAT_O ? MAP_ATTN : (m == MAT_DN ? MAP_H : MAP_XN);
-}
-__device__ __forceinline__ int group_tiles(const Params& p, int g) {
-  const int tiles = p.NPAD / p.NTILE;
-  const int rem = tiles - g * p.TG;
-  return rem < p.TG ? rem : p.TG;
-}
-
-// ------------------------------------------------------------------ warp 0: weight producer
-// Walks (step, layer, GEMM matrix, unit, token group, K atom) — the exact order the MMA lane
-// consumes — and keeps the ring full. It never waits on activations.
-__device__ __noinline__ void run_producer(const Params& p, const Ctx& c) {
-  // Every field is read once into registers: the inline-asm memory clobbers would otherwise
-  // force a reload through the generic Params/Ctx references after each TMA / mbarrier op.
-  const uint64_t pol = policy_evict_first();
-  const int R = c.ring_slots, nsteps = p.nsteps, L = p.L, ngroups = p.ngroups;
-  uint8_t* const ring = c.ring;
-  Bars* const bars = c.bars;
-  int* const err = p.err;
-  const CUtensorMap* const wmaps = &p.maps[MAP_W_QKV];
-  unsigned long long* const trace = p.trace;
-  const int tstep = p.trace_step, tlayer = p.trace_layer;
-  const GemmUnit* gul[4];
-  int gcnt[4];
-#pragma unroll
-  for (int m = 0; m < 4; ++m) { gul[m] = c.gu[m]; gcnt[m] = c.gcnt[m]; }
-  uint32_t it = 0;
-  bool ok = true;
-  for (int step = 0; ok && step < nsteps; ++step)
-    for (int l = 0; ok && l < L; ++l)
-      for (int m = 0; ok && m < 4; ++m) {
-        const int rows = mat_rows(m);
-        for (int u = 0; ok && u < gcnt[m]; ++u) {
-          const GemmUnit gu = gul[m][u];
-          for (int g = 0; ok && g < ngroups; ++g)
-            for (int j = 0; j < gu.natoms; ++j, ++it) {
-              const int slot = it % R, round = it / R;
-              if (round > 0 && !mbar_wait(&bars->wempty[slot], (round - 1) & 1, err, KERR_PRODUCER)) {
-                ok = false;
-                break;
-              }
-              if (leader()) {
-                if (trace && u == 0 && g == 0 && j == 0 && step == tstep && l == tlayer) {
-                  const int stg = m == MAT_QKV ? ST_QKV : m == MAT_O ? ST_O : m == MAT_GU ? ST_GU : ST_DN;
-                  trace[((size_t)stg * gridDim.x + blockIdx.x) * kTrStride + kTrProdIssue] = clock64();
-                }
-                mbar_expect_tx(&bars->wfull[slot], kAtomBytes);
-                tma_load_2d(ring + (size_t)slot * kAtomBytes, wmaps + m, &bars->wfull[slot], (gu.katom0 + j) * 64,
-                            l * rows + gu.mtile * 128, pol);
-              }
-              __syncwarp();
-            }
-        }
-      }
-  // Drain: never leave a TMA write into shared memory in flight at exit.
-  const uint32_t first = it > (uint32_t)R ? it - R : 0;
-  for (uint32_t k = first; k < it; ++k) mbar_wait(&bars->wfull[k % R], (k / R) & 1, err, KERR_PRODUCER);
-}
-
-// ------------------------------------------------------------------ warp 1 lane 0: GEMM MMAs
-// MMA-lane state; lives in shared memory (one instance per CTA, touched by one thread).
-struct MmaState {
-  uint32_t wit;          // weight-ring items consumed
-  uint32_t bload;        // activation batches loaded (phase of bfull)
-  uint32_t bfree;        // activation batches released (phase of bempty)
-  uint32_t acc;          // accumulator buffers used
-  uint32_t nq, nu;       // attention: Q loads, units
-  int last_q;
-  int k_pre;             // the next attention unit's prefix K is already loading (prefetched)
-};
-
-// Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
-// on ONE barrier so the MMA lane pays a single wait per batch. Item (j, i) sits at
-// work + ((j - j0) * nt + i) * tile bytes.
-// Register copy of what the GEMM MMA loop needs (see run_producer for why).
-struct MmaCtx {
-  uint8_t* ring;
-  uint8_t* work;
-  Bars* bars;
-  int* err;
-  const CUtensorMap* amap;
-  uint32_t tmem;
-  int R, batoms, NTILE, TG, ngroups, tiles, box_atoms;
-};
-
-// Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
-// on ONE barrier so the MMA lane pays a single wait per batch. Item (j, i) sits at
-// work + ((j - j0) * nt + i) * tile bytes.
-__device__ __forceinline__ void load_b_batch(const MmaCtx& k, const GemmUnit& gu, int g, int nt, int j0, int j1) {
-  if (!leader()) return;
-  const uint32_t tile = k.NTILE * 128;
-  mbar_expect_tx(&k.bars->bfull, (uint32_t)((j1 - j0) * nt) * tile);
-  const uint64_t pol = policy_evict_last();
-  const int y0 = g * k.TG * k.NTILE;
-  // tile-major: item (j, i) at work + (i * (j1 - j0) + (j - j0)) * tile; one 3D box = box_atoms atoms
-  for (int i = 0; i < nt; ++i)
-    for (int j = j0; j < j1; j += k.box_atoms)
-      tma_load_3d(k.work + (size_t)(i * (j1 - j0) + (j - j0)) * tile, k.amap, &k.bars->bfull, 0, y0 + i * k.NTILE,
-                  gu.katom0 + j, pol);
-}
-
-__device__ __noinline__ bool mma_gemm(const Params& p, const Ctx& c, MmaState& st_shared, int m) {
-  FA_ONE(trace_mark(12));
-  MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
-  MmaCtx k;
-  k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[act_map(m)];
-  k.tmem = c.tmem; k.R = c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG; k.ngroups = p.ngroups;
-  k.tiles = p.NPAD / p.NTILE;
-  k.box_atoms = p.box_atoms;
-  const GemmUnit* const units = c.gu[m];
-  const int nunits = c.gcnt[m];
-  const uint32_t idesc = idesc_bf16(128, k.NTILE);
-  const uint32_t tile = k.NTILE * 128;
-  Bars* const bars = k.bars;
-  for (int u = 0; u < nunits; ++u) {
-    const GemmUnit gu = units[u];
-    for (int g = 0; g < k.ngroups; ++g) {
-      const int nt = min(k.TG, k.tiles - g * k.TG);
-      const int per_batch = max(1, k.batoms / nt);  // K atoms per activation batch
-      int j1 = min((int)gu.natoms, per_batch);
-      if (u == 0 && g == 0) FA_ONE(trace_mark(13));
-      load_b_batch(k, gu, g, nt, 0, j1);
-      if (u == 0 && g == 0) FA_ONE(trace_mark(kTrMmaPre));
-      const int a = st.acc & 1;
-      if (st.acc >= 2 && !mbar_wait(&bars->acc_empty[a], ((st.acc >> 1) - 1) & 1, k.err, KERR_MMA)) return false;
-      tc_fence_after();
-      const uint32_t tacc = k.tmem + a * 256;
-      for (int j0 = 0; j0 < gu.natoms;) {
-        if (!mbar_wait(&bars->bfull, st.bload & 1, k.err, KERR_MMA)) return false;
-        ++st.bload;
-        if (u == 0 && g == 0 && j0 == 0) FA_ONE(trace_mark(kTrMmaB0));
-        for (int j = j0; j < j1; ++j) {
-          const int wslot = st.wit % k.R;
-          if (!mbar_wait(&bars->wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
-          if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(kTrMmaW0));
-          const uint64_t da = sdesc_sw128(k.ring + (size_t)wslot * kAtomBytes);
-          if (leader()) {
-            for (int i = 0; i < nt; ++i) {
-              const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j - j0)) * tile);
-#pragma unroll
-              for (int s = 0; s < 4; ++s) tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, (j | s) != 0);
-            }
-            tc_commit(&bars->wempty[wslot]);
-          }
-          __syncwarp();
-          ++st.wit;
-        }
-        j0 = j1;
-        if (j0 < gu.natoms) {  // reuse the activation area: wait for this batch's MMAs first
-          FA_ONE(tc_commit(&bars->bempty));
-          if (!mbar_wait(&bars->bempty, st.bfree & 1, k.err, KERR_MMA)) return false;
-          ++st.bfree;
-          j1 = min((int)gu.natoms, j0 + per_batch);
-          load_b_batch(k, gu, g, nt, j0, j1);
-        }
-      }
-      FA_ONE(tc_commit(&bars->acc_full[a]));
-      ++st.acc;
-    }
-  }
-  // The next stage overwrites the activation area: its TMA loads must follow these MMAs.
-  FA_ONE(tc_commit(&bars->bempty));
-  if (!mbar_wait(&bars->bempty, st.bfree & 1, k.err, KERR_MMA)) return false;
-  ++st.bfree;
-  FA_ONE(trace_mark(kTrMmaDone));
-  if (leader()) st_shared = st;
-  __syncwarp();
-  return true;
-}
-
 // ------------------------------------------------------------------ warps 2-5: GEMM epilogues
 // TMEM lane = packed weight row (32 * quadrant + lane), columns = tokens of the tile.
 // Packed row orders (host packer) put rotary partners and gate/up partners 16 lanes apart in
@@ -637,54 +341,30 @@ __device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu
   }
 }
 
-__device__ __noinline__ uint32_t epi_gemm(const Params& p, const Ctx& c, uint32_t ecnt, int m) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
-  const int row = qd * 32 + lane;
-  EpiCtx e;
-  e.NT = p.NT; e.T = p.T; e.NPAD = p.NPAD; e.invT = p.invT; e.rope_cos = p.rope_cos; e.rope_sin = p.rope_sin;
-  e.q = p.q; e.sk = p.sk; e.svt = p.svt; e.hbuf = p.hbuf; e.part = p.part; e.stage = c.stage;
-  const int NTILE = p.NTILE, TG = p.TG, ngroups = p.ngroups, tiles = p.NPAD / p.NTILE;
-  int* const err = p.err;
-  Bars* const bars = c.bars;
-  const uint32_t taddr = c.tmem + ((uint32_t)(qd * 32) << 16);
-  const GemmUnit* const units = c.gu[m];
-  const int nunits = c.gcnt[m];
-  for (int u = 0; u < nunits; ++u) {
-    const GemmUnit gu = units[u];
-    for (int g = 0; g < ngroups; ++g) {
-      const int nt = min(TG, tiles - g * TG);
-      const int a = ecnt & 1;
-      if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;
-      if (u == 0 && g == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
-      tc_fence_after();
-      const bool staged = (m == MAT_GU) || (m == MAT_QKV && gu.mtile < 18);
-      for (int i = 0; i < nt; ++i) {
-#pragma unroll 1
-        for (int c64 = 0; c64 < NTILE; c64 += 64) {
-          const int nb0 = g * TG * NTILE + i * NTILE + c64;
-#pragma unroll 1
-          for (int cc = 0; cc < 64; cc += 16) {
-            float v[16];
-            tmem_ld16(taddr + a * 256 + i * NTILE + c64 + cc, v);
-            tc_wait_ld();
-            if (u == 0 && g == 0 && i == 0 && c64 + cc == 0 && threadIdx.x == 64) trace_mark(14);
-            epi_tile(e, gu, m, qd, lane, row, nb0 + cc, nb0, v);
-            if (u == 0 && g == 0 && i == 0 && c64 + cc == 0 && threadIdx.x == 64) trace_mark(15);
-          }
-          if (staged) {
-            sync_epi();
-            epi_copy_out(e, gu, m, nb0);
-            sync_epi();
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&bars->acc_empty[a]);
-      ++ecnt;
-    }
+// ------------------------------------------------------------------ model traits for the engine
+struct Pi05Model {
+  using Params = pi05::Params;
+  using Epi = EpiCtx;
+  static constexpr int kMats = 4;  // per layer, in consumption order: QKV, O, gate/up, down
+  __device__ static int rows(int m) { return m == MAT_QKV ? QKV_ROWS : (m == MAT_GU ? 2 * F : D); }
+  __device__ static int wmap(int m) { return MAP_W_QKV + m; }
+  __device__ static int act_map(int m) { return m == MAT_O ? MAP_ATTN : (m == MAT_DN ? MAP_H : MAP_XN); }
+  __device__ static int trace_stage(int m) {
+    return m == MAT_QKV ? ST_QKV : m == MAT_O ? ST_O : m == MAT_GU ? ST_GU : ST_DN;
   }
-  return ecnt;
-}
+  __device__ static void epi_load(Epi& e, const Params& p, const Ctx& c, int) {
+    e.NT = p.NT; e.T = p.T; e.NPAD = p.NPAD; e.invT = p.invT; e.rope_cos = p.rope_cos; e.rope_sin = p.rope_sin;
+    e.q = p.q; e.sk = p.sk; e.svt = p.svt; e.hbuf = p.hbuf; e.part = p.part; e.stage = c.stage;
+  }
+  __device__ static bool staged(int m, const GemmUnit& gu) { return m == MAT_GU || (m == MAT_QKV && gu.mtile < 18); }
+  __device__ static void epi_tile(const Epi& e, const GemmUnit& gu, int m, int qd, int lane, int row, int nb, int nb0,
+                                  const float* v) {
+    pi05::epi_tile(e, gu, m, qd, lane, row, nb, nb0, v);
+  }
+  __device__ static void epi_copy_out(const Epi& e, const GemmUnit& gu, int m, int nb0) {
+    pi05::epi_copy_out(e, gu, m, nb0);
+  }
+};
 
 // ------------------------------------------------------------------ attention (split-KV)
 // Unit = (observation b, head pair hp, key chunk). 128 query rows = 2 heads x 64 (padded)
@@ -790,12 +470,6 @@ __device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& s
   if (leader()) st_shared = st;
   __syncwarp();
   return true;
-}
-
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
 }
 
 // Softmax of one 128-query-row tile over NK keys, all in one TMEM round trip: thread r owns
@@ -936,12 +610,12 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   __syncthreads();
   {  // this CTA's work lists, read once from global memory
     int ng = 0;
-    for (int m = 0; m < 4; ++m) ng += s_plan.g_cnt[m];
+    for (int m = 0; m < Pi05Model::kMats; ++m) ng += s_plan.g_cnt[m];
     for (int i = threadIdx.x; i < ng; i += blockDim.x) s_gu[i] = p.gunits[s_plan.g_off[0] + i];
     for (int i = threadIdx.x; i < s_plan.a_cnt; i += blockDim.x) s_au[i] = p.aunits[s_plan.a_off + i];
   }
   if (threadIdx.x == 0) {
-  for (int m = 0, off = 0; m < 4; ++m) {
+  for (int m = 0, off = 0; m < Pi05Model::kMats; ++m) {
     c.gu[m] = s_gu + off;
     c.gcnt[m] = s_plan.g_cnt[m];
     off += s_plan.g_cnt[m];
@@ -981,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   __syncthreads();
 
   if (warp == 0) {
-    run_producer(p, c);
+    run_producer<Pi05Model>(p, c);
     __syncwarp();
   } else {
     const bool is_mma = (warp == 1);
@@ -1013,8 +687,8 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
       for (int l = 0; ok && l < p.L; ++l) {
         const float* mod_in = mod_ptr(p, step, l, 0);
         const float* mod_post = mod_ptr(p, step, l, 1);
-        if (is_mma) mma_gemm(p, c, st, MAT_QKV);
-        if (is_epi) ecnt = epi_gemm(p, c, ecnt, MAT_QKV);
+        if (is_mma) mma_gemm<Pi05Model>(p, c, st, MAT_QKV);
+        if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, MAT_QKV, l);
         epi_done();
         if (!(ok = grid_barrier(p, gen++, tr(ST_ATTN, step, l)))) break;
         mark(ST_QKV);
@@ -1029,8 +703,8 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
         epi_done();
         if (!(ok = grid_barrier(p, gen++, tr(ST_O, step, l)))) break;
         mark(ST_MERGE);
-        if (is_mma) mma_gemm(p, c, st, MAT_O);
-        if (is_epi) ecnt = epi_gemm(p, c, ecnt, MAT_O);
+        if (is_mma) mma_gemm<Pi05Model>(p, c, st, MAT_O);
+        if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, MAT_O, l);
         epi_done();
         if (!(ok = grid_barrier(p, gen++, tr(ST_NORM2, step, l)))) break;
         mark(ST_O);
@@ -1038,13 +712,13 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
         epi_done();
         if (!(ok = grid_barrier(p, gen++, tr(ST_GU, step, l)))) break;
         mark(ST_NORM2);
-        if (is_mma) mma_gemm(p, c, st, MAT_GU);
-        if (is_epi) ecnt = epi_gemm(p, c, ecnt, MAT_GU);
+        if (is_mma) mma_gemm<Pi05Model>(p, c, st, MAT_GU);
+        if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, MAT_GU, l);
         epi_done();
         if (!(ok = grid_barrier(p, gen++, tr(ST_DN, step, l)))) break;
         mark(ST_GU);
-        if (is_mma) mma_gemm(p, c, st, MAT_DN);
-        if (is_epi) ecnt = epi_gemm(p, c, ecnt, MAT_DN);
+        if (is_mma) mma_gemm<Pi05Model>(p, c, st, MAT_DN);
+        if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, MAT_DN, l);
         epi_done();
         if (!(ok = grid_barrier(p, gen++, tr(l + 1 < p.L ? ST_NORM1 : ST_FINAL, step, l)))) break;
         mark(ST_DN);
