@@ -1,0 +1,215 @@
+// Host-side pieces shared by the model engines behind the C ABI: the handle, error reporting,
+// device allocation, weight staging / row-gather packing, and TMA descriptor builders.
+#pragma once
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/flashact.h"
+#include "fa_pi05.cuh"
+
+using bf16 = __nv_bfloat16;
+using fa::pi05::Params;
+using fa::GemmUnit;
+using fa::AttnUnit;
+using fa::CtaPlan;
+
+struct Ma2State;
+
+// ------------------------------------------------------------------ handle
+struct fa_handle {
+  fa_model_kind kind;
+  fa_config cfg;
+  int device = 0;
+  int num_sms = 0;
+  std::string err;
+  bool weights_ready = false, kv_ready = false, timing = false;
+  int last_launches = 0;
+  int split_o = 4, split_dn = 8, attn_penalty = 8;
+  // bound batch
+  int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LPAD = 0;
+  std::vector<int> valid_len;
+  // device memory
+  std::vector<void*> allocs;
+  bf16 *w_qkv = nullptr, *w_o = nullptr, *w_gu = nullptr, *w_dn = nullptr;
+  float *mods = nullptr, *mod_final = nullptr;
+  float *w_ain = nullptr, *b_ain = nullptr, *w_aout = nullptr, *b_aout = nullptr;
+  float *x_t = nullptr, *x = nullptr, *part = nullptr, *oml = nullptr;
+  bf16* opart = nullptr;
+  bf16 *xn = nullptr, *attn = nullptr, *hbuf = nullptr, *q = nullptr, *sk = nullptr, *svt = nullptr;
+  bf16 *kcache = nullptr, *vtcache = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  int *d_valid = nullptr, *d_nchunks = nullptr;
+  unsigned int* ctrl = nullptr;  // [0] barrier counter, [1] error word
+  unsigned long long* stage_ns = nullptr;
+  GemmUnit* d_gunits = nullptr;
+  AttnUnit* d_aunits = nullptr;
+  CtaPlan* d_plans = nullptr;
+  size_t n_gunits_cap = 0, n_aunits_cap = 0;
+  unsigned long long* trace = nullptr;
+  int trace_step = -1, trace_layer = -1;
+  Params params;
+  Ma2State* ma2 = nullptr;  // MolmoAct2 engine state (FA_MODEL_MOLMOACT2 handles)
+};
+
+extern thread_local std::string g_create_err;
+
+static inline fa_status fail(fa_handle* h, fa_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (h) h->err = buf; else g_create_err = buf;
+  return st;
+}
+#define FA_CUDA(h, call)                                                                        \
+  do {                                                                                          \
+    cudaError_t e_ = (call);                                                                    \
+    if (e_ != cudaSuccess) return fail(h, FA_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                       __FILE__, __LINE__);                                     \
+  } while (0)
+
+template <class T>
+static fa_status dalloc(fa_handle* h, T** out, size_t count) {
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, count * sizeof(T) + 16);
+  if (e != cudaSuccess) return fail(h, FA_ERR_OOM, "cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
+  e = cudaMemset(p, 0, count * sizeof(T) + 16);
+  if (e != cudaSuccess) return fail(h, FA_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(e));
+  h->allocs.push_back(p);
+  *out = reinterpret_cast<T*>(p);
+  return FA_OK;
+}
+
+static bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+static size_t dtype_size(fa_dtype t) { return t == FA_DT_F32 ? 4 : 2; }
+
+__device__ __forceinline__ float load_as_float(const void* p, size_t i, int dt) {
+  if (dt == FA_DT_F32) return reinterpret_cast<const float*>(p)[i];
+  if (dt == FA_DT_BF16) return __bfloat162float(reinterpret_cast<const bf16*>(p)[i]);
+  return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+// ------------------------------------------------------------------ device helper kernels
+// Row-gather pack: dst[l][r][k] = bf16(src_{sel(r)}[l][row(r)][k]). rowmap[r] = (source id, row).
+struct PackSrc {
+  const void* ptr[3];
+  int dtype[3];
+  int rows[3];  // rows per layer of each source
+};
+static __global__ void pack_rows_kernel(PackSrc s, const int2* rowmap, bf16* dst, int R, int K, int L) {
+  const size_t total = (size_t)L * R * K;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int k = (int)(i % K);
+    const size_t lr = i / K;
+    const int r = (int)(lr % R), l = (int)(lr / R);
+    const int2 m = rowmap[r];
+    const size_t si = ((size_t)l * s.rows[m.x] + m.y) * K + k;
+    dst[i] = __float2bfloat16(load_as_float(s.ptr[m.x], si, s.dtype[m.x]));
+  }
+}
+static __global__ void to_f32_kernel(const void* src, int dt, float* dst, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = load_as_float(src, i, dt);
+}
+static inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
+
+// ------------------------------------------------------------------ TMA descriptors
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+// 2D bf16 map over a row-major [outer][inner] array, 128-byte swizzle, box {box_inner, box_outer}.
+static fa_status make_map(fa_handle* h, CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+                          uint32_t box_inner, uint32_t box_outer) {
+  auto enc = get_encode();
+  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FA_OK;
+}
+
+// 3D bf16 map viewing a row-major [rows][K] array as [K/64 atoms][rows][64]: one box
+// {64, box_rows, box_atoms} lands in shared memory as box_atoms consecutive 128B-swizzled atoms.
+static fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
+                           uint32_t box_rows, uint32_t box_atoms) {
+  auto enc = get_encode();
+  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {64, rows, K / 64};
+  cuuint64_t strides[2] = {K * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, box_atoms};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled (3D) failed (%d)", (int)r);
+  return FA_OK;
+}
+
+// Returns a device pointer holding `t` (staging host data into `tmp` when needed).
+static fa_status stage_tensor(fa_handle* h, const fa_tensor& t, size_t count, const char* name, const void** dptr,
+                              std::vector<void*>& tmp) {
+  if (!t.ptr) return fail(h, FA_ERR_INVALID, "weight '%s' is null", name);
+  if (t.dtype != FA_DT_F32 && t.dtype != FA_DT_BF16 && t.dtype != FA_DT_F16)
+    return fail(h, FA_ERR_INVALID, "weight '%s' has unsupported dtype %d", name, (int)t.dtype);
+  if (is_device_ptr(t.ptr)) { *dptr = t.ptr; return FA_OK; }
+  void* d = nullptr;
+  const size_t bytes = count * dtype_size(t.dtype);
+  if (cudaMalloc(&d, bytes) != cudaSuccess) return fail(h, FA_ERR_OOM, "staging '%s' (%zu bytes)", name, bytes);
+  tmp.push_back(d);
+  FA_CUDA(h, cudaMemcpy(d, t.ptr, bytes, cudaMemcpyHostToDevice));
+  *dptr = d;
+  return FA_OK;
+}
+
+static fa_status pack_matrix(fa_handle* h, const std::vector<int2>& rowmap, PackSrc src, bf16* dst, int K,
+                             std::vector<void*>& tmp) {
+  int2* d_map = nullptr;
+  FA_CUDA(h, cudaMalloc(&d_map, rowmap.size() * sizeof(int2)));
+  tmp.push_back(d_map);
+  FA_CUDA(h, cudaMemcpy(d_map, rowmap.data(), rowmap.size() * sizeof(int2), cudaMemcpyHostToDevice));
+  pack_rows_kernel<<<h->num_sms * 8, 256>>>(src, d_map, dst, (int)rowmap.size(), K, h->cfg.num_layers);
+  FA_CUDA(h, cudaGetLastError());
+  return FA_OK;
+}
+
+
+// MolmoAct2 engine (host_ma2.cu), reached through the C ABI's model dispatch.
+fa_status ma2_create(const fa_config& cfg, int device, fa_handle* h);
+fa_status ma2_bind(fa_handle* h, int batch, const void* k, const void* v, int src_rows, const int* valid_len,
+                   cudaStream_t s);
+fa_status ma2_sample(fa_handle* h, int batch, const float* noise, float* out, cudaStream_t s);
+fa_status ma2_set_modulation(fa_handle* h, const float* mods, const float* mod_final);
+void ma2_set_debug(fa_handle* h);
+void ma2_destroy(fa_handle* h);

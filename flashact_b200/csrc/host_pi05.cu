@@ -1,23 +1,11 @@
 // Host side of the C ABI (include/flashact.h) for the pi0.5 engine: device buffers, on-device
 // weight packing and conditioning, prefix-KV bind, work planning, TMA descriptors, launch.
-#include <cudaTypedefs.h>
-#include <cuda_runtime.h>
+#include "host_common.cuh"
 
-#include <algorithm>
-#include <cmath>
-#include <cstdarg>
-#include <cstdio>
-#include <cstdlib>
-#include <cstring>
-#include <mutex>
-#include <string>
-#include <vector>
-
-#include "../../include/flashact.h"
-#include "fa_pi05.cuh"
-
+using namespace fa;
 using namespace fa::pi05;
-using bf16 = __nv_bfloat16;
+
+thread_local std::string g_create_err;
 
 namespace fa {
 namespace pi05 {
@@ -25,110 +13,6 @@ __global__ void pi05_denoise_kernel(const __grid_constant__ Params p);
 }
 }  // namespace fa
 
-// ------------------------------------------------------------------ handle
-struct fa_handle {
-  fa_model_kind kind;
-  fa_config cfg;
-  int device = 0;
-  int num_sms = 0;
-  std::string err;
-  bool weights_ready = false, kv_ready = false, timing = false;
-  int last_launches = 0;
-  int split_o = 4, split_dn = 8, attn_penalty = 8;
-  // bound batch
-  int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LPAD = 0;
-  std::vector<int> valid_len;
-  // device memory
-  std::vector<void*> allocs;
-  bf16 *w_qkv = nullptr, *w_o = nullptr, *w_gu = nullptr, *w_dn = nullptr;
-  float *mods = nullptr, *mod_final = nullptr;
-  float *w_ain = nullptr, *b_ain = nullptr, *w_aout = nullptr, *b_aout = nullptr;
-  float *x_t = nullptr, *x = nullptr, *part = nullptr, *oml = nullptr;
-  bf16* opart = nullptr;
-  bf16 *xn = nullptr, *attn = nullptr, *hbuf = nullptr, *q = nullptr, *sk = nullptr, *svt = nullptr;
-  bf16 *kcache = nullptr, *vtcache = nullptr;
-  float *rope_cos = nullptr, *rope_sin = nullptr;
-  int *d_valid = nullptr, *d_nchunks = nullptr;
-  unsigned int* ctrl = nullptr;  // [0] barrier counter, [1] error word
-  unsigned long long* stage_ns = nullptr;
-  GemmUnit* d_gunits = nullptr;
-  AttnUnit* d_aunits = nullptr;
-  CtaPlan* d_plans = nullptr;
-  size_t n_gunits_cap = 0, n_aunits_cap = 0;
-  unsigned long long* trace = nullptr;
-  int trace_step = -1, trace_layer = -1;
-  Params params;
-};
-
-static thread_local std::string g_create_err;
-
-static fa_status fail(fa_handle* h, fa_status st, const char* fmt, ...) {
-  char buf[512];
-  va_list ap;
-  va_start(ap, fmt);
-  vsnprintf(buf, sizeof(buf), fmt, ap);
-  va_end(ap);
-  if (h) h->err = buf; else g_create_err = buf;
-  return st;
-}
-#define FA_CUDA(h, call)                                                                        \
-  do {                                                                                          \
-    cudaError_t e_ = (call);                                                                    \
-    if (e_ != cudaSuccess) return fail(h, FA_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
-                                       __FILE__, __LINE__);                                     \
-  } while (0)
-
-template <class T>
-static fa_status dalloc(fa_handle* h, T** out, size_t count) {
-  void* p = nullptr;
-  cudaError_t e = cudaMalloc(&p, count * sizeof(T) + 16);
-  if (e != cudaSuccess) return fail(h, FA_ERR_OOM, "cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
-  e = cudaMemset(p, 0, count * sizeof(T) + 16);
-  if (e != cudaSuccess) return fail(h, FA_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(e));
-  h->allocs.push_back(p);
-  *out = reinterpret_cast<T*>(p);
-  return FA_OK;
-}
-
-static bool is_device_ptr(const void* p) {
-  cudaPointerAttributes a;
-  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
-}
-
-static size_t dtype_size(fa_dtype t) { return t == FA_DT_F32 ? 4 : 2; }
-
-__device__ __forceinline__ float load_as_float(const void* p, size_t i, int dt) {
-  if (dt == FA_DT_F32) return reinterpret_cast<const float*>(p)[i];
-  if (dt == FA_DT_BF16) return __bfloat162float(reinterpret_cast<const bf16*>(p)[i]);
-  return __half2float(reinterpret_cast<const __half*>(p)[i]);
-}
-
-// ------------------------------------------------------------------ device helper kernels
-// Row-gather pack: dst[l][r][k] = bf16(src_{sel(r)}[l][row(r)][k]). rowmap[r] = (source id, row).
-struct PackSrc {
-  const void* ptr[3];
-  int dtype[3];
-  int rows[3];  // rows per layer of each source
-};
-__global__ void pack_rows_kernel(PackSrc s, const int2* rowmap, bf16* dst, int R, int K, int L) {
-  const size_t total = (size_t)L * R * K;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int k = (int)(i % K);
-    const size_t lr = i / K;
-    const int r = (int)(lr % R), l = (int)(lr / R);
-    const int2 m = rowmap[r];
-    const size_t si = ((size_t)l * s.rows[m.x] + m.y) * K + k;
-    dst[i] = __float2bfloat16(load_as_float(s.ptr[m.x], si, s.dtype[m.x]));
-  }
-}
-__global__ void to_f32_kernel(const void* src, int dt, float* dst, size_t n) {
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    dst[i] = load_as_float(src, i, dt);
-}
 // openpi create_sinusoidal_pos_embedding(t, 1024, min_period=4e-3, max_period=4.0):
 // period_i = min * (max/min)^(i/511); emb = [sin(2 pi t / period) | cos(2 pi t / period)].
 // Computed in double like the reference's float64 path, stored fp32. t_s = 1 - s/N.
@@ -224,13 +108,39 @@ __global__ void rope_kernel(const int* valid, int B, int T, float* cs, float* sn
 }
 
 // ------------------------------------------------------------------ create / destroy
-static int round_up(int a, int b) { return (a + b - 1) / b * b; }
 
 extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int device, fa_handle** out) {
   if (!cfg || !out) return fail(nullptr, FA_ERR_INVALID, "null argument");
   *out = nullptr;
-  if (kind != FA_MODEL_PI05) return fail(nullptr, FA_ERR_UNSUPPORTED, "model kind %d not built into this library", (int)kind);
+  if (kind != FA_MODEL_PI05 && kind != FA_MODEL_MOLMOACT2)
+    return fail(nullptr, FA_ERR_UNSUPPORTED, "model kind %d not built into this library", (int)kind);
   const fa_config& c = *cfg;
+  if (kind == FA_MODEL_MOLMOACT2) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+      cudaGetLastError();
+      return fail(nullptr, FA_ERR_INVALID, "device %d not available", device);
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return fail(nullptr, FA_ERR_CUDA, "cudaGetDeviceProperties failed");
+    if (prop.major != 10 || prop.minor != 0)
+      return fail(nullptr, FA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a (B200)", device, prop.major, prop.minor);
+    fa_handle* h = new fa_handle();
+    h->kind = kind;
+    h->cfg = c;
+    h->device = device;
+    h->num_sms = prop.multiProcessorCount;
+    h->params.inject_barrier = -1;  // fault injection off
+    h->params.spin_limit = 1u << 24;
+    const fa_status st = ma2_create(c, device, h);
+    if (st != FA_OK) {
+      g_create_err = h->err;
+      fa_destroy(h);
+      return st;
+    }
+    *out = h;
+    return FA_OK;
+  }
   if (c.width != D || c.num_heads != H || c.num_kv_heads != 1 || c.head_dim != HD || c.mlp_dim != F)
     return fail(nullptr, FA_ERR_INVALID, "pi0.5 expert geometry must be width 1024, 8 heads, 1 kv head, head_dim 256, mlp 4096");
   if (c.num_layers < 1 || c.num_layers > 64 || c.horizon < 1 || c.horizon > TPAD || c.action_dim < 1 || c.action_dim > 32 ||
@@ -295,7 +205,7 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   ALLOC(d_valid, MB);
   ALLOC(d_nchunks, MB);
   ALLOC(ctrl, 2);
-  ALLOC(stage_ns, NUM_STAGES);
+  ALLOC(stage_ns, kMaxStages);
   ALLOC(d_plans, h->num_sms);
 #undef ALLOC
   if (cudaFuncSetAttribute(fa::pi05::pi05_denoise_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDyn) != cudaSuccess)
@@ -311,6 +221,7 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
 extern "C" void fa_destroy(fa_handle* h) {
   if (!h) return;
   cudaSetDevice(h->device);
+  ma2_destroy(h);
   for (void* p : h->allocs) cudaFree(p);
   delete h;
 }
@@ -319,33 +230,6 @@ extern "C" const char* fa_last_error(fa_handle* h) { return h ? h->err.c_str() :
 extern "C" int fa_last_launch_count(fa_handle* h) { return h ? h->last_launches : 0; }
 
 // ------------------------------------------------------------------ weights
-// Returns a device pointer holding `t` (staging host data into `tmp` when needed).
-static fa_status stage_tensor(fa_handle* h, const fa_tensor& t, size_t count, const char* name, const void** dptr,
-                              std::vector<void*>& tmp) {
-  if (!t.ptr) return fail(h, FA_ERR_INVALID, "weight '%s' is null", name);
-  if (t.dtype != FA_DT_F32 && t.dtype != FA_DT_BF16 && t.dtype != FA_DT_F16)
-    return fail(h, FA_ERR_INVALID, "weight '%s' has unsupported dtype %d", name, (int)t.dtype);
-  if (is_device_ptr(t.ptr)) { *dptr = t.ptr; return FA_OK; }
-  void* d = nullptr;
-  const size_t bytes = count * dtype_size(t.dtype);
-  if (cudaMalloc(&d, bytes) != cudaSuccess) return fail(h, FA_ERR_OOM, "staging '%s' (%zu bytes)", name, bytes);
-  tmp.push_back(d);
-  FA_CUDA(h, cudaMemcpy(d, t.ptr, bytes, cudaMemcpyHostToDevice));
-  *dptr = d;
-  return FA_OK;
-}
-
-static fa_status pack_matrix(fa_handle* h, const std::vector<int2>& rowmap, PackSrc src, bf16* dst, int K,
-                             std::vector<void*>& tmp) {
-  int2* d_map = nullptr;
-  FA_CUDA(h, cudaMalloc(&d_map, rowmap.size() * sizeof(int2)));
-  tmp.push_back(d_map);
-  FA_CUDA(h, cudaMemcpy(d_map, rowmap.data(), rowmap.size() * sizeof(int2), cudaMemcpyHostToDevice));
-  pack_rows_kernel<<<h->num_sms * 8, 256>>>(src, d_map, dst, (int)rowmap.size(), K, h->cfg.num_layers);
-  FA_CUDA(h, cudaGetLastError());
-  return FA_OK;
-}
-
 static fa_status run_linear(fa_handle* h, const void* W, fa_dtype wdt, const void* b, fa_dtype bdt, const float* in, int S,
                             int IN, int OUT, float* out, size_t out_stride, int act) {
   const size_t smem = (size_t)S * IN * sizeof(float);
@@ -464,55 +348,11 @@ extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w
 
 extern "C" fa_status fa_set_modulation(fa_handle* h, const float* mods, const float* mod_final) {
   if (!h || !mods || !mod_final) return fail(h, FA_ERR_INVALID, "null argument");
+  if (h->kind == FA_MODEL_MOLMOACT2) return ma2_set_modulation(h, mods, mod_final);
   FA_CUDA(h, cudaSetDevice(h->device));
   const size_t n = (size_t)h->cfg.num_steps * h->cfg.num_layers * 2 * MOD;
   FA_CUDA(h, cudaMemcpy(h->mods, mods, n * 4, cudaMemcpyDefault));
   FA_CUDA(h, cudaMemcpy(h->mod_final, mod_final, (size_t)h->cfg.num_steps * MOD * 4, cudaMemcpyDefault));
-  return FA_OK;
-}
-
-// ------------------------------------------------------------------ TMA descriptors
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-// 2D bf16 map over a row-major [outer][inner] array, 128-byte swizzle, box {box_inner, box_outer}.
-static fa_status make_map(fa_handle* h, CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
-                          uint32_t box_inner, uint32_t box_outer) {
-  auto enc = get_encode();
-  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * 2};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return FA_OK;
-}
-
-// 3D bf16 map viewing a row-major [rows][K] array as [K/64 atoms][rows][64]: one box
-// {64, box_rows, box_atoms} lands in shared memory as box_atoms consecutive 128B-swizzled atoms.
-static fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
-                           uint32_t box_rows, uint32_t box_atoms) {
-  auto enc = get_encode();
-  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[3] = {64, rows, K / 64};
-  cuuint64_t strides[2] = {K * 2, 128};
-  cuuint32_t box[3] = {64, box_rows, box_atoms};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled (3D) failed (%d)", (int)r);
   return FA_OK;
 }
 
@@ -648,6 +488,8 @@ static fa_status build_params(fa_handle* h) {
 extern "C" fa_status fa_bind_prefix_kv(fa_handle* h, int batch, const void* k, const void* v, int src_rows,
                                        const int* valid_len, fa_kv_layout layout, fa_stream stream) {
   if (!h) return fail(h, FA_ERR_INVALID, "null handle");
+  if (h->kind == FA_MODEL_MOLMOACT2)
+    return ma2_bind(h, batch, k, v, src_rows, valid_len, reinterpret_cast<cudaStream_t>(stream));
   if (batch < 1 || batch > h->cfg.max_batch) return fail(h, FA_ERR_INVALID, "batch %d outside 1..%d", batch, h->cfg.max_batch);
   if (!valid_len) return fail(h, FA_ERR_INVALID, "valid_len is null");
   if (layout != FA_KV_COMPACT_SPLIT_HALF && layout != FA_KV_FLASHRT_INTERLEAVED) return fail(h, FA_ERR_INVALID, "unknown kv layout");
@@ -702,14 +544,15 @@ extern "C" fa_status fa_set_stage_timing(fa_handle* h, int enable) {
 extern "C" fa_status fa_get_stage_cycles(fa_handle* h, uint64_t* out, int n) {
   if (!h || !out) return fail(h, FA_ERR_INVALID, "null argument");
   FA_CUDA(h, cudaSetDevice(h->device));
-  unsigned long long tmp[NUM_STAGES];
+  unsigned long long tmp[kMaxStages];
   FA_CUDA(h, cudaMemcpy(tmp, h->stage_ns, sizeof(tmp), cudaMemcpyDeviceToHost));
-  for (int i = 0; i < n; ++i) out[i] = i < NUM_STAGES ? tmp[i] : 0;
+  for (int i = 0; i < n; ++i) out[i] = i < kMaxStages ? tmp[i] : 0;
   return FA_OK;
 }
 
 extern "C" fa_status fa_sample_actions(fa_handle* h, int batch, const float* noise, float* actions_out, fa_stream stream) {
   if (!h || !noise || !actions_out) return fail(h, FA_ERR_INVALID, "null argument");
+  if (h->kind == FA_MODEL_MOLMOACT2) return ma2_sample(h, batch, noise, actions_out, reinterpret_cast<cudaStream_t>(stream));
   if (!h->weights_ready) return fail(h, FA_ERR_STATE, "weights not loaded");
   if (!h->kv_ready) return fail(h, FA_ERR_STATE, "prefix KV not bound");
   if (batch != h->B) return fail(h, FA_ERR_INVALID, "batch %d differs from the bound batch %d", batch, h->B);
@@ -742,7 +585,7 @@ extern "C" fa_status fa_sync(fa_handle* h, fa_stream stream) {
 // Diagnostics: arm (step >= 0) or read back (step < 0) a clock64 trace of one (step, layer).
 extern "C" fa_status fa_debug_trace(fa_handle* h, int step, int layer, unsigned long long* host_out, int n) {
   if (!h) return FA_ERR_INVALID;
-  const size_t need = (size_t)NUM_STAGES * h->num_sms * kTrStride;
+  const size_t need = (size_t)kMaxStages * h->num_sms * kTrStride;
   FA_CUDA(h, cudaSetDevice(h->device));
   if (step < 0) {
     if (!h->trace) return fail(h, FA_ERR_STATE, "trace not armed");
@@ -757,6 +600,7 @@ extern "C" fa_status fa_debug_trace(fa_handle* h, int step, int layer, unsigned 
   h->trace_step = h->params.trace_step = step;
   h->trace_layer = h->params.trace_layer = layer;
   h->params.trace = h->trace;
+  ma2_set_debug(h);
   return FA_OK;
 }
 
@@ -764,6 +608,7 @@ extern "C" fa_status fa_set_fault_injection(fa_handle* h, int barrier_index, uns
   if (!h) return FA_ERR_INVALID;
   h->params.inject_barrier = barrier_index;
   h->params.spin_limit = spin_limit ? spin_limit : (1u << 24);
+  ma2_set_debug(h);
   return FA_OK;
 }
 

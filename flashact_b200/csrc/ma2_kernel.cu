@@ -1,0 +1,586 @@
+// MolmoAct2 action-expert flow megakernel for B200 (sm_100a).
+//
+// One cooperative launch runs all N Euler steps x 36 DiT blocks (reference semantics:
+// src/molmoact2/mk_ma2.cu:103-576; schedule benchmarks/molmoact2/eval_numerics.py:59-75).
+// Per block: adaRMS (self) -> QKV GEMM + bias -> self-attention over the action tokens
+// (weightless RMS qk-norm, half-split RoPE over 48 pairs) -> out GEMM + bias, gated residual ->
+// adaRMS (cross) -> cross-q GEMM + bias -> cross-attention over the bound context (per-head RMS
+// q-norm, split over key chunks, merged) -> out GEMM + bias, gated residual -> adaRMS (mlp) ->
+// gate/up GEMM + bias, SiLU gate -> down GEMM + bias, gated residual. Final adaRMS, velocity
+// head on the valid action dims, x_t += dt v.
+//
+// The six GEMMs per block run on the shared tcgen05 engine (fa_engine.cuh): TMA-streamed
+// weight tiles, fp32 accumulators in TMEM, fused epilogues. The attention stages are small at
+// this horizon (T <= 32) and run on the CUDA cores of the epilogue warps.
+#include "fa_engine.cuh"
+#include "fa_ma2.cuh"
+
+namespace fa {
+namespace ma2 {
+
+constexpr float kEps = 1e-6f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ int tok_b(const Params& p, int n) { return tok_bi(p.invT, n); }
+__device__ __forceinline__ const float* mod_ptr(const Params& p, int step, int l, int norm) {
+  return p.mods + ((size_t)(step * p.L + l) * 3 + norm) * MOD;
+}
+
+// ------------------------------------------------------------------ norms (warps 2-5)
+// A 768-wide row held as 6 values per thread: dims 2e + 256 k + {0, 1}, k = 0..2.
+__device__ __forceinline__ void row_load_residual(const Params& p, int n, const float* gate, int nsplit,
+                                                  float v[6]) {
+  const int e = threadIdx.x - 64;
+  float2 x[3], acc[3], g[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const int d = 2 * e + 256 * k;
+    x[k] = __ldcg(reinterpret_cast<const float2*>(p.x + (size_t)n * D + d));
+    acc[k] = make_float2(0.f, 0.f);
+    g[k] = nsplit > 0 ? __ldg(reinterpret_cast<const float2*>(gate + d)) : acc[k];
+  }
+  for (int s = 0; s < nsplit; ++s) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const float2 q = __ldcg(reinterpret_cast<const float2*>(p.part + ((size_t)s * p.NPAD + n) * D + 2 * e + 256 * k));
+      acc[k].x += q.x;
+      acc[k].y += q.y;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    if (nsplit > 0) {
+      x[k].x += g[k].x * acc[k].x;
+      x[k].y += g[k].y * acc[k].y;
+      *reinterpret_cast<float2*>(p.x + (size_t)n * D + 2 * e + 256 * k) = x[k];
+    }
+    v[2 * k] = x[k].x;
+    v[2 * k + 1] = x[k].y;
+  }
+}
+
+// xn = x * rsqrt(mean(x^2) + 1e-6) * (1 + scale) + shift -> bf16 (mk_ma2.cu:130-158).
+__device__ __forceinline__ void row_rms_store(const Params& p, int n, const float v[6], const float* mod, float* red) {
+  const int e = threadIdx.x - 64;
+  float2 sc[3], sh[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    sc[k] = __ldg(reinterpret_cast<const float2*>(mod + 2 * e + 256 * k));
+    sh[k] = __ldg(reinterpret_cast<const float2*>(mod + D + 2 * e + 256 * k));
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 6; ++i) ss += v[i] * v[i];
+  ss = epi_sum(ss, red);
+  const float r = rsqrtf(ss * (1.0f / D) + kEps);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    __nv_bfloat162 o = __floats2bfloat162_rn(v[2 * k] * r * (1.f + sc[k].x) + sh[k].x,
+                                             v[2 * k + 1] * r * (1.f + sc[k].y) + sh[k].y);
+    *reinterpret_cast<__nv_bfloat162*>(p.xn + (size_t)n * D + 2 * e + 256 * k) = o;
+  }
+}
+
+// x += gate * sum_s part[s] (partials already carry the bias), xn = adaRMS(x; mod).
+__device__ __noinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
+  for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
+    float v[6];
+    row_load_residual(p, n, gate, nsplit, v);
+    row_rms_store(p, n, v, mod, red);
+  }
+}
+
+// x = W_ain x_t + b_ain (mk_ma2.cu:259-268), then the first adaRMS of block 0 of `step`.
+__device__ void embed_norm_token(const Params& p, int n, int step, const float* xt, float* red) {
+  const int e = threadIdx.x - 64;
+  float v[6];
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    const int d = 2 * e + 256 * (i >> 1) + (i & 1);
+    float acc = p.b_ain[d];
+    const float* w = p.w_ain + (size_t)d * p.AD;
+    for (int a = 0; a < p.AD; ++a) acc = fmaf(w[a], xt[a], acc);
+    v[i] = acc;
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+    *reinterpret_cast<float2*>(p.x + (size_t)n * D + 2 * e + 256 * k) = make_float2(v[2 * k], v[2 * k + 1]);
+  row_rms_store(p, n, v, mod_ptr(p, step, 0, 0), red);
+}
+
+__device__ __noinline__ void stage_embed(const Params& p, float* xt_s, float* red) {
+  const int e = threadIdx.x - 64;
+  for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
+    if (e < p.AD) xt_s[e] = p.x_t[(size_t)n * p.AD + e];
+    sync_epi();
+    embed_norm_token(p, n, 0, xt_s, red);
+    sync_epi();
+  }
+}
+
+// Final adaRMS (scale, shift), velocity head on the valid action dims, x_t += dt v
+// (mk_ma2.cu:558-575), then the next step's embed + first norm.
+__device__ __noinline__ void stage_final(const Params& p, int step, float* xf, float* xt_s, float* red) {
+  const int e = threadIdx.x - 64, lane = e & 31, w = e >> 5;
+  const float* gate = mod_ptr(p, step, p.L - 1, 2) + 2 * D;
+  const float* modf = p.mod_final + (size_t)step * 2 * D;
+  for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
+    float v[6];
+    row_load_residual(p, n, gate, p.split[MAT_DN], v);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 6; ++i) ss += v[i] * v[i];
+    ss = epi_sum(ss, red);
+    const float r = rsqrtf(ss * (1.0f / D) + kEps);
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const int d = 2 * e + 256 * (i >> 1) + (i & 1);
+      xf[d] = v[i] * r * (1.f + modf[d]) + modf[D + d];
+    }
+    sync_epi();
+    for (int a = w; a < p.AD; a += 4) {
+      const float* wr = p.w_aout + (size_t)a * D;
+      float acc = 0.f;
+      for (int d = lane; d < D; d += 32) acc = fmaf(wr[d], xf[d], acc);
+      acc = warp_sum(acc);
+      if (lane == 0) {
+        float nv = p.x_t[(size_t)n * p.AD + a];
+        if (a < p.adim) nv += p.dt * (acc + p.b_aout[a]);  // padded action dims are left untouched
+        p.x_t[(size_t)n * p.AD + a] = nv;
+        xt_s[a] = nv;
+      }
+    }
+    sync_epi();
+    if (step + 1 < p.nsteps) embed_norm_token(p, n, step + 1, xt_s, red);
+    sync_epi();
+  }
+}
+
+// ------------------------------------------------------------------ self-attention (warps 2-5)
+// Unit = (observation b, head h): the T action tokens attend to each other. q, k get a
+// weightless RMS norm over the 96 head dims and half-split RoPE (pairs i, i+48) at positions
+// 0..T-1 from the bound tables; scale 1/sqrt(96) (mk_ma2.cu:293-384).
+__device__ __noinline__ void stage_self_attn(const Params& p, float* sm) {
+  const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
+  const int T = p.T;
+  float* qs = sm;                  // [32][97]
+  float* ks = qs + TMAX * 97;      // [32][97]
+  float* vs = ks + TMAX * 97;      // [32][96]
+  float* ps = vs + TMAX * 96;      // [32][33]
+  const float scale = 0.10206207261596577f;  // 1/sqrt(96)
+  for (int u = blockIdx.x; u < p.B * H; u += gridDim.x) {
+    const int b = u / H, h = u % H;
+    for (int idx = e; idx < 3 * T * HD; idx += 128) {
+      const int sec = idx / (T * HD), rem = idx % (T * HD), t = rem / HD, d = rem % HD;
+      const float val = __bfloat162float(p.qkv[(size_t)(b * T + t) * QKV_ROWS + sec * D + h * HD + d]);
+      if (sec == 0) qs[t * 97 + d] = val;
+      else if (sec == 1) ks[t * 97 + d] = val;
+      else vs[t * 96 + d] = val;
+    }
+    sync_epi();
+    for (int row = wq; row < 2 * T; row += 4) {  // RMS over the head dims, q rows then k rows
+      float* rp = row < T ? qs + row * 97 : ks + (row - T) * 97;
+      const float a0 = rp[lane], a1 = rp[lane + 32], a2 = rp[lane + 64];
+      const float r = rsqrtf(warp_sum(a0 * a0 + a1 * a1 + a2 * a2) * (1.0f / HD) + kEps);
+      rp[lane] = a0 * r;
+      rp[lane + 32] = a1 * r;
+      rp[lane + 64] = a2 * r;
+    }
+    sync_epi();
+    for (int idx = e; idx < 2 * T * 48; idx += 128) {  // half-split RoPE
+      const int row = idx / 48, i = idx % 48, t = row < T ? row : row - T;
+      float* rp = row < T ? qs + row * 97 : ks + t * 97;
+      const float c = p.rope_cos[t * 48 + i], s = p.rope_sin[t * 48 + i];
+      const float x1 = rp[i], x2 = rp[i + 48];
+      rp[i] = x1 * c - x2 * s;
+      rp[i + 48] = x1 * s + x2 * c;
+    }
+    sync_epi();
+    for (int idx = e; idx < T * T; idx += 128) {
+      const int t = idx / T, j = idx % T;
+      float acc = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < HD; ++d) acc = fmaf(qs[t * 97 + d], ks[j * 97 + d], acc);
+      ps[t * 33 + j] = acc * scale;
+    }
+    sync_epi();
+    for (int t = wq; t < T; t += 4) {  // softmax over the T keys, one warp per query
+      const float s = lane < T ? ps[t * 33 + lane] : -INFINITY;
+      const float m = warp_max(s);
+      const float ex = lane < T ? __expf(s - m) : 0.f;
+      const float sum = warp_sum(ex);
+      if (lane < T) ps[t * 33 + lane] = ex / sum;
+    }
+    sync_epi();
+    for (int idx = e; idx < T * HD; idx += 128) {
+      const int t = idx / HD, d = idx % HD;
+      float acc = 0.f;
+      for (int j = 0; j < T; ++j) acc = fmaf(ps[t * 33 + j], vs[j * 96 + d], acc);
+      p.sattn[(size_t)(b * T + t) * D + h * HD + d] = __float2bfloat16(acc);
+    }
+    sync_epi();
+  }
+}
+
+// ------------------------------------------------------------------ cross-attention (warps 2-5)
+// Unit = (observation b, head h, context chunk c of 128 keys). q = RMS-normalised cross query
+// of head h (mk_ma2.cu:398-422); scores over the chunk's valid keys, scale 1/sqrt(96); the
+// chunk's normalised output and (max, sum) go to opart / oml for stage_merge.
+__device__ __noinline__ void stage_cross_attn(const Params& p, const Ctx& c, int l, float* sm) {
+  const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
+  const int T = p.T;
+  float* qs = sm;                                                  // [32][96], pre-scaled
+  float* ps = qs + TMAX * HD;                                      // [32][129]
+  float* wred = ps + TMAX * 129;                                   // [4][32] warp partials
+  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(wred + 4 * TMAX);  // [128][96]
+  const float qscale = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 units
+  for (int u = 0; u < c.acnt; ++u) {
+    const AttnUnit au = c.au[u];
+    const int b = au.b, h = au.hp, ch = au.chunk;
+    const int lk = p.ctx_len[b];
+    const int nvalid = min(KC, lk - ch * KC);
+    const size_t krow0 = ((size_t)(b * p.L + l) * p.LKPAD + ch * KC);
+    for (int idx = e; idx < T * HD; idx += 128) {
+      const int t = idx / HD, d = idx % HD;
+      qs[idx] = __bfloat162float(p.qc[(size_t)(b * T + t) * D + h * HD + d]);
+    }
+    for (int idx = e; idx < KC * (HD / 8); idx += 128) {  // V chunk, 16-byte rows pieces
+      const int j = idx / (HD / 8), seg = idx % (HD / 8);
+      *reinterpret_cast<uint4*>(vs + j * HD + seg * 8) =
+          __ldg(reinterpret_cast<const uint4*>(p.vctx + (krow0 + j) * D + h * HD + seg * 8));
+    }
+    sync_epi();
+    for (int t = wq; t < T; t += 4) {  // per-head RMS of the query, then fold in the scale
+      float* rp = qs + t * HD;
+      const float a0 = rp[lane], a1 = rp[lane + 32], a2 = rp[lane + 64];
+      const float r = rsqrtf(warp_sum(a0 * a0 + a1 * a1 + a2 * a2) * (1.0f / HD) + kEps) * qscale;
+      rp[lane] = a0 * r;
+      rp[lane + 32] = a1 * r;
+      rp[lane + 64] = a2 * r;
+    }
+    sync_epi();
+    // scores: thread = key e of the chunk, its 96-dim key row in registers
+    float kr[HD];
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(p.kctx + (krow0 + e) * D + h * HD);
+#pragma unroll
+      for (int s8 = 0; s8 < HD / 8; ++s8) {
+        const uint4 raw = __ldg(src + s8);
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(b2[q]);
+          kr[s8 * 8 + 2 * q] = f.x;
+          kr[s8 * 8 + 2 * q + 1] = f.y;
+        }
+      }
+    }
+    const bool valid = e < nvalid;
+#pragma unroll 1
+    for (int t = 0; t < T; ++t) {
+      float acc = 0.f;
+#pragma unroll
+      for (int d = 0; d < HD; ++d) acc = fmaf(qs[t * HD + d], kr[d], acc);
+      const float s = valid ? acc : -INFINITY;
+      ps[t * 129 + e] = s;
+      const float wm = warp_max(s);
+      if (lane == 0) wred[wq * TMAX + t] = wm;
+    }
+    sync_epi();
+    // probabilities and row sums (max over the 4 warps' partials)
+    for (int t = wq; t < T; t += 4) {
+      const float m = fmaxf(fmaxf(wred[t], wred[TMAX + t]), fmaxf(wred[2 * TMAX + t], wred[3 * TMAX + t]));
+      float sum = 0.f;
+      for (int j = lane; j < KC; j += 32) {
+        const float s = ps[t * 129 + j];
+        const float pj = (j < nvalid) ? fast_exp2(s - m) : 0.f;
+        ps[t * 129 + j] = pj;
+        sum += pj;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        const size_t o = (((size_t)(b * H + h) * MAX_CH + ch) * TMAX + t) * 2;
+        p.oml[o] = nvalid > 0 ? m : -INFINITY;
+        p.oml[o + 1] = sum;
+        qs[t * HD] = sum > 0.f ? 1.f / sum : 0.f;  // reuse q row 0 slot: q is no longer needed
+      }
+    }
+    sync_epi();
+    for (int idx = e; idx < T * HD; idx += 128) {  // O = P V over the chunk, normalised
+      const int t = idx / HD, d = idx % HD;
+      float acc = 0.f;
+#pragma unroll 4
+      for (int j = 0; j < KC; ++j) acc = fmaf(ps[t * 129 + j], __bfloat162float(vs[j * HD + d]), acc);
+      const float inv = qs[t * HD];
+      p.opart[(((size_t)(b * H + h) * MAX_CH + ch) * TMAX + t) * HD + d] = __float2bfloat16(acc * inv);
+    }
+    sync_epi();
+  }
+}
+
+// Merge of the context chunks per (token, head): out = sum_c w_c O_c / sum_c w_c,
+// w_c = 2^(m_c - M) l_c. One warp per (token, head); lane c holds chunk c's (max, sum).
+__device__ __noinline__ void stage_merge(const Params& p) {
+  const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
+  for (int item = blockIdx.x * 4 + wq; item < p.NT * H; item += gridDim.x * 4) {
+    const int n = item / H, h = item % H;
+    const int b = tok_b(p, n), t = n - b * p.T;
+    const int nch = (p.ctx_len[b] + KC - 1) / KC;
+    const size_t base = (size_t)(b * H + h) * MAX_CH;
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (lane < nch) ml = __ldcg(reinterpret_cast<const float2*>(p.oml + ((base + lane) * TMAX + t) * 2));
+    const float M = warp_max(ml.x);
+    const float w_own = (lane < nch && ml.y > 0.f) ? fast_exp2(ml.x - M) * ml.y : 0.f;
+    const float wsum = warp_sum(w_own);
+    float acc[3] = {0.f, 0.f, 0.f};
+    for (int cidx = 0; cidx < nch; ++cidx) {
+      const float wgt = __shfl_sync(0xffffffffu, w_own, cidx);
+      const __nv_bfloat16* src = p.opart + ((base + cidx) * TMAX + t) * HD;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) acc[k] += wgt * __bfloat162float(__ldcg(src + lane + 32 * k));
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) p.cattn[(size_t)n * D + h * HD + lane + 32 * k] = __float2bfloat16(acc[k] * inv);
+  }
+}
+
+// ------------------------------------------------------------------ GEMM epilogues and model traits
+struct Ma2Epi {
+  int NT, NPAD;
+  uint8_t* stage;
+  __nv_bfloat16* qkv;
+  __nv_bfloat16* qc;
+  __nv_bfloat16* hbuf;
+  float* part;
+  const float* bias[NUM_MATS];  // this layer's bias of each matrix (gate bias for MAT_GU)
+  const float* b_up;            // this layer's up bias
+};
+
+__device__ __forceinline__ int mat_rows(int m) { return m == MAT_QKV ? QKV_ROWS : (m == MAT_GU ? 2 * F : D); }
+
+struct Ma2Model {
+  using Params = ma2::Params;
+  using Epi = Ma2Epi;
+  static constexpr int kMats = NUM_MATS;  // QKV, self-out, cross-q, cross-out, gate/up, down
+  __device__ static int rows(int m) { return mat_rows(m); }
+  __device__ static int wmap(int m) { return MAP_W_QKV + m; }
+  __device__ static int act_map(int m) {
+    return m == MAT_SO ? MAP_SATTN : m == MAT_CO ? MAP_CATTN : m == MAT_DN ? MAP_H : MAP_XN;
+  }
+  __device__ static int trace_stage(int m) {
+    const int st[NUM_MATS] = {ST_QKV, ST_SO, ST_CQ, ST_CO, ST_GU, ST_DN};
+    return st[m];
+  }
+  __device__ static void epi_load(Epi& e, const Params& p, const Ctx& c, int l) {
+    e.NT = p.NT; e.NPAD = p.NPAD; e.stage = c.stage; e.qkv = p.qkv; e.qc = p.qc; e.hbuf = p.hbuf; e.part = p.part;
+#pragma unroll
+    for (int m = 0; m < NUM_MATS; ++m) e.bias[m] = p.bias[m] + (size_t)l * (m == MAT_GU ? F : (m == MAT_QKV ? QKV_ROWS : D));
+    e.b_up = p.b_up + (size_t)l * F;
+  }
+  __device__ static bool staged(int m, const GemmUnit&) { return m == MAT_QKV || m == MAT_CQ || m == MAT_GU; }
+  // 16 tokens (nb..nb+15) of accumulator row `row` of unit gu (mk_ma2.cu:224-251 epilogues).
+  __device__ static void epi_tile(const Epi& e, const GemmUnit& gu, int m, int qd, int lane, int row, int nb,
+                                  int nb0, const float* v) {
+    if (m == MAT_QKV || m == MAT_CQ) {  // + bias, bf16, staged as [token][128 rows]
+      const float bias = e.bias[m][gu.mtile * 128 + row];
+      __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(e.stage) + (nb - nb0) * 128 + row;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) st[k * 128] = __float2bfloat16(v[k] + bias);
+    } else if (m == MAT_GU) {  // lanes 0-15 gate rows, 16-31 up rows of one feature: silu(g) * u
+      const int f = 64 * gu.mtile + 16 * qd + (lane & 15);
+      const float bias = lane < 16 ? e.bias[MAT_GU][f] : e.b_up[f];
+      float gu_v[16], up[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) gu_v[k] = v[k] + bias;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) up[k] = __shfl_xor_sync(0xffffffffu, gu_v[k], 16);
+      if (lane < 16) {
+        __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(e.stage) + (nb - nb0) * 64 + 16 * qd + lane;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) st[k * 64] = __float2bfloat16(gu_v[k] / (1.f + __expf(-gu_v[k])) * up[k]);
+      }
+    } else {  // self-out / cross-out / down: fp32 K-split partial, bias carried by split 0
+      const float bias = gu.split == 0 ? e.bias[m][gu.mtile * 128 + row] : 0.f;
+      float* dst = e.part + ((size_t)gu.split * e.NPAD + nb) * D + gu.mtile * 128 + row;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) dst[(size_t)k * D] = v[k] + bias;
+    }
+  }
+  __device__ static void epi_copy_out(const Epi& e, const GemmUnit& gu, int m, int nb0) {
+    const int t_ = threadIdx.x - 64;
+    if (m == MAT_GU) {  // 64 tokens x 128 B
+      for (int it = t_; it < 64 * 8; it += 128) {
+        const int t = it >> 3, seg = it & 7, n = nb0 + t;
+        if (n >= e.NT) continue;
+        *reinterpret_cast<uint4*>(e.hbuf + (size_t)n * F + 64 * gu.mtile + seg * 8) =
+            *reinterpret_cast<const uint4*>(e.stage + t * 128 + seg * 16);
+      }
+    } else {  // 64 tokens x 256 B into qkv [NPAD][2304] or qc [NPAD][768]
+      __nv_bfloat16* out = m == MAT_QKV ? e.qkv : e.qc;
+      const int stride = m == MAT_QKV ? QKV_ROWS : D;
+      for (int it = t_; it < 64 * 16; it += 128) {
+        const int t = it >> 4, seg = it & 15, n = nb0 + t;
+        if (n >= e.NT) continue;
+        *reinterpret_cast<uint4*>(out + (size_t)n * stride + gu.mtile * 128 + seg * 8) =
+            *reinterpret_cast<const uint4*>(e.stage + t * 256 + seg * 16);
+      }
+    }
+  }
+};
+
+// ------------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ Bars bars;
+  __shared__ uint32_t s_tmem;
+  __shared__ float s_red[8];
+  __shared__ float s_xt[32];
+  __shared__ CtaPlan s_plan;
+  __shared__ GemmUnit s_gu[kMaxGU];
+  __shared__ AttnUnit s_au[kMaxAU];
+  __shared__ Ctx s_c;
+  __shared__ MmaState s_st;
+  const int warp = threadIdx.x >> 5;
+  Ctx& c = s_c;
+  if (threadIdx.x == 0) {
+    s_plan = p.plans[blockIdx.x];
+    g_trp = nullptr;
+    s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = 0;
+    s_st.last_q = -1;
+    s_st.k_pre = 0;
+  }
+  __syncthreads();
+  {
+    int ng = 0;
+    for (int m = 0; m < NUM_MATS; ++m) ng += s_plan.g_cnt[m];
+    for (int i = threadIdx.x; i < ng; i += blockDim.x) s_gu[i] = p.gunits[s_plan.g_off[0] + i];
+    for (int i = threadIdx.x; i < s_plan.a_cnt; i += blockDim.x) s_au[i] = p.aunits[s_plan.a_off + i];
+  }
+  if (threadIdx.x == 0) {
+    for (int m = 0, off = 0; m < NUM_MATS; ++m) {
+      c.gu[m] = s_gu + off;
+      c.gcnt[m] = s_plan.g_cnt[m];
+      off += s_plan.g_cnt[m];
+    }
+    c.au = s_au;
+    c.acnt = s_plan.a_cnt;
+    c.batoms = min(kMaxBAtoms, s_plan.b_bytes / (p.NTILE * 128));
+    c.ring_slots = s_plan.ring_slots;
+    c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    c.work = c.ring + (size_t)c.ring_slots * kAtomBytes;
+    c.stage = c.work + max(s_plan.b_bytes, kMinWork);
+    c.bars = &bars;
+    for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], 1); }
+    mbar_init(&bars.bfull, 1);
+    mbar_init(&bars.bempty, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&bars.acc_full[i], 1); mbar_init(&bars.acc_empty[i], 128); }
+    mbar_init(&bars.drain, 1);
+    fence_mbar_init();
+    for (int i = 0; i < NUM_MAPS; ++i) tma_prefetch_desc(&p.maps[i]);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) c.tmem = s_tmem;
+  __syncthreads();
+
+  if (warp == 0) {
+    run_producer<Ma2Model>(p, c);
+    __syncwarp();
+  } else {
+    const bool is_mma = (warp == 1);
+    const bool is_epi = warp >= 2;
+    MmaState& st = s_st;
+    uint32_t ecnt = 0, gen = 0;
+    uint64_t t_prev = globaltimer();
+    const bool timing = p.stage_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 32;
+    auto mark = [&](int s) {
+      if (timing) {
+        const uint64_t t = globaltimer();
+        p.stage_ns[s] += t - t_prev;
+        t_prev = t;
+      }
+    };
+    auto tr = [&](int stage, int step, int l) -> unsigned long long* {
+      if (!p.trace || step != p.trace_step || l != p.trace_layer) return nullptr;
+      return p.trace + ((size_t)stage * gridDim.x + blockIdx.x) * kTrStride;
+    };
+    float* vsm = reinterpret_cast<float*>(c.work);  // vector-stage scratch (no TMA in flight there)
+    bool ok = true;
+    if (is_epi) stage_embed(p, s_xt, s_red);
+    ok = grid_barrier(p, gen++, tr(ST_QKV, 0, 0));
+    mark(ST_NORM1);
+    auto gemm = [&](int m, int l) {
+      if (is_mma) mma_gemm<Ma2Model>(p, c, st, m);
+      if (is_epi) ecnt = epi_gemm<Ma2Model>(p, c, ecnt, m, l);
+    };
+    for (int step = 0; ok && step < p.nsteps; ++step) {
+      for (int l = 0; ok && l < p.L; ++l) {
+        const float* m_self = mod_ptr(p, step, l, 0);
+        const float* m_cross = mod_ptr(p, step, l, 1);
+        const float* m_mlp = mod_ptr(p, step, l, 2);
+        gemm(MAT_QKV, l);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_SELF, step, l)))) break;
+        mark(ST_QKV);
+        if (is_epi) stage_self_attn(p, vsm);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_SO, step, l)))) break;
+        mark(ST_SELF);
+        gemm(MAT_SO, l);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_NORM2, step, l)))) break;
+        mark(ST_SO);
+        if (is_epi) stage_norm(p, m_self + 2 * D, p.split[MAT_SO], m_cross, s_red);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_CQ, step, l)))) break;
+        mark(ST_NORM2);
+        gemm(MAT_CQ, l);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_CROSS, step, l)))) break;
+        mark(ST_CQ);
+        if (is_epi) stage_cross_attn(p, c, l, vsm);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_MERGE, step, l)))) break;
+        mark(ST_CROSS);
+        if (is_epi) stage_merge(p);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_CO, step, l)))) break;
+        mark(ST_MERGE);
+        gemm(MAT_CO, l);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_NORM3, step, l)))) break;
+        mark(ST_CO);
+        if (is_epi) stage_norm(p, m_cross + 2 * D, p.split[MAT_CO], m_mlp, s_red);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_GU, step, l)))) break;
+        mark(ST_NORM3);
+        gemm(MAT_GU, l);
+        if (!(ok = grid_barrier(p, gen++, tr(ST_DN, step, l)))) break;
+        mark(ST_GU);
+        gemm(MAT_DN, l);
+        if (!(ok = grid_barrier(p, gen++, tr(l + 1 < p.L ? ST_NORM1 : ST_FINAL, step, l)))) break;
+        mark(ST_DN);
+        if (l + 1 < p.L) {
+          if (is_epi) stage_norm(p, m_mlp + 2 * D, p.split[MAT_DN], mod_ptr(p, step, l + 1, 0), s_red);
+          if (!(ok = grid_barrier(p, gen++, tr(ST_QKV, step, l + 1)))) break;
+          mark(ST_NORM1);
+        } else {
+          if (is_epi) stage_final(p, step, vsm, s_xt, s_red);
+          if (!(ok = grid_barrier(p, gen++, tr(ST_QKV, step + 1, 0)))) break;
+          mark(ST_FINAL);
+        }
+      }
+    }
+    if (is_mma) {
+      FA_ONE(tc_commit(&bars.drain));
+      mbar_wait(&bars.drain, 0, p.err, KERR_MMA);
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(s_tmem, 512);
+  }
+}
+
+}  // namespace ma2
+}  // namespace fa

@@ -31,7 +31,7 @@ class Pi05ActionExpert:
         self.lib = C.load_library()
         self.device = device
         self.cfg = C.FaConfig(num_layers, 1024, 8, 1, 256, 4096, horizon, action_dim, max_prefix, max_batch,
-                              num_steps)
+                              num_steps, 0)
         self.horizon, self.action_dim, self.max_batch = horizon, action_dim, max_batch
         h = ctypes.c_void_p()
         st = self.lib.fa_create(C.FA_MODEL_PI05, ctypes.byref(self.cfg), device, ctypes.byref(h))

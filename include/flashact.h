@@ -56,7 +56,11 @@ typedef enum { FA_KV_COMPACT_SPLIT_HALF = 0, FA_KV_FLASHRT_INTERLEAVED = 1 } fa_
 
 /* Model geometry. pi0.5: width 1024, 8 query heads, 1 KV head, head_dim 256, mlp 4096 are
  * fixed by the architecture; num_layers (18), horizon (50), action_dim (32), max_prefix,
- * max_batch and num_steps (10) are free. */
+ * max_batch and num_steps (10) are free. MolmoAct2: width 768, 8 heads, 8 KV heads (cross
+ * attention), head_dim 96, mlp 3072 are fixed; num_layers (36), horizon (<= 32, 30 as wired in
+ * the reference), action_dim (32), valid_action_dim (6 for SO100), max_prefix (the bound
+ * cross-attention context, 493 tokens in the reference run), num_steps (10; t = 0 -> 1,
+ * dt = +1/N). */
 typedef struct fa_config {
   int num_layers;
   int width;
@@ -69,6 +73,8 @@ typedef struct fa_config {
   int max_prefix; /* capacity of the bound prefix KV per observation     */
   int max_batch;  /* observations per fa_sample_actions call             */
   int num_steps;  /* Euler steps N; pi0.5 integrates t = 1 -> 0, dt=-1/N */
+  int valid_action_dim; /* MolmoAct2: action dims updated by the Euler step (the rest keep
+                           their input value, src/molmoact2/mk_ma2.cu:565); 0 = all          */
 } fa_config;
 
 /* One weight tensor. ptr may be host or device memory (CUDA unified addressing decides). */
@@ -96,6 +102,21 @@ typedef struct fa_pi05_weights {
   fa_tensor aout_w, aout_b;         /* [AD][1024], [AD]                                    */
 } fa_pi05_weights;
 
+/* MolmoAct2 action-expert weights (benchmarks/molmoact2/eval_numerics.py:77-100 names), stacked
+ * over the L blocks, [out][in] row-major: self_attn.qkv, self_attn.out_proj, cross_attn.q_proj,
+ * cross_attn.out_proj, mlp.{gate,up,down}_proj (+ biases), action_embed, final_layer.linear. */
+typedef struct fa_ma2_weights {
+  fa_tensor w_qkv, b_qkv;     /* [L][2304][768], [L][2304] */
+  fa_tensor w_so, b_so;       /* [L][768][768],  [L][768]  */
+  fa_tensor w_cq, b_cq;       /* [L][768][768],  [L][768]  */
+  fa_tensor w_co, b_co;       /* [L][768][768],  [L][768]  */
+  fa_tensor w_gate, b_gate;   /* [L][3072][768], [L][3072] */
+  fa_tensor w_up, b_up;       /* [L][3072][768], [L][3072] */
+  fa_tensor w_down, b_down;   /* [L][768][3072], [L][768]  */
+  fa_tensor ain_w, ain_b;     /* [768][AD], [768]          */
+  fa_tensor aout_w, aout_b;   /* [AD][768], [AD] (aout used in bf16 like the reference) */
+} fa_ma2_weights;
+
 /* Creates a handle on `device`. Fails with FA_ERR_UNSUPPORTED on a GPU that is not sm_100. */
 FA_API fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int device, fa_handle** out);
 
@@ -105,12 +126,28 @@ FA_API fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int device,
  * Synchronous. Replaces HybridPi05._pack_weights. */
 FA_API fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt);
 
-/* Overrides the modulations with precomputed ones: mods [num_steps][L][2][3072] fp32 (input /
- * post-attention adaRMS; each scale|shift|gate) and mod_final [num_steps][3072] (scale|shift
- * used). Device or host pointers. This is the form the reference's launch() receives
+/* MolmoAct2: packs the weights (bf16 GEMM weights, fp32 biases). Synchronous. The
+ * modulations are an input of this model (the model's own modulation cache, which the reference
+ * also passes to its kernel): set them with fa_set_modulation. */
+FA_API fa_status fa_ma2_load_weights(fa_handle* h, const fa_ma2_weights* w);
+
+/* MolmoAct2: RoPE tables of the self-attention, cos / sin [horizon][48] fp32 (host or device),
+ * as the model's rope cache provides them (eval_numerics.py:110-113). fa_create installs the
+ * theta = 10000 tables at positions 0..horizon-1 by default. */
+FA_API fa_status fa_ma2_set_rope(fa_handle* h, const float* cos_tab, const float* sin_tab);
+
+/* Overrides the modulations with precomputed ones. pi0.5: mods [num_steps][L][2][3072] fp32
+ * (input / post-attention adaRMS; each scale|shift|gate) and mod_final [num_steps][3072]
+ * (scale|shift used). MolmoAct2: mods [num_steps][L][3][3][768] ((self, cross, mlp) x (scale,
+ * shift, gate)) and mod_final [num_steps][2][768] (scale, shift), src/molmoact2/binding.cpp:
+ * 37-38. Device or host pointers. This is the form the reference's launch() receives
  * (src/pi05/binding.cpp:31, `mods`, `mod_final`). */
 FA_API fa_status fa_set_modulation(fa_handle* h, const float* mods, const float* mod_final);
 
+/* MolmoAct2: `k`, `v` are the per-block projected cross-attention context K and V,
+ * [batch][L][src_rows][768] bf16 (8 heads x 96, K already normed as the model's prepare_context
+ * produces it), with the first valid_len[b] rows valid (compacted); `layout` is ignored.
+ * pi0.5: */
 /* Binds the cached VLM prefix KV of `batch` observations (device pointers, bf16). K and V are
  * [batch][L][src_rows][256]; valid_len (host array, batch entries) gives each observation's
  * number of valid (compacted) prefix tokens, <= src_rows <= max_prefix. The action tokens'

@@ -30,7 +30,7 @@ def test_create_without_gpu_fails_cleanly():
     if torch.cuda.is_available():
         return
     lib = _capi.load_library(build())
-    cfg = _capi.FaConfig(18, 1024, 8, 1, 256, 4096, 50, 32, 968, 1, 10)
+    cfg = _capi.FaConfig(18, 1024, 8, 1, 256, 4096, 50, 32, 968, 1, 10, 0)
     h = ctypes.c_void_p()
     st = lib.fa_create(_capi.FA_MODEL_PI05, ctypes.byref(cfg), 0, ctypes.byref(h))
     assert st in (_capi.FA_ERR_INVALID, _capi.FA_ERR_CUDA, _capi.FA_ERR_UNSUPPORTED)
@@ -39,6 +39,7 @@ def test_create_without_gpu_fails_cleanly():
 
 
 def test_struct_layouts():
-    assert ctypes.sizeof(_capi.FaConfig) == 11 * 4
+    assert ctypes.sizeof(_capi.FaConfig) == 12 * 4
+    assert ctypes.sizeof(_capi.FaMa2Weights) == 18 * 16
     assert ctypes.sizeof(_capi.FaTensor) == 16
     assert ctypes.sizeof(_capi.FaPi05Weights) == 21 * 16
