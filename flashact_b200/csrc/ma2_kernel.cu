@@ -157,29 +157,59 @@ __device__ __noinline__ void stage_final(const Params& p, int step, float* xf, f
 }
 
 // ------------------------------------------------------------------ self-attention (warps 2-5)
-// Unit = (observation b, head h): the T action tokens attend to each other. q, k get a
-// weightless RMS norm over the 96 head dims and half-split RoPE (pairs i, i+48) at positions
-// 0..T-1 from the bound tables; scale 1/sqrt(96) (mk_ma2.cu:293-384).
+// Unit = (observation b, head h, group of 8 query tokens): the queries attend to all T action
+// tokens of the observation. q, k get a weightless RMS norm over the 96 head dims and half-split
+// RoPE (pairs i, i+48) at positions 0..T-1 from the bound tables; scale 1/sqrt(96)
+// (mk_ma2.cu:293-384). Every global load of a phase is issued before its first use.
+constexpr int kSelfQ = 8;  // query tokens per self-attention unit
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& raw, float* dst) {
+  const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __bfloat1622float2(b2[q]);
+    dst[2 * q] = f.x;
+    dst[2 * q + 1] = f.y;
+  }
+}
+
 __device__ __noinline__ void stage_self_attn(const Params& p, float* sm) {
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   const int T = p.T;
-  float* qs = sm;                  // [32][97]
-  float* ks = qs + TMAX * 97;      // [32][97]
+  const int ngroups = (T + kSelfQ - 1) / kSelfQ;
+  float* ks = sm;                  // [32][97] keys (normed + rotated)
   float* vs = ks + TMAX * 97;      // [32][96]
-  float* ps = vs + TMAX * 96;      // [32][33]
+  float* qs = vs + TMAX * 96;      // [8][97]
+  float* ps = qs + kSelfQ * 97;    // [8][33]
   const float scale = 0.10206207261596577f;  // 1/sqrt(96)
-  for (int u = blockIdx.x; u < p.B * H; u += gridDim.x) {
-    const int b = u / H, h = u % H;
-    for (int idx = e; idx < 3 * T * HD; idx += 128) {
-      const int sec = idx / (T * HD), rem = idx % (T * HD), t = rem / HD, d = rem % HD;
-      const float val = __bfloat162float(p.qkv[(size_t)(b * T + t) * QKV_ROWS + sec * D + h * HD + d]);
-      if (sec == 0) qs[t * 97 + d] = val;
-      else if (sec == 1) ks[t * 97 + d] = val;
-      else vs[t * 96 + d] = val;
+  for (int u = blockIdx.x; u < p.B * H * ngroups; u += gridDim.x) {
+    const int b = u / (H * ngroups), h = (u / ngroups) % H, g = u % ngroups;
+    const int t0 = g * kSelfQ, nq = min(kSelfQ, T - t0);
+    // rows: k (T), v (T), q (nq); 12 16-byte pieces per 96-dim row
+    const int nrows = 2 * T + nq;
+    uint4 raw[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int idx = e + it * 128;
+      if (idx < nrows * 12) {
+        const int row = idx / 12, seg = idx % 12;
+        const int sec = row < T ? 1 : (row < 2 * T ? 2 : 0);
+        const int t = row < T ? row : (row < 2 * T ? row - T : t0 + row - 2 * T);
+        raw[it] = __ldg(reinterpret_cast<const uint4*>(p.qkv + (size_t)(b * T + t) * QKV_ROWS + sec * D + h * HD) + seg);
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int idx = e + it * 128;
+      if (idx < nrows * 12) {
+        const int row = idx / 12, seg = idx % 12;
+        float* dst = row < T ? ks + row * 97 : (row < 2 * T ? vs + (row - T) * 96 : qs + (row - 2 * T) * 97);
+        bf16x8_to_f32(raw[it], dst + seg * 8);
+      }
     }
     sync_epi();
-    for (int row = wq; row < 2 * T; row += 4) {  // RMS over the head dims, q rows then k rows
-      float* rp = row < T ? qs + row * 97 : ks + (row - T) * 97;
+    for (int row = wq; row < T + nq; row += 4) {  // RMS over the head dims: key rows, then query rows
+      float* rp = row < T ? ks + row * 97 : qs + (row - T) * 97;
       const float a0 = rp[lane], a1 = rp[lane + 32], a2 = rp[lane + 64];
       const float r = rsqrtf(warp_sum(a0 * a0 + a1 * a1 + a2 * a2) * (1.0f / HD) + kEps);
       rp[lane] = a0 * r;
@@ -187,16 +217,16 @@ __device__ __noinline__ void stage_self_attn(const Params& p, float* sm) {
       rp[lane + 64] = a2 * r;
     }
     sync_epi();
-    for (int idx = e; idx < 2 * T * 48; idx += 128) {  // half-split RoPE
-      const int row = idx / 48, i = idx % 48, t = row < T ? row : row - T;
-      float* rp = row < T ? qs + row * 97 : ks + t * 97;
-      const float c = p.rope_cos[t * 48 + i], s = p.rope_sin[t * 48 + i];
+    for (int idx = e; idx < (T + nq) * 48; idx += 128) {  // half-split RoPE
+      const int row = idx / 48, i = idx % 48, t = row < T ? row : t0 + row - T;
+      float* rp = row < T ? ks + row * 97 : qs + (row - T) * 97;
+      const float c = p.rope_cos[t * 48 + i], sn = p.rope_sin[t * 48 + i];
       const float x1 = rp[i], x2 = rp[i + 48];
-      rp[i] = x1 * c - x2 * s;
-      rp[i + 48] = x1 * s + x2 * c;
+      rp[i] = x1 * c - x2 * sn;
+      rp[i + 48] = x1 * sn + x2 * c;
     }
     sync_epi();
-    for (int idx = e; idx < T * T; idx += 128) {
+    for (int idx = e; idx < nq * T; idx += 128) {
       const int t = idx / T, j = idx % T;
       float acc = 0.f;
 #pragma unroll 8
@@ -204,19 +234,24 @@ __device__ __noinline__ void stage_self_attn(const Params& p, float* sm) {
       ps[t * 33 + j] = acc * scale;
     }
     sync_epi();
-    for (int t = wq; t < T; t += 4) {  // softmax over the T keys, one warp per query
-      const float s = lane < T ? ps[t * 33 + lane] : -INFINITY;
-      const float m = warp_max(s);
-      const float ex = lane < T ? __expf(s - m) : 0.f;
+    for (int t = wq; t < nq; t += 4) {  // softmax over the T keys, one warp per query
+      const float sc = lane < T ? ps[t * 33 + lane] : -INFINITY;
+      const float m = warp_max(sc);
+      const float ex = lane < T ? __expf(sc - m) : 0.f;
       const float sum = warp_sum(ex);
       if (lane < T) ps[t * 33 + lane] = ex / sum;
     }
     sync_epi();
-    for (int idx = e; idx < T * HD; idx += 128) {
-      const int t = idx / HD, d = idx % HD;
-      float acc = 0.f;
-      for (int j = 0; j < T; ++j) acc = fmaf(ps[t * 33 + j], vs[j * 96 + d], acc);
-      p.sattn[(size_t)(b * T + t) * D + h * HD + d] = __float2bfloat16(acc);
+    for (int idx = e; idx < nq * (HD / 2); idx += 128) {  // two dims per thread
+      const int t = idx / (HD / 2), d = 2 * (idx % (HD / 2));
+      float a0 = 0.f, a1 = 0.f;
+      for (int j = 0; j < T; ++j) {
+        const float pj = ps[t * 33 + j];
+        a0 = fmaf(pj, vs[j * 96 + d], a0);
+        a1 = fmaf(pj, vs[j * 96 + d + 1], a1);
+      }
+      *reinterpret_cast<__nv_bfloat162*>(p.sattn + (size_t)(b * T + t0 + t) * D + h * HD + d) =
+          __floats2bfloat162_rn(a0, a1);
     }
     sync_epi();
   }
@@ -240,14 +275,29 @@ __device__ __noinline__ void stage_cross_attn(const Params& p, const Ctx& c, int
     const int lk = p.ctx_len[b];
     const int nvalid = min(KC, lk - ch * KC);
     const size_t krow0 = ((size_t)(b * p.L + l) * p.LKPAD + ch * KC);
-    for (int idx = e; idx < T * HD; idx += 128) {
-      const int t = idx / HD, d = idx % HD;
-      qs[idx] = __bfloat162float(p.qc[(size_t)(b * T + t) * D + h * HD + d]);
-    }
-    for (int idx = e; idx < KC * (HD / 8); idx += 128) {  // V chunk, 16-byte rows pieces
-      const int j = idx / (HD / 8), seg = idx % (HD / 8);
-      *reinterpret_cast<uint4*>(vs + j * HD + seg * 8) =
-          __ldg(reinterpret_cast<const uint4*>(p.vctx + (krow0 + j) * D + h * HD + seg * 8));
+    {  // Q rows (T x 12 pieces) and the V chunk (128 x 12 pieces), all loads issued first
+      uint4 qraw[3], vraw[12];
+#pragma unroll
+      for (int it = 0; it < 3; ++it) {
+        const int idx = e + it * 128;
+        if (idx < T * 12)
+          qraw[it] = __ldg(reinterpret_cast<const uint4*>(p.qc + (size_t)(b * T + idx / 12) * D + h * HD) + idx % 12);
+      }
+#pragma unroll
+      for (int it = 0; it < 12; ++it) {
+        const int idx = e + it * 128;
+        vraw[it] = __ldg(reinterpret_cast<const uint4*>(p.vctx + (krow0 + idx / 12) * D + h * HD) + idx % 12);
+      }
+#pragma unroll
+      for (int it = 0; it < 3; ++it) {
+        const int idx = e + it * 128;
+        if (idx < T * 12) bf16x8_to_f32(qraw[it], qs + (idx / 12) * HD + (idx % 12) * 8);
+      }
+#pragma unroll
+      for (int it = 0; it < 12; ++it) {
+        const int idx = e + it * 128;
+        *reinterpret_cast<uint4*>(vs + (idx / 12) * HD + (idx % 12) * 8) = vraw[it];
+      }
     }
     sync_epi();
     for (int t = wq; t < T; t += 4) {  // per-head RMS of the query, then fold in the scale
@@ -306,13 +356,35 @@ __device__ __noinline__ void stage_cross_attn(const Params& p, const Ctx& c, int
       }
     }
     sync_epi();
-    for (int idx = e; idx < T * HD; idx += 128) {  // O = P V over the chunk, normalised
-      const int t = idx / HD, d = idx % HD;
-      float acc = 0.f;
-#pragma unroll 4
-      for (int j = 0; j < KC; ++j) acc = fmaf(ps[t * 129 + j], __bfloat162float(vs[j * HD + d]), acc);
-      const float inv = qs[t * HD];
-      p.opart[(((size_t)(b * H + h) * MAX_CH + ch) * TMAX + t) * HD + d] = __float2bfloat16(acc * inv);
+    // O = P V over the chunk: thread = (3 tokens, 8 dims), 24 accumulators, one 16-byte V row
+    // piece and 3 probabilities per key
+    if (e < 12 * ((T + 2) / 3)) {
+      const int d8 = e % 12, tg = (e / 12) * 3;
+      float acc[3][8] = {};
+      for (int j = 0; j < KC; ++j) {
+        float vv[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(vs + j * HD + d8 * 8), vv);
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          const float pj = tg + q < T ? ps[(tg + q) * 129 + j] : 0.f;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[q][k] = fmaf(pj, vv[k], acc[q][k]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const int t = tg + q;
+        if (t >= T) continue;
+        const float inv = qs[t * HD];
+        uint32_t w4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[q][2 * k] * inv, acc[q][2 * k + 1] * inv);
+          w4[k] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(p.opart + (((size_t)(b * H + h) * MAX_CH + ch) * TMAX + t) * HD + d8 * 8) =
+            make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
     }
     sync_epi();
   }

@@ -37,8 +37,9 @@ def pi05_dequantised_case(c):
     return c2
 
 
-def run_pi05_ref(ext, c):
-    """Reference pi0.5 megakernel (18 layers, <= 16 tokens) on case c; returns x_t [Tv][32]."""
+def prepare_pi05_ref(ext, c):
+    """Packs case c for the reference pi0.5 megakernel; returns (launch, read): launch() runs the
+    kernel once from the initial noise, read() returns x_t [Tv][32]."""
     Tv, Lp, N = c.T, c.Lp, c.num_steps
     dev = torch.device("cuda")
     # quantise per original row (row permutations commute with per-row scales)
@@ -80,18 +81,32 @@ def run_pi05_ref(ext, c):
     f16 = lambda *s: torch.zeros(*s, dtype=torch.float16, device=dev)
     xt_d = x_t.to(dev)
     empty = torch.empty(0, dtype=torch.bfloat16, device=dev)
-    ext.launch(w1, wo, w2, w3, s1, so_, s2, s3, mods.contiguous().to(dev), modf.contiguous().to(dev),
-               cos.contiguous().to(dev), sin.contiguous().to(dev), c.w["ain_w"].float().contiguous().to(dev),
-               c.w["ain_b"].float().to(dev), c.w["aout_w"].float().contiguous().to(dev), c.w["aout_b"].float().to(dev),
-               empty, empty, 0, kc.to(dev), vt.to(dev), Lp, Lmax, N, Tv, xt_d, f32(2 * T5, D5), f32(4, T5, D5),
-               torch.zeros(16, dtype=torch.int64, device=dev), f16(T5, D5), f16(T5, 2048), f16(T5, 2048),
-               f16(T5, F5), f32(8, T5, Lmax), f16(8, T5, Lmax), 148, 256)
+    x0 = xt_d.clone()
+
+    args = [w1, wo, w2, w3, s1, so_, s2, s3, mods.contiguous().to(dev), modf.contiguous().to(dev),
+                   cos.contiguous().to(dev), sin.contiguous().to(dev), c.w["ain_w"].float().contiguous().to(dev),
+                   c.w["ain_b"].float().to(dev), c.w["aout_w"].float().contiguous().to(dev), c.w["aout_b"].float().to(dev),
+                   empty, empty, 0, kc.to(dev), vt.to(dev), Lp, Lmax, N, Tv, xt_d, f32(2 * T5, D5), f32(4, T5, D5),
+                   torch.zeros(16, dtype=torch.int64, device=dev), f16(T5, D5), f16(T5, 2048), f16(T5, 2048),
+                   f16(T5, F5), f32(8, T5, Lmax), f16(8, T5, Lmax), 148, 256]  # device arguments, built once
+
+    def launch():
+        xt_d.copy_(x0)
+        ext.launch(*args)
+
+    return launch, lambda: xt_d[:Tv].cpu()
+
+
+def run_pi05_ref(ext, c):
+    """Reference pi0.5 megakernel (18 layers, <= 16 tokens) on case c; returns x_t [Tv][32]."""
+    launch, read = prepare_pi05_ref(ext, c)
+    launch()
     torch.cuda.synchronize()
-    return xt_d[:Tv].cpu()
+    return read()
 
 
-def run_ma2_ref(ext, c):
-    """Reference MolmoAct2 megakernel (36 blocks, 32 tokens) on case c; returns x_t [Tv][32]."""
+def prepare_ma2_ref(ext, c):
+    """Packs case c for the reference MolmoAct2 megakernel; returns (launch, read)."""
     NL, T, D, F, AD = 36, 32, 768, 3072, 32
     dev = torch.device("cuda")
     bf = lambda t: t.to(torch.bfloat16).contiguous().to(dev)
@@ -114,13 +129,27 @@ def run_ma2_ref(ext, c):
     xt_d = x_t.to(dev)
     bufs = [torch.zeros(T, D, dtype=torch.bfloat16, device=dev) for _ in range(8)]
     bufs.append(torch.zeros(T, F, dtype=torch.bfloat16, device=dev))
-    ext.launch(ws, bs, fp(c.mods), fp(c.mod_final), fp(cosf), fp(sinf), fp(c.w["w_ain"]), fp(c.w["b_ain"]),
-               bf(c.w["w_aout"]), fp(c.w["b_aout"]), bf(kctx), bf(vtctx), Lk, Lkmax, c.T, c.adim, c.num_steps, xt_d,
-               torch.zeros(T, D, device=dev), torch.zeros(3, T, D, device=dev),
-               torch.zeros(16, dtype=torch.int64, device=dev), bufs, torch.zeros(8, T, Lkmax, device=dev),
-               torch.zeros(8, T, Lkmax, dtype=torch.bfloat16, device=dev), 148, 256)
+    x0 = xt_d.clone()
+
+    args = [ws, bs, fp(c.mods), fp(c.mod_final), fp(cosf), fp(sinf), fp(c.w["w_ain"]), fp(c.w["b_ain"]),
+                   bf(c.w["w_aout"]), fp(c.w["b_aout"]), bf(kctx), bf(vtctx), Lk, Lkmax, c.T, c.adim, c.num_steps, xt_d,
+                   torch.zeros(T, D, device=dev), torch.zeros(3, T, D, device=dev),
+                   torch.zeros(16, dtype=torch.int64, device=dev), bufs, torch.zeros(8, T, Lkmax, device=dev),
+                   torch.zeros(8, T, Lkmax, dtype=torch.bfloat16, device=dev), 148, 256]  # device arguments, built once
+
+    def launch():
+        xt_d.copy_(x0)
+        ext.launch(*args)
+
+    return launch, lambda: xt_d[:c.T].cpu()
+
+
+def run_ma2_ref(ext, c):
+    """Reference MolmoAct2 megakernel (36 blocks, 32 tokens) on case c; returns x_t [Tv][32]."""
+    launch, read = prepare_ma2_ref(ext, c)
+    launch()
     torch.cuda.synchronize()
-    return xt_d[:c.T].cpu()
+    return read()
 
 
 def ma2_bf16_case(c):
