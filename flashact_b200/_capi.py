@@ -54,11 +54,13 @@ class FlashActError(RuntimeError):
 _lib = None
 
 
-def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
-    """Loads libflashact.so; raises (never falls back) when it has not been built."""
+def load_library(path: str = None) -> ctypes.CDLL:
+    """Loads libflashact.so (or the build named by $FLASHACT_LIB, for A/B comparisons of two
+    builds); raises (never falls back) when it has not been built."""
     global _lib
     if _lib is not None:
         return _lib
+    path = path or os.environ.get("FLASHACT_LIB") or LIB_PATH
     if not os.path.exists(path):
         raise FlashActError(FA_ERR_UNSUPPORTED, f"{path} missing: run `python -m flashact_b200.build`")
     lib = ctypes.CDLL(path)

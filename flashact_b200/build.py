@@ -26,23 +26,25 @@ def _stale() -> bool:
     return any(os.path.getmtime(s) > t for s in srcs)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
+def build(force: bool = False, verbose: bool = False, out: str = None, extra_flags=()) -> str:
+    """Compiles SOURCES into LIB (or `out`, with `extra_flags` added: for side-by-side variants)."""
+    lib = out or LIB
+    if out is None and not extra_flags and not force and not _stale():
         return LIB
     os.makedirs(LIB_DIR, exist_ok=True)
     objs = []
     for src in SOURCES:
         obj = os.path.join(LIB_DIR, src.replace(".cu", ".o"))
-        cmd = [NVCC, *FLAGS, "-rdc=false", "-c", os.path.join(CSRC, src), "-o", obj]
+        cmd = [NVCC, *FLAGS, *extra_flags, "-rdc=false", "-c", os.path.join(CSRC, src), "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
         objs.append(obj)
-    subprocess.run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", LIB], check=True)
+    subprocess.run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", lib], check=True)
     for o in objs:
         os.remove(o)
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":

@@ -52,9 +52,15 @@ __device__ __forceinline__ int tok_bi(float invT, int n) { return (int)(((float)
 // when the stage is not traced); g_t0 is the stage's start clock. Set by the barrier thread.
 __shared__ unsigned long long* g_trp;
 __shared__ unsigned long long g_t0;
+// Compiled in only with -DFA_TRACE (diagnostic builds): the marks cost instruction-cache space
+// in every stage.
 __device__ __forceinline__ void trace_mark(int slot) {
+#ifdef FA_TRACE
   unsigned long long* tr = g_trp;
   if (tr) tr[slot] = clock64() - g_t0;
+#else
+  (void)slot;
+#endif
 }
 
 // gelu with the tanh approximation (src/pi05/mk6.cu:79-82).
@@ -93,9 +99,13 @@ __device__ __noinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned lon
     __threadfence();
     fence_proxy_async_global();
     s_ok = ok;
+#ifdef FA_TRACE
     g_t0 = clock64();
     g_trp = next_tr;
     if (next_tr) next_tr[kTrStart] = g_t0;
+#else
+    (void)next_tr;
+#endif
   }
   sync_main();
   return s_ok != 0;
@@ -120,6 +130,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 // The producer and MMA roles run as whole warps (uniform control flow, every lane waits on
 // the same barriers) and only lane 0 issues TMA / tcgen05 / commit instructions.
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ bool leader() { return (threadIdx.x & 31) == 0; }
 #define FA_ONE(stmt)      \
   do {                    \
@@ -134,7 +145,7 @@ struct Bars {
   uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
 };
 struct Ctx {
-  uint8_t* ring;  // ring_slots x 16 KB
+  uint8_t* ring;  // ring_slots x (wg x 16 KB)
   uint8_t* work;  // activation atoms (GEMM) or Q | K/V | P (attention)
   Bars* bars;
   uint32_t tmem;
@@ -155,14 +166,15 @@ __device__ __forceinline__ int group_tiles(const P& p, int g) {
 }
 
 // ------------------------------------------------------------------ warp 0: weight producer
-// Walks (step, layer, GEMM matrix, unit, token group, K atom) — the exact order the MMA lane
-// consumes — and keeps the ring full. It never waits on activations.
+// Walks (step, layer, GEMM matrix, unit, token group, K-atom group) — the exact order the MMA
+// lane consumes — and keeps the ring full. It never waits on activations.
 template <class Model>
 __device__ __noinline__ void run_producer(const typename Model::Params& p, const Ctx& c) {
   // Every field is read once into registers: the inline-asm memory clobbers would otherwise
   // force a reload through the generic Params/Ctx references after each TMA / mbarrier op.
   const uint64_t pol = policy_evict_first();
-  const int R = c.ring_slots, nsteps = p.nsteps, L = p.L, ngroups = p.ngroups;
+  const int R = c.ring_slots, nsteps = p.nsteps, L = p.L, ngroups = p.ngroups, wg = p.wg;
+  const uint32_t slot_bytes = (uint32_t)wg * kAtomBytes;
   uint8_t* const ring = c.ring;
   Bars* const bars = c.bars;
   int* const err = p.err;
@@ -182,20 +194,22 @@ __device__ __noinline__ void run_producer(const typename Model::Params& p, const
         for (int u = 0; ok && u < gcnt[m]; ++u) {
           const GemmUnit gu = gul[m][u];
           for (int g = 0; ok && g < ngroups; ++g)
-            for (int j = 0; j < gu.natoms; ++j, ++it) {
+            for (int j = 0; j < gu.natoms; j += wg, ++it) {
               const int slot = it % R, round = it / R;
               if (round > 0 && !mbar_wait(&bars->wempty[slot], (round - 1) & 1, err, KERR_PRODUCER)) {
                 ok = false;
                 break;
               }
               if (leader()) {
+#ifdef FA_TRACE
                 if (trace && u == 0 && g == 0 && j == 0 && step == tstep && l == tlayer) {
                   const int stg = Model::trace_stage(m);
                   trace[((size_t)stg * gridDim.x + blockIdx.x) * kTrStride + kTrProdIssue] = clock64();
                 }
-                mbar_expect_tx(&bars->wfull[slot], kAtomBytes);
-                tma_load_2d(ring + (size_t)slot * kAtomBytes, maps + Model::wmap(m), &bars->wfull[slot], (gu.katom0 + j) * 64,
-                            l * rows + gu.mtile * 128, pol);
+#endif
+                mbar_expect_tx(&bars->wfull[slot], slot_bytes);
+                tma_load_3d(ring + (size_t)slot * slot_bytes, maps + Model::wmap(m), &bars->wfull[slot], 0,
+                            l * rows + gu.mtile * 128, gu.katom0 + j, pol);
               }
               __syncwarp();
             }
@@ -209,7 +223,7 @@ __device__ __noinline__ void run_producer(const typename Model::Params& p, const
 // ------------------------------------------------------------------ warp 1 lane 0: GEMM MMAs
 // MMA-lane state; lives in shared memory (one instance per CTA, touched by one thread).
 struct MmaState {
-  uint32_t wit;          // weight-ring items consumed
+  uint32_t wit;          // weight-ring slots consumed
   uint32_t bload;        // activation batches loaded (phase of bfull)
   uint32_t bfree;        // activation batches released (phase of bempty)
   uint32_t acc;          // accumulator buffers used
@@ -229,7 +243,7 @@ struct MmaCtx {
   int* err;
   const CUtensorMap* amap;
   uint32_t tmem;
-  int R, batoms, NTILE, TG, ngroups, tiles, box_atoms;
+  int R, batoms, NTILE, TG, ngroups, tiles, box_atoms, wg;
 };
 
 // Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
@@ -257,6 +271,7 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
   k.tmem = c.tmem; k.R = c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG; k.ngroups = p.ngroups;
   k.tiles = p.NPAD / p.NTILE;
   k.box_atoms = p.box_atoms;
+  k.wg = p.wg;
   const GemmUnit* const units = c.gu[m];
   const int nunits = c.gcnt[m];
   const uint32_t idesc = idesc_bf16(128, k.NTILE);
@@ -266,7 +281,10 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
     const GemmUnit gu = units[u];
     for (int g = 0; g < k.ngroups; ++g) {
       const int nt = min(k.TG, k.tiles - g * k.TG);
-      const int per_batch = max(1, k.batoms / nt);  // K atoms per activation batch
+      // K atoms per activation batch: whole activation boxes (the host sizes the area for one)
+      // (and whole weight slots: both granules are powers of two, so their max is a multiple of each)
+      const int gran = max(k.box_atoms, k.wg);
+      const int per_batch = max(gran, (k.batoms / nt) / gran * gran);
       int j1 = min((int)gu.natoms, per_batch);
       if (u == 0 && g == 0) FA_ONE(trace_mark(13));
       load_b_batch(k, gu, g, nt, 0, j1);
@@ -279,16 +297,22 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
         if (!mbar_wait(&bars->bfull, st.bload & 1, k.err, KERR_MMA)) return false;
         ++st.bload;
         if (u == 0 && g == 0 && j0 == 0) FA_ONE(trace_mark(kTrMmaB0));
-        for (int j = j0; j < j1; ++j) {
+        for (int j = j0; j < j1; j += k.wg) {  // one ring slot = wg weight atoms
           const int wslot = st.wit % k.R;
           if (!mbar_wait(&bars->wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
           if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(kTrMmaW0));
-          const uint64_t da = sdesc_sw128(k.ring + (size_t)wslot * kAtomBytes);
+          if (u == 0 && g == 0 && j == 4) FA_ONE(trace_mark(9));
+          if (u == 0 && g == 0 && j == 8) FA_ONE(trace_mark(10));
+          if (u == 0 && g == 0 && j == 12) FA_ONE(trace_mark(11));
           if (leader()) {
-            for (int i = 0; i < nt; ++i) {
-              const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j - j0)) * tile);
+            for (int jj = 0; jj < k.wg; ++jj) {
+              const uint64_t da = sdesc_sw128(k.ring + ((size_t)wslot * k.wg + jj) * kAtomBytes);
+              for (int i = 0; i < nt; ++i) {
+                const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j + jj - j0)) * tile);
 #pragma unroll
-              for (int s = 0; s < 4; ++s) tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, (j | s) != 0);
+                for (int s = 0; s < 4; ++s)
+                  tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, ((j + jj) | s) != 0);
+              }
             }
             tc_commit(&bars->wempty[wslot]);
           }
@@ -300,6 +324,7 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
           FA_ONE(tc_commit(&bars->bempty));
           if (!mbar_wait(&bars->bempty, st.bfree & 1, k.err, KERR_MMA)) return false;
           ++st.bfree;
+          if (u == 0 && g == 0) FA_ONE(trace_mark(14));
           j1 = min((int)gu.natoms, j0 + per_batch);
           load_b_batch(k, gu, g, nt, j0, j1);
         }
@@ -320,46 +345,46 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
 
 // GEMM epilogue driver (warps 2-5): waits for each accumulator, walks it in 16-token chunks
 // through Model::epi_tile and, for staged outputs, copies each 64-token sub-tile out with
-// Model::epi_copy_out.
+// Model::epi_copy_out. Each model hook has ONE call site: instruction-cache space is a
+// first-order cost in a persistent kernel whose per-layer code cycles through every stage.
+// (A K-split of the RoPE / GeGLU matrices with an in-stage reduction through L2 was measured
+// slower than full-K tiles at bs=1: its extra dependent L2 round trips outweigh the shorter MMA
+// chains.)
 template <class Model>
 __device__ __noinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int row = qd * 32 + lane;
-  typename Model::Epi e;
-  Model::epi_load(e, p, c, l);
   const int NTILE = p.NTILE, TG = p.TG, ngroups = p.ngroups, tiles = p.NPAD / p.NTILE;
   int* const err = p.err;
   Bars* const bars = c.bars;
   const uint32_t taddr = c.tmem + ((uint32_t)(qd * 32) << 16);
   const GemmUnit* const units = c.gu[m];
   const int nunits = c.gcnt[m];
+  typename Model::Epi e;
+  Model::epi_load(e, p, c, l);
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
+    const bool staged = Model::staged(m, gu);
     for (int g = 0; g < ngroups; ++g) {
-      const int nt = min(TG, tiles - g * TG);
+      const int nchunks = min(TG, tiles - g * TG) * NTILE / 16;
       const int a = ecnt & 1;
       if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;
-      if (u == 0 && g == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
       tc_fence_after();
-      const bool staged = Model::staged(m, gu);
-      for (int i = 0; i < nt; ++i) {
+      const int tok0 = g * TG * NTILE;
+      for (int sub = 0; sub < (nchunks + 3) >> 2; ++sub) {  // 64-token sub-tiles
+        const int c0 = sub * 4, c1 = min(nchunks, sub * 4 + 4);
+        const int nb0 = tok0 + sub * 64;
 #pragma unroll 1
-        for (int c64 = 0; c64 < NTILE; c64 += 64) {
-          const int nb0 = g * TG * NTILE + i * NTILE + c64;
-#pragma unroll 1
-          for (int cc = 0; cc < 64; cc += 16) {
-            float v[16];
-            tmem_ld16(taddr + a * 256 + i * NTILE + c64 + cc, v);
-            tc_wait_ld();
-            if (u == 0 && g == 0 && i == 0 && c64 + cc == 0 && threadIdx.x == 64) trace_mark(14);
-            Model::epi_tile(e, gu, m, qd, lane, row, nb0 + cc, nb0, v);
-            if (u == 0 && g == 0 && i == 0 && c64 + cc == 0 && threadIdx.x == 64) trace_mark(15);
-          }
-          if (staged) {
-            sync_epi();
-            Model::epi_copy_out(e, gu, m, nb0);
-            sync_epi();
-          }
+        for (int q = c0; q < c1; ++q) {
+          float v[16];
+          tmem_ld16(taddr + a * 256 + q * 16, v);
+          tc_wait_ld();
+          Model::epi_tile(e, gu, m, qd, lane, row, tok0 + q * 16, nb0, v);
+        }
+        if (staged) {
+          sync_epi();
+          Model::epi_copy_out(e, gu, m, nb0, 0, (c1 - c0) * 16);
+          sync_epi();
         }
       }
       tc_fence_before();

@@ -10,6 +10,11 @@ constexpr int kThreads = 192;              // warp 0 producer, warp 1 MMA, warps
 constexpr int kAtomBytes = 128 * 64 * 2;   // one 128-row x 64-col bf16 atom, 128-byte swizzle
 constexpr int kSmemUse = 224 * 1024;       // dynamic shared memory used (ring + work area)
 constexpr int kSmemDyn = kSmemUse + 1024;  // + alignment slack
+// Weight atoms per ring slot (Params::wg, 1..kMaxWG): one 3D TMA box of wg consecutive K-atoms
+// of a 128-row tile. A single SM sustains about 4 TMA loads in flight, so larger boxes raise its
+// streaming rate (measured on B200: 16 KB boxes ~68 GB/s per SM; 64 KB boxes ~120 GB/s with two
+// in flight).
+constexpr int kMaxWG = 4;
 constexpr int kMaxRing = 12;               // weight-ring slots
 constexpr int kMaxBBytes = 128 * 1024;     // activation (B operand) area of a GEMM CTA, upper bound
 constexpr int kMaxBAtoms = 16;             // activation atoms resident at once
@@ -18,6 +23,9 @@ constexpr int kMaxAU = 64;                 // attention units per CTA per layer
 constexpr int kMaxMats = 6;                // GEMM matrices per layer
 constexpr int kStageBytes = 16 * 1024;     // epilogue staging area
 constexpr int kMaxStages = 16;             // traced stage kinds
+constexpr int kMaxGroupCtr = 256;          // K-split group counters (one per 128-row tile of a grouped matrix)
+constexpr int kGroupMaxTokens = 256;       // K-split groups only for batches of at most this many padded tokens
+constexpr int kCtrlWords = 2 + kMaxGroupCtr;  // launch control words: barrier, error, group counters
 
 struct GemmUnit {
   uint16_t mtile;   // 128-row tile of the packed weight

@@ -77,6 +77,7 @@ struct Params {
   // control
   unsigned int* bar;
   int* err;
+  int wg;  // weight atoms per ring slot / TMA box
   unsigned long long* stage_ns;
   int inject_barrier;
   unsigned int spin_limit;

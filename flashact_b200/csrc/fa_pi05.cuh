@@ -74,6 +74,7 @@ struct Params {
   // control
   unsigned int* bar;             // grid-barrier counter, zeroed before each launch
   int* err;                      // 0 = ok; otherwise the first failure code
+  int wg;  // weight atoms per ring slot / TMA box
   unsigned long long* stage_ns;  // [NUM_STAGES] or null
   // host-side fault injection for tests: CTA 0 skips arriving at grid barrier number
   // `inject_barrier` (-1 = off); every grid-barrier spin gives up after `spin_limit` polls.

@@ -56,8 +56,9 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t phase) {
 // Bounded parity wait. Returns false (and raises *err) when the limit is hit or another
 // role already raised the error word. A non-blocking test comes first so that an already
 // completed phase does not take the try_wait suspend path.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* err, int code) {
-  if (mbar_test_wait(bar, phase)) return true;
+// Bounded wait: the already-complete case stays inline; the spin (with its error exit) is one
+// out-of-line copy, which keeps the hot loops that wait on many barriers small.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t phase, volatile int* err, int code) {
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, phase)) return true;
     if ((i & 255u) == 255u) {
@@ -67,6 +68,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatil
   }
   atomicCAS((int*)err, 0, code);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* err, int code) {
+  if (mbar_test_wait(bar, phase)) return true;
+  return mbar_wait_slow(bar, phase, err, code);
 }
 
 // ---------------------------------------------------------------- fences

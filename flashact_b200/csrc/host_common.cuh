@@ -35,6 +35,9 @@ struct fa_handle {
   bool weights_ready = false, kv_ready = false, timing = false;
   int last_launches = 0;
   int split_o = 4, split_dn = 8, attn_penalty = 8;
+  int bmax_bytes = 64 * 1024;  // activation-area cap of a GEMM CTA
+  int ring_max = 12;           // weight-ring depth cap
+  int wg = 4;                  // weight atoms per ring slot (bound batch)
   // bound batch
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LPAD = 0;
   std::vector<int> valid_len;

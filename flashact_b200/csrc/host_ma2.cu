@@ -27,6 +27,7 @@ struct Ma2State {
   CtaPlan* d_plans = nullptr;
   size_t gcap = 0, acap = 0;
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LKPAD = 0, adim = 0;
+  int wg = 4;  // weight atoms per ring slot
   int split[M::NUM_MATS] = {1, 3, 1, 3, 1, 6};
   std::vector<int> ctx;
   bool weights = false, mods_set = false, bound = false;
@@ -238,6 +239,11 @@ static fa_status ma2_plan(fa_handle* h) {
   }
   std::vector<std::vector<GemmUnit>> per((size_t)nblk * M::NUM_MATS);
   const int order[M::NUM_MATS] = {M::MAT_GU, M::MAT_QKV, M::MAT_DN, M::MAT_SO, M::MAT_CQ, M::MAT_CO};
+  // weight atoms per ring slot: 64 KB boxes for one token tile, 32 KB otherwise; divides every unit
+  s->wg = s->NTILE == 64 ? fa::kMaxWG : 2;
+  if (const char* e = getenv("FA_WG")) s->wg = std::max(1, std::min(s->wg, atoi(e)));
+  for (int m = 0; m < M::NUM_MATS; ++m)
+    while ((kMatK[m] / 64 / s->split[m]) % s->wg != 0) s->wg >>= 1;
   for (int oi = 0; oi < M::NUM_MATS; ++oi) {
     const int m = order[oi];
     const int mtiles = kMatRows[m] / 128, katoms = kMatK[m] / 64, split = s->split[m], per_split = katoms / split;
@@ -257,19 +263,21 @@ static fa_status ma2_plan(fa_handle* h) {
   const int tile = s->NTILE * 128;
   for (int i = 0; i < nblk; ++i) {
     int bb = tile, ng = 0;
+    const int ntg = std::min(s->TG, s->NPAD / s->NTILE);  // token tiles per group
     for (int m = 0; m < M::NUM_MATS; ++m) {
       ng += (int)per[(size_t)i * M::NUM_MATS + m].size();
-      for (const GemmUnit& x : per[(size_t)i * M::NUM_MATS + m]) bb = std::max(bb, (int)x.natoms * s->TG * tile);
+      for (const GemmUnit& x : per[(size_t)i * M::NUM_MATS + m]) bb = std::max(bb, (int)x.natoms * ntg * tile);
     }
     if (ng > fa::kMaxGU || plans[i].a_cnt > fa::kMaxAU)
       return fail(h, FA_ERR_INVALID, "batch too large for the per-CTA work lists (%d GEMM, %d attention units)", ng,
                   plans[i].a_cnt);
     bb = std::min(bb, std::min(fa::kMaxBBytes, fa::kMaxBAtoms * tile));
+    bb = std::max(bb, tile * ntg * std::max(s->NTILE == 64 ? 4 : 2, s->wg));  // one activation box and weight slot per token tile
     if (plans[i].a_cnt > 0) bb = std::max(tile, std::min(bb, 64 * 1024));
     plans[i].b_bytes = bb;
     const int work = std::max(bb, M::kMinWork) + fa::kStageBytes;
-    plans[i].ring_slots = std::min(fa::kMaxRing, (fa::kSmemUse - work) / fa::kAtomBytes);
-    if (plans[i].ring_slots < 2) return fail(h, FA_ERR_INVALID, "shared-memory plan leaves no weight ring");
+    plans[i].ring_slots = std::min(fa::kMaxRing, (fa::kSmemUse - work) / (s->wg * fa::kAtomBytes));
+    if (plans[i].ring_slots < 1) return fail(h, FA_ERR_INVALID, "shared-memory plan leaves no weight ring");
     for (int m = 0; m < M::NUM_MATS; ++m) {
       plans[i].g_off[m] = (int)gu.size();
       plans[i].g_cnt[m] = (int)per[(size_t)i * M::NUM_MATS + m].size();
@@ -299,7 +307,7 @@ static fa_status ma2_params(fa_handle* h) {
   const int L = h->cfg.num_layers;
   fa_status st;
   for (int m = 0; m < M::NUM_MATS; ++m)
-    if ((st = make_map(h, &p.maps[M::MAP_W_QKV + m], s->w[m], kMatK[m], (uint64_t)L * kMatRows[m], 64, 128)) != FA_OK)
+    if ((st = make_map3(h, &p.maps[M::MAP_W_QKV + m], s->w[m], kMatK[m], (uint64_t)L * kMatRows[m], 128, s->wg)) != FA_OK)
       return st;
   const uint32_t ba = s->NTILE == 64 ? 4 : 2;
   if ((st = make_map3(h, &p.maps[M::MAP_XN], s->xn, M::D, s->NPAD, s->NTILE, ba)) != FA_OK) return st;
@@ -307,6 +315,7 @@ static fa_status ma2_params(fa_handle* h) {
   if ((st = make_map3(h, &p.maps[M::MAP_CATTN], s->cattn, M::D, s->NPAD, s->NTILE, ba)) != FA_OK) return st;
   if ((st = make_map3(h, &p.maps[M::MAP_H], s->hbuf, M::F, s->NPAD, s->NTILE, ba)) != FA_OK) return st;
   p.box_atoms = (int)ba;
+  p.wg = s->wg;
   p.L = L; p.T = h->cfg.horizon; p.B = s->B; p.NT = s->NT; p.NPAD = s->NPAD; p.NTILE = s->NTILE; p.TG = s->TG;
   p.ngroups = s->ngroups; p.nsteps = h->cfg.num_steps; p.AD = h->cfg.action_dim; p.adim = s->adim; p.LKPAD = s->LKPAD;
   for (int m = 0; m < M::NUM_MATS; ++m) p.split[m] = s->split[m];

@@ -168,6 +168,8 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   auto pow2 = [](int v) { int r = 1; while (r * 2 <= v) r *= 2; return r; };
   if (const char* e = getenv("FA_SPLIT_O")) h->split_o = pow2(std::max(1, std::min(8, atoi(e))));
   if (const char* e = getenv("FA_SPLIT_DN")) h->split_dn = pow2(std::max(1, std::min(8, atoi(e))));
+  if (const char* e = getenv("FA_RING_MAX")) h->ring_max = std::max(2, atoi(e));
+  if (const char* e = getenv("FA_BMAX_KB")) h->bmax_bytes = std::max(8, std::min(128, atoi(e))) * 1024;
   if (const char* e = getenv("FA_ATTN_PENALTY")) h->attn_penalty = std::max(0, atoi(e));
   auto bad = [&](fa_status st) { g_create_err = h->err; fa_destroy(h); return st; };
   if (cudaSetDevice(device) != cudaSuccess) return bad(fail(h, FA_ERR_CUDA, "cudaSetDevice(%d) failed", device));
@@ -204,7 +206,7 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   ALLOC(rope_sin, (size_t)MB * T * 128);
   ALLOC(d_valid, MB);
   ALLOC(d_nchunks, MB);
-  ALLOC(ctrl, 2);
+  ALLOC(ctrl, kCtrlWords);
   ALLOC(stage_ns, kMaxStages);
   ALLOC(d_plans, h->num_sms);
 #undef ALLOC
@@ -362,6 +364,9 @@ extern "C" fa_status fa_set_modulation(fa_handle* h, const float* mods, const fl
 // observation, 4 head pairs x (prefix chunks + 1 suffix chunk). Attention units go to the first
 // CTAs in contiguous runs (same head pair -> Q reuse); each GEMM stage is then spread so that
 // no CTA holds two units of one stage before all CTAs hold one, ties broken by total bytes.
+// K atoms per activation TMA load (32 KB boxes).
+static int act_box_atoms(const fa_handle* h) { return h->NTILE == 64 ? 4 : 2; }
+
 static fa_status build_plan(fa_handle* h) {
   const int nblk = h->num_sms;
   std::vector<AttnUnit> au;
@@ -384,6 +389,13 @@ static fa_status build_plan(fa_handle* h) {
   }
   struct Spec { int mtiles, katoms, split; };
   const Spec spec[4] = {{20, D / 64, 1}, {8, QD / 64, h->split_o}, {64, D / 64, 1}, {8, F / 64, h->split_dn}};
+  // Weight atoms per ring slot: 64 KB boxes when one token tile is in flight, 32 KB otherwise
+  // (keeps an attention CTA's activation batch, which must hold whole slots, inside 64 KB); never
+  // more than divides every unit's K range.
+  h->wg = h->NTILE == 64 ? kMaxWG : 2;
+  if (const char* e = getenv("FA_WG")) h->wg = std::max(1, std::min(h->wg, atoi(e)));
+  for (int m = 0; m < 4; ++m)
+    while ((spec[m].katoms / spec[m].split) % h->wg != 0) h->wg >>= 1;
   std::vector<std::vector<GemmUnit>> per(nblk * 4);
   const int order[4] = {MAT_QKV, MAT_GU, MAT_DN, MAT_O};
   for (int oi = 0; oi < 4; ++oi) {
@@ -406,19 +418,23 @@ static fa_status build_plan(fa_handle* h) {
   for (int i = 0; i < nblk; ++i) {
     // Activation area: the largest (unit, token group) K-range of this CTA, whole if it fits.
     int bb = tile, ng = 0;
+    const int ntg = std::min(h->TG, h->NPAD / h->NTILE);  // token tiles per group
     for (int m = 0; m < 4; ++m) {
       ng += (int)per[i * 4 + m].size();
-      for (const GemmUnit& x : per[i * 4 + m]) bb = std::max(bb, (int)x.natoms * h->TG * tile);
+      for (const GemmUnit& x : per[i * 4 + m]) bb = std::max(bb, (int)x.natoms * ntg * tile);
     }
     if (ng > kMaxGU || plans[i].a_cnt > kMaxAU)
       return fail(h, FA_ERR_INVALID, "batch too large for the per-CTA work lists (%d GEMM, %d attention units)", ng,
                   plans[i].a_cnt);
-    bb = std::min(bb, std::min(kMaxBBytes, kMaxBAtoms * tile));
+    // Capped so that the weight ring stays deep (larger K ranges load in several batches).
+    bb = std::min(bb, std::min(std::min(kMaxBBytes, h->bmax_bytes), kMaxBAtoms * tile));
+    bb = std::max(bb, tile * ntg * std::max(act_box_atoms(h), h->wg));  // one activation box and weight slot per token tile
     const int work = plans[i].a_cnt > 0 ? kAttnWork : bb + 16 * 1024;  // + epilogue staging
     // Attention CTAs keep their activation area inside the Q region (first 64 KB) so that the
     // prefix-K prefetch into the K/V area survives the GEMM stages in between.
     plans[i].b_bytes = plans[i].a_cnt > 0 ? std::max(tile, std::min(bb, 64 * 1024)) : bb;
-    plans[i].ring_slots = std::min(kMaxRing, (kSmemUse - work) / kAtomBytes);
+    plans[i].ring_slots = std::min(std::min(kMaxRing, h->ring_max), (kSmemUse - work) / (h->wg * kAtomBytes));
+    if (plans[i].ring_slots < 1) return fail(h, FA_ERR_INVALID, "shared-memory plan leaves no weight ring");
     for (int m = 0; m < 4; ++m) {
       plans[i].g_off[m] = (int)gu.size();
       plans[i].g_cnt[m] = (int)per[i * 4 + m].size();
@@ -446,13 +462,14 @@ static fa_status build_params(fa_handle* h) {
   memset(&p, 0, sizeof(p));
   const int L = h->cfg.num_layers, B = h->B;
   fa_status st;
-#define MAP(i, base, inner, outer, bi, bo) if ((st = make_map(h, &p.maps[i], base, inner, outer, bi, bo)) != FA_OK) return st
-  MAP(MAP_W_QKV, h->w_qkv, D, (uint64_t)L * QKV_ROWS, 64, 128);
-  MAP(MAP_W_O, h->w_o, QD, (uint64_t)L * D, 64, 128);
-  MAP(MAP_W_GU, h->w_gu, D, (uint64_t)L * 2 * F, 64, 128);
-  MAP(MAP_W_DN, h->w_dn, F, (uint64_t)L * D, 64, 128);
-#undef MAP
-  const uint32_t ba = h->NTILE == 64 ? 4 : 2;  // 32 KB per activation TMA load
+  // weights: 3D boxes of wg K-atoms x 128 rows (one ring slot per load)
+#define MAPW(i, base, K, rows) if ((st = make_map3(h, &p.maps[i], base, K, rows, 128, h->wg)) != FA_OK) return st
+  MAPW(MAP_W_QKV, h->w_qkv, D, (uint64_t)L * QKV_ROWS);
+  MAPW(MAP_W_O, h->w_o, QD, (uint64_t)L * D);
+  MAPW(MAP_W_GU, h->w_gu, D, (uint64_t)L * 2 * F);
+  MAPW(MAP_W_DN, h->w_dn, F, (uint64_t)L * D);
+#undef MAPW
+  const uint32_t ba = (uint32_t)act_box_atoms(h);
 #define MAP3(i, base, K, rows, br, bat) if ((st = make_map3(h, &p.maps[i], base, K, rows, br, bat)) != FA_OK) return st
   MAP3(MAP_XN, h->xn, D, h->NPAD, h->NTILE, ba);
   MAP3(MAP_ATTN, h->attn, QD, h->NPAD, h->NTILE, ba);
@@ -464,6 +481,7 @@ static fa_status build_params(fa_handle* h) {
   MAP3(MAP_SVT, h->svt, TPAD, (uint64_t)B * HD, 128, 1);
 #undef MAP3
   p.box_atoms = (int)ba;
+  p.wg = h->wg;
   p.L = L; p.T = h->cfg.horizon; p.B = B; p.NT = h->NT; p.NPAD = h->NPAD; p.NTILE = h->NTILE; p.TG = h->TG;
   p.ngroups = h->ngroups; p.nsteps = h->cfg.num_steps; p.LPAD = h->LPAD; p.AD = h->cfg.action_dim;
   p.split_o = h->split_o; p.split_dn = h->split_dn;
@@ -561,7 +579,7 @@ extern "C" fa_status fa_sample_actions(fa_handle* h, int batch, const float* noi
   const size_t bytes = (size_t)h->NT * h->cfg.action_dim * sizeof(float);
   Params& p = h->params;
   p.stage_ns = h->timing ? h->stage_ns : nullptr;
-  FA_CUDA(h, cudaMemsetAsync(h->ctrl, 0, 2 * sizeof(unsigned int), s));
+  FA_CUDA(h, cudaMemsetAsync(h->ctrl, 0, kCtrlWords * sizeof(unsigned int), s));
   if (h->timing) FA_CUDA(h, cudaMemsetAsync(h->stage_ns, 0, NUM_STAGES * sizeof(unsigned long long), s));
   FA_CUDA(h, cudaMemcpyAsync(h->x_t, noise, bytes, cudaMemcpyDefault, s));
   void* args[] = {&p};
@@ -578,13 +596,19 @@ extern "C" fa_status fa_sync(fa_handle* h, fa_stream stream) {
   FA_CUDA(h, cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
   unsigned int ctrl[2];
   FA_CUDA(h, cudaMemcpy(ctrl, h->ctrl, sizeof(ctrl), cudaMemcpyDeviceToHost));
-  if (ctrl[1] != 0) return fail(h, FA_ERR_TIMEOUT, "in-kernel wait ran out (code %u)", ctrl[1]);
+  if (ctrl[1] != 0)
+    return fail(h, FA_ERR_TIMEOUT, "in-kernel wait ran out (code %u; %u grid-barrier arrivals, %u CTAs)", ctrl[1], ctrl[0],
+                (unsigned)h->num_sms);
   return FA_OK;
 }
 
 // Diagnostics: arm (step >= 0) or read back (step < 0) a clock64 trace of one (step, layer).
 extern "C" fa_status fa_debug_trace(fa_handle* h, int step, int layer, unsigned long long* host_out, int n) {
   if (!h) return FA_ERR_INVALID;
+#ifndef FA_TRACE
+  (void)step; (void)layer; (void)host_out; (void)n;
+  return fail(h, FA_ERR_UNSUPPORTED, "stage tracing is compiled in only by a -DFA_TRACE build");
+#endif
   const size_t need = (size_t)kMaxStages * h->num_sms * kTrStride;
   FA_CUDA(h, cudaSetDevice(h->device));
   if (step < 0) {

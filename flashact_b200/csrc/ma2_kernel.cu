@@ -479,11 +479,12 @@ struct Ma2Model {
       for (int k = 0; k < 16; ++k) dst[(size_t)k * D] = v[k] + bias;
     }
   }
-  __device__ static void epi_copy_out(const Epi& e, const GemmUnit& gu, int m, int nb0) {
+  // Copies staged rows (tokens) [r0, r1) of the 64-token sub-tile at nb0.
+  __device__ static void epi_copy_out(const Epi& e, const GemmUnit& gu, int m, int nb0, int r0, int r1) {
     const int t_ = threadIdx.x - 64;
     if (m == MAT_GU) {  // 64 tokens x 128 B
-      for (int it = t_; it < 64 * 8; it += 128) {
-        const int t = it >> 3, seg = it & 7, n = nb0 + t;
+      for (int it = t_; it < (r1 - r0) * 8; it += 128) {
+        const int t = r0 + (it >> 3), seg = it & 7, n = nb0 + t;
         if (n >= e.NT) continue;
         *reinterpret_cast<uint4*>(e.hbuf + (size_t)n * F + 64 * gu.mtile + seg * 8) =
             *reinterpret_cast<const uint4*>(e.stage + t * 128 + seg * 16);
@@ -491,8 +492,8 @@ struct Ma2Model {
     } else {  // 64 tokens x 256 B into qkv [NPAD][2304] or qc [NPAD][768]
       __nv_bfloat16* out = m == MAT_QKV ? e.qkv : e.qc;
       const int stride = m == MAT_QKV ? QKV_ROWS : D;
-      for (int it = t_; it < 64 * 16; it += 128) {
-        const int t = it >> 4, seg = it & 15, n = nb0 + t;
+      for (int it = t_; it < (r1 - r0) * 16; it += 128) {
+        const int t = r0 + (it >> 4), seg = it & 15, n = nb0 + t;
         if (n >= e.NT) continue;
         *reinterpret_cast<uint4*>(out + (size_t)n * stride + gu.mtile * 128 + seg * 8) =
             *reinterpret_cast<const uint4*>(e.stage + t * 256 + seg * 16);
@@ -540,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     c.batoms = min(kMaxBAtoms, s_plan.b_bytes / (p.NTILE * 128));
     c.ring_slots = s_plan.ring_slots;
     c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    c.work = c.ring + (size_t)c.ring_slots * kAtomBytes;
+    c.work = c.ring + (size_t)c.ring_slots * p.wg * kAtomBytes;
     c.stage = c.work + max(s_plan.b_bytes, kMinWork);
     c.bars = &bars;
     for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], 1); }

@@ -103,7 +103,9 @@ __device__ __noinline__ void stage_norm(const Params& p, const float* gate, int 
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     float v[8];
     load_residual(p, n, gate, nsplit, v);
+    if (n == (int)blockIdx.x && threadIdx.x == 64) trace_mark(9);
     rms_store(p, n, v, mod, red);
+    if (n == (int)blockIdx.x && threadIdx.x == 64) trace_mark(10);
   }
 }
 
@@ -316,12 +318,13 @@ __device__ __forceinline__ void epi_tile(const EpiCtx& p, const GemmUnit& gu, in
   }
 }
 
-// Coalesced copy of a staged 64-token sub-tile to its destination (16-byte stores).
-__device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu, int m, int nb0) {
+// Coalesced copy of staged rows (tokens) [r0, r1) of the 64-token sub-tile at nb0 to their
+// destination (16-byte stores).
+__device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu, int m, int nb0, int r0, int r1) {
   const int e = threadIdx.x - 64;
   if (m == MAT_GU) {  // 64 rows (tokens) x 128 B: 8 threads per row
-    for (int it = e; it < 64 * 8; it += 128) {
-      const int t = it >> 3, seg = it & 7, n = nb0 + t;
+    for (int it = e; it < (r1 - r0) * 8; it += 128) {
+      const int t = r0 + (it >> 3), seg = it & 7, n = nb0 + t;
       if (n >= p.NT) continue;
       const uint4 val = *reinterpret_cast<const uint4*>(p.stage + t * 128 + seg * 16);
       *reinterpret_cast<uint4*>(p.hbuf + (size_t)n * F + 64 * gu.mtile + seg * 8) = val;
@@ -329,8 +332,8 @@ __device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu
   } else {  // Q / K: 64 rows x 256 B, dims [0, 64) -> 64 pb + ..., dims [64, 128) -> 128 + 64 pb + ...
     const int mt = gu.mtile;
     const int pb = mt < 16 ? (mt & 1) : mt - 16;
-    for (int it = e; it < 64 * 16; it += 128) {
-      const int t = it >> 4, seg = it & 15, n = nb0 + t;
+    for (int it = e; it < (r1 - r0) * 16; it += 128) {
+      const int t = r0 + (it >> 4), seg = it & 15, n = nb0 + t;
       if (n >= p.NT) continue;
       const int b = tok_bi(p.invT, n), tt = n - b * p.T;
       const int dim = 64 * pb + (seg & 7) * 8 + (seg >> 3) * 128;
@@ -361,8 +364,8 @@ struct Pi05Model {
                                   const float* v) {
     pi05::epi_tile(e, gu, m, qd, lane, row, nb, nb0, v);
   }
-  __device__ static void epi_copy_out(const Epi& e, const GemmUnit& gu, int m, int nb0) {
-    pi05::epi_copy_out(e, gu, m, nb0);
+  __device__ static void epi_copy_out(const Epi& e, const GemmUnit& gu, int m, int nb0, int r0, int r1) {
+    pi05::epi_copy_out(e, gu, m, nb0, r0, r1);
   }
 };
 
@@ -625,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   c.batoms = min(kMaxBAtoms, s_plan.b_bytes / (p.NTILE * 128));
   c.ring_slots = s_plan.ring_slots;
   c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  c.work = c.ring + (size_t)c.ring_slots * kAtomBytes;
+  c.work = c.ring + (size_t)c.ring_slots * p.wg * kAtomBytes;
   // epilogue staging: the P area on attention CTAs (idle outside the attention stage), else the
   // 16 KB after the activation area
   c.stage = s_plan.a_cnt > 0 ? c.work + kPOff : c.work + s_plan.b_bytes;

@@ -184,7 +184,8 @@ FA_API int fa_last_launch_count(fa_handle* h);
  * fa_sync reports FA_ERR_TIMEOUT; the context stays usable. Reset by fa_bind_prefix_kv. */
 FA_API fa_status fa_set_fault_injection(fa_handle* h, int barrier_index, unsigned int spin_limit);
 
-/* Diagnostics: with step >= 0, arm a trace of one (step, layer) of the following launches;
+/* Diagnostics (builds compiled with -DFA_TRACE; otherwise FA_ERR_UNSUPPORTED): with step >= 0,
+ * arm a trace of one (step, layer) of the following launches;
  * with step < 0, copy n stamps to host_out, laid out [9 stages][num_SMs][16]: per CTA the
  * stage-start clock64, then offsets in cycles (first weight tile ready, activation tiles ready,
  * last MMA committed, first accumulator ready, epilogue done, barrier arrive), the absolute
