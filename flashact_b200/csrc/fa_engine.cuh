@@ -83,9 +83,16 @@ __device__ __noinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned lon
   if (threadIdx.x == 32) {
     trace_mark(kTrBarArrive);
     int ok = 1;
-    __threadfence();
     fence_proxy_async_global();
+#ifdef FA_BAR_FENCE
+    __threadfence();
     if (!(blockIdx.x == 0 && (int)gen == p.inject_barrier)) atomicAdd(p.bar, 1u);
+#else
+    // release-add: orders this CTA's earlier writes (made visible to this thread by the CTA
+    // barrier above) before the arrival, without a separate full fence
+    if (!(blockIdx.x == 0 && (int)gen == p.inject_barrier))
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
+#endif
     const uint32_t target = (gen + 1) * gridDim.x;
     uint32_t i = 0;
     for (;; ++i) {
@@ -96,7 +103,9 @@ __device__ __noinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned lon
       if (i > p.spin_limit) { atomicCAS(p.err, 0, KERR_BARRIER); ok = 0; break; }
       if (i > 64) __nanosleep(32);
     }
+#ifdef FA_BAR_FENCE
     __threadfence();
+#endif
     fence_proxy_async_global();
     s_ok = ok;
 #ifdef FA_TRACE
@@ -187,8 +196,11 @@ __device__ __noinline__ void run_producer(const typename Model::Params& p, const
   for (int m = 0; m < Model::kMats; ++m) { gul[m] = c.gu[m]; gcnt[m] = c.gcnt[m]; }
   uint32_t it = 0;
   bool ok = true;
+#pragma unroll 1
   for (int step = 0; ok && step < nsteps; ++step)
+#pragma unroll 1
     for (int l = 0; ok && l < L; ++l)
+#pragma unroll 1
       for (int m = 0; ok && m < Model::kMats; ++m) {
         const int rows = Model::rows(m);
         for (int u = 0; ok && u < gcnt[m]; ++u) {
@@ -256,7 +268,9 @@ __device__ __forceinline__ void load_b_batch(const MmaCtx& k, const GemmUnit& gu
   const uint64_t pol = policy_evict_last();
   const int y0 = g * k.TG * k.NTILE;
   // tile-major: item (j, i) at work + (i * (j1 - j0) + (j - j0)) * tile; one 3D box = box_atoms atoms
+#pragma unroll 1
   for (int i = 0; i < nt; ++i)
+#pragma unroll 1
     for (int j = j0; j < j1; j += k.box_atoms)
       tma_load_3d(k.work + (size_t)(i * (j1 - j0) + (j - j0)) * tile, k.amap, &k.bars->bfull, 0, y0 + i * k.NTILE,
                   gu.katom0 + j, pol);
@@ -277,8 +291,10 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
   const uint32_t idesc = idesc_bf16(128, k.NTILE);
   const uint32_t tile = k.NTILE * 128;
   Bars* const bars = k.bars;
+  #pragma unroll 1
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
+    #pragma unroll 1
     for (int g = 0; g < k.ngroups; ++g) {
       const int nt = min(k.TG, k.tiles - g * k.TG);
       // K atoms per activation batch: whole activation boxes (the host sizes the area for one)
@@ -293,10 +309,12 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
       if (st.acc >= 2 && !mbar_wait(&bars->acc_empty[a], ((st.acc >> 1) - 1) & 1, k.err, KERR_MMA)) return false;
       tc_fence_after();
       const uint32_t tacc = k.tmem + a * 256;
+      #pragma unroll 1
       for (int j0 = 0; j0 < gu.natoms;) {
         if (!mbar_wait(&bars->bfull, st.bload & 1, k.err, KERR_MMA)) return false;
         ++st.bload;
         if (u == 0 && g == 0 && j0 == 0) FA_ONE(trace_mark(kTrMmaB0));
+        #pragma unroll 1
         for (int j = j0; j < j1; j += k.wg) {  // one ring slot = wg weight atoms
           const int wslot = st.wit % k.R;
           if (!mbar_wait(&bars->wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
@@ -305,8 +323,10 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
           if (u == 0 && g == 0 && j == 8) FA_ONE(trace_mark(10));
           if (u == 0 && g == 0 && j == 12) FA_ONE(trace_mark(11));
           if (leader()) {
+            #pragma unroll 1
             for (int jj = 0; jj < k.wg; ++jj) {
               const uint64_t da = sdesc_sw128(k.ring + ((size_t)wslot * k.wg + jj) * kAtomBytes);
+              #pragma unroll 1
               for (int i = 0; i < nt; ++i) {
                 const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j + jj - j0)) * tile);
 #pragma unroll
