@@ -1,7 +1,11 @@
-"""Benchmark of the pi0.5 flow-matching denoise loop (p50 denoise-loop latency at
-bs=1; action chunks/s at bs=64 across 1-8 B200).
+"""Benchmark of the flow-matching denoise loop (p50 denoise-loop latency at bs=1;
+action chunks/s at bs=64 across 1-8 B200).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--model pi05|molmoact2]
+                  [--impl ours|reference]
+
+Default workload: pi0.5 C1. --model molmoact2 runs C3 (configs[3]: 36 DiT
+blocks, width 768, T=30 with 6 valid action dims, 493 context tokens, 10 steps, seed 1).
 
 One "step" = one call of the public API that runs the whole 10-step x 18-layer Euler loop for
 the rank's batch (fa_sample_actions). Synthetic inputs follow BASELINE.json configs[1]
@@ -31,9 +35,16 @@ L, T, AD, LP, NSTEPS = 18, 50, 32, 968, 10
 W_BYTES_BF16 = 622_854_144            # expert GEMM weights streamed per Euler step (bf16)
 KV_BYTES = 2 * L * LP * 256 * 2       # prefix K+V read per Euler step per observation (bf16)
 GEMM_PARAMS = W_BYTES_BF16 // 2
+# MolmoAct2 C3: 36 blocks x (qkv 2304x768 + 3 x 768x768 + gate/up 2x3072x768 + down 768x3072) bf16
+MA2_L, MA2_T, MA2_LK = 36, 30, 493
+MA2_W_BYTES = MA2_L * (2304 * 768 + 3 * 768 * 768 + 2 * 3072 * 768 + 768 * 3072) * 2  # 764,411,904
+MA2_BIAS_BYTES = MA2_L * (2304 + 3 * 768 + 2 * 3072 + 768) * 4
+MA2_KV_BYTES = 2 * MA2_L * MA2_LK * 768 * 2  # cross-attention K+V per Euler step per observation
 
 
-def algorithmic_bytes(batch):
+def algorithmic_bytes(batch, model="pi05"):
+    if model == "molmoact2":
+        return NSTEPS * (MA2_W_BYTES + MA2_BIAS_BYTES + batch * MA2_KV_BYTES)
     return NSTEPS * (W_BYTES_BF16 + batch * KV_BYTES)
 
 
@@ -125,10 +136,17 @@ def barrier(world):
         dist.barrier()
 
 
-def cpu_sample(case, threads):
+def cpu_sample(case, threads, model="pi05"):
     """Times one Euler step of the CPU oracle (1/N of a chunk) on the host cores."""
-    from oracle import pi05_oracle as O
     torch.set_num_threads(threads)
+    if model == "molmoact2":
+        from oracle import molmoact2_oracle as M
+        one = M.Ma2Case(**{**case.__dict__, "num_steps": 1, "B": 1, "mods": case.mods[:1],
+                           "mod_final": case.mod_final[:1]})
+        t0 = time.perf_counter()
+        M.flow(one, max_obs=1)
+        return time.perf_counter() - t0
+    from oracle import pi05_oracle as O
     mods, mod_final = O.modulations(case.w, case.L, case.num_steps)
     one = O.Pi05Case(**{**case.__dict__, "num_steps": 1, "B": 1})
     t0 = time.perf_counter()
@@ -136,29 +154,46 @@ def cpu_sample(case, threads):
     return time.perf_counter() - t0
 
 
+def make_case(model, seed, B):
+    if model == "molmoact2":
+        from oracle import molmoact2_oracle as M
+        return M.make_case(seed=1 + seed, L=MA2_L, T=MA2_T, Lk=MA2_LK, B=B, num_steps=NSTEPS)
+    from oracle import pi05_oracle as O
+    return O.make_case(seed=seed, L=L, T=T, AD=AD, Lp=LP, B=B, num_steps=NSTEPS)
+
+
+WORKLOAD = {
+    "pi05": "pi0.5 action-expert denoise, BASELINE configs[1] (C1): 18 layers, width 1024, 8q/1kv heads x 256, "
+            "GeGLU 4096, T=50, AD=32, prefix 968, 10 Euler steps",
+    "molmoact2": "MolmoAct2 action-expert flow, BASELINE configs[3] (C3): 36 DiT blocks, width 768, 8 heads x 96, "
+                 "SiLU MLP 3072, T=30 (6 valid action dims), AD=32, cross-attention context 493, 10 Euler steps",
+}
+METRICS = {
+    "pi05": "pi0.5 10-step denoise throughput, action chunks/s (bs per GPU; ms_per_step = mean latency of one chunk batch)",
+    "molmoact2": "MolmoAct2 10-step denoise throughput, action chunks/s (bs per GPU; ms_per_step = mean latency of one chunk batch)",
+}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    from oracle import pi05_oracle as O
     threads = os.cpu_count() or 1
-    case = O.make_case(seed=0, L=L, T=T, AD=AD, Lp=LP, B=1, num_steps=NSTEPS)
+    case = make_case(args.model, 0, 1)
     for _ in range(max(args.warmup, 0)):
-        cpu_sample(case, threads)
-    times = [cpu_sample(case, threads) for _ in range(args.steps)]
+        cpu_sample(case, threads, args.model)
+    times = [cpu_sample(case, threads, args.model) for _ in range(args.steps)]
     step_s = statistics.mean(times)  # one Euler step of one observation
     value = 1.0 / (step_s * NSTEPS)
-    line = {"metric": METRIC, "value": value, "unit": "chunks/s", "impl": "reference", "n_gpus": args.gpus,
+    line = {"metric": METRICS[args.model], "value": value, "unit": "chunks/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000 * NSTEPS,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "pi0.5 action-expert denoise C0 (CPU fp32 restatement of the openpi path)",
-                       "batch_per_rank": 1, "layers": L, "horizon": T, "prefix": LP, "euler_steps": NSTEPS},
+            "config": {"workload": WORKLOAD[args.model] + " (CPU fp32 restatement of the reference path)",
+                       "batch_per_rank": 1},
             "cpu_baseline": {"value": value, "unit": "chunks/s", "cores": threads, "kind": "port",
                              "sample": "each step = 1 of the 10 Euler steps of one bs=1 chunk, scaled x10"},
             "e2e": {"value": value, "unit": "chunks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
-
-METRIC = "pi0.5 10-step denoise throughput, action chunks/s (bs per GPU; ms_per_step = mean latency of one chunk batch)"
 
 
 def main():
@@ -168,6 +203,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1, help="observations per GPU")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="pi05", choices=["pi05", "molmoact2"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":  # host-CPU arm: rank 0 alone works, no process group needed
@@ -175,15 +211,20 @@ def main():
         return
     world, rank, local = dist_setup()
 
-    from flashact_b200 import Pi05ActionExpert
-    from oracle import pi05_oracle as O
+    from flashact_b200 import MolmoAct2ActionExpert, Pi05ActionExpert
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     B = args.batch
-    case = O.make_case(seed=rank, L=L, T=T, AD=AD, Lp=LP, B=B, num_steps=NSTEPS)
-    eng = Pi05ActionExpert(case.w, num_layers=L, horizon=T, action_dim=AD, max_prefix=LP, max_batch=B,
-                           num_steps=NSTEPS, device=local)
-    eng.bind_prefix_kv(case.k.to(torch.bfloat16).to(dev), case.v.to(torch.bfloat16).to(dev), case.valid_len)
+    case = make_case(args.model, rank, B)  # each rank: its own observations (prefix KV / context, noise)
+    if args.model == "molmoact2":
+        eng = MolmoAct2ActionExpert(case.w, case.mods, case.mod_final, num_layers=MA2_L, horizon=MA2_T, action_dim=AD,
+                                    valid_action_dim=case.adim, max_context=MA2_LK, max_batch=B, num_steps=NSTEPS,
+                                    device=local, rope_cos=case.rope_cos, rope_sin=case.rope_sin)
+        eng.bind_context(case.kctx, case.vctx, [MA2_LK] * B)
+    else:
+        eng = Pi05ActionExpert(case.w, num_layers=L, horizon=T, action_dim=AD, max_prefix=LP, max_batch=B,
+                               num_steps=NSTEPS, device=local)
+        eng.bind_prefix_kv(case.k.to(torch.bfloat16).to(dev), case.v.to(torch.bfloat16).to(dev), case.valid_len)
     noise_d = case.noise.to(dev)
     out_d = torch.empty_like(noise_d)
     noise_h = case.noise.clone().pin_memory()
@@ -231,29 +272,29 @@ def main():
     value = world * B * 1000.0 / ms_step
     e2e_value = world * B * 1000.0 / (e2e_ms / args.steps)
     peak, peak_kind = measured_peaks()
-    achieved = algorithmic_bytes(B) / (ms_step * 1e-3) / 1e9
+    achieved = algorithmic_bytes(B, args.model) / (ms_step * 1e-3) / 1e9
     line = {
-        "metric": METRIC, "value": value, "unit": "chunks/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRICS[args.model], "value": value, "unit": "chunks/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "p50_ms": p50, "min_ms": per[0],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) prefix KV and noise)",
-        "config": {"workload": "pi0.5 action-expert denoise, BASELINE configs[1] (C1): 18 layers, width 1024, "
-                               "8q/1kv heads x 256, GeGLU 4096, T=50, AD=32, prefix 968, 10 Euler steps",
+        "config": {"workload": WORKLOAD[args.model],
                    "batch_per_gpu": B, "global_batch": B * world, "parallelism": f"batch shards x{world}",
-                   "l2": "no flush: the 623 MB bf16 weight stream per Euler step exceeds the 126 MB L2"},
+                   "l2": "no flush: the bf16 weight stream per Euler step (623 MB pi0.5, 764 MB MolmoAct2) exceeds "
+                         "the 126 MB L2"},
         "e2e": {"value": e2e_value, "unit": "chunks/s", "h2d_bytes_per_step": int(noise_h.numel() * 4),
                 "d2h_bytes_per_step": int(out_h.numel() * 4)},
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": None,
-                     "algorithmic_bytes_per_launch": algorithmic_bytes(B),
+                     "algorithmic_bytes_per_launch": algorithmic_bytes(B, args.model),
                      "note": "achieved = N x (bf16 weights + B x prefix KV) per launch / mean launch time"},
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        t = cpu_sample(case, threads)
+        t = cpu_sample(case, threads, args.model)
         line["cpu_baseline"] = {"value": 1.0 / (t * NSTEPS), "unit": "chunks/s", "cores": threads, "kind": "port",
                                 "sample": "1 of the 10 Euler steps of one bs=1 chunk (CPU fp32 oracle), scaled x10"}
     if rank == 0:

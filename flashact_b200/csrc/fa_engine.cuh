@@ -181,8 +181,10 @@ template <class Model>
 __device__ __noinline__ void run_producer(const typename Model::Params& p, const Ctx& c) {
   // Every field is read once into registers: the inline-asm memory clobbers would otherwise
   // force a reload through the generic Params/Ctx references after each TMA / mbarrier op.
-  const uint64_t pol = policy_evict_first();
-  const int R = c.ring_slots, nsteps = p.nsteps, L = p.L, ngroups = p.ngroups, wg = p.wg;
+  // bs=1: every weight byte is read once per Euler step (evict first); several token groups
+  // re-read each weight tile shortly after one another (keep it in L2)
+  const uint64_t pol = p.ngroups > 1 ? policy_evict_normal() : policy_evict_first();
+  const int R = c.ring_slots, nsteps = p.nsteps, L = p.L, wg = p.wg;
   const uint32_t slot_bytes = (uint32_t)wg * kAtomBytes;
   uint8_t* const ring = c.ring;
   Bars* const bars = c.bars;
@@ -205,8 +207,8 @@ __device__ __noinline__ void run_producer(const typename Model::Params& p, const
         const int rows = Model::rows(m);
         for (int u = 0; ok && u < gcnt[m]; ++u) {
           const GemmUnit gu = gul[m][u];
-          for (int g = 0; ok && g < ngroups; ++g)
-            for (int j = 0; j < gu.natoms; j += wg, ++it) {
+#pragma unroll 1
+          for (int j = 0; j < gu.natoms; j += wg, ++it) {
               const int slot = it % R, round = it / R;
               if (round > 0 && !mbar_wait(&bars->wempty[slot], (round - 1) & 1, err, KERR_PRODUCER)) {
                 ok = false;
@@ -214,7 +216,7 @@ __device__ __noinline__ void run_producer(const typename Model::Params& p, const
               }
               if (leader()) {
 #ifdef FA_TRACE
-                if (trace && u == 0 && g == 0 && j == 0 && step == tstep && l == tlayer) {
+                if (trace && u == 0 && j == 0 && step == tstep && l == tlayer) {
                   const int stg = Model::trace_stage(m);
                   trace[((size_t)stg * gridDim.x + blockIdx.x) * kTrStride + kTrProdIssue] = clock64();
                 }
@@ -255,7 +257,7 @@ struct MmaCtx {
   int* err;
   const CUtensorMap* amap;
   uint32_t tmem;
-  int R, batoms, NTILE, TG, ngroups, tiles, box_atoms, wg;
+  int R, batoms, NTILE, TG, tiles, box_atoms, wg;
 };
 
 // Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
@@ -282,7 +284,7 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
   MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
   MmaCtx k;
   k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[Model::act_map(m)];
-  k.tmem = c.tmem; k.R = c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG; k.ngroups = p.ngroups;
+  k.tmem = c.tmem; k.R = c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG;
   k.tiles = p.NPAD / p.NTILE;
   k.box_atoms = p.box_atoms;
   k.wg = p.wg;
@@ -294,8 +296,8 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
   #pragma unroll 1
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
-    #pragma unroll 1
-    for (int g = 0; g < k.ngroups; ++g) {
+        {
+      const int g = gu.grp;
       const int nt = min(k.TG, k.tiles - g * k.TG);
       // K atoms per activation batch: whole activation boxes (the host sizes the area for one)
       // (and whole weight slots: both granules are powers of two, so their max is a multiple of each)
@@ -374,7 +376,7 @@ template <class Model>
 __device__ __noinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int row = qd * 32 + lane;
-  const int NTILE = p.NTILE, TG = p.TG, ngroups = p.ngroups, tiles = p.NPAD / p.NTILE;
+  const int NTILE = p.NTILE, TG = p.TG, tiles = p.NPAD / p.NTILE;
   int* const err = p.err;
   Bars* const bars = c.bars;
   const uint32_t taddr = c.tmem + ((uint32_t)(qd * 32) << 16);
@@ -385,7 +387,8 @@ __device__ __noinline__ uint32_t epi_gemm(const typename Model::Params& p, const
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
     const bool staged = Model::staged(m, gu);
-    for (int g = 0; g < ngroups; ++g) {
+    {
+      const int g = gu.grp;
       const int nchunks = min(TG, tiles - g * TG) * NTILE / 16;
       const int a = ecnt & 1;
       if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;

@@ -32,6 +32,7 @@ struct GemmUnit {
   uint16_t katom0;  // first 64-wide K atom
   uint16_t natoms;  // K atoms in this unit
   uint16_t split;   // index of the fp32 partial slice it writes (K-split stages)
+  uint16_t grp;     // token group: token tiles [grp * TG, grp * TG + TG) (one TMEM accumulator)
 };
 struct AttnUnit {
   uint16_t b, hp, chunk, is_suffix;  // observation, head (pair), key chunk, action-token chunk flag

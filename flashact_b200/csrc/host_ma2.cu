@@ -29,6 +29,7 @@ struct Ma2State {
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LKPAD = 0, adim = 0;
   int wg = 4;  // weight atoms per ring slot
   int split[M::NUM_MATS] = {1, 3, 1, 3, 1, 6};
+  int split_eff[M::NUM_MATS] = {1, 3, 1, 3, 1, 6};  // K-splits used for the bound batch
   std::vector<int> ctx;
   bool weights = false, mods_set = false, bound = false;
 };
@@ -242,22 +243,36 @@ static fa_status ma2_plan(fa_handle* h) {
   // weight atoms per ring slot: 64 KB boxes for one token tile, 32 KB otherwise; divides every unit
   s->wg = s->NTILE == 64 ? fa::kMaxWG : 2;
   if (const char* e = getenv("FA_WG")) s->wg = std::max(1, std::min(s->wg, atoi(e)));
+  // K-splits: the configured factor, stepped down to a smaller divisor of the K range while the
+  // stage would hold more than two units per CTA (large batches fill the GPU through their
+  // token groups instead)
+  for (int m = 0; m < M::NUM_MATS; ++m) {
+    int sp = s->split[m];
+    const int katoms = kMatK[m] / 64, mtiles = kMatRows[m] / 128;
+    while (sp > 1 && mtiles * sp * s->ngroups > 2 * nblk) {
+      int d = sp - 1;
+      while (d > 1 && katoms % d != 0) --d;
+      sp = d;
+    }
+    s->split_eff[m] = sp;
+  }
   for (int m = 0; m < M::NUM_MATS; ++m)
-    while ((kMatK[m] / 64 / s->split[m]) % s->wg != 0) s->wg >>= 1;
+    while ((kMatK[m] / 64 / s->split_eff[m]) % s->wg != 0) s->wg >>= 1;
   for (int oi = 0; oi < M::NUM_MATS; ++oi) {
     const int m = order[oi];
-    const int mtiles = kMatRows[m] / 128, katoms = kMatK[m] / 64, split = s->split[m], per_split = katoms / split;
+    const int mtiles = kMatRows[m] / 128, katoms = kMatK[m] / 64, split = s->split_eff[m], per_split = katoms / split;
     std::vector<int> cnt(nblk, 0);
-    for (int mt = 0; mt < mtiles; ++mt)
-      for (int sp = 0; sp < split; ++sp) {
-        int best = 0;
-        for (int i = 1; i < nblk; ++i)
-          if (cnt[i] < cnt[best] || (cnt[i] == cnt[best] && load[i] < load[best])) best = i;
-        per[(size_t)best * M::NUM_MATS + m].push_back(
-            {(uint16_t)mt, (uint16_t)(sp * per_split), (uint16_t)per_split, (uint16_t)sp});
-        cnt[best]++;
-        load[best] += per_split;
-      }
+    for (int g = 0; g < s->ngroups; ++g)
+      for (int mt = 0; mt < mtiles; ++mt)
+        for (int sp = 0; sp < split; ++sp) {
+          int best = 0;
+          for (int i = 1; i < nblk; ++i)
+            if (cnt[i] < cnt[best] || (cnt[i] == cnt[best] && load[i] < load[best])) best = i;
+          per[(size_t)best * M::NUM_MATS + m].push_back(
+              {(uint16_t)mt, (uint16_t)(sp * per_split), (uint16_t)per_split, (uint16_t)sp, (uint16_t)g});
+          cnt[best]++;
+          load[best] += per_split * std::min(s->TG, s->NPAD / s->NTILE - g * s->TG);
+        }
   }
   std::vector<GemmUnit> gu;
   const int tile = s->NTILE * 128;
@@ -318,7 +333,7 @@ static fa_status ma2_params(fa_handle* h) {
   p.wg = s->wg;
   p.L = L; p.T = h->cfg.horizon; p.B = s->B; p.NT = s->NT; p.NPAD = s->NPAD; p.NTILE = s->NTILE; p.TG = s->TG;
   p.ngroups = s->ngroups; p.nsteps = h->cfg.num_steps; p.AD = h->cfg.action_dim; p.adim = s->adim; p.LKPAD = s->LKPAD;
-  for (int m = 0; m < M::NUM_MATS; ++m) p.split[m] = s->split[m];
+  for (int m = 0; m < M::NUM_MATS; ++m) p.split[m] = s->split_eff[m];
   p.dt = 1.0f / (float)h->cfg.num_steps;
   p.invT = 1.0f / (float)h->cfg.horizon;
   p.gunits = s->d_gunits; p.aunits = s->d_aunits; p.plans = s->d_plans; p.ctx_len = s->d_ctx;

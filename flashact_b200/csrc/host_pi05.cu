@@ -387,8 +387,16 @@ static fa_status build_plan(fa_handle* h) {
     plans[i].a_cnt = hi - lo;
     load[i] = (long)plans[i].a_cnt * h->attn_penalty;
   }
+  // K-splits of O and down: the configured factor, halved while the stage would hold more than
+  // two units per CTA (large batches fill the GPU through their token groups instead).
+  auto eff_split = [&](int mtiles, int split) {
+    while (split > 1 && mtiles * split * h->ngroups > 2 * nblk) split >>= 1;
+    return split;
+  };
+  h->split_o_eff = eff_split(8, h->split_o);
+  h->split_dn_eff = eff_split(8, h->split_dn);
   struct Spec { int mtiles, katoms, split; };
-  const Spec spec[4] = {{20, D / 64, 1}, {8, QD / 64, h->split_o}, {64, D / 64, 1}, {8, F / 64, h->split_dn}};
+  const Spec spec[4] = {{20, D / 64, 1}, {8, QD / 64, h->split_o_eff}, {64, D / 64, 1}, {8, F / 64, h->split_dn_eff}};
   // Weight atoms per ring slot: 64 KB boxes when one token tile is in flight, 32 KB otherwise
   // (keeps an attention CTA's activation batch, which must hold whole slots, inside 64 KB); never
   // more than divides every unit's K range.
@@ -403,15 +411,17 @@ static fa_status build_plan(fa_handle* h) {
     const Spec& s = spec[m];
     const int per_split = s.katoms / s.split;
     std::vector<int> cnt(nblk, 0);
-    for (int mt = 0; mt < s.mtiles; ++mt)
-      for (int sp = 0; sp < s.split; ++sp) {
-        int best = 0;
-        for (int i = 1; i < nblk; ++i)
-          if (cnt[i] < cnt[best] || (cnt[i] == cnt[best] && load[i] < load[best])) best = i;
-        per[best * 4 + m].push_back({(uint16_t)mt, (uint16_t)(sp * per_split), (uint16_t)per_split, (uint16_t)sp});
-        cnt[best]++;
-        load[best] += per_split;
-      }
+    for (int g = 0; g < h->ngroups; ++g)
+      for (int mt = 0; mt < s.mtiles; ++mt)
+        for (int sp = 0; sp < s.split; ++sp) {
+          int best = 0;
+          for (int i = 1; i < nblk; ++i)
+            if (cnt[i] < cnt[best] || (cnt[i] == cnt[best] && load[i] < load[best])) best = i;
+          per[best * 4 + m].push_back(
+              {(uint16_t)mt, (uint16_t)(sp * per_split), (uint16_t)per_split, (uint16_t)sp, (uint16_t)g});
+          cnt[best]++;
+          load[best] += per_split * std::min(h->TG, h->NPAD / h->NTILE - g * h->TG);
+        }
   }
   std::vector<GemmUnit> gu;
   const int tile = h->NTILE * 128;
@@ -484,7 +494,7 @@ static fa_status build_params(fa_handle* h) {
   p.wg = h->wg;
   p.L = L; p.T = h->cfg.horizon; p.B = B; p.NT = h->NT; p.NPAD = h->NPAD; p.NTILE = h->NTILE; p.TG = h->TG;
   p.ngroups = h->ngroups; p.nsteps = h->cfg.num_steps; p.LPAD = h->LPAD; p.AD = h->cfg.action_dim;
-  p.split_o = h->split_o; p.split_dn = h->split_dn;
+  p.split_o = h->split_o_eff; p.split_dn = h->split_dn_eff;
   p.dt = -1.0f / (float)h->cfg.num_steps;
   p.invT = 1.0f / (float)h->cfg.horizon;
   p.gunits = h->d_gunits; p.aunits = h->d_aunits; p.plans = h->d_plans;

@@ -74,6 +74,12 @@ class MolmoAct2ActionExpert:
             self._check(self.lib.fa_sync(self.h, _stream_ptr(stream)))
         return out
 
+    def sync(self, stream=None):
+        self._check(self.lib.fa_sync(self.h, _stream_ptr(stream)))
+
+    def launch_count(self) -> int:
+        return int(self.lib.fa_last_launch_count(self.h))
+
     def set_stage_timing(self, enable=True):
         self._check(self.lib.fa_set_stage_timing(self.h, int(enable)))
 
