@@ -117,7 +117,9 @@ def dist_setup():
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
-        dist.init_process_group(backend=backend)
+            dist.init_process_group(backend=backend, device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group(backend=backend)
     return world, rank, local
 
 
@@ -162,6 +164,19 @@ def make_case(model, seed, B):
     return O.make_case(seed=seed, L=L, T=T, AD=AD, Lp=LP, B=B, num_steps=NSTEPS)
 
 
+def shard_case(model, case, lo, hi):
+    """Observations [lo, hi) of a seeded global case (weights shared)."""
+    import copy
+    sub = copy.copy(case)
+    sub.B = hi - lo
+    sub.noise = case.noise[lo:hi]
+    if model == "molmoact2":
+        sub.kctx, sub.vctx = case.kctx[lo:hi], case.vctx[lo:hi]
+    else:
+        sub.k, sub.v, sub.valid_len = case.k[lo:hi], case.v[lo:hi], case.valid_len[lo:hi]
+    return sub
+
+
 WORKLOAD = {
     "pi05": "pi0.5 action-expert denoise, BASELINE configs[1] (C1): 18 layers, width 1024, 8q/1kv heads x 256, "
             "GeGLU 4096, T=50, AD=32, prefix 968, 10 Euler steps",
@@ -201,7 +216,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=1, help="observations per GPU")
+    ap.add_argument("--batch", type=int, default=1, help="observations per GPU (weak scaling)")
+    ap.add_argument("--global-batch", type=int, default=0,
+                    help="observations in total, sharded across the GPUs (strong scaling; BASELINE C2 = 64)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="pi05", choices=["pi05", "molmoact2"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -214,8 +231,15 @@ def main():
     from flashact_b200 import MolmoAct2ActionExpert, Pi05ActionExpert
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    B = args.batch
-    case = make_case(args.model, rank, B)  # each rank: its own observations (prefix KV / context, noise)
+    if args.global_batch > 0:  # one global batch, contiguous shards (flashact_b200.sharding)
+        from flashact_b200.sharding import shard_range
+        lo, hi = shard_range(args.global_batch, world, rank)
+        B = hi - lo
+        full = make_case(args.model, 0, args.global_batch)
+        case = shard_case(args.model, full, lo, hi)
+    else:
+        B = args.batch
+        case = make_case(args.model, rank, B)  # each rank: its own observations (prefix KV / context, noise)
     if args.model == "molmoact2":
         eng = MolmoAct2ActionExpert(case.w, case.mods, case.mod_final, num_layers=MA2_L, horizon=MA2_T, action_dim=AD,
                                     valid_action_dim=case.adim, max_context=MA2_LK, max_batch=B, num_steps=NSTEPS,
@@ -269,17 +293,22 @@ def main():
     barrier(world)
 
     ms_step = total_ms / args.steps
-    value = world * B * 1000.0 / ms_step
-    e2e_value = world * B * 1000.0 / (e2e_ms / args.steps)
+    total_batch = args.global_batch if args.global_batch > 0 else world * B
+    value = total_batch * 1000.0 / ms_step
+    e2e_value = total_batch * 1000.0 / (e2e_ms / args.steps)
+    if world > 1 and args.global_batch > 0:  # the one data exchange: gather the action chunks (untimed)
+        from flashact_b200.sharding import gather_actions
+        gathered = gather_actions(out_d, args.global_batch)
+        assert gathered.shape[0] == args.global_batch
     peak, peak_kind = measured_peaks()
     achieved = algorithmic_bytes(B, args.model) / (ms_step * 1e-3) / 1e9
     line = {
         "metric": METRICS[args.model], "value": value, "unit": "chunks/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "p50_ms": p50, "min_ms": per[0],
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) prefix KV and noise)",
+        "higher_is_better": True, "scaling": "strong" if args.global_batch > 0 else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) prefix KV and noise)",
         "config": {"workload": WORKLOAD[args.model],
-                   "batch_per_gpu": B, "global_batch": B * world, "parallelism": f"batch shards x{world}",
+                   "batch_per_gpu": B, "global_batch": total_batch, "parallelism": f"batch shards x{world}",
                    "l2": "no flush: the bf16 weight stream per Euler step (623 MB pi0.5, 764 MB MolmoAct2) exceeds "
                          "the 126 MB L2"},
         "e2e": {"value": e2e_value, "unit": "chunks/s", "h2d_bytes_per_step": int(noise_h.numel() * 4),
