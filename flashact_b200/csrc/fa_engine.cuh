@@ -77,7 +77,7 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 // counter only grows, so barrier k completes when it reaches (k+1) * gridDim.x. Bounded: on
 // timeout (or when another CTA already failed) it raises *err and returns false.
 template <class P>
-__device__ __noinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned long long* next_tr) {
+__device__ __forceinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned long long* next_tr) {
   __shared__ int s_ok;
   sync_main();
   if (threadIdx.x == 32) {
@@ -178,7 +178,7 @@ __device__ __forceinline__ int group_tiles(const P& p, int g) {
 // Walks (step, layer, GEMM matrix, unit, token group, K-atom group) — the exact order the MMA
 // lane consumes — and keeps the ring full. It never waits on activations.
 template <class Model>
-__device__ __noinline__ void run_producer(const typename Model::Params& p, const Ctx& c) {
+__device__ __forceinline__ void run_producer(const typename Model::Params& p, const Ctx& c) {
   // Every field is read once into registers: the inline-asm memory clobbers would otherwise
   // force a reload through the generic Params/Ctx references after each TMA / mbarrier op.
   // bs=1: every weight byte is read once per Euler step (evict first); several token groups
@@ -279,7 +279,7 @@ __device__ __forceinline__ void load_b_batch(const MmaCtx& k, const GemmUnit& gu
 }
 
 template <class Model>
-__device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
+__device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
   FA_ONE(trace_mark(12));
   MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
   MmaCtx k;
@@ -373,7 +373,7 @@ __device__ __noinline__ bool mma_gemm(const typename Model::Params& p, const Ctx
 // slower than full-K tiles at bs=1: its extra dependent L2 round trips outweigh the shorter MMA
 // chains.)
 template <class Model>
-__device__ __noinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l) {
+__device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int row = qd * 32 + lane;
   const int NTILE = p.NTILE, TG = p.TG, tiles = p.NPAD / p.NTILE;

@@ -82,7 +82,7 @@ __device__ __forceinline__ void row_rms_store(const Params& p, int n, const floa
 }
 
 // x += gate * sum_s part[s] (partials already carry the bias), xn = adaRMS(x; mod).
-__device__ __noinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
+__device__ __forceinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     float v[6];
     row_load_residual(p, n, gate, nsplit, v);
@@ -173,7 +173,7 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& raw, float* dst) {
   }
 }
 
-__device__ __noinline__ void stage_self_attn(const Params& p, float* sm) {
+__device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   const int T = p.T;
   const int ngroups = (T + kSelfQ - 1) / kSelfQ;
@@ -261,7 +261,7 @@ __device__ __noinline__ void stage_self_attn(const Params& p, float* sm) {
 // Unit = (observation b, head h, context chunk c of 128 keys). q = RMS-normalised cross query
 // of head h (mk_ma2.cu:398-422); scores over the chunk's valid keys, scale 1/sqrt(96); the
 // chunk's normalised output and (max, sum) go to opart / oml for stage_merge.
-__device__ __noinline__ void stage_cross_attn(const Params& p, const Ctx& c, int l, float* sm) {
+__device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, int l, float* sm) {
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   const int T = p.T;
   float* qs = sm;                                                  // [32][96], pre-scaled
@@ -392,7 +392,7 @@ __device__ __noinline__ void stage_cross_attn(const Params& p, const Ctx& c, int
 
 // Merge of the context chunks per (token, head): out = sum_c w_c O_c / sum_c w_c,
 // w_c = 2^(m_c - M) l_c. One warp per (token, head); lane c holds chunk c's (max, sum).
-__device__ __noinline__ void stage_merge(const Params& p) {
+__device__ __forceinline__ void stage_merge(const Params& p) {
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   for (int item = blockIdx.x * 4 + wq; item < p.NT * H; item += gridDim.x * 4) {
     const int n = item / H, h = item % H;
@@ -588,56 +588,54 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     if (is_epi) stage_embed(p, s_xt, s_red);
     ok = grid_barrier(p, gen++, tr(ST_QKV, 0, 0));
     mark(ST_NORM1);
-    auto gemm = [&](int m, int l) {
-      if (is_mma) mma_gemm<Ma2Model>(p, c, st, m);
-      if (is_epi) ecnt = epi_gemm<Ma2Model>(p, c, ecnt, m, l);
+    // One pass of the loop body per stage; every role function has ONE call site (inlined, no
+    // ABI calls between stages). Stage order per block: QKV, self-attention, self-out, norm(mca),
+    // cross-q, cross-attention, merge, cross-out, norm(mlp), gate/up, down, norm1 | final.
+    // (selects instead of arrays: a runtime-indexed array would live in local memory)
+    auto gemm_of = [](int s) {
+      return s == 0 ? MAT_QKV : s == 2 ? MAT_SO : s == 4 ? MAT_CQ : s == 7 ? MAT_CO : s == 9 ? MAT_GU
+           : s == 10 ? MAT_DN : -1;
     };
+    auto timed = [](int s) {
+      return s == 0 ? ST_QKV : s == 1 ? ST_SELF : s == 2 ? ST_SO : s == 3 ? ST_NORM2 : s == 4 ? ST_CQ
+           : s == 5 ? ST_CROSS : s == 6 ? ST_MERGE : s == 7 ? ST_CO : s == 8 ? ST_NORM3 : s == 9 ? ST_GU
+           : s == 10 ? ST_DN : ST_NORM1;
+    };
+#pragma unroll 1
     for (int step = 0; ok && step < p.nsteps; ++step) {
+#pragma unroll 1
       for (int l = 0; ok && l < p.L; ++l) {
         const float* m_self = mod_ptr(p, step, l, 0);
         const float* m_cross = mod_ptr(p, step, l, 1);
         const float* m_mlp = mod_ptr(p, step, l, 2);
-        gemm(MAT_QKV, l);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_SELF, step, l)))) break;
-        mark(ST_QKV);
-        if (is_epi) stage_self_attn(p, vsm);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_SO, step, l)))) break;
-        mark(ST_SELF);
-        gemm(MAT_SO, l);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_NORM2, step, l)))) break;
-        mark(ST_SO);
-        if (is_epi) stage_norm(p, m_self + 2 * D, p.split[MAT_SO], m_cross, s_red);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_CQ, step, l)))) break;
-        mark(ST_NORM2);
-        gemm(MAT_CQ, l);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_CROSS, step, l)))) break;
-        mark(ST_CQ);
-        if (is_epi) stage_cross_attn(p, c, l, vsm);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_MERGE, step, l)))) break;
-        mark(ST_CROSS);
-        if (is_epi) stage_merge(p);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_CO, step, l)))) break;
-        mark(ST_MERGE);
-        gemm(MAT_CO, l);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_NORM3, step, l)))) break;
-        mark(ST_CO);
-        if (is_epi) stage_norm(p, m_cross + 2 * D, p.split[MAT_CO], m_mlp, s_red);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_GU, step, l)))) break;
-        mark(ST_NORM3);
-        gemm(MAT_GU, l);
-        if (!(ok = grid_barrier(p, gen++, tr(ST_DN, step, l)))) break;
-        mark(ST_GU);
-        gemm(MAT_DN, l);
-        if (!(ok = grid_barrier(p, gen++, tr(l + 1 < p.L ? ST_NORM1 : ST_FINAL, step, l)))) break;
-        mark(ST_DN);
-        if (l + 1 < p.L) {
-          if (is_epi) stage_norm(p, m_mlp + 2 * D, p.split[MAT_DN], mod_ptr(p, step, l + 1, 0), s_red);
-          if (!(ok = grid_barrier(p, gen++, tr(ST_QKV, step, l + 1)))) break;
-          mark(ST_NORM1);
-        } else {
-          if (is_epi) stage_final(p, step, vsm, s_xt, s_red);
-          if (!(ok = grid_barrier(p, gen++, tr(ST_QKV, step + 1, 0)))) break;
-          mark(ST_FINAL);
+        const bool last_layer = l + 1 == p.L;
+#pragma unroll 1
+        for (int s = 0; s < 12; ++s) {
+          const int m = gemm_of(s);
+          if (m >= 0) {
+            if (is_mma) mma_gemm<Ma2Model>(p, c, st, m);
+            if (is_epi) ecnt = epi_gemm<Ma2Model>(p, c, ecnt, m, l);
+          } else if (s == 1) {
+            if (is_epi) stage_self_attn(p, vsm);
+          } else if (s == 5) {
+            if (is_epi) stage_cross_attn(p, c, l, vsm);
+          } else if (s == 6) {
+            if (is_epi) stage_merge(p);
+          } else if (s == 3 || s == 8 || !last_layer) {  // norm(mca) | norm(mlp) | next block's norm(msa)
+            if (is_epi) {
+              const float* gate = (s == 3 ? m_self : s == 8 ? m_cross : m_mlp) + 2 * D;
+              const int ns = p.split[s == 3 ? MAT_SO : s == 8 ? MAT_CO : MAT_DN];
+              const float* mod = s == 3 ? m_cross : s == 8 ? m_mlp : mod_ptr(p, step, l + 1, 0);
+              stage_norm(p, gate, ns, mod, s_red);
+            }
+          } else if (is_epi) {
+            stage_final(p, step, vsm, s_xt, s_red);
+          }
+          const int nxt = s < 11 ? timed(s + 1) : ST_QKV;
+          const int nstep = s < 11 ? step : (last_layer ? step + 1 : step);
+          const int nl = s < 11 ? l : (last_layer ? 0 : l + 1);
+          if (!(ok = grid_barrier(p, gen++, tr(nxt == ST_NORM1 && last_layer ? ST_FINAL : nxt, nstep, nl)))) break;
+          mark(s == 11 && last_layer ? ST_FINAL : timed(s));
         }
       }
     }

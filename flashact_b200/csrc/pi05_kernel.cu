@@ -99,7 +99,7 @@ __device__ __forceinline__ const float* mod_ptr(const Params& p, int step, int l
 }
 
 // norm stage: x += gate * sum(partials); xn = adaRMS(x; mod). One token per CTA iteration.
-__device__ __noinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
+__device__ __forceinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     float v[8];
     load_residual(p, n, gate, nsplit, v);
@@ -181,7 +181,7 @@ __device__ __noinline__ void stage_final(const Params& p, int step, float* xf, f
 // Merge the per-chunk attention partials (flash-decoding combine): for each (token, head),
 // out = sum_c w_c O_c / sum_c w_c with w_c = 2^(m_c - M) l_c (maxima kept in log2 units).
 // One warp per (token, head); lane c reads chunk c's (max, sum), lanes own 8 dims each.
-__device__ __noinline__ void stage_merge(const Params& p) {
+__device__ __forceinline__ void stage_merge(const Params& p) {
   // register copies: the asm memory clobbers would force reloads through the references
   const int p_NT = p.NT;
   const int p_T = p.T;
@@ -377,7 +377,7 @@ struct Pi05Model {
 // (TMEM cols 128..383) -> normalised partial + (max, sum) to global, merged by stage_merge.
 constexpr int kQOff = 0, kKVOff = 64 * 1024, kPOff = 128 * 1024;
 
-__device__ __noinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& st_shared, int l, bool last) {
+__device__ __forceinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState& st_shared, int l, bool last) {
   // register copies: the asm memory clobbers would force reloads through the references
   const int c_acnt = c.acnt;
   const AttnUnit* const c_au = c.au;
@@ -522,7 +522,7 @@ __device__ __forceinline__ float2 softmax_row(uint32_t taddr, int nvalid, uint8_
 
 constexpr int kOPitch = HD * 2 + 16;  // staged bf16 output row, padded against bank conflicts
 
-__device__ __noinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint32_t anu) {
+__device__ __forceinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint32_t anu) {
   // register copies: the asm memory clobbers would force reloads through the references
   const int nunits = c.acnt;
   const AttnUnit* const units = c.au;
@@ -686,55 +686,54 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
     if (is_epi) stage_embed(p, s_xt, s_red);
     ok = grid_barrier(p, gen++, tr(ST_QKV, 0, 0));
     mark(ST_NORM1);
+    // One pass of the loop body per stage, each role function reached from ONE call site so
+    // that it is inlined: no ABI calls (and no register save / restore through local memory,
+    // which misses the small L1 beside 224 KB of shared memory) between stages.
+    // Stage order per layer: QKV, attention, merge, O, norm2, gate/up, down, norm1 | final.
+    // (selects instead of arrays: a runtime-indexed array would live in local memory)
+    auto gemm_of = [](int s) { return s == 0 ? MAT_QKV : s == 3 ? MAT_O : s == 5 ? MAT_GU : s == 6 ? MAT_DN : -1; };
+    auto timed = [](int s) {
+      return s == 0 ? ST_QKV : s == 1 ? ST_ATTN : s == 2 ? ST_MERGE : s == 3 ? ST_O : s == 4 ? ST_NORM2
+           : s == 5 ? ST_GU : s == 6 ? ST_DN : ST_NORM1;
+    };
+#pragma unroll 1
     for (int step = 0; ok && step < p.nsteps; ++step) {
+#pragma unroll 1
       for (int l = 0; ok && l < p.L; ++l) {
         const float* mod_in = mod_ptr(p, step, l, 0);
         const float* mod_post = mod_ptr(p, step, l, 1);
-        if (is_mma) mma_gemm<Pi05Model>(p, c, st, MAT_QKV);
-        if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, MAT_QKV, l);
-        epi_done();
-        if (!(ok = grid_barrier(p, gen++, tr(ST_ATTN, step, l)))) break;
-        mark(ST_QKV);
-        if (is_mma && leader()) st.last_q = -1;
-        __syncwarp();
-        if (is_mma) mma_attn(p, c, st, l, step + 1 == p.nsteps && l + 1 == p.L);
-        if (is_epi) anu = epi_attn(p, c, anu);
-        epi_done();
-        if (!(ok = grid_barrier(p, gen++, tr(ST_MERGE, step, l)))) break;
-        mark(ST_ATTN);
-        if (is_epi) stage_merge(p);
-        epi_done();
-        if (!(ok = grid_barrier(p, gen++, tr(ST_O, step, l)))) break;
-        mark(ST_MERGE);
-        if (is_mma) mma_gemm<Pi05Model>(p, c, st, MAT_O);
-        if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, MAT_O, l);
-        epi_done();
-        if (!(ok = grid_barrier(p, gen++, tr(ST_NORM2, step, l)))) break;
-        mark(ST_O);
-        if (is_epi) stage_norm(p, mod_in + 2 * D, p.split_o, mod_post, s_red);
-        epi_done();
-        if (!(ok = grid_barrier(p, gen++, tr(ST_GU, step, l)))) break;
-        mark(ST_NORM2);
-        if (is_mma) mma_gemm<Pi05Model>(p, c, st, MAT_GU);
-        if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, MAT_GU, l);
-        epi_done();
-        if (!(ok = grid_barrier(p, gen++, tr(ST_DN, step, l)))) break;
-        mark(ST_GU);
-        if (is_mma) mma_gemm<Pi05Model>(p, c, st, MAT_DN);
-        if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, MAT_DN, l);
-        epi_done();
-        if (!(ok = grid_barrier(p, gen++, tr(l + 1 < p.L ? ST_NORM1 : ST_FINAL, step, l)))) break;
-        mark(ST_DN);
-        if (l + 1 < p.L) {
-          if (is_epi) stage_norm(p, mod_post + 2 * D, p.split_dn, mod_ptr(p, step, l + 1, 0), s_red);
+        const bool last_layer = l + 1 == p.L;
+#pragma unroll 1
+        for (int s = 0; s < 8; ++s) {
+          const int m = gemm_of(s);
+          if (m >= 0) {
+            if (is_mma) mma_gemm<Pi05Model>(p, c, st, m);
+            if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, m, l);
+          } else if (s == 1) {
+            if (is_mma) {
+              if (leader()) st.last_q = -1;
+              __syncwarp();
+              mma_attn(p, c, st, l, step + 1 == p.nsteps && last_layer);
+            }
+            if (is_epi) anu = epi_attn(p, c, anu);
+          } else if (s == 2) {
+            if (is_epi) stage_merge(p);
+          } else if (s == 4 || !last_layer) {  // norm2 | norm1 of the next layer
+            if (is_epi) {
+              const bool n2 = s == 4;
+              stage_norm(p, (n2 ? mod_in : mod_post) + 2 * D, n2 ? p.split_o : p.split_dn,
+                         n2 ? mod_post : mod_ptr(p, step, l + 1, 0), s_red);
+            }
+          } else if (is_epi) {
+            stage_final(p, step, reinterpret_cast<float*>(c.work), s_xt, s_red);  // work area idle here
+          }
           epi_done();
-          if (!(ok = grid_barrier(p, gen++, tr(ST_QKV, step, l + 1)))) break;
-          mark(ST_NORM1);
-        } else {
-          if (is_epi) stage_final(p, step, reinterpret_cast<float*>(c.work), s_xt, s_red);  // work area idle here
-          epi_done();
-          if (!(ok = grid_barrier(p, gen++, tr(ST_QKV, step + 1, 0)))) break;
-          mark(ST_FINAL);
+          // trace / timing ids: the stage that starts after this barrier, the stage that ended
+          const int nxt = s < 7 ? timed(s + 1) : ST_QKV;
+          const int nstep = s < 7 ? step : (last_layer ? step + 1 : step);
+          const int nl = s < 7 ? l : (last_layer ? 0 : l + 1);
+          if (!(ok = grid_barrier(p, gen++, tr(nxt == ST_NORM1 && last_layer ? ST_FINAL : nxt, nstep, nl)))) break;
+          mark(s == 7 && last_layer ? ST_FINAL : timed(s));
         }
       }
     }
