@@ -13,7 +13,7 @@ FA_DT_F32, FA_DT_BF16, FA_DT_F16 = 0, 1, 2
 FA_KV_COMPACT_SPLIT_HALF, FA_KV_FLASHRT_INTERLEAVED = 0, 1
 
 # Every function the header declares (checked by tests/test_capi.py against include/flashact.h).
-EXPORTS = ["fa_create", "fa_pi05_load_weights", "fa_ma2_load_weights", "fa_ma2_set_rope", "fa_set_modulation", "fa_bind_prefix_kv", "fa_sample_actions",
+EXPORTS = ["fa_create", "fa_pi05_load_weights", "fa_ma2_load_weights", "fa_ma2_set_rope", "fa_set_modulation", "fa_bind_prefix_kv", "fa_bind_prefix_kv_masked", "fa_sample_actions",
            "fa_sync", "fa_set_stage_timing", "fa_get_stage_cycles", "fa_last_launch_count",
            "fa_set_fault_injection", "fa_debug_trace", "fa_pi05_modulations_noalloc", "fa_last_error", "fa_destroy"]
 
@@ -72,6 +72,7 @@ def load_library(path: str = None) -> ctypes.CDLL:
         "fa_ma2_set_rope": (S, [H, P, P]),
         "fa_set_modulation": (S, [H, P, P]),
         "fa_bind_prefix_kv": (S, [H, I, P, P, I, ctypes.POINTER(ctypes.c_int), I, P]),
+        "fa_bind_prefix_kv_masked": (S, [H, I, P, P, I, P, I, P]),
         "fa_sample_actions": (S, [H, I, P, P, P]),
         "fa_sync": (S, [H, P]),
         "fa_set_stage_timing": (S, [H, I]),

@@ -54,6 +54,9 @@ struct fa_handle {
   float *rope_cos = nullptr, *rope_sin = nullptr;
   int *d_valid = nullptr, *d_nchunks = nullptr;
   unsigned int* ctrl = nullptr;  // [0] barrier counter, [1] error word
+  int* d_rowmap = nullptr;       // masked binds: [batch][src_rows] source row of each kept row
+  int* d_counts = nullptr;       // masked binds: kept rows per observation
+  size_t rowmap_cap = 0;
   unsigned long long* stage_ns = nullptr;
   GemmUnit* d_gunits = nullptr;
   AttnUnit* d_aunits = nullptr;
@@ -92,6 +95,72 @@ static fa_status dalloc(fa_handle* h, T** out, size_t count) {
   if (e != cudaSuccess) return fail(h, FA_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(e));
   h->allocs.push_back(p);
   *out = reinterpret_cast<T*>(p);
+  return FA_OK;
+}
+
+// Masked binds: for each observation b (one block each), the source rows whose keep flag is set,
+// in order: rowmap[b][i] = i-th kept row, counts[b] = number kept (the reference's
+// compact_kv / `kv[0][mask]` gather, src/pi05/pack_weights.py:60-70,
+// benchmarks/molmoact2/eval_e2e.py:108-125, done on the device).
+static __global__ void rowmap_kernel(const unsigned char* keep, int src_rows, int* rowmap, int* counts) {
+  __shared__ int warp_tot[32];
+  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5, nt = blockDim.x;
+  const int per = (src_rows + nt - 1) / nt, r0 = t * per, r1 = min(src_rows, r0 + per);
+  const unsigned char* kb = keep + (size_t)b * src_rows;
+  int mine = 0;
+  for (int r = r0; r < r1; ++r) mine += kb[r] != 0;
+  int incl = mine;  // inclusive scan over the block
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int v = lane < nt / 32 ? warp_tot[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    warp_tot[lane] = v;  // inclusive prefix of warp totals
+  }
+  __syncthreads();
+  int pos = incl - mine + (w > 0 ? warp_tot[w - 1] : 0);
+  for (int r = r0; r < r1; ++r)
+    if (kb[r]) rowmap[(size_t)b * src_rows + pos++] = r;
+  if (t == nt - 1) counts[b] = pos;
+}
+
+
+// Builds the row map of a masked bind on `stream` (into the handle's reusable buffers) and
+// returns the kept-row counts on the host (the bind plans its attention work from them).
+static fa_status masked_rows(fa_handle* h, int batch, int src_rows, const unsigned char* keep, cudaStream_t stream,
+                             std::vector<int>& counts) {
+  if (!keep || batch < 1 || src_rows < 1) return fail(h, FA_ERR_INVALID, "masked bind: bad mask arguments");
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, keep) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+    cudaGetLastError();
+    return fail(h, FA_ERR_INVALID, "masked bind: the keep mask must be device memory");
+  }
+  const size_t need = (size_t)batch * src_rows;
+  if (need > h->rowmap_cap) {
+    int *rm = nullptr, *ct = nullptr;
+    if (cudaMalloc(&rm, need * sizeof(int)) != cudaSuccess) return fail(h, FA_ERR_OOM, "masked bind: row map");
+    if (cudaMalloc(&ct, (size_t)batch * sizeof(int) + 16) != cudaSuccess) {
+      cudaFree(rm);
+      return fail(h, FA_ERR_OOM, "masked bind: counts");
+    }
+    h->allocs.push_back(rm);
+    h->allocs.push_back(ct);
+    h->d_rowmap = rm;
+    h->d_counts = ct;
+    h->rowmap_cap = need;
+  }
+  rowmap_kernel<<<batch, 1024, 0, stream>>>(keep, src_rows, h->d_rowmap, h->d_counts);
+  FA_CUDA(h, cudaGetLastError());
+  counts.resize(batch);
+  FA_CUDA(h, cudaMemcpyAsync(counts.data(), h->d_counts, batch * sizeof(int), cudaMemcpyDeviceToHost, stream));
+  FA_CUDA(h, cudaStreamSynchronize(stream));
   return FA_OK;
 }
 
@@ -212,7 +281,7 @@ static fa_status pack_matrix(fa_handle* h, const std::vector<int2>& rowmap, Pack
 // MolmoAct2 engine (host_ma2.cu), reached through the C ABI's model dispatch.
 fa_status ma2_create(const fa_config& cfg, int device, fa_handle* h);
 fa_status ma2_bind(fa_handle* h, int batch, const void* k, const void* v, int src_rows, const int* valid_len,
-                   cudaStream_t s);
+                   cudaStream_t s, const int* rowmap);
 fa_status ma2_sample(fa_handle* h, int batch, const float* noise, float* out, cudaStream_t s);
 fa_status ma2_set_modulation(fa_handle* h, const float* mods, const float* mod_final);
 void ma2_set_debug(fa_handle* h);

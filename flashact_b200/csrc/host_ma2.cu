@@ -37,15 +37,18 @@ struct Ma2State {
 static constexpr int kMatRows[M::NUM_MATS] = {M::QKV_ROWS, M::D, M::D, M::D, 2 * M::F, M::D};
 static constexpr int kMatK[M::NUM_MATS] = {M::D, M::D, M::D, M::D, M::D, M::F};
 
-// Context bind: dst[b][l][r][:] = src[b][l][r][:] for r < len[b], zero up to LKPAD.
-static __global__ void ma2_bind_ctx_kernel(const bf16* src, int src_rows, const int* len, int L, int LKPAD, bf16* dst) {
+// Context bind: dst[b][l][r][:] = src[b][l][map(r)][:] for r < len[b] (map = identity, or the
+// kept rows of a masked bind), zero up to LKPAD.
+static __global__ void ma2_bind_ctx_kernel(const bf16* src, int src_rows, const int* len, const int* rowmap, int L,
+                                           int LKPAD, bf16* dst) {
   const int b = blockIdx.z, l = blockIdx.y;
   const int n = len[b];
   const size_t per = (size_t)LKPAD * M::D / 8;  // 16-byte pieces
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (size_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / (M::D / 8)), seg = (int)(i % (M::D / 8));
     uint4 val = make_uint4(0, 0, 0, 0);
-    if (r < n) val = *reinterpret_cast<const uint4*>(src + (((size_t)b * L + l) * src_rows + r) * M::D + seg * 8);
+    const int sr = rowmap && r < n ? rowmap[(size_t)b * src_rows + r] : r;
+    if (r < n) val = *reinterpret_cast<const uint4*>(src + (((size_t)b * L + l) * src_rows + sr) * M::D + seg * 8);
     *reinterpret_cast<uint4*>(dst + (((size_t)b * L + l) * LKPAD + r) * M::D + seg * 8) = val;
   }
 }
@@ -360,7 +363,7 @@ void ma2_set_debug(fa_handle* h) {
 }
 
 fa_status ma2_bind(fa_handle* h, int batch, const void* k, const void* v, int src_rows, const int* ctx_len,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const int* rowmap) {
   Ma2State* s = h->ma2;
   if (batch < 1 || batch > h->cfg.max_batch) return fail(h, FA_ERR_INVALID, "batch %d outside 1..%d", batch, h->cfg.max_batch);
   if (!ctx_len || !k || !v) return fail(h, FA_ERR_INVALID, "null argument");
@@ -385,8 +388,8 @@ fa_status ma2_bind(fa_handle* h, int batch, const void* k, const void* v, int sr
   if ((st = ma2_plan(h)) != FA_OK) return st;
   if ((st = ma2_params(h)) != FA_OK) return st;
   const dim3 grid(std::max(1, s->LKPAD * M::D / 8 / 256 / 4), L, batch);
-  ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)k, src_rows, s->d_ctx, L, s->LKPAD, s->kctx);
-  ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)v, src_rows, s->d_ctx, L, s->LKPAD, s->vctx);
+  ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)k, src_rows, s->d_ctx, rowmap, L, s->LKPAD, s->kctx);
+  ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)v, src_rows, s->d_ctx, rowmap, L, s->LKPAD, s->vctx);
   FA_CUDA(h, cudaGetLastError());
   FA_CUDA(h, cudaStreamSynchronize(stream));
   s->bound = true;

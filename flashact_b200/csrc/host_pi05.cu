@@ -65,8 +65,8 @@ __global__ void linear_f32_kernel(const void* W, int wdt, const void* b, int bdt
 // Prefix KV bind: K -> kcache[b][l][LPAD][256] (split-half RoPE order), V -> vtcache[b][l][256][LPAD]
 // (transposed), rows >= valid_len zero. Interleaved sources (FlashRT) have rotary pairs at
 // (2d, 2d+1): d -> d, d+1 -> d+128 (src/pi05/mk6.cu:258-277 does the same de-interleave).
-__global__ void bind_k_kernel(const bf16* k, int src_rows, const int* valid, int L, int LPAD, int interleaved,
-                              bf16* kc) {
+__global__ void bind_k_kernel(const bf16* k, int src_rows, const int* valid, const int* rowmap, int L, int LPAD,
+                              int interleaved, bf16* kc) {
   const int b = blockIdx.z, l = blockIdx.y;
   const int vl = valid[b];
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < LPAD * HD; i += gridDim.x * blockDim.x) {
@@ -75,19 +75,22 @@ __global__ void bind_k_kernel(const bf16* k, int src_rows, const int* valid, int
     if (r < vl) {
       int sd = d;
       if (interleaved) sd = d < 128 ? 2 * d : 2 * (d - 128) + 1;
-      v = k[(((size_t)b * L + l) * src_rows + r) * HD + sd];
+      const int sr = rowmap ? rowmap[(size_t)b * src_rows + r] : r;  // kept row of a masked bind
+      v = k[(((size_t)b * L + l) * src_rows + sr) * HD + sd];
     }
     kc[(((size_t)b * L + l) * LPAD + r) * HD + d] = v;
   }
 }
-__global__ void bind_vt_kernel(const bf16* v, int src_rows, const int* valid, int L, int LPAD, bf16* vt) {
+__global__ void bind_vt_kernel(const bf16* v, int src_rows, const int* valid, const int* rowmap, int L, int LPAD,
+                               bf16* vt) {
   __shared__ bf16 tile[32][33];
   const int b = blockIdx.z / L, l = blockIdx.z % L;
   const int vl = valid[b];
   const int r0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int r = r0 + i, d = d0 + threadIdx.x;
-    tile[i][threadIdx.x] = r < vl ? v[(((size_t)b * L + l) * src_rows + r) * HD + d] : __float2bfloat16(0.f);
+    const int sr = rowmap && r < vl ? rowmap[(size_t)b * src_rows + r] : r;
+    tile[i][threadIdx.x] = r < vl ? v[(((size_t)b * L + l) * src_rows + sr) * HD + d] : __float2bfloat16(0.f);
   }
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -252,7 +255,18 @@ extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w
     ~Cleanup() { for (void* p : t) cudaFree(p); }
   } cleanup{tmp};
   fa_status st;
-  const void *wq, *wk, *wv, *wo, *wg, *wu, *wd, *lniw, *lnib, *lnpw, *lnpb, *nw, *nb, *tiw, *tib, *tow, *tob, *aiw, *aib, *aow, *aob;
+  const void *wq, *wk, *wv, *wo, *wg, *wu, *wd, *lniw = nullptr, *lnib = nullptr, *lnpw = nullptr, *lnpb = nullptr,
+             *nw = nullptr, *nb = nullptr, *tiw = nullptr, *tib = nullptr, *tow = nullptr, *tob = nullptr, *aiw, *aib,
+             *aow, *aob;
+  // The conditioning weights (time MLP, adaRMS denses) are optional as a group: without them the
+  // caller supplies the modulations with fa_set_modulation, as the reference's launch() takes them.
+  const fa_tensor* cond_w[10] = {&w->ln_in_w, &w->ln_in_b, &w->ln_post_w, &w->ln_post_b, &w->norm_w,
+                               &w->norm_b,  &w->time_in_w, &w->time_in_b, &w->time_out_w, &w->time_out_b};
+  int ncond = 0;
+  for (const fa_tensor* t : cond_w) ncond += t->ptr != nullptr;
+  if (ncond != 0 && ncond != 10)
+    return fail(h, FA_ERR_INVALID, "conditioning weights must be all given or all null (%d of 10 given)", ncond);
+  const bool with_cond = ncond == 10;
 #define STAGE(var, field, count) \
   if ((st = stage_tensor(h, w->field, (size_t)(count), #field, &var, tmp)) != FA_OK) return st
   STAGE(wq, wq, (size_t)L * QD * D);
@@ -262,16 +276,18 @@ extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w
   STAGE(wg, w_gate, (size_t)L * F * D);
   STAGE(wu, w_up, (size_t)L * F * D);
   STAGE(wd, w_down, (size_t)L * D * F);
-  STAGE(lniw, ln_in_w, (size_t)L * MOD * D);
-  STAGE(lnib, ln_in_b, (size_t)L * MOD);
-  STAGE(lnpw, ln_post_w, (size_t)L * MOD * D);
-  STAGE(lnpb, ln_post_b, (size_t)L * MOD);
-  STAGE(nw, norm_w, (size_t)MOD * D);
-  STAGE(nb, norm_b, MOD);
-  STAGE(tiw, time_in_w, (size_t)D * D);
-  STAGE(tib, time_in_b, D);
-  STAGE(tow, time_out_w, (size_t)D * D);
-  STAGE(tob, time_out_b, D);
+  if (with_cond) {
+    STAGE(lniw, ln_in_w, (size_t)L * MOD * D);
+    STAGE(lnib, ln_in_b, (size_t)L * MOD);
+    STAGE(lnpw, ln_post_w, (size_t)L * MOD * D);
+    STAGE(lnpb, ln_post_b, (size_t)L * MOD);
+    STAGE(nw, norm_w, (size_t)MOD * D);
+    STAGE(nb, norm_b, MOD);
+    STAGE(tiw, time_in_w, (size_t)D * D);
+    STAGE(tib, time_in_b, D);
+    STAGE(tow, time_out_w, (size_t)D * D);
+    STAGE(tob, time_out_b, D);
+  }
   STAGE(aiw, ain_w, (size_t)D * AD);
   STAGE(aib, ain_b, D);
   STAGE(aow, aout_w, (size_t)AD * D);
@@ -316,6 +332,11 @@ extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w
   to_f32_kernel<<<1, 64>>>(aob, w->aout_b.dtype, h->b_aout, AD);
   FA_CUDA(h, cudaGetLastError());
 
+  if (!with_cond) {  // modulations come from fa_set_modulation
+    FA_CUDA(h, cudaDeviceSynchronize());
+    h->weights_ready = true;
+    return FA_OK;
+  }
   // Conditioning for the fixed schedule t_s = 1 - s/N (src/pi05/hybrid_model.py:111-128):
   // cond = silu(W_out silu(W_in emb + b_in) + b_out); mods = Dense_{in,post}(cond); final = Dense_norm(cond).
   float *emb = nullptr, *h1 = nullptr, *cond = nullptr;
@@ -513,11 +534,30 @@ static fa_status build_params(fa_handle* h) {
   return FA_OK;
 }
 
+static fa_status bind_impl(fa_handle* h, int batch, const void* k, const void* v, int src_rows, const int* valid_len,
+                           fa_kv_layout layout, fa_stream stream, const int* rowmap);
+
 extern "C" fa_status fa_bind_prefix_kv(fa_handle* h, int batch, const void* k, const void* v, int src_rows,
                                        const int* valid_len, fa_kv_layout layout, fa_stream stream) {
   if (!h) return fail(h, FA_ERR_INVALID, "null handle");
+  return bind_impl(h, batch, k, v, src_rows, valid_len, layout, stream, nullptr);
+}
+
+extern "C" fa_status fa_bind_prefix_kv_masked(fa_handle* h, int batch, const void* k, const void* v, int src_rows,
+                                              const unsigned char* keep, fa_kv_layout layout, fa_stream stream) {
+  if (!h) return fail(h, FA_ERR_INVALID, "null handle");
+  if (batch < 1 || batch > h->cfg.max_batch) return fail(h, FA_ERR_INVALID, "batch %d outside 1..%d", batch, h->cfg.max_batch);
+  FA_CUDA(h, cudaSetDevice(h->device));
+  std::vector<int> counts;
+  fa_status st = masked_rows(h, batch, src_rows, keep, reinterpret_cast<cudaStream_t>(stream), counts);
+  if (st != FA_OK) return st;
+  return bind_impl(h, batch, k, v, src_rows, counts.data(), layout, stream, h->d_rowmap);
+}
+
+static fa_status bind_impl(fa_handle* h, int batch, const void* k, const void* v, int src_rows, const int* valid_len,
+                           fa_kv_layout layout, fa_stream stream, const int* rowmap) {
   if (h->kind == FA_MODEL_MOLMOACT2)
-    return ma2_bind(h, batch, k, v, src_rows, valid_len, reinterpret_cast<cudaStream_t>(stream));
+    return ma2_bind(h, batch, k, v, src_rows, valid_len, reinterpret_cast<cudaStream_t>(stream), rowmap);
   if (batch < 1 || batch > h->cfg.max_batch) return fail(h, FA_ERR_INVALID, "batch %d outside 1..%d", batch, h->cfg.max_batch);
   if (!valid_len) return fail(h, FA_ERR_INVALID, "valid_len is null");
   if (layout != FA_KV_COMPACT_SPLIT_HALF && layout != FA_KV_FLASHRT_INTERLEAVED) return fail(h, FA_ERR_INVALID, "unknown kv layout");
@@ -551,10 +591,10 @@ extern "C" fa_status fa_bind_prefix_kv(fa_handle* h, int batch, const void* k, c
   if ((st = build_params(h)) != FA_OK) return st;
   const int sr = std::max(src_rows, 1);
   bind_k_kernel<<<dim3(std::max(1, h->LPAD * HD / 256 / 4), L, batch), 256, 0, s>>>(
-      (const bf16*)k, sr, h->d_valid, L, h->LPAD, layout == FA_KV_FLASHRT_INTERLEAVED, h->kcache);
+      (const bf16*)k, sr, h->d_valid, rowmap, L, h->LPAD, layout == FA_KV_FLASHRT_INTERLEAVED, h->kcache);
   FA_CUDA(h, cudaGetLastError());
-  bind_vt_kernel<<<dim3(h->LPAD / 32, HD / 32, batch * L), dim3(32, 8), 0, s>>>((const bf16*)v, sr, h->d_valid, L, h->LPAD,
-                                                                              h->vtcache);
+  bind_vt_kernel<<<dim3(h->LPAD / 32, HD / 32, batch * L), dim3(32, 8), 0, s>>>((const bf16*)v, sr, h->d_valid, rowmap, L,
+                                                                              h->LPAD, h->vtcache);
   FA_CUDA(h, cudaGetLastError());
   rope_kernel<<<64, 256, 0, s>>>(h->d_valid, batch, T, h->rope_cos, h->rope_sin);
   FA_CUDA(h, cudaGetLastError());

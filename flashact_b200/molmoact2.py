@@ -54,14 +54,22 @@ class MolmoAct2ActionExpert:
         m, mf = mods.float().contiguous(), mod_final.float().contiguous()
         self._check(self.lib.fa_set_modulation(self.h, m.data_ptr(), mf.data_ptr()))
 
-    def bind_context(self, k: torch.Tensor, v: torch.Tensor, ctx_len, stream=None):
-        """k, v: [B][L][rows][768] projected cross-attention context, first ctx_len[b] rows valid."""
+    def bind_context(self, k: torch.Tensor, v: torch.Tensor, ctx_len=None, stream=None,
+                     keep_mask: torch.Tensor | None = None):
+        """k, v: [B][L][rows][768] projected cross-attention context: either the first ctx_len[b]
+        rows are valid, or keep_mask [B][rows] marks them (the model's cross mask == its max;
+        gathered on the device)."""
         k = k.to(device=f"cuda:{self.device}", dtype=torch.bfloat16).contiguous()
         v = v.to(device=f"cuda:{self.device}", dtype=torch.bfloat16).contiguous()
         B, rows = k.shape[0], k.shape[2]
-        lens = (ctypes.c_int * B)(*[int(x) for x in ctx_len])
-        self._check(self.lib.fa_bind_prefix_kv(self.h, B, k.data_ptr(), v.data_ptr(), rows, lens, 0,
-                                               _stream_ptr(stream)))
+        if keep_mask is not None:
+            m = keep_mask.to(device=f"cuda:{self.device}", dtype=torch.uint8).contiguous()
+            self._check(self.lib.fa_bind_prefix_kv_masked(self.h, B, k.data_ptr(), v.data_ptr(), rows, m.data_ptr(), 0,
+                                                          _stream_ptr(stream)))
+        else:
+            lens = (ctypes.c_int * B)(*[int(x) for x in ctx_len])
+            self._check(self.lib.fa_bind_prefix_kv(self.h, B, k.data_ptr(), v.data_ptr(), rows, lens, 0,
+                                                   _stream_ptr(stream)))
         self.batch = B
 
     def sample_actions(self, noise: torch.Tensor, out=None, stream=None, sync=True):

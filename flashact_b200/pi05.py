@@ -42,7 +42,10 @@ class Pi05ActionExpert:
         keep = []
         w = C.FaPi05Weights()
         for name in C.PI05_WEIGHT_FIELDS:
-            t = weights[name]
+            t = weights.get(name)
+            if t is None:  # conditioning weights left out: modulations are passed in (mods, mod_final)
+                setattr(w, name, C.FaTensor(None, C.FA_DT_F32))
+                continue
             if t.dtype not in _DT:
                 t = t.float()
             t = t.contiguous()
@@ -57,15 +60,23 @@ class Pi05ActionExpert:
     def _check(self, st):
         C.check(self.lib, self.h, st)
 
-    def bind_prefix_kv(self, k: torch.Tensor, v: torch.Tensor, valid_len, layout: str = "compact", stream=None):
-        """k, v: [B][L][rows][256] bf16 on this device (other dtypes converted)."""
+    def bind_prefix_kv(self, k: torch.Tensor, v: torch.Tensor, valid_len=None, layout: str = "compact", stream=None,
+                       keep_mask: torch.Tensor | None = None):
+        """k, v: [B][L][rows][256] bf16 on this device (other dtypes converted). Either valid_len
+        (the first valid_len[b] rows are the compacted prefix) or keep_mask [B][rows] (the
+        prefix pad mask: its True rows, in order, are gathered on the device)."""
         k = k.to(device=f"cuda:{self.device}", dtype=torch.bfloat16).contiguous()
         v = v.to(device=f"cuda:{self.device}", dtype=torch.bfloat16).contiguous()
         B, rows = k.shape[0], k.shape[2]
-        vl = (ctypes.c_int * B)(*[int(x) for x in valid_len])
         lay = C.FA_KV_FLASHRT_INTERLEAVED if layout == "flashrt" else C.FA_KV_COMPACT_SPLIT_HALF
-        self._check(self.lib.fa_bind_prefix_kv(self.h, B, k.data_ptr(), v.data_ptr(), rows, vl, lay,
-                                               _stream_ptr(stream)))
+        if keep_mask is not None:
+            m = keep_mask.to(device=f"cuda:{self.device}", dtype=torch.uint8).contiguous()
+            self._check(self.lib.fa_bind_prefix_kv_masked(self.h, B, k.data_ptr(), v.data_ptr(), rows, m.data_ptr(), lay,
+                                                          _stream_ptr(stream)))
+        else:
+            vl = (ctypes.c_int * B)(*[int(x) for x in valid_len])
+            self._check(self.lib.fa_bind_prefix_kv(self.h, B, k.data_ptr(), v.data_ptr(), rows, vl, lay,
+                                                   _stream_ptr(stream)))
         self.batch = B
 
     def sample_actions(self, noise: torch.Tensor, out: torch.Tensor | None = None, stream=None,

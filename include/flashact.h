@@ -123,7 +123,9 @@ FA_API fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int device,
 /* Packs the weights into the engine's streaming layout on the device and computes, on the
  * device, the time embedding -> conditioning MLP -> per-layer adaRMS modulations for the
  * configured fixed schedule (reference: host-side in src/pi05/hybrid_model.py:111-128).
- * Synchronous. Replaces HybridPi05._pack_weights. */
+ * The ten conditioning tensors (ln_*, norm_*, time_*) may all be null: the modulations are then
+ * set with fa_set_modulation, as the reference's launch() receives them precomputed
+ * (src/pi05/binding.cpp:31). Synchronous. Replaces HybridPi05._pack_weights. */
 FA_API fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt);
 
 /* MolmoAct2: packs the weights (bf16 GEMM weights, fp32 biases). Synchronous. The
@@ -155,6 +157,15 @@ FA_API fa_status fa_set_modulation(fa_handle* h, const float* mods, const float*
  * de-interleave runs on `stream`. Replaces compact_kv + the kcache/vtcache fill. */
 FA_API fa_status fa_bind_prefix_kv(fa_handle* h, int batch, const void* k, const void* v, int src_rows,
                             const int* valid_len, fa_kv_layout layout, fa_stream stream);
+
+/* Same as fa_bind_prefix_kv for an UNcompacted prefix / context: keep is a device array
+ * [batch][src_rows] (nonzero = valid token, e.g. the prefix pad mask, or MolmoAct2's
+ * cross-attention mask == its max); the valid rows of each observation, in order, are gathered
+ * on the device as the bound prefix (the compaction the reference does with torch ops before
+ * its launch: compact_kv in src/pi05/pack_weights.py:60-70, and benchmarks/molmoact2/
+ * eval_e2e.py:108-125). Synchronises `stream` once to read the valid counts back. */
+FA_API fa_status fa_bind_prefix_kv_masked(fa_handle* h, int batch, const void* k, const void* v, int src_rows,
+                                          const unsigned char* keep, fa_kv_layout layout, fa_stream stream);
 
 /* Runs the whole N-step x L-layer Euler denoise loop as one cooperative megakernel.
  * noise: [batch][T][AD] fp32 initial x_1; actions_out: [batch][T][AD] fp32 final x_0. Either

@@ -40,6 +40,18 @@ def pi05_dequantised_case(c):
 def prepare_pi05_ref(ext, c):
     """Packs case c for the reference pi0.5 megakernel; returns (launch, read): launch() runs the
     kernel once from the initial noise, read() returns x_t [Tv][32]."""
+    args, xt_d, x0 = pi05_ref_args(c)
+
+    def launch():
+        xt_d.copy_(x0)
+        ext.launch(*args)
+
+    return launch, lambda: xt_d[:c.T].cpu()
+
+
+def pi05_ref_args(c):
+    """The reference pi0.5 launch() arguments for case c (device tensors, packed like
+    src/pi05/hybrid_model.py:76-133), its x_t tensor and x_t's initial value."""
     Tv, Lp, N = c.T, c.Lp, c.num_steps
     dev = torch.device("cuda")
     # quantise per original row (row permutations commute with per-row scales)
@@ -89,12 +101,7 @@ def prepare_pi05_ref(ext, c):
                    empty, empty, 0, kc.to(dev), vt.to(dev), Lp, Lmax, N, Tv, xt_d, f32(2 * T5, D5), f32(4, T5, D5),
                    torch.zeros(16, dtype=torch.int64, device=dev), f16(T5, D5), f16(T5, 2048), f16(T5, 2048),
                    f16(T5, F5), f32(8, T5, Lmax), f16(8, T5, Lmax), 148, 256]  # device arguments, built once
-
-    def launch():
-        xt_d.copy_(x0)
-        ext.launch(*args)
-
-    return launch, lambda: xt_d[:Tv].cpu()
+    return args, xt_d, x0
 
 
 def run_pi05_ref(ext, c):
@@ -107,6 +114,18 @@ def run_pi05_ref(ext, c):
 
 def prepare_ma2_ref(ext, c):
     """Packs case c for the reference MolmoAct2 megakernel; returns (launch, read)."""
+    args, xt_d, x0 = ma2_ref_args(c)
+
+    def launch():
+        xt_d.copy_(x0)
+        ext.launch(*args)
+
+    return launch, lambda: xt_d[:c.T].cpu()
+
+
+def ma2_ref_args(c):
+    """The reference MolmoAct2 launch() arguments for case c
+    (benchmarks/molmoact2/eval_numerics.py:77-150 packing), its x_t tensor and initial value."""
     NL, T, D, F, AD = 36, 32, 768, 3072, 32
     dev = torch.device("cuda")
     bf = lambda t: t.to(torch.bfloat16).contiguous().to(dev)
@@ -136,12 +155,7 @@ def prepare_ma2_ref(ext, c):
                    torch.zeros(T, D, device=dev), torch.zeros(3, T, D, device=dev),
                    torch.zeros(16, dtype=torch.int64, device=dev), bufs, torch.zeros(8, T, Lkmax, device=dev),
                    torch.zeros(8, T, Lkmax, dtype=torch.bfloat16, device=dev), 148, 256]  # device arguments, built once
-
-    def launch():
-        xt_d.copy_(x0)
-        ext.launch(*args)
-
-    return launch, lambda: xt_d[:c.T].cpu()
+    return args, xt_d, x0
 
 
 def run_ma2_ref(ext, c):

@@ -43,3 +43,20 @@ def test_struct_layouts():
     assert ctypes.sizeof(_capi.FaMa2Weights) == 18 * 16
     assert ctypes.sizeof(_capi.FaTensor) == 16
     assert ctypes.sizeof(_capi.FaPi05Weights) == 21 * 16
+
+
+def test_compat_launch_signatures():
+    """flashact_b200.compat mirrors the reference's pybind launch() signatures argument for
+    argument (src/pi05/binding.cpp:28-37, src/molmoact2/binding.cpp:28-35)."""
+    import inspect
+
+    from flashact_b200 import compat
+    pi05 = ["w1", "wo", "w2", "w3", "s1", "so_", "s2", "s3", "mods", "mod_final", "rope_cos", "rope_sin", "w_ain",
+            "b_ain", "w_aout", "b_aout", "kvsrc_k", "kvsrc_v", "srows", "kcache", "vtcache", "Lp", "Lmax",
+            "num_steps", "Tv", "x_t", "x", "xp", "stage_cycles", "xn", "q", "attn", "hmlp", "scores", "probs",
+            "nblocks", "nthreads"]
+    ma2 = ["ws", "bs", "mods", "mod_final", "rope_cos", "rope_sin", "w_ain", "b_ain", "w_aout", "b_aout", "kctx",
+           "vtctx", "Lk", "Lkmax", "Tv", "adim", "num_steps", "x_t", "x", "xp", "stage_cycles", "bufs", "scores",
+           "probs", "nblocks", "nthreads"]
+    assert list(inspect.signature(compat.pi05_launch).parameters) == pi05
+    assert list(inspect.signature(compat.ma2_launch).parameters) == ma2

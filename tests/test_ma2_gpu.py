@@ -53,3 +53,29 @@ def test_ma2_config_c3(require_gpu):
     mx, cos = err(out[..., :c.adim], M.flow(c)[..., :c.adim])
     print(f"MolmoAct2 C3 max_abs={mx:.4g} cos={cos:.7f}")
     assert mx < TOL and cos > 0.999, (mx, cos)
+
+
+def test_ma2_masked_context_equals_host_compaction(require_gpu):
+    """The cross-attention context gathered on the device from a keep mask (the model's cross mask
+    == its max, benchmarks/molmoact2/eval_e2e.py:108-125) equals binding the host-compacted one."""
+    from flashact_b200 import MolmoAct2ActionExpert
+    c = M.make_case(seed=53, L=2, T=30, Lk=200, B=2, num_steps=2)
+    g = torch.Generator().manual_seed(5)
+    rows = 260
+    keep = torch.rand(c.B, rows, generator=g) < 0.75
+    kfull = torch.randn(c.B, c.L, rows, 768, generator=g).to(torch.bfloat16)
+    vfull = torch.randn(c.B, c.L, rows, 768, generator=g).to(torch.bfloat16)
+    counts = keep.sum(1).tolist()
+    kc = torch.zeros_like(kfull)
+    vc = torch.zeros_like(vfull)
+    for b in range(c.B):
+        kc[b, :, : counts[b]] = kfull[b][:, keep[b]]
+        vc[b, :, : counts[b]] = vfull[b][:, keep[b]]
+    eng = MolmoAct2ActionExpert(c.w, c.mods, c.mod_final, num_layers=c.L, horizon=c.T, action_dim=c.AD,
+                                valid_action_dim=c.adim, max_context=rows, max_batch=c.B, num_steps=c.num_steps,
+                                rope_cos=c.rope_cos, rope_sin=c.rope_sin)
+    eng.bind_context(kfull, vfull, keep_mask=keep)
+    out_masked = eng.sample_actions(c.noise.cuda()).cpu()
+    eng.bind_context(kc, vc, counts)
+    out_compact = eng.sample_actions(c.noise.cuda()).cpu()
+    assert torch.equal(out_masked, out_compact)

@@ -75,3 +75,26 @@ def test_barrier_timeout_reported(require_gpu):
     eng.inject_fault(-1, 0)
     again = eng.sample_actions(c.noise.cuda()).cpu()
     assert torch.equal(good, again)
+
+
+def test_masked_bind_equals_host_compaction(require_gpu):
+    """fa_bind_prefix_kv_masked gathers the pad-masked prefix on the device; the result must be
+    bit-identical to binding the host-compacted prefix (compact_kv, src/pi05/pack_weights.py:60-70)."""
+    c = O.make_case(seed=21, L=2, T=50, AD=32, Lp=300, B=2, num_steps=2)
+    g = torch.Generator().manual_seed(3)
+    rows = 360
+    keep = torch.rand(c.B, rows, generator=g) < 0.8
+    kfull = torch.randn(c.B, c.L, rows, 256, generator=g).to(torch.bfloat16)
+    vfull = torch.randn(c.B, c.L, rows, 256, generator=g).to(torch.bfloat16)
+    counts = keep.sum(1).tolist()
+    kc = torch.zeros(c.B, c.L, rows, 256, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    for b in range(c.B):
+        kc[b, :, : counts[b]] = kfull[b][:, keep[b]]
+        vc[b, :, : counts[b]] = vfull[b][:, keep[b]]
+    eng = engine_for(c)
+    eng.bind_prefix_kv(kfull.cuda(), vfull.cuda(), keep_mask=keep.cuda())
+    out_masked = eng.sample_actions(c.noise.cuda()).cpu()
+    eng.bind_prefix_kv(kc.cuda(), vc.cuda(), counts)
+    out_compact = eng.sample_actions(c.noise.cuda()).cpu()
+    assert torch.equal(out_masked, out_compact)

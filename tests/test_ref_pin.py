@@ -53,3 +53,39 @@ def test_molmoact2_oracle_matches_reference_kernel(require_gpu):
     print(f"MolmoAct2 reference kernel vs oracle: max_abs={mx:.4g} cos={cos:.7f}")
     assert torch.isfinite(ref_kernel).all()
     assert mx < 1.5e-2 and cos > 0.9999, (mx, cos)
+
+
+def test_pi05_compat_launch_matches_reference_kernel(require_gpu):
+    """flashact_b200.compat.pi05_launch takes the reference launch() arguments unchanged (FP8
+    packed weights, fp16 kcache / vtcache, x_t in place) and must reproduce the reference kernel."""
+    from flashact_b200 import compat
+    ext = _ext("mk_v6_ref")
+    c = O.make_case(**R.PI05_PIN)
+    ref_kernel = R.run_pi05_ref(ext, c)
+    args, xt_d, x0 = R.pi05_ref_args(c)
+    xt_d.copy_(x0)
+    compat.pi05_launch(*args)
+    torch.cuda.synchronize()
+    ours = xt_d[:c.T].cpu()
+    compat.clear_cache()
+    mx, cos = err(ours, ref_kernel)
+    print(f"pi0.5 compat launch vs reference kernel: max_abs={mx:.4g} cos={cos:.7f}")
+    assert mx < 2e-2 and cos > 0.9999, (mx, cos)
+
+
+def test_ma2_compat_launch_matches_reference_kernel(require_gpu):
+    """flashact_b200.compat.ma2_launch with the reference MolmoAct2 launch() arguments."""
+    from flashact_b200 import compat
+    ext = _ext("mk_ma2_ref")
+    c = M.make_case(**R.MA2_PIN)
+    ref_kernel = R.run_ma2_ref(ext, c)
+    args, xt_d, x0 = R.ma2_ref_args(c)
+    xt_d.copy_(x0)
+    compat.ma2_launch(*args)
+    torch.cuda.synchronize()
+    ours = xt_d[:c.T].cpu()
+    compat.clear_cache()
+    mx, cos = err(ours[:, :c.adim], ref_kernel[:, :c.adim])
+    print(f"MolmoAct2 compat launch vs reference kernel: max_abs={mx:.4g} cos={cos:.7f}")
+    assert mx < 2e-2 and cos > 0.9999, (mx, cos)
+    assert torch.equal(ours[:, c.adim:], ref_kernel[:, c.adim:])
