@@ -42,6 +42,27 @@ MA2_BIAS_BYTES = MA2_L * (2304 + 3 * 768 + 2 * 3072 + 768) * 4
 MA2_KV_BYTES = 2 * MA2_L * MA2_LK * 768 * 2  # cross-attention K+V per Euler step per observation
 
 
+# DRAM bytes (read + write) of one megakernel launch on the bench workload, from one ncu capture
+# of `bench.py --steps 1 --warmup 3 --no-cpu-baseline` (metrics dram__bytes_read.sum and
+# dram__bytes_write.sum, -k regex:pi05_denoise -s 3 -c 1; summary kept under profiles/).
+NCU_TRAFFIC = {("pi05", 1): 6_245_817_344 + 3_806_208}
+
+
+def set_shape(layers, euler_steps):
+    """Smaller cases for profiling (--layers / --euler-steps); the defaults are the BASELINE ones."""
+    global L, NSTEPS, W_BYTES_BF16, KV_BYTES, GEMM_PARAMS, MA2_L, MA2_W_BYTES, MA2_BIAS_BYTES, MA2_KV_BYTES
+    if layers:
+        W_BYTES_BF16 = W_BYTES_BF16 // L * layers
+        KV_BYTES = KV_BYTES // L * layers
+        GEMM_PARAMS = W_BYTES_BF16 // 2
+        MA2_W_BYTES = MA2_W_BYTES // MA2_L * layers
+        MA2_BIAS_BYTES = MA2_BIAS_BYTES // MA2_L * layers
+        MA2_KV_BYTES = MA2_KV_BYTES // MA2_L * layers
+        L = MA2_L = layers
+    if euler_steps:
+        NSTEPS = euler_steps
+
+
 def algorithmic_bytes(batch, model="pi05"):
     if model == "molmoact2":
         return NSTEPS * (MA2_W_BYTES + MA2_BIAS_BYTES + batch * MA2_KV_BYTES)
@@ -63,7 +84,7 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms during the timed region."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -74,7 +95,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -214,7 +235,7 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1, help="observations per GPU (weak scaling)")
     ap.add_argument("--global-batch", type=int, default=0,
@@ -222,7 +243,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="pi05", choices=["pi05", "molmoact2"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="profiling only: fewer expert layers than the config")
+    ap.add_argument("--euler-steps", type=int, default=0, help="profiling only: fewer Euler steps than the config")
     args = ap.parse_args()
+    set_shape(args.layers, args.euler_steps)
     if args.impl == "reference":  # host-CPU arm: rank 0 alone works, no process group needed
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
@@ -307,7 +331,8 @@ def main():
         "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "p50_ms": p50, "min_ms": per[0],
         "higher_is_better": True, "scaling": "strong" if args.global_batch > 0 else "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) prefix KV and noise)",
-        "config": {"workload": WORKLOAD[args.model],
+        "config": {"workload": WORKLOAD[args.model] + (f" [profiling case: {L} layers, {NSTEPS} Euler steps]"
+                                                       if args.layers or args.euler_steps else ""),
                    "batch_per_gpu": B, "global_batch": total_batch, "parallelism": f"batch shards x{world}",
                    "l2": "no flush: the bf16 weight stream per Euler step (623 MB pi0.5, 764 MB MolmoAct2) exceeds "
                          "the 126 MB L2"},
@@ -316,7 +341,7 @@ def main():
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": None,
+                     "traffic": (NCU_TRAFFIC.get((args.model, B)) if not (args.layers or args.euler_steps) else None),
                      "algorithmic_bytes_per_launch": algorithmic_bytes(B, args.model),
                      "note": "achieved = N x (bf16 weights + B x prefix KV) per launch / mean launch time"},
         "clocks": clk.summary(),
