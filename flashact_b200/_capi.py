@@ -13,7 +13,7 @@ FA_DT_F32, FA_DT_BF16, FA_DT_F16 = 0, 1, 2
 FA_KV_COMPACT_SPLIT_HALF, FA_KV_FLASHRT_INTERLEAVED = 0, 1
 
 # Every function the header declares (checked by tests/test_capi.py against include/flashact.h).
-EXPORTS = ["fa_create", "fa_pi05_load_weights", "fa_ma2_load_weights", "fa_ma2_set_rope", "fa_set_modulation", "fa_bind_prefix_kv", "fa_bind_prefix_kv_masked", "fa_sample_actions",
+EXPORTS = ["fa_create", "fa_pi05_load_weights", "fa_pi05_load_weights_q", "fa_ma2_load_weights", "fa_ma2_set_rope", "fa_set_modulation", "fa_bind_prefix_kv", "fa_bind_prefix_kv_masked", "fa_sample_actions",
            "fa_sync", "fa_set_stage_timing", "fa_get_stage_cycles", "fa_last_launch_count",
            "fa_set_fault_injection", "fa_debug_trace", "fa_pi05_modulations_noalloc", "fa_last_error", "fa_destroy"]
 
@@ -39,6 +39,17 @@ class FaPi05Weights(ctypes.Structure):
 
 MA2_WEIGHT_FIELDS = ["w_qkv", "b_qkv", "w_so", "b_so", "w_cq", "b_cq", "w_co", "b_co", "w_gate", "b_gate", "w_up",
                      "b_up", "w_down", "b_down", "ain_w", "ain_b", "aout_w", "aout_b"]
+
+
+class FaQScale(ctypes.Structure):
+    _fields_ = [("scale", ctypes.c_void_p), ("tensor", ctypes.c_void_p)]
+
+
+PI05_QUANT_FIELDS = ["wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"]
+
+
+class FaPi05QScales(ctypes.Structure):
+    _fields_ = [(n, FaQScale) for n in PI05_QUANT_FIELDS]
 
 
 class FaMa2Weights(ctypes.Structure):
@@ -68,6 +79,7 @@ def load_library(path: str = None) -> ctypes.CDLL:
     sig = {
         "fa_create": (S, [I, ctypes.POINTER(FaConfig), I, ctypes.POINTER(ctypes.c_void_p)]),
         "fa_pi05_load_weights": (S, [H, ctypes.POINTER(FaPi05Weights), I]),
+        "fa_pi05_load_weights_q": (S, [H, ctypes.POINTER(FaPi05Weights), I, ctypes.POINTER(FaPi05QScales)]),
         "fa_ma2_load_weights": (S, [H, ctypes.POINTER(FaMa2Weights)]),
         "fa_ma2_set_rope": (S, [H, P, P]),
         "fa_set_modulation": (S, [H, P, P]),

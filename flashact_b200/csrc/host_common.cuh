@@ -2,6 +2,7 @@
 // device allocation, weight staging / row-gather packing, and TMA descriptor builders.
 #pragma once
 #include <cudaTypedefs.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -187,7 +188,23 @@ struct PackSrc {
   const void* ptr[3];
   int dtype[3];
   int rows[3];  // rows per layer of each source
+  // quantised sources (fa_pi05_load_weights_q): 0 = plain dtype, 1 = FP8 E4M3 codes x per-row
+  // fp32 scale, 2 = NVFP4 (E2M1 codes x E4M3 per-16 block scale x fp32 per-layer scale)
+  int quant;
+  const void* scale[3];
+  const float* tensor[3];
 };
+// E2M1 (sign, 2 exponent bits with bias 1, 1 mantissa bit): 0, 0.5, 1, 1.5, 2, 3, 4, 6.
+__device__ __forceinline__ float e2m1_value(unsigned v) {
+  const unsigned e = (v >> 1) & 3u, m = v & 1u;
+  const float mag = e == 0 ? 0.5f * (float)m : (1.0f + 0.5f * (float)m) * (float)(1u << (e - 1));
+  return (v & 8u) ? -mag : mag;
+}
+__device__ __forceinline__ float e4m3_value(unsigned char c) {
+  __nv_fp8_e4m3 f;
+  f.__x = c;
+  return (float)f;
+}
 static __global__ void pack_rows_kernel(PackSrc s, const int2* rowmap, bf16* dst, int R, int K, int L) {
   const size_t total = (size_t)L * R * K;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -195,8 +212,20 @@ static __global__ void pack_rows_kernel(PackSrc s, const int2* rowmap, bf16* dst
     const size_t lr = i / K;
     const int r = (int)(lr % R), l = (int)(lr / R);
     const int2 m = rowmap[r];
-    const size_t si = ((size_t)l * s.rows[m.x] + m.y) * K + k;
-    dst[i] = __float2bfloat16(load_as_float(s.ptr[m.x], si, s.dtype[m.x]));
+    const size_t srow = (size_t)l * s.rows[m.x] + m.y;
+    const size_t si = srow * K + k;
+    float v;
+    if (s.quant == 1) {
+      v = e4m3_value(reinterpret_cast<const unsigned char*>(s.ptr[m.x])[si]) *
+          reinterpret_cast<const float*>(s.scale[m.x])[srow];
+    } else if (s.quant == 2) {
+      const unsigned char b = reinterpret_cast<const unsigned char*>(s.ptr[m.x])[si >> 1];
+      const float bs = e4m3_value(reinterpret_cast<const unsigned char*>(s.scale[m.x])[srow * (K / 16) + k / 16]);
+      v = e2m1_value((k & 1) ? (b >> 4) : (b & 15u)) * bs * s.tensor[m.x][l];
+    } else {
+      v = load_as_float(s.ptr[m.x], si, s.dtype[m.x]);
+    }
+    dst[i] = __float2bfloat16(v);
   }
 }
 static __global__ void to_f32_kernel(const void* src, int dt, float* dst, size_t n) {
@@ -247,6 +276,19 @@ static fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint6
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled (3D) failed (%d)", (int)r);
+  return FA_OK;
+}
+
+// Returns a device pointer holding `bytes` of `p` (staging host data into `tmp` when needed).
+static fa_status stage_bytes(fa_handle* h, const void* p, size_t bytes, const char* name, const void** dptr,
+                             std::vector<void*>& tmp) {
+  if (!p) return fail(h, FA_ERR_INVALID, "'%s' is null", name);
+  if (is_device_ptr(p)) { *dptr = p; return FA_OK; }
+  void* d = nullptr;
+  if (cudaMalloc(&d, bytes) != cudaSuccess) return fail(h, FA_ERR_OOM, "staging '%s' (%zu bytes)", name, bytes);
+  tmp.push_back(d);
+  FA_CUDA(h, cudaMemcpy(d, p, bytes, cudaMemcpyHostToDevice));
+  *dptr = d;
   return FA_OK;
 }
 

@@ -244,9 +244,24 @@ static fa_status run_linear(fa_handle* h, const void* W, fa_dtype wdt, const voi
   return FA_OK;
 }
 
+static fa_status load_weights_impl(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt, const fa_pi05_qscales* q);
+
 extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt) {
   if (!h || !w) return fail(h, FA_ERR_INVALID, "null argument");
-  if (fmt != FA_WFMT_BF16) return fail(h, FA_ERR_UNSUPPORTED, "weight format %d not available yet (bf16 only)", (int)fmt);
+  if (fmt != FA_WFMT_BF16)
+    return fail(h, FA_ERR_INVALID, "quantised weights go through fa_pi05_load_weights_q (they need scales)");
+  return load_weights_impl(h, w, fmt, nullptr);
+}
+
+extern "C" fa_status fa_pi05_load_weights_q(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt,
+                                            const fa_pi05_qscales* q) {
+  if (!h || !w || !q) return fail(h, FA_ERR_INVALID, "null argument");
+  if (fmt != FA_WFMT_FP8 && fmt != FA_WFMT_NVFP4) return fail(h, FA_ERR_INVALID, "unknown quantised format %d", (int)fmt);
+  return load_weights_impl(h, w, fmt, q);
+}
+
+static fa_status load_weights_impl(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt, const fa_pi05_qscales* q) {
+  if (h->kind != FA_MODEL_PI05) return fail(h, FA_ERR_INVALID, "not a pi0.5 handle");
   FA_CUDA(h, cudaSetDevice(h->device));
   const int L = h->cfg.num_layers, AD = h->cfg.action_dim, S = h->cfg.num_steps;
   std::vector<void*> tmp;
@@ -269,13 +284,33 @@ extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w
   const bool with_cond = ncond == 10;
 #define STAGE(var, field, count) \
   if ((st = stage_tensor(h, w->field, (size_t)(count), #field, &var, tmp)) != FA_OK) return st
-  STAGE(wq, wq, (size_t)L * QD * D);
-  STAGE(wk, wk, (size_t)L * HD * D);
-  STAGE(wv, wv, (size_t)L * HD * D);
-  STAGE(wo, wo, (size_t)L * D * QD);
-  STAGE(wg, w_gate, (size_t)L * F * D);
-  STAGE(wu, w_up, (size_t)L * F * D);
-  STAGE(wd, w_down, (size_t)L * D * F);
+  // GEMM weights: plain tensors, or codes + scales of a quantised format
+  const int qmode = fmt == FA_WFMT_FP8 ? 1 : fmt == FA_WFMT_NVFP4 ? 2 : 0;
+  const void* qs[7] = {nullptr};   // row (FP8) or block (NVFP4) scales, device
+  const float* qt[7] = {nullptr};  // NVFP4 per-layer tensor scales, device
+  {
+    const fa_tensor* wt[7] = {&w->wq, &w->wk, &w->wv, &w->wo, &w->w_gate, &w->w_up, &w->w_down};
+    const void** dst[7] = {&wq, &wk, &wv, &wo, &wg, &wu, &wd};
+    const int rows[7] = {QD, HD, HD, D, F, F, D}, cols[7] = {D, D, D, QD, D, D, F};
+    const char* names[7] = {"wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"};
+    const fa_qscale* sc[7] = {q ? &q->wq : nullptr, q ? &q->wk : nullptr, q ? &q->wv : nullptr, q ? &q->wo : nullptr,
+                              q ? &q->w_gate : nullptr, q ? &q->w_up : nullptr, q ? &q->w_down : nullptr};
+    for (int i = 0; i < 7; ++i) {
+      const size_t n = (size_t)L * rows[i] * cols[i];
+      if (qmode == 0) {
+        if ((st = stage_tensor(h, *wt[i], n, names[i], dst[i], tmp)) != FA_OK) return st;
+        continue;
+      }
+      if ((st = stage_bytes(h, wt[i]->ptr, qmode == 1 ? n : n / 2, names[i], dst[i], tmp)) != FA_OK) return st;
+      const size_t sbytes = qmode == 1 ? (size_t)L * rows[i] * 4 : n / 16;
+      if ((st = stage_bytes(h, sc[i]->scale, sbytes, names[i], &qs[i], tmp)) != FA_OK) return st;
+      if (qmode == 2) {
+        const void* t = nullptr;
+        if ((st = stage_bytes(h, sc[i]->tensor, (size_t)L * 4, names[i], &t, tmp)) != FA_OK) return st;
+        qt[i] = reinterpret_cast<const float*>(t);
+      }
+    }
+  }
   if (with_cond) {
     STAGE(lniw, ln_in_w, (size_t)L * MOD * D);
     STAGE(lnib, ln_in_b, (size_t)L * MOD);
@@ -308,11 +343,13 @@ extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w
         m1[mt * 128 + r] = make_int2(2, (mt - 18) * 128 + r);
       }
     }
-  PackSrc s1 = {{wq, wk, wv}, {w->wq.dtype, w->wk.dtype, w->wv.dtype}, {QD, HD, HD}};
+  PackSrc s1 = {{wq, wk, wv}, {w->wq.dtype, w->wk.dtype, w->wv.dtype}, {QD, HD, HD}, qmode, {qs[0], qs[1], qs[2]},
+                {qt[0], qt[1], qt[2]}};
   if ((st = pack_matrix(h, m1, s1, h->w_qkv, D, tmp)) != FA_OK) return st;
   std::vector<int2> mo(D);
   for (int r = 0; r < D; ++r) mo[r] = make_int2(0, r);
-  PackSrc so = {{wo, wo, wo}, {w->wo.dtype, w->wo.dtype, w->wo.dtype}, {D, D, D}};
+  PackSrc so = {{wo, wo, wo}, {w->wo.dtype, w->wo.dtype, w->wo.dtype}, {D, D, D}, qmode, {qs[3], qs[3], qs[3]},
+                {qt[3], qt[3], qt[3]}};
   if ((st = pack_matrix(h, mo, so, h->w_o, QD, tmp)) != FA_OK) return st;
   // gate/up rows: tile mt, row 32*q + lane -> feature 64*mt + 16*q + (lane & 15); lanes < 16 gate.
   std::vector<int2> m2(2 * F);
@@ -321,9 +358,11 @@ extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w
       const int qd = r >> 5, lane = r & 31;
       m2[mt * 128 + r] = make_int2(lane < 16 ? 0 : 1, 64 * mt + 16 * qd + (lane & 15));
     }
-  PackSrc s2 = {{wg, wu, wu}, {w->w_gate.dtype, w->w_up.dtype, w->w_up.dtype}, {F, F, F}};
+  PackSrc s2 = {{wg, wu, wu}, {w->w_gate.dtype, w->w_up.dtype, w->w_up.dtype}, {F, F, F}, qmode, {qs[4], qs[5], qs[5]},
+                {qt[4], qt[5], qt[5]}};
   if ((st = pack_matrix(h, m2, s2, h->w_gu, D, tmp)) != FA_OK) return st;
-  PackSrc s3 = {{wd, wd, wd}, {w->w_down.dtype, w->w_down.dtype, w->w_down.dtype}, {D, D, D}};
+  PackSrc s3 = {{wd, wd, wd}, {w->w_down.dtype, w->w_down.dtype, w->w_down.dtype}, {D, D, D}, qmode,
+                {qs[6], qs[6], qs[6]}, {qt[6], qt[6], qt[6]}};
   if ((st = pack_matrix(h, mo, s3, h->w_dn, F, tmp)) != FA_OK) return st;
 
   to_f32_kernel<<<64, 256>>>(aiw, w->ain_w.dtype, h->w_ain, (size_t)D * AD);

@@ -27,7 +27,10 @@ class Pi05ActionExpert:
     flashact_b200._capi.PI05_WEIGHT_FIELDS, [out][in] row-major, stacked over layers."""
 
     def __init__(self, weights: dict, *, num_layers=18, horizon=50, action_dim=32, max_prefix=968, max_batch=1,
-                 num_steps=10, device: int = 0, mods=None, mod_final=None):
+                 num_steps=10, device: int = 0, mods=None, mod_final=None, wfmt: str = "bf16", qscales=None):
+        """wfmt "fp8" / "nvfp4": the seven GEMM weights are codes (uint8) and qscales maps each of
+        them to its scales -- fp8: per-row fp32 [L][rows]; nvfp4: (E4M3 block scales as uint8
+        [L][rows][K/16], fp32 per-layer scale [L]) -- see fa_qscale in include/flashact.h."""
         self.lib = C.load_library()
         self.device = device
         self.cfg = C.FaConfig(num_layers, 1024, 8, 1, 256, 4096, horizon, action_dim, max_prefix, max_batch,
@@ -46,12 +49,29 @@ class Pi05ActionExpert:
             if t is None:  # conditioning weights left out: modulations are passed in (mods, mod_final)
                 setattr(w, name, C.FaTensor(None, C.FA_DT_F32))
                 continue
-            if t.dtype not in _DT:
+            quantised = wfmt != "bf16" and name in C.PI05_QUANT_FIELDS
+            if t.dtype not in _DT and not quantised:
                 t = t.float()
             t = t.contiguous()
             keep.append(t)
-            setattr(w, name, C.FaTensor(t.data_ptr(), _DT[t.dtype]))
-        self._check(self.lib.fa_pi05_load_weights(self.h, ctypes.byref(w), C.FA_WFMT_BF16))
+            setattr(w, name, C.FaTensor(t.data_ptr(), _DT.get(t.dtype, C.FA_DT_F32)))
+        if wfmt == "bf16":
+            self._check(self.lib.fa_pi05_load_weights(self.h, ctypes.byref(w), C.FA_WFMT_BF16))
+        else:
+            qs = C.FaPi05QScales()
+            for name in C.PI05_QUANT_FIELDS:
+                sc = qscales[name]
+                blk, ten = (sc if isinstance(sc, (tuple, list)) else (sc, None))
+                blk = blk.contiguous()
+                keep.append(blk)
+                tp = None
+                if ten is not None:
+                    ten = ten.float().contiguous()
+                    keep.append(ten)
+                    tp = ten.data_ptr()
+                setattr(qs, name, C.FaQScale(blk.data_ptr(), tp))
+            fmt = {"fp8": C.FA_WFMT_FP8, "nvfp4": C.FA_WFMT_NVFP4}[wfmt]
+            self._check(self.lib.fa_pi05_load_weights_q(self.h, ctypes.byref(w), fmt, ctypes.byref(qs)))
         if mods is not None:
             m = mods.float().contiguous()
             mf = mod_final.float().contiguous()

@@ -102,6 +102,21 @@ typedef struct fa_pi05_weights {
   fa_tensor aout_w, aout_b;         /* [AD][1024], [AD]                                    */
 } fa_pi05_weights;
 
+/* Scales of one quantised GEMM weight (fa_pi05_load_weights_q).
+ *  FP8 (E4M3, the reference's per-output-row scheme, src/pi05/hybrid_model.py:105-110): the
+ *    weight's ptr holds uint8 codes [L][rows][K]; scale = fp32 [L][rows]; value = code * scale.
+ *  NVFP4: ptr holds E2M1 codes, two per byte (even k in the low nibble) [L][rows][K/2];
+ *    scale = E4M3 block scales [L][rows][K/16] (one per 16 consecutive k); tensor = fp32 [L];
+ *    value = code * block_scale * tensor[l].
+ * ptrs may be host or device memory. */
+typedef struct fa_qscale {
+  const void* scale;
+  const float* tensor; /* NVFP4 only */
+} fa_qscale;
+typedef struct fa_pi05_qscales {
+  fa_qscale wq, wk, wv, wo, w_gate, w_up, w_down;
+} fa_pi05_qscales;
+
 /* MolmoAct2 action-expert weights (benchmarks/molmoact2/eval_numerics.py:77-100 names), stacked
  * over the L blocks, [out][in] row-major: self_attn.qkv, self_attn.out_proj, cross_attn.q_proj,
  * cross_attn.out_proj, mlp.{gate,up,down}_proj (+ biases), action_embed, final_layer.linear. */
@@ -127,6 +142,14 @@ FA_API fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int device,
  * set with fa_set_modulation, as the reference's launch() receives them precomputed
  * (src/pi05/binding.cpp:31). Synchronous. Replaces HybridPi05._pack_weights. */
 FA_API fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt);
+
+/* Quantised pi0.5 GEMM weights (fmt FA_WFMT_FP8 or FA_WFMT_NVFP4; see fa_qscale): the seven
+ * GEMM tensors of `w` carry the codes (their dtype field is ignored), `s` their scales; the other
+ * fields as for fa_pi05_load_weights. The engine dequantises them once, on the device, into its
+ * bf16 streaming layout (value = code x scale, exact for FP8 and for the E2M1 x E4M3 product),
+ * so a quantised model runs the bf16 kernel with the quantised model's numerics; the weight
+ * stream itself stays bf16. Replaces the FP8 branch of HybridPi05._pack_weights. */
+FA_API fa_status fa_pi05_load_weights_q(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt, const fa_pi05_qscales* s);
 
 /* MolmoAct2: packs the weights (bf16 GEMM weights, fp32 biases). Synchronous. The
  * modulations are an input of this model (the model's own modulation cache, which the reference

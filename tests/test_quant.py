@@ -1,0 +1,95 @@
+"""Quantised pi0.5 weights (FP8 per-row E4M3, NVFP4 E2M1 with E4M3 block scales).
+
+CPU: the quantisers in oracle/quant.py round-trip within the formats' resolution.
+GPU: the engine loaded through fa_pi05_load_weights_q must match the fp32 oracle run on the
+DEQUANTISED weights at the bf16 bar (max-abs 2e-2); the quantisation error itself (against the
+unquantised fp32 and bf16 references) is measured on BASELINE config C4 (prefix 1736, bs=1) and
+bounded by the stated tolerances below (FP8 0.1, NVFP4 0.3 max-abs on the action chunk)."""
+import pytest
+import torch
+
+from oracle import pi05_oracle as O
+from oracle import quant as Q
+from tests.pi05_util import err
+
+GEMM = ["wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"]
+TOL_FP8_VS_FP32 = 0.1
+TOL_NVFP4_VS_FP32 = 0.3
+
+
+def test_fp8_roundtrip_cpu():
+    w = torch.randn(2, 64, 256, generator=torch.Generator().manual_seed(1)) * 0.02
+    c, s = Q.fp8_rowwise(w)
+    d = Q.fp8_dequant(c, s)
+    # E4M3 has 3 mantissa bits: relative rounding error <= 2^-4 of each value (plus subnormals)
+    assert ((d - w).abs() <= w.abs() * 2 ** -4 + s[..., None] * 2 ** -9).all()
+    assert (d.abs().amax(-1) - w.abs().amax(-1)).abs().max() < 1e-6  # row max is representable
+
+
+def test_nvfp4_roundtrip_cpu():
+    w = torch.randn(2, 32, 128, generator=torch.Generator().manual_seed(2)) * 0.02
+    p, bs, ts = Q.nvfp4(w)
+    assert p.shape == (2, 32, 64) and bs.shape == (2, 32, 8) and ts.shape == (2,)
+    d = Q.nvfp4_dequant(p, bs, ts)
+    scale = (bs.view(torch.float8_e4m3fn).float() * ts[:, None, None]).repeat_interleave(16, -1)
+    # E2M1 spacing is at most 2 (between 4 and 6) in units of the block scale; nearest rounding
+    assert ((d - w).abs() <= scale * 1.0 + 1e-7).all()
+    assert (d / scale.clamp(min=1e-30)).abs().max() <= 6.0 + 1e-5
+
+
+def _quantise(case, fmt):
+    w = dict(case.w)
+    qs, deq = {}, {}
+    for n in GEMM:
+        if fmt == "fp8":
+            c, s = Q.fp8_rowwise(case.w[n])
+            w[n], qs[n], deq[n] = c, s, Q.fp8_dequant(c, s)
+        else:
+            p, bs, ts = Q.nvfp4(case.w[n])
+            w[n], qs[n], deq[n] = p, (bs, ts), Q.nvfp4_dequant(p, bs, ts)
+    return w, qs, deq
+
+
+def _run(case, fmt):
+    from flashact_b200 import Pi05ActionExpert
+    w, qs, deq = _quantise(case, fmt)
+    eng = Pi05ActionExpert(w, num_layers=case.L, horizon=case.T, action_dim=case.AD, max_prefix=case.Lp,
+                           max_batch=case.B, num_steps=case.num_steps, wfmt=fmt, qscales=qs)
+    eng.bind_prefix_kv(case.k.to(torch.bfloat16).cuda(), case.v.to(torch.bfloat16).cuda(), case.valid_len)
+    out = eng.sample_actions(case.noise.cuda()).cpu()
+    eng.close()
+    return out, deq
+
+
+def _oracle(case, weights=None, weight_dtype=torch.float32):
+    c2 = O.Pi05Case(**{**case.__dict__})
+    c2.w = {**case.w, **(weights or {})}
+    c2.k, c2.v = case.k.to(torch.bfloat16).float(), case.v.to(torch.bfloat16).float()
+    return O.denoise(c2, weight_dtype=weight_dtype)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp8", "nvfp4"])
+def test_quantised_engine_matches_dequantised_oracle(require_gpu, fmt):
+    c = O.make_case(seed=61, L=2, T=50, AD=32, Lp=300, B=1, num_steps=3)
+    out, deq = _run(c, fmt)
+    mx, cos = err(out, _oracle(c, deq))
+    print(f"{fmt} engine vs fp32 oracle on the dequantised weights: max_abs={mx:.4g} cos={cos:.7f}")
+    assert mx < 2e-2 and cos > 0.9999, (mx, cos)
+
+
+@pytest.mark.gpu
+def test_c4_quantisation_error(require_gpu):
+    """prefix 1736 (6 x 256 image + 200 text), bs=1, 10 steps; the FP8 and
+    NVFP4 action chunks against the unquantised fp32 and bf16 references."""
+    c = O.make_case(seed=7, L=18, T=50, AD=32, Lp=1736, B=1, num_steps=10)
+    ref32 = _oracle(c)
+    ref16 = _oracle(c, weight_dtype=torch.bfloat16)
+    res = {}
+    for fmt in ("fp8", "nvfp4"):
+        out, _ = _run(c, fmt)
+        res[fmt] = (err(out, ref32), err(out, ref16))
+        print(f"C4 {fmt}: vs fp32 max_abs={res[fmt][0][0]:.4g} cos={res[fmt][0][1]:.6f}; "
+              f"vs bf16 max_abs={res[fmt][1][0]:.4g} cos={res[fmt][1][1]:.6f}")
+    assert res["fp8"][0][0] < TOL_FP8_VS_FP32
+    assert res["nvfp4"][0][0] < TOL_NVFP4_VS_FP32
