@@ -21,8 +21,8 @@ constexpr int F = 3072;      // SiLU-gated MLP hidden
 constexpr int QKV_ROWS = 3 * D;
 constexpr int MOD = 3 * D;   // scale | shift | gate of one norm
 constexpr int TMAX = 32;     // action tokens per observation (padded)
-constexpr int KC = 128;      // context keys per cross-attention chunk
-constexpr int MAX_CH = 32;   // context chunks per observation (context <= 4096 tokens)
+constexpr int KC = 32;       // context keys per cross-attention chunk (one key per lane)
+constexpr int MAX_CH = 128;  // context chunks per observation (context <= 4096 tokens)
 constexpr int kMinWork = 64 * 1024;  // every CTA keeps this much work area for the vector stages
 
 enum Mat : int { MAT_QKV = 0, MAT_SO, MAT_CQ, MAT_CO, MAT_GU, MAT_DN, NUM_MATS };

@@ -258,16 +258,18 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
 }
 
 // ------------------------------------------------------------------ cross-attention (warps 2-5)
-// Unit = (observation b, head h, context chunk c of 128 keys). q = RMS-normalised cross query
-// of head h (mk_ma2.cu:398-422); scores over the chunk's valid keys, scale 1/sqrt(96); the
-// chunk's normalised output and (max, sum) go to opart / oml for stage_merge.
+// Unit = (observation b, head h, context chunk c of 32 keys). q = RMS-normalised cross query of
+// head h (mk_ma2.cu:398-422); scores over the chunk's valid keys, scale 1/sqrt(96); the chunk's
+// normalised output and (max, sum) go to opart / oml for stage_merge. Lane j of every warp owns
+// key j (its 96-dim row in registers); warp w owns tokens w, w + 4, ...: a token's 32 scores sit
+// in one warp, so its max and sum are warp reductions.
 __device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, int l, float* sm) {
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   const int T = p.T;
-  float* qs = sm;                                                  // [32][96], pre-scaled
-  float* ps = qs + TMAX * HD;                                      // [32][129]
-  float* wred = ps + TMAX * 129;                                   // [4][32] warp partials
-  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(wred + 4 * TMAX);  // [128][96]
+  float* qs = sm;                                                  // [32][96], normed, pre-scaled
+  float* ps = qs + TMAX * HD;                                      // [32][33] probabilities
+  float* rinv = ps + TMAX * 33;                                    // [32] 1 / row sum
+  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(rinv + TMAX);  // [32][96] V chunk
   const float qscale = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 units
   for (int u = 0; u < c.acnt; ++u) {
     const AttnUnit au = c.au[u];
@@ -275,29 +277,27 @@ __device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, 
     const int lk = p.ctx_len[b];
     const int nvalid = min(KC, lk - ch * KC);
     const size_t krow0 = ((size_t)(b * p.L + l) * p.LKPAD + ch * KC);
-    {  // Q rows (T x 12 pieces) and the V chunk (128 x 12 pieces), all loads issued first
-      uint4 qraw[3], vraw[12];
+    float kr[HD];
+    {  // Q rows (T x 12 pieces), the V chunk (32 x 12) and this lane's key row: loads first
+      uint4 qraw[3], vraw[3], kraw[12];
 #pragma unroll
       for (int it = 0; it < 3; ++it) {
         const int idx = e + it * 128;
         if (idx < T * 12)
           qraw[it] = __ldg(reinterpret_cast<const uint4*>(p.qc + (size_t)(b * T + idx / 12) * D + h * HD) + idx % 12);
-      }
-#pragma unroll
-      for (int it = 0; it < 12; ++it) {
-        const int idx = e + it * 128;
         vraw[it] = __ldg(reinterpret_cast<const uint4*>(p.vctx + (krow0 + idx / 12) * D + h * HD) + idx % 12);
       }
+      const uint4* ksrc = reinterpret_cast<const uint4*>(p.kctx + (krow0 + lane) * D + h * HD);
+#pragma unroll
+      for (int s8 = 0; s8 < 12; ++s8) kraw[s8] = __ldg(ksrc + s8);
 #pragma unroll
       for (int it = 0; it < 3; ++it) {
         const int idx = e + it * 128;
         if (idx < T * 12) bf16x8_to_f32(qraw[it], qs + (idx / 12) * HD + (idx % 12) * 8);
-      }
-#pragma unroll
-      for (int it = 0; it < 12; ++it) {
-        const int idx = e + it * 128;
         *reinterpret_cast<uint4*>(vs + (idx / 12) * HD + (idx % 12) * 8) = vraw[it];
       }
+#pragma unroll
+      for (int s8 = 0; s8 < 12; ++s8) bf16x8_to_f32(kraw[s8], kr + s8 * 8);
     }
     sync_epi();
     for (int t = wq; t < T; t += 4) {  // per-head RMS of the query, then fold in the scale
@@ -309,64 +309,40 @@ __device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, 
       rp[lane + 64] = a2 * r;
     }
     sync_epi();
-    // scores: thread = key e of the chunk, its 96-dim key row in registers
-    float kr[HD];
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(p.kctx + (krow0 + e) * D + h * HD);
-#pragma unroll
-      for (int s8 = 0; s8 < HD / 8; ++s8) {
-        const uint4 raw = __ldg(src + s8);
-        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = __bfloat1622float2(b2[q]);
-          kr[s8 * 8 + 2 * q] = f.x;
-          kr[s8 * 8 + 2 * q + 1] = f.y;
-        }
-      }
-    }
-    const bool valid = e < nvalid;
+    const bool valid = lane < nvalid;
 #pragma unroll 1
-    for (int t = 0; t < T; ++t) {
-      float acc = 0.f;
+    for (int t = wq; t < T; t += 4) {  // scores, max, probabilities, sum of token t (one warp)
+      const float4* q4 = reinterpret_cast<const float4*>(qs + t * HD);
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int d = 0; d < HD; ++d) acc = fmaf(qs[t * HD + d], kr[d], acc);
-      const float s = valid ? acc : -INFINITY;
-      ps[t * 129 + e] = s;
-      const float wm = warp_max(s);
-      if (lane == 0) wred[wq * TMAX + t] = wm;
-    }
-    sync_epi();
-    // probabilities and row sums (max over the 4 warps' partials)
-    for (int t = wq; t < T; t += 4) {
-      const float m = fmaxf(fmaxf(wred[t], wred[TMAX + t]), fmaxf(wred[2 * TMAX + t], wred[3 * TMAX + t]));
-      float sum = 0.f;
-      for (int j = lane; j < KC; j += 32) {
-        const float s = ps[t * 129 + j];
-        const float pj = (j < nvalid) ? fast_exp2(s - m) : 0.f;
-        ps[t * 129 + j] = pj;
-        sum += pj;
+      for (int d4 = 0; d4 < HD / 4; ++d4) {
+        const float4 q = q4[d4];
+        a4[d4 & 3] = fmaf(q.x, kr[4 * d4], fmaf(q.y, kr[4 * d4 + 1], fmaf(q.z, kr[4 * d4 + 2], fmaf(q.w, kr[4 * d4 + 3], a4[d4 & 3]))));
       }
-      sum = warp_sum(sum);
+      const float s = valid ? (a4[0] + a4[1]) + (a4[2] + a4[3]) : -INFINITY;
+      const float m = warp_max(s);
+      const float pj = valid ? fast_exp2(s - m) : 0.f;
+      const float sum = warp_sum(pj);
+      ps[t * 33 + lane] = pj;
       if (lane == 0) {
         const size_t o = (((size_t)(b * H + h) * MAX_CH + ch) * TMAX + t) * 2;
         p.oml[o] = nvalid > 0 ? m : -INFINITY;
         p.oml[o + 1] = sum;
-        qs[t * HD] = sum > 0.f ? 1.f / sum : 0.f;  // reuse q row 0 slot: q is no longer needed
+        rinv[t] = sum > 0.f ? 1.f / sum : 0.f;
       }
     }
     sync_epi();
-    // O = P V over the chunk: thread = (3 tokens, 8 dims), 24 accumulators, one 16-byte V row
-    // piece and 3 probabilities per key
+    // O = P V over the chunk: thread = (3 tokens, 8 dims), 24 accumulators
     if (e < 12 * ((T + 2) / 3)) {
       const int d8 = e % 12, tg = (e / 12) * 3;
       float acc[3][8] = {};
+#pragma unroll 4
       for (int j = 0; j < KC; ++j) {
         float vv[8];
         bf16x8_to_f32(*reinterpret_cast<const uint4*>(vs + j * HD + d8 * 8), vv);
 #pragma unroll
         for (int q = 0; q < 3; ++q) {
-          const float pj = tg + q < T ? ps[(tg + q) * 129 + j] : 0.f;
+          const float pj = tg + q < T ? ps[(tg + q) * 33 + j] : 0.f;
 #pragma unroll
           for (int k = 0; k < 8; ++k) acc[q][k] = fmaf(pj, vv[k], acc[q][k]);
         }
@@ -375,7 +351,7 @@ __device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, 
       for (int q = 0; q < 3; ++q) {
         const int t = tg + q;
         if (t >= T) continue;
-        const float inv = qs[t * HD];
+        const float inv = rinv[t];
         uint32_t w4[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -391,25 +367,46 @@ __device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, 
 }
 
 // Merge of the context chunks per (token, head): out = sum_c w_c O_c / sum_c w_c,
-// w_c = 2^(m_c - M) l_c. One warp per (token, head); lane c holds chunk c's (max, sum).
+// w_c = 2^(m_c - M) l_c. One warp per (token, head); lane j holds chunks j, j + 32, ...
 __device__ __forceinline__ void stage_merge(const Params& p) {
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
+  constexpr int kPer = MAX_CH / 32;
   for (int item = blockIdx.x * 4 + wq; item < p.NT * H; item += gridDim.x * 4) {
     const int n = item / H, h = item % H;
     const int b = tok_b(p, n), t = n - b * p.T;
     const int nch = (p.ctx_len[b] + KC - 1) / KC;
     const size_t base = (size_t)(b * H + h) * MAX_CH;
-    float2 ml = make_float2(-INFINITY, 0.f);
-    if (lane < nch) ml = __ldcg(reinterpret_cast<const float2*>(p.oml + ((base + lane) * TMAX + t) * 2));
-    const float M = warp_max(ml.x);
-    const float w_own = (lane < nch && ml.y > 0.f) ? fast_exp2(ml.x - M) * ml.y : 0.f;
-    const float wsum = warp_sum(w_own);
-    float acc[3] = {0.f, 0.f, 0.f};
-    for (int cidx = 0; cidx < nch; ++cidx) {
-      const float wgt = __shfl_sync(0xffffffffu, w_own, cidx);
-      const __nv_bfloat16* src = p.opart + ((base + cidx) * TMAX + t) * HD;
+    float2 ml[kPer];
+    float mloc = -INFINITY;
 #pragma unroll
-      for (int k = 0; k < 3; ++k) acc[k] += wgt * __bfloat162float(__ldcg(src + lane + 32 * k));
+    for (int g = 0; g < kPer; ++g) {
+      const int cidx = lane + 32 * g;
+      ml[g] = cidx < nch ? __ldcg(reinterpret_cast<const float2*>(p.oml + ((base + cidx) * TMAX + t) * 2))
+                         : make_float2(-INFINITY, 0.f);
+      mloc = fmaxf(mloc, ml[g].x);
+    }
+    const float M = warp_max(mloc);
+    float w_own[kPer], wloc = 0.f;
+#pragma unroll
+    for (int g = 0; g < kPer; ++g) {
+      w_own[g] = ml[g].y > 0.f ? fast_exp2(ml[g].x - M) * ml[g].y : 0.f;
+      wloc += w_own[g];
+    }
+    const float wsum = warp_sum(wloc);
+    float acc[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+    for (int g = 0; g < kPer; ++g) {
+      if (32 * g >= nch) break;
+#pragma unroll 4
+      for (int j = 0; j < 32; ++j) {
+        const int cidx = 32 * g + j;
+        const float wgt = __shfl_sync(0xffffffffu, w_own[g], j);
+        if (cidx < nch) {
+          const __nv_bfloat16* src = p.opart + ((base + cidx) * TMAX + t) * HD;
+#pragma unroll
+          for (int k = 0; k < 3; ++k) acc[k] += wgt * __bfloat162float(__ldcg(src + lane + 32 * k));
+        }
+      }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
