@@ -181,7 +181,9 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
   float* vs = ks + TMAX * 97;      // [32][96]
   float* qs = vs + TMAX * 96;      // [8][97]
   float* ps = qs + kSelfQ * 97;    // [8][33]
+  float* rc = ps + kSelfQ * 33;    // [T][48] RoPE cos, then [T][48] sin
   const float scale = 0.10206207261596577f;  // 1/sqrt(96)
+  const int T48 = T * 48;
   for (int u = blockIdx.x; u < p.B * H * ngroups; u += gridDim.x) {
     const int b = u / (H * ngroups), h = (u / ngroups) % H, g = u % ngroups;
     const int t0 = g * kSelfQ, nq = min(kSelfQ, T - t0);
@@ -197,6 +199,10 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
         const int t = row < T ? row : (row < 2 * T ? row - T : t0 + row - 2 * T);
         raw[it] = __ldg(reinterpret_cast<const uint4*>(p.qkv + (size_t)(b * T + t) * QKV_ROWS + sec * D + h * HD) + seg);
       }
+    }
+    for (int i = e; i < T48 / 4; i += 128) {  // RoPE tables into shared memory (loads in flight with the rows')
+      reinterpret_cast<float4*>(rc)[i] = __ldg(reinterpret_cast<const float4*>(p.rope_cos) + i);
+      reinterpret_cast<float4*>(rc + T48)[i] = __ldg(reinterpret_cast<const float4*>(p.rope_sin) + i);
     }
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
@@ -220,7 +226,7 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
     for (int idx = e; idx < (T + nq) * 48; idx += 128) {  // half-split RoPE
       const int row = idx / 48, i = idx % 48, t = row < T ? row : t0 + row - T;
       float* rp = row < T ? ks + row * 97 : qs + (row - T) * 97;
-      const float c = p.rope_cos[t * 48 + i], sn = p.rope_sin[t * 48 + i];
+      const float c = rc[t * 48 + i], sn = rc[T48 + t * 48 + i];
       const float x1 = rp[i], x2 = rp[i + 48];
       rp[i] = x1 * c - x2 * sn;
       rp[i + 48] = x1 * sn + x2 * c;
@@ -397,7 +403,7 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
 #pragma unroll
     for (int g = 0; g < kPer; ++g) {
       if (32 * g >= nch) break;
-#pragma unroll 4
+#pragma unroll 8
       for (int j = 0; j < 32; ++j) {
         const int cidx = 32 * g + j;
         const float wgt = __shfl_sync(0xffffffffu, w_own[g], j);
