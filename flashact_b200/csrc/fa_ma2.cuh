@@ -65,11 +65,10 @@ struct Params {
   // state / scratch
   float* x_t;                 // [NT][AD]
   float* x;                   // [NPAD][768]
-  float* part;                // [12][NPAD][768] K-split partials
+  float* part;                // [12][NPAD][768] K-split partials (self-out, cross-q, cross-out, down)
   __nv_bfloat16* xn;          // [NPAD][768]
   __nv_bfloat16* qkv;         // [NPAD][2304] self-attention q | k | v (+bias)
   __nv_bfloat16* sattn;       // [NPAD][768]
-  __nv_bfloat16* qc;          // [NPAD][768] cross-attention queries (+bias, before the head norm)
   __nv_bfloat16* cattn;       // [NPAD][768]
   __nv_bfloat16* hbuf;        // [NPAD][3072]
   __nv_bfloat16* opart;       // [B][8][MAX_CH][TMAX][96] per-chunk normalised cross-attention output

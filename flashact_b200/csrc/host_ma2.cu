@@ -19,7 +19,7 @@ struct Ma2State {
   float *mods = nullptr, *mod_final = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
   float *w_ain = nullptr, *b_ain = nullptr, *w_aout = nullptr, *b_aout = nullptr;
   float *x_t = nullptr, *x = nullptr, *part = nullptr, *oml = nullptr;
-  bf16 *xn = nullptr, *qkv = nullptr, *sattn = nullptr, *qc = nullptr, *cattn = nullptr, *hbuf = nullptr;
+  bf16 *xn = nullptr, *qkv = nullptr, *sattn = nullptr, *cattn = nullptr, *hbuf = nullptr;
   bf16 *opart = nullptr, *kctx = nullptr, *vctx = nullptr, *aout_bf16 = nullptr;
   int* d_ctx = nullptr;
   GemmUnit* d_gunits = nullptr;
@@ -28,8 +28,8 @@ struct Ma2State {
   size_t gcap = 0, acap = 0;
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LKPAD = 0, adim = 0;
   int wg = 4;  // weight atoms per ring slot
-  int split[M::NUM_MATS] = {1, 3, 1, 3, 1, 6};
-  int split_eff[M::NUM_MATS] = {1, 3, 1, 3, 1, 6};  // K-splits used for the bound batch
+  int split[M::NUM_MATS] = {1, 3, 3, 3, 1, 6};
+  int split_eff[M::NUM_MATS] = {1, 3, 3, 3, 1, 6};  // K-splits used for the bound batch
   std::vector<int> ctx;
   bool weights = false, mods_set = false, bound = false;
 };
@@ -94,7 +94,6 @@ fa_status ma2_create(const fa_config& c, int device, fa_handle* h) {
   ALLOC(s->xn, (size_t)NPADm * M::D);
   ALLOC(s->qkv, (size_t)NPADm * M::QKV_ROWS);
   ALLOC(s->sattn, (size_t)NPADm * M::D);
-  ALLOC(s->qc, (size_t)NPADm * M::D);
   ALLOC(s->cattn, (size_t)NPADm * M::D);
   ALLOC(s->hbuf, (size_t)NPADm * M::F);
   ALLOC(s->opart, (size_t)MB * M::H * M::MAX_CH * M::TMAX * M::HD);
@@ -345,7 +344,7 @@ static fa_status ma2_params(fa_handle* h) {
   p.b_up = s->b_up;
   p.w_ain = s->w_ain; p.b_ain = s->b_ain; p.w_aout = s->w_aout; p.b_aout = s->b_aout;
   p.kctx = s->kctx; p.vctx = s->vctx;
-  p.x_t = s->x_t; p.x = s->x; p.part = s->part; p.xn = s->xn; p.qkv = s->qkv; p.sattn = s->sattn; p.qc = s->qc;
+  p.x_t = s->x_t; p.x = s->x; p.part = s->part; p.xn = s->xn; p.qkv = s->qkv; p.sattn = s->sattn;
   p.cattn = s->cattn; p.hbuf = s->hbuf; p.opart = s->opart; p.oml = s->oml;
   p.bar = h->ctrl; p.err = reinterpret_cast<int*>(h->ctrl + 1);
   ma2_set_debug(h);

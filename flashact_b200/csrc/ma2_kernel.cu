@@ -284,22 +284,45 @@ __device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, 
     const int nvalid = min(KC, lk - ch * KC);
     const size_t krow0 = ((size_t)(b * p.L + l) * p.LKPAD + ch * KC);
     float kr[HD];
-    {  // Q rows (T x 12 pieces), the V chunk (32 x 12) and this lane's key row: loads first
-      uint4 qraw[3], vraw[3], kraw[12];
+    {  // the V chunk (32 x 12 pieces), this lane's key row and the cross query (the K-split
+       // partials of the cross-q projection, bias on split 0, summed in split order): loads first
+      uint4 vraw[3], kraw[12];
 #pragma unroll
       for (int it = 0; it < 3; ++it) {
         const int idx = e + it * 128;
-        if (idx < T * 12)
-          qraw[it] = __ldg(reinterpret_cast<const uint4*>(p.qc + (size_t)(b * T + idx / 12) * D + h * HD) + idx % 12);
         vraw[it] = __ldg(reinterpret_cast<const uint4*>(p.vctx + (krow0 + idx / 12) * D + h * HD) + idx % 12);
       }
       const uint4* ksrc = reinterpret_cast<const uint4*>(p.kctx + (krow0 + lane) * D + h * HD);
 #pragma unroll
       for (int s8 = 0; s8 < 12; ++s8) kraw[s8] = __ldg(ksrc + s8);
+      const int nsq = p.split[MAT_CQ];
+      float4 qa[6];  // T rows x 24 float4 pieces, <= 6 per thread; one round trip per split
+#pragma unroll
+      for (int it = 0; it < 6; ++it) {
+        const int idx = e + it * 128;
+        if (idx < T * 24)
+          qa[it] = __ldcg(reinterpret_cast<const float4*>(p.part + (size_t)(b * T + idx / 24) * D + h * HD + (idx % 24) * 4));
+      }
+#pragma unroll 1
+      for (int sp = 1; sp < nsq; ++sp) {
+#pragma unroll
+        for (int it = 0; it < 6; ++it) {
+          const int idx = e + it * 128;
+          if (idx < T * 24) {
+            const float4 bq = __ldcg(reinterpret_cast<const float4*>(
+                p.part + ((size_t)sp * p.NPAD + b * T + idx / 24) * D + h * HD + (idx % 24) * 4));
+            qa[it].x += bq.x; qa[it].y += bq.y; qa[it].z += bq.z; qa[it].w += bq.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < 6; ++it) {
+        const int idx = e + it * 128;
+        if (idx < T * 24) *reinterpret_cast<float4*>(qs + (idx / 24) * HD + (idx % 24) * 4) = qa[it];
+      }
 #pragma unroll
       for (int it = 0; it < 3; ++it) {
         const int idx = e + it * 128;
-        if (idx < T * 12) bf16x8_to_f32(qraw[it], qs + (idx / 12) * HD + (idx % 12) * 8);
         *reinterpret_cast<uint4*>(vs + (idx / 12) * HD + (idx % 12) * 8) = vraw[it];
       }
 #pragma unroll
@@ -425,7 +448,6 @@ struct Ma2Epi {
   int NT, NPAD;
   uint8_t* stage;
   __nv_bfloat16* qkv;
-  __nv_bfloat16* qc;
   __nv_bfloat16* hbuf;
   float* part;
   const float* bias[NUM_MATS];  // this layer's bias of each matrix (gate bias for MAT_GU)
@@ -448,16 +470,16 @@ struct Ma2Model {
     return st[m];
   }
   __device__ static void epi_load(Epi& e, const Params& p, const Ctx& c, int l) {
-    e.NT = p.NT; e.NPAD = p.NPAD; e.stage = c.stage; e.qkv = p.qkv; e.qc = p.qc; e.hbuf = p.hbuf; e.part = p.part;
+    e.NT = p.NT; e.NPAD = p.NPAD; e.stage = c.stage; e.qkv = p.qkv; e.hbuf = p.hbuf; e.part = p.part;
 #pragma unroll
     for (int m = 0; m < NUM_MATS; ++m) e.bias[m] = p.bias[m] + (size_t)l * (m == MAT_GU ? F : (m == MAT_QKV ? QKV_ROWS : D));
     e.b_up = p.b_up + (size_t)l * F;
   }
-  __device__ static bool staged(int m, const GemmUnit&) { return m == MAT_QKV || m == MAT_CQ || m == MAT_GU; }
+  __device__ static bool staged(int m, const GemmUnit&) { return m == MAT_QKV || m == MAT_GU; }
   // 16 tokens (nb..nb+15) of accumulator row `row` of unit gu (mk_ma2.cu:224-251 epilogues).
   __device__ static void epi_tile(const Epi& e, const GemmUnit& gu, int m, int qd, int lane, int row, int nb,
                                   int nb0, const float* v) {
-    if (m == MAT_QKV || m == MAT_CQ) {  // + bias, bf16, staged as [token][128 rows]
+    if (m == MAT_QKV) {  // + bias, bf16, staged as [token][128 rows]
       const float bias = e.bias[m][gu.mtile * 128 + row];
       __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(e.stage) + (nb - nb0) * 128 + row;
 #pragma unroll
@@ -475,7 +497,7 @@ struct Ma2Model {
 #pragma unroll
         for (int k = 0; k < 16; ++k) st[k * 64] = __float2bfloat16(gu_v[k] / (1.f + __expf(-gu_v[k])) * up[k]);
       }
-    } else {  // self-out / cross-out / down: fp32 K-split partial, bias carried by split 0
+    } else {  // self-out / cross-q / cross-out / down: fp32 K-split partial, bias carried by split 0
       const float bias = gu.split == 0 ? e.bias[m][gu.mtile * 128 + row] : 0.f;
       float* dst = e.part + ((size_t)gu.split * e.NPAD + nb) * D + gu.mtile * 128 + row;
 #pragma unroll
@@ -492,9 +514,9 @@ struct Ma2Model {
         *reinterpret_cast<uint4*>(e.hbuf + (size_t)n * F + 64 * gu.mtile + seg * 8) =
             *reinterpret_cast<const uint4*>(e.stage + t * 128 + seg * 16);
       }
-    } else {  // 64 tokens x 256 B into qkv [NPAD][2304] or qc [NPAD][768]
-      __nv_bfloat16* out = m == MAT_QKV ? e.qkv : e.qc;
-      const int stride = m == MAT_QKV ? QKV_ROWS : D;
+    } else {  // 64 tokens x 256 B into qkv [NPAD][2304]
+      __nv_bfloat16* out = e.qkv;
+      const int stride = QKV_ROWS;
       for (int it = t_; it < (r1 - r0) * 16; it += 128) {
         const int t = r0 + (it >> 4), seg = it & 15, n = nb0 + t;
         if (n >= e.NT) continue;
