@@ -207,8 +207,12 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
         const int rows = Model::rows(m);
         for (int u = 0; ok && u < gcnt[m]; ++u) {
           const GemmUnit gu = gul[m][u];
+          // half-row units: 64-row boxes of 2 x wg atoms (the same slot bytes)
+          const int aps = gu.half ? 2 * wg : wg;
+          const int map = gu.half ? Model::wmap_half(m) : Model::wmap(m);
+          const int row0 = l * rows + gu.mtile * 128 + (gu.half == 2 ? 64 : 0);
 #pragma unroll 1
-          for (int j = 0; j < gu.natoms; j += wg, ++it) {
+          for (int j = 0; j < gu.natoms; j += aps, ++it) {
               const int slot = it % R, round = it / R;
               if (round > 0 && !mbar_wait(&bars->wempty[slot], (round - 1) & 1, err, KERR_PRODUCER)) {
                 ok = false;
@@ -222,8 +226,7 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
                 }
 #endif
                 mbar_expect_tx(&bars->wfull[slot], slot_bytes);
-                tma_load_3d(ring + (size_t)slot * slot_bytes, maps + Model::wmap(m), &bars->wfull[slot], 0,
-                            l * rows + gu.mtile * 128, gu.katom0 + j, pol);
+                tma_load_3d(ring + (size_t)slot * slot_bytes, maps + map, &bars->wfull[slot], 0, row0, gu.katom0 + j, pol);
               }
               __syncwarp();
             }
@@ -301,7 +304,8 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
       const int nt = min(k.TG, k.tiles - g * k.TG);
       // K atoms per activation batch: whole activation boxes (the host sizes the area for one)
       // (and whole weight slots: both granules are powers of two, so their max is a multiple of each)
-      const int gran = max(k.box_atoms, k.wg);
+      const int aps = gu.half ? 2 * k.wg : k.wg;  // weight atoms per ring slot
+      const int gran = max(k.box_atoms, aps);
       const int per_batch = max(gran, (k.batoms / nt) / gran * gran);
       int j1 = min((int)gu.natoms, per_batch);
       if (u == 0 && g == 0) FA_ONE(trace_mark(13));
@@ -316,8 +320,11 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
         if (!mbar_wait(&bars->bfull, st.bload & 1, k.err, KERR_MMA)) return false;
         ++st.bload;
         if (u == 0 && g == 0 && j0 == 0) FA_ONE(trace_mark(kTrMmaB0));
-        #pragma unroll 1
-        for (int j = j0; j < j1; j += k.wg) {  // one ring slot = wg weight atoms
+                // A operand of atom jj: a 128-row SW128 tile (16 KB); a half-row unit's 64-row atoms are
+        // 8 KB apart, so rows 64..127 of each MMA read the next atom (results ignored)
+        const uint32_t astride = gu.half ? kAtomBytes / 2 : kAtomBytes;
+#pragma unroll 1
+        for (int j = j0; j < j1; j += aps) {  // one ring slot = aps weight atoms
           const int wslot = st.wit % k.R;
           if (!mbar_wait(&bars->wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
           if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(kTrMmaW0));
@@ -326,8 +333,8 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
           if (u == 0 && g == 0 && j == 12) FA_ONE(trace_mark(11));
           if (leader()) {
             #pragma unroll 1
-            for (int jj = 0; jj < k.wg; ++jj) {
-              const uint64_t da = sdesc_sw128(k.ring + ((size_t)wslot * k.wg + jj) * kAtomBytes);
+            for (int jj = 0; jj < aps; ++jj) {
+              const uint64_t da = sdesc_sw128(k.ring + (size_t)wslot * k.wg * kAtomBytes + (size_t)jj * astride);
               #pragma unroll 1
               for (int i = 0; i < nt; ++i) {
                 const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j + jj - j0)) * tile);
@@ -375,7 +382,6 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
 template <class Model>
 __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
-  const int row = qd * 32 + lane;
   const int NTILE = p.NTILE, TG = p.TG, tiles = p.NPAD / p.NTILE;
   int* const err = p.err;
   Bars* const bars = c.bars;
@@ -387,6 +393,11 @@ __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, co
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
     const bool staged = Model::staged(m, gu);
+    // half-row units: the 64 valid rows sit in TMEM lanes 0..63 (quadrants 0, 1); they are the
+    // tile's rows 64 (half - 1) + 0..63, i.e. quadrants qd + 2 (half - 1) of a full tile
+    const bool active = gu.half == 0 || qd < 2;
+    const int qd_e = gu.half == 2 ? qd + 2 : qd;
+    const int row_e = qd_e * 32 + lane;
     {
       const int g = gu.grp;
       const int nchunks = min(TG, tiles - g * TG) * NTILE / 16;
@@ -398,11 +409,11 @@ __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, co
         const int c0 = sub * 4, c1 = min(nchunks, sub * 4 + 4);
         const int nb0 = tok0 + sub * 64;
 #pragma unroll 1
-        for (int q = c0; q < c1; ++q) {
+        for (int q = c0; q < c1 && active; ++q) {
           float v[16];
           tmem_ld16(taddr + a * 256 + q * 16, v);
           tc_wait_ld();
-          Model::epi_tile(e, gu, m, qd, lane, row, tok0 + q * 16, nb0, v);
+          Model::epi_tile(e, gu, m, qd_e, lane, row_e, tok0 + q * 16, nb0, v);
         }
         if (staged) {
           sync_epi();

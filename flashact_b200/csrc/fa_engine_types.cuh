@@ -33,6 +33,9 @@ struct GemmUnit {
   uint16_t natoms;  // K atoms in this unit
   uint16_t split;   // index of the fp32 partial slice it writes (K-split stages)
   uint16_t grp;     // token group: token tiles [grp * TG, grp * TG + TG) (one TMEM accumulator)
+  uint16_t half;    // 0: all 128 rows of the tile; 1 / 2: rows [0, 64) / [64, 128) only (the
+                    // weight stream of one SM halves; the MMA stays M = 128, rows 64..127 of its
+                    // result are ignored)
 };
 struct AttnUnit {
   uint16_t b, hp, chunk, is_suffix;  // observation, head (pair), key chunk, action-token chunk flag

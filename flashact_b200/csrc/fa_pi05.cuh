@@ -29,6 +29,7 @@ enum Mat : int { MAT_QKV = 0, MAT_O = 1, MAT_GU = 2, MAT_DN = 3 };
 enum Map : int {
   MAP_W_QKV = 0, MAP_W_O, MAP_W_GU, MAP_W_DN,  // weights, box {64, 128}
   MAP_XN, MAP_ATTN, MAP_H,                     // activations, 3D box {64, NTILE, box_atoms}
+  MAP_W_QKV_H, MAP_W_GU_H,                     // 64-row weight boxes of the half-row units
   MAP_Q, MAP_K, MAP_VT, MAP_SK, MAP_SVT,       // attention operands, 3D boxes of whole tiles
   NUM_MAPS
 };

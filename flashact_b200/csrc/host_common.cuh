@@ -40,6 +40,7 @@ struct fa_handle {
   int bmax_bytes = 64 * 1024;  // activation-area cap of a GEMM CTA
   int ring_max = 12;           // weight-ring depth cap
   int wg = 4;                  // weight atoms per ring slot (bound batch)
+  bool half_units = true;      // 64-row QKV / gate-up units at one token tile
   // bound batch
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LPAD = 0;
   std::vector<int> valid_len;

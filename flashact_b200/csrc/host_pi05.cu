@@ -172,6 +172,7 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   if (const char* e = getenv("FA_SPLIT_O")) h->split_o = pow2(std::max(1, std::min(8, atoi(e))));
   if (const char* e = getenv("FA_SPLIT_DN")) h->split_dn = pow2(std::max(1, std::min(8, atoi(e))));
   if (const char* e = getenv("FA_RING_MAX")) h->ring_max = std::max(2, atoi(e));
+  if (const char* e = getenv("FA_HALF_UNITS")) h->half_units = atoi(e) != 0;
   if (const char* e = getenv("FA_BMAX_KB")) h->bmax_bytes = std::max(8, std::min(128, atoi(e))) * 1024;
   if (const char* e = getenv("FA_ATTN_PENALTY")) h->attn_penalty = std::max(0, atoi(e));
   auto bad = [&](fa_status st) { g_create_err = h->err; fa_destroy(h); return st; };
@@ -427,6 +428,9 @@ extern "C" fa_status fa_set_modulation(fa_handle* h, const float* mods, const fl
 // K atoms per activation TMA load (32 KB boxes).
 static int act_box_atoms(const fa_handle* h) { return h->NTILE == 64 ? 4 : 2; }
 
+// 64-row units for QKV and gate/up while the bound batch is one 64-token tile.
+static bool use_half_units(const fa_handle* h) { return h->half_units && h->NTILE == 64 && h->ngroups == 1; }
+
 static fa_status build_plan(fa_handle* h) {
   const int nblk = h->num_sms;
   std::vector<AttnUnit> au;
@@ -470,18 +474,22 @@ static fa_status build_plan(fa_handle* h) {
     const int m = order[oi];
     const Spec& s = spec[m];
     const int per_split = s.katoms / s.split;
+    // QKV and gate/up at one 64-token tile: 64-row units (each SM streams half a tile, which its
+    // weight ring holds whole; RoPE / GeGLU partners stay in one unit)
+    const int halves = (use_half_units(h) && (m == MAT_QKV || m == MAT_GU)) ? 2 : 1;
     std::vector<int> cnt(nblk, 0);
     for (int g = 0; g < h->ngroups; ++g)
       for (int mt = 0; mt < s.mtiles; ++mt)
-        for (int sp = 0; sp < s.split; ++sp) {
-          int best = 0;
-          for (int i = 1; i < nblk; ++i)
-            if (cnt[i] < cnt[best] || (cnt[i] == cnt[best] && load[i] < load[best])) best = i;
-          per[best * 4 + m].push_back(
-              {(uint16_t)mt, (uint16_t)(sp * per_split), (uint16_t)per_split, (uint16_t)sp, (uint16_t)g});
-          cnt[best]++;
-          load[best] += per_split * std::min(h->TG, h->NPAD / h->NTILE - g * h->TG);
-        }
+        for (int hf = 0; hf < halves; ++hf)
+          for (int sp = 0; sp < s.split; ++sp) {
+            int best = 0;
+            for (int i = 1; i < nblk; ++i)
+              if (cnt[i] < cnt[best] || (cnt[i] == cnt[best] && load[i] < load[best])) best = i;
+            per[best * 4 + m].push_back({(uint16_t)mt, (uint16_t)(sp * per_split), (uint16_t)per_split, (uint16_t)sp,
+                                         (uint16_t)g, (uint16_t)(halves == 2 ? hf + 1 : 0)});
+            cnt[best]++;
+            load[best] += per_split * std::min(h->TG, h->NPAD / h->NTILE - g * h->TG) / halves;
+          }
   }
   std::vector<GemmUnit> gu;
   const int tile = h->NTILE * 128;
@@ -498,7 +506,7 @@ static fa_status build_plan(fa_handle* h) {
                   plans[i].a_cnt);
     // Capped so that the weight ring stays deep (larger K ranges load in several batches).
     bb = std::min(bb, std::min(std::min(kMaxBBytes, h->bmax_bytes), kMaxBAtoms * tile));
-    bb = std::max(bb, tile * ntg * std::max(act_box_atoms(h), h->wg));  // one activation box and weight slot per token tile
+    bb = std::max(bb, tile * ntg * std::max(act_box_atoms(h), use_half_units(h) ? 2 * h->wg : h->wg));  // one activation box and weight slot per token tile
     const int work = plans[i].a_cnt > 0 ? kAttnWork : bb + 16 * 1024;  // + epilogue staging
     // Attention CTAs keep their activation area inside the Q region (first 64 KB) so that the
     // prefix-K prefetch into the K/V area survives the GEMM stages in between.
@@ -539,6 +547,9 @@ static fa_status build_params(fa_handle* h) {
   MAPW(MAP_W_GU, h->w_gu, D, (uint64_t)L * 2 * F);
   MAPW(MAP_W_DN, h->w_dn, F, (uint64_t)L * D);
 #undef MAPW
+  // half-row units: 64-row boxes of 2 x wg atoms (one ring slot)
+  if ((st = make_map3(h, &p.maps[MAP_W_QKV_H], h->w_qkv, D, (uint64_t)L * QKV_ROWS, 64, 2 * h->wg)) != FA_OK) return st;
+  if ((st = make_map3(h, &p.maps[MAP_W_GU_H], h->w_gu, D, (uint64_t)L * 2 * F, 64, 2 * h->wg)) != FA_OK) return st;
   const uint32_t ba = (uint32_t)act_box_atoms(h);
 #define MAP3(i, base, K, rows, br, bat) if ((st = make_map3(h, &p.maps[i], base, K, rows, br, bat)) != FA_OK) return st
   MAP3(MAP_XN, h->xn, D, h->NPAD, h->NTILE, ba);

@@ -462,6 +462,7 @@ struct Ma2Model {
   static constexpr int kMats = NUM_MATS;  // QKV, self-out, cross-q, cross-out, gate/up, down
   __device__ static int rows(int m) { return mat_rows(m); }
   __device__ static int wmap(int m) { return MAP_W_QKV + m; }
+  __device__ static int wmap_half(int m) { return MAP_W_QKV + m; }  // no half-row units here
   __device__ static int act_map(int m) {
     return m == MAT_SO ? MAP_SATTN : m == MAT_CO ? MAP_CATTN : m == MAT_DN ? MAP_H : MAP_XN;
   }

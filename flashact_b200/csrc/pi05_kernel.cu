@@ -322,10 +322,11 @@ __device__ __forceinline__ void epi_tile(const EpiCtx& p, const GemmUnit& gu, in
 // destination (16-byte stores).
 __device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu, int m, int nb0, int r0, int r1) {
   const int e = threadIdx.x - 64;
+  // a half-row unit wrote half of the staged row: features / dims of quadrants 2 (half - 1) + {0, 1}
   if (m == MAT_GU) {  // 64 rows (tokens) x 128 B: 8 threads per row
     for (int it = e; it < (r1 - r0) * 8; it += 128) {
       const int t = r0 + (it >> 3), seg = it & 7, n = nb0 + t;
-      if (n >= p.NT) continue;
+      if (n >= p.NT || (gu.half && (seg >> 2) != gu.half - 1)) continue;
       const uint4 val = *reinterpret_cast<const uint4*>(p.stage + t * 128 + seg * 16);
       *reinterpret_cast<uint4*>(p.hbuf + (size_t)n * F + 64 * gu.mtile + seg * 8) = val;
     }
@@ -334,7 +335,7 @@ __device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu
     const int pb = mt < 16 ? (mt & 1) : mt - 16;
     for (int it = e; it < (r1 - r0) * 16; it += 128) {
       const int t = r0 + (it >> 4), seg = it & 15, n = nb0 + t;
-      if (n >= p.NT) continue;
+      if (n >= p.NT || (gu.half && ((seg & 7) >> 2) != gu.half - 1)) continue;
       const int b = tok_bi(p.invT, n), tt = n - b * p.T;
       const int dim = 64 * pb + (seg & 7) * 8 + (seg >> 3) * 128;
       __nv_bfloat16* dst = mt < 16 ? p.q + ((size_t)(b * H + (mt >> 1)) * TPAD + tt) * HD + dim
@@ -351,6 +352,7 @@ struct Pi05Model {
   static constexpr int kMats = 4;  // per layer, in consumption order: QKV, O, gate/up, down
   __device__ static int rows(int m) { return m == MAT_QKV ? QKV_ROWS : (m == MAT_GU ? 2 * F : D); }
   __device__ static int wmap(int m) { return MAP_W_QKV + m; }
+  __device__ static int wmap_half(int m) { return m == MAT_QKV ? MAP_W_QKV_H : MAP_W_GU_H; }
   __device__ static int act_map(int m) { return m == MAT_O ? MAP_ATTN : (m == MAT_DN ? MAP_H : MAP_XN); }
   __device__ static int trace_stage(int m) {
     return m == MAT_QKV ? ST_QKV : m == MAT_O ? ST_O : m == MAT_GU ? ST_GU : ST_DN;
