@@ -167,6 +167,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+
 // Shared-memory matrix descriptor for a K-major operand stored as 128-byte-swizzled atoms:
 // rows of 128 bytes (64 bf16), 8-row groups 1024 bytes apart. The atom base must be 1024-byte
 // aligned; stepping K by 16 bf16 inside an atom adds 32 bytes to the start address.
