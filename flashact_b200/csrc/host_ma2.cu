@@ -28,6 +28,7 @@ struct Ma2State {
   size_t gcap = 0, acap = 0;
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LKPAD = 0, adim = 0;
   int wg = 4;  // weight atoms per ring slot
+  int ba = 4;  // activation atoms per TMA box
   int split[M::NUM_MATS] = {1, 3, 3, 3, 1, 6};
   int split_eff[M::NUM_MATS] = {1, 3, 3, 3, 1, 6};  // K-splits used for the bound batch
   std::vector<int> ctx;
@@ -64,9 +65,15 @@ fa_status ma2_create(const fa_config& c, int device, fa_handle* h) {
   if (cudaSetDevice(device) != cudaSuccess) return fail(h, FA_ERR_CUDA, "cudaSetDevice(%d) failed", device);
   Ma2State* s = new Ma2State();
   h->ma2 = s;
-  if (const char* e = getenv("FA_MA2_SPLIT_DN")) {
-    const int v = atoi(e);
-    if (v == 1 || v == 2 || v == 3 || v == 4 || v == 6 || v == 12) s->split[M::MAT_DN] = v;
+  // Tuning knob: FA_MA2_SPLITS="qkv,so,cq,co,gu,dn" K-split factors (each must divide the
+  // matrix's K atoms: 12 for the 768-wide inputs, 48 for down; qkv and gu stay 1 -- their
+  // epilogues need whole sums).
+  if (const char* e = getenv("FA_MA2_SPLITS")) {
+    int v[M::NUM_MATS];
+    if (sscanf(e, "%d,%d,%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3], &v[4], &v[5]) == M::NUM_MATS)
+      for (int m = 0; m < M::NUM_MATS; ++m)
+        if (v[m] >= 1 && (kMatK[m] / 64) % v[m] == 0 && (m != M::MAT_QKV && m != M::MAT_GU ? true : v[m] == 1))
+          s->split[m] = v[m];
   }
   s->adim = c.valid_action_dim > 0 ? c.valid_action_dim : c.action_dim;
   const int L = c.num_layers, S = c.num_steps, MB = c.max_batch;
@@ -260,6 +267,10 @@ static fa_status ma2_plan(fa_handle* h) {
   }
   for (int m = 0; m < M::NUM_MATS; ++m)
     while ((kMatK[m] / 64 / s->split_eff[m]) % s->wg != 0) s->wg >>= 1;
+  // activation TMA box (32 KB) in K atoms, never more than divides every unit's K range
+  s->ba = s->NTILE == 64 ? 4 : 2;
+  for (int m = 0; m < M::NUM_MATS; ++m)
+    while ((kMatK[m] / 64 / s->split_eff[m]) % s->ba != 0) s->ba >>= 1;
   for (int oi = 0; oi < M::NUM_MATS; ++oi) {
     const int m = order[oi];
     const int mtiles = kMatRows[m] / 128, katoms = kMatK[m] / 64, split = s->split_eff[m], per_split = katoms / split;
@@ -289,7 +300,7 @@ static fa_status ma2_plan(fa_handle* h) {
       return fail(h, FA_ERR_INVALID, "batch too large for the per-CTA work lists (%d GEMM, %d attention units)", ng,
                   plans[i].a_cnt);
     bb = std::min(bb, std::min(fa::kMaxBBytes, fa::kMaxBAtoms * tile));
-    bb = std::max(bb, tile * ntg * std::max(s->NTILE == 64 ? 4 : 2, s->wg));  // one activation box and weight slot per token tile
+    bb = std::max(bb, tile * ntg * std::max(s->ba, s->wg));  // one activation box and weight slot per token tile
     if (plans[i].a_cnt > 0) bb = std::max(tile, std::min(bb, 64 * 1024));
     plans[i].b_bytes = bb;
     const int work = std::max(bb, M::kMinWork) + fa::kStageBytes;
@@ -326,7 +337,7 @@ static fa_status ma2_params(fa_handle* h) {
   for (int m = 0; m < M::NUM_MATS; ++m)
     if ((st = make_map3(h, &p.maps[M::MAP_W_QKV + m], s->w[m], kMatK[m], (uint64_t)L * kMatRows[m], 128, s->wg)) != FA_OK)
       return st;
-  const uint32_t ba = s->NTILE == 64 ? 4 : 2;
+  const uint32_t ba = (uint32_t)s->ba;
   if ((st = make_map3(h, &p.maps[M::MAP_XN], s->xn, M::D, s->NPAD, s->NTILE, ba)) != FA_OK) return st;
   if ((st = make_map3(h, &p.maps[M::MAP_SATTN], s->sattn, M::D, s->NPAD, s->NTILE, ba)) != FA_OK) return st;
   if ((st = make_map3(h, &p.maps[M::MAP_CATTN], s->cattn, M::D, s->NPAD, s->NTILE, ba)) != FA_OK) return st;

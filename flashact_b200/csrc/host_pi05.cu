@@ -426,7 +426,12 @@ extern "C" fa_status fa_set_modulation(fa_handle* h, const float* mods, const fl
 // CTAs in contiguous runs (same head pair -> Q reuse); each GEMM stage is then spread so that
 // no CTA holds two units of one stage before all CTAs hold one, ties broken by total bytes.
 // K atoms per activation TMA load (32 KB boxes).
-static int act_box_atoms(const fa_handle* h) { return h->NTILE == 64 ? 4 : 2; }
+// Never more than divides every unit's K range (O and down are K-split).
+static int act_box_atoms(const fa_handle* h) {
+  int ba = h->NTILE == 64 ? 4 : 2;
+  while (ba > 1 && ((QD / 64 / h->split_o_eff) % ba != 0 || (F / 64 / h->split_dn_eff) % ba != 0)) ba >>= 1;
+  return ba;
+}
 
 // 64-row units for QKV and gate/up while the bound batch is one 64-token tile.
 static bool use_half_units(const fa_handle* h) { return h->half_units && h->NTILE == 64 && h->ngroups == 1; }
