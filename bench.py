@@ -85,13 +85,16 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons, sampled every 100 ms from before the warm-up so that
+    the sampler is running when the timed region starts; summary() keeps the samples received
+    between mark_start() and mark_end() (the timed region, host clock)."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index, self.rows, self.proc = index, [], None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -108,7 +111,14 @@ class ClockSampler:
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) == 6:
-                self.rows.append(parts)
+                self.rows.append((time.monotonic(), parts))
+
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
+        time.sleep(0.15)  # the sample taken just before the end is still in the pipe
 
     def __exit__(self, *a):
         if self.proc:
@@ -119,14 +129,15 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if not self.rows:
+        rows = [r for t, r in self.rows if self.t0 is not None and self.t0 <= t <= (self.t1 or t) + 0.15]
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[2:]) if v.strip().lower() == "active"})
+        reasons = sorted({n for r in rows for n, v in zip(names, r[2:]) if v.strip().lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(self.rows[0][1]) if self.rows[0][1].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "sm_max_mhz": float(rows[0][1]) if rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
 
 
 def dist_setup():
@@ -280,6 +291,7 @@ def main():
     out_h = torch.empty_like(noise_h).pin_memory()
     stream = torch.cuda.current_stream()
 
+    clk = ClockSampler(local).__enter__()  # running before the timed region starts
     for _ in range(max(args.warmup, 3)):
         eng.sample_actions(noise_d, out_d)
 
@@ -287,16 +299,18 @@ def main():
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier(world)
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record()
-        for e0, e1 in ev:
-            e0.record()
-            eng.sample_actions(noise_d, out_d, sync=False)
-            e1.record()
-        t_end.record()
-        torch.cuda.synchronize()
+    clk.mark_start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for e0, e1 in ev:
+        e0.record()
+        eng.sample_actions(noise_d, out_d, sync=False)
+        e1.record()
+    t_end.record()
+    torch.cuda.synchronize()
+    clk.mark_end()
+    clk.__exit__()
     eng.sync()
     barrier(world)
     total_ms = max_over_ranks(t_start.elapsed_time(t_end), world, dev)
