@@ -3,6 +3,8 @@ import ctypes
 import os
 import re
 
+import pytest
+
 from flashact_b200 import _capi
 from flashact_b200.build import build
 
@@ -60,3 +62,37 @@ def test_compat_launch_signatures():
            "probs", "nblocks", "nthreads"]
     assert list(inspect.signature(compat.pi05_launch).parameters) == pi05
     assert list(inspect.signature(compat.ma2_launch).parameters) == ma2
+
+
+def _build_c_probe(tmp_path):
+    import shutil
+    import subprocess
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not available")
+    lib = os.path.join(ROOT, "flashact_b200", "_lib")
+    exe = str(tmp_path / "capi_probe")
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    os.path.join(ROOT, "tests", "c", "capi_probe.c"), "-L", lib, "-lflashact",
+                    f"-Wl,-rpath,{lib}", "-o", exe], check=True)
+    return exe
+
+
+def test_c_caller_without_gpu(tmp_path):
+    """A plain C program links libflashact.so through include/flashact.h; without a GPU,
+    fa_create returns an error status and message instead of crashing."""
+    import subprocess
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present: covered by test_c_caller_with_gpu")
+    exe = _build_c_probe(tmp_path)
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+
+
+@pytest.mark.gpu
+def test_c_caller_with_gpu(tmp_path, require_gpu):
+    """The same C program on a GPU: create succeeds, sampling before weights is FA_ERR_STATE."""
+    import subprocess
+    exe = _build_c_probe(tmp_path)
+    r = subprocess.run([exe, "gpu"], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
