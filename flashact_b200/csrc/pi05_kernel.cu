@@ -53,8 +53,10 @@ __device__ __forceinline__ void rms_store(const Params& p, int n, const float v[
 
 // Loads x[n] and folds in `nsplit` fp32 partials scaled by `gate`: x += gate * sum_s part[s]
 // (the gated residual of the previous sub-block, summed in a fixed order: deterministic).
-// All loads are issued before any use so the row costs one memory round trip.
-__device__ __forceinline__ void load_residual(const Params& p, int n, const float* gate, int nsplit, float v[8]) {
+// All loads are issued before any use so the row costs one memory round trip; the partials
+// travel by cp.async into the shared scratch `scr` (32 KB) instead of 64 registers.
+__device__ __forceinline__ void load_residual(const Params& p, int n, const float* gate, int nsplit, float v[8],
+                                              float4* scr) {
   const int e = threadIdx.x - 64;
   float4 x[2], acc[2], g[2];
 #pragma unroll
@@ -65,19 +67,20 @@ __device__ __forceinline__ void load_residual(const Params& p, int n, const floa
     g[hlf] = nsplit > 0 ? __ldg(reinterpret_cast<const float4*>(gate + d)) : acc[hlf];
   }
   if (nsplit > 0) {
-    float4 q[8][2];
 #pragma unroll
     for (int s = 0; s < 8; ++s)
 #pragma unroll
       for (int hlf = 0; hlf < 2; ++hlf)
-        if (s < nsplit)
-          q[s][hlf] = __ldcg(reinterpret_cast<const float4*>(p.part + ((size_t)s * p.NPAD + n) * D + hlf * 512 + e * 4));
+        if (s < nsplit)  // [split][half][thread]: conflict-free read-back
+          cp_async16(scr + (s * 2 + hlf) * 128 + e, p.part + ((size_t)s * p.NPAD + n) * D + hlf * 512 + e * 4);
+    cp_async_wait_all();
 #pragma unroll
     for (int s = 0; s < 8; ++s)
 #pragma unroll
       for (int hlf = 0; hlf < 2; ++hlf)
         if (s < nsplit) {
-          acc[hlf].x += q[s][hlf].x; acc[hlf].y += q[s][hlf].y; acc[hlf].z += q[s][hlf].z; acc[hlf].w += q[s][hlf].w;
+          const float4 q = scr[(s * 2 + hlf) * 128 + e];
+          acc[hlf].x += q.x; acc[hlf].y += q.y; acc[hlf].z += q.z; acc[hlf].w += q.w;
         }
 #pragma unroll
     for (int hlf = 0; hlf < 2; ++hlf) {
@@ -99,10 +102,11 @@ __device__ __forceinline__ const float* mod_ptr(const Params& p, int step, int l
 }
 
 // norm stage: x += gate * sum(partials); xn = adaRMS(x; mod). One token per CTA iteration.
-__device__ __forceinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
+__device__ __forceinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red,
+                                           float4* scr) {
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     float v[8];
-    load_residual(p, n, gate, nsplit, v);
+    load_residual(p, n, gate, nsplit, v, scr);
     if (n == (int)blockIdx.x && threadIdx.x == 64) trace_mark(9);
     rms_store(p, n, v, mod, red);
     if (n == (int)blockIdx.x && threadIdx.x == 64) trace_mark(10);
@@ -149,7 +153,7 @@ __device__ __noinline__ void stage_final(const Params& p, int step, float* xf, f
   const float* modf = p.mod_final + (size_t)step * MOD;
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     float v[8];
-    load_residual(p, n, gate, p.split_dn, v);
+    load_residual(p, n, gate, p.split_dn, v, reinterpret_cast<float4*>(xf + 2048));  // scratch after xf
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
@@ -723,8 +727,10 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
           } else if (s == 4 || !last_layer) {  // norm2 | norm1 of the next layer
             if (is_epi) {
               const bool n2 = s == 4;
+              // the partials' scratch: the first 32 KB of the work area (idle in a norm stage; on
+              // attention CTAs the Q region, clear of the prefetched K)
               stage_norm(p, (n2 ? mod_in : mod_post) + 2 * D, n2 ? p.split_o : p.split_dn,
-                         n2 ? mod_post : mod_ptr(p, step, l + 1, 0), s_red);
+                         n2 ? mod_post : mod_ptr(p, step, l + 1, 0), s_red, reinterpret_cast<float4*>(c.work));
             }
           } else if (is_epi) {
             stage_final(p, step, reinterpret_cast<float*>(c.work), s_xt, s_red);  // work area idle here
