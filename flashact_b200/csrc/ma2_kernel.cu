@@ -28,8 +28,10 @@ __device__ __forceinline__ const float* mod_ptr(const Params& p, int step, int l
 
 // ------------------------------------------------------------------ norms (warps 2-5)
 // A 768-wide row held as 6 values per thread: dims 2e + 256 k + {0, 1}, k = 0..2.
+// The partials travel by cp.async into the shared scratch `scr` ([split][3][128] float2, at most
+// 36 KB): all of them are in flight at once without holding registers.
 __device__ __forceinline__ void row_load_residual(const Params& p, int n, const float* gate, int nsplit,
-                                                  float v[6]) {
+                                                  float v[6], float2* scr) {
   const int e = threadIdx.x - 64;
   float2 x[3], acc[3], g[3];
 #pragma unroll
@@ -39,10 +41,15 @@ __device__ __forceinline__ void row_load_residual(const Params& p, int n, const 
     acc[k] = make_float2(0.f, 0.f);
     g[k] = nsplit > 0 ? __ldg(reinterpret_cast<const float2*>(gate + d)) : acc[k];
   }
-  for (int s = 0; s < nsplit; ++s) {
+  for (int s = 0; s < nsplit; ++s)
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      cp_async8(scr + (s * 3 + k) * 128 + e, p.part + ((size_t)s * p.NPAD + n) * D + 2 * e + 256 * k);
+  cp_async_wait_all();
+  for (int s = 0; s < nsplit; ++s) {  // in split order: deterministic
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      const float2 q = __ldcg(reinterpret_cast<const float2*>(p.part + ((size_t)s * p.NPAD + n) * D + 2 * e + 256 * k));
+      const float2 q = scr[(s * 3 + k) * 128 + e];
       acc[k].x += q.x;
       acc[k].y += q.y;
     }
@@ -82,10 +89,11 @@ __device__ __forceinline__ void row_rms_store(const Params& p, int n, const floa
 }
 
 // x += gate * sum_s part[s] (partials already carry the bias), xn = adaRMS(x; mod).
-__device__ __forceinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red) {
+__device__ __forceinline__ void stage_norm(const Params& p, const float* gate, int nsplit, const float* mod, float* red,
+                                           float2* scr) {
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     float v[6];
-    row_load_residual(p, n, gate, nsplit, v);
+    row_load_residual(p, n, gate, nsplit, v, scr);
     row_rms_store(p, n, v, mod, red);
   }
 }
@@ -126,7 +134,7 @@ __device__ __noinline__ void stage_final(const Params& p, int step, float* xf, f
   const float* modf = p.mod_final + (size_t)step * 2 * D;
   for (int n = blockIdx.x; n < p.NT; n += gridDim.x) {
     float v[6];
-    row_load_residual(p, n, gate, p.split[MAT_DN], v);
+    row_load_residual(p, n, gate, p.split[MAT_DN], v, reinterpret_cast<float2*>(xf + 2048));  // scratch after xf
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < 6; ++i) ss += v[i] * v[i];
@@ -652,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
               const float* gate = (s == 3 ? m_self : s == 8 ? m_cross : m_mlp) + 2 * D;
               const int ns = p.split[s == 3 ? MAT_SO : s == 8 ? MAT_CO : MAT_DN];
               const float* mod = s == 3 ? m_cross : s == 8 ? m_mlp : mod_ptr(p, step, l + 1, 0);
-              stage_norm(p, gate, ns, mod, s_red);
+              stage_norm(p, gate, ns, mod, s_red, reinterpret_cast<float2*>(vsm));  // work area idle here
             }
           } else if (is_epi) {
             stage_final(p, step, vsm, s_xt, s_red);

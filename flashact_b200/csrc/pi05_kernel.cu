@@ -211,17 +211,26 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
     const float wgt_own = (lane < nc && ml.y > 0.f) ? exp2f(ml.x - M) * ml.y : 0.f;
     const float wsum = warp_sum(wgt_own);
     float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-    for (int c = 0; c < nc; ++c) {
-      const float wgt = __shfl_sync(0xffffffffu, wgt_own, c);
-      const int cc = c < npc ? c : MAX_CH;
-      const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base + cc) * 128 + r) * HD + lane * 8));
-      const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-      const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-      const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.z));
-      const float2 f3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.w));
-      const float4 o0 = make_float4(f0.x, f0.y, f1.x, f1.y), o1 = make_float4(f2.x, f2.y, f3.x, f3.y);
-      acc0.x += wgt * o0.x; acc0.y += wgt * o0.y; acc0.z += wgt * o0.z; acc0.w += wgt * o0.w;
-      acc1.x += wgt * o1.x; acc1.y += wgt * o1.y; acc1.z += wgt * o1.z; acc1.w += wgt * o1.w;
+#pragma unroll 1
+    for (int c0 = 0; c0 < nc; c0 += 8) {  // 8 chunks' partial rows in flight at once
+      uint4 raw[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = c0 + j, cc = c < npc ? c : MAX_CH;
+        if (c < nc) raw[j] = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base + cc) * 128 + r) * HD + lane * 8));
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float wgt = __shfl_sync(0xffffffffu, wgt_own, (c0 + j) & 31);
+        if (c0 + j < nc) {
+          const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[j].x));
+          const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[j].y));
+          const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[j].z));
+          const float2 f3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[j].w));
+          acc0.x += wgt * f0.x; acc0.y += wgt * f0.y; acc0.z += wgt * f1.x; acc0.w += wgt * f1.y;
+          acc1.x += wgt * f2.x; acc1.y += wgt * f2.y; acc1.z += wgt * f3.x; acc1.w += wgt * f3.y;
+        }
+      }
     }
     const float inv = 1.f / wsum;
     __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0.x * inv, acc0.y * inv);
