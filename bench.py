@@ -46,7 +46,7 @@ MA2_KV_BYTES = 2 * MA2_L * MA2_LK * 768 * 2  # cross-attention K+V per Euler ste
 # of `bench.py [--model molmoact2] --steps 1 --warmup 3 --no-cpu-baseline` (metrics
 # dram__bytes_read.sum and dram__bytes_write.sum, -k regex:<kernel> -s 3 -c 1; summaries kept
 # under profiles/).
-NCU_TRAFFIC = {("pi05", 1): 6_249_283_072 + 5_314_560, ("molmoact2", 1): 7_736_443_136 + 3_800_064}
+NCU_TRAFFIC = {("pi05", 1): 6_252_512_512 + 5_673_216, ("molmoact2", 1): 7_739_515_904 + 3_610_112}
 
 
 def set_shape(layers, euler_steps):
