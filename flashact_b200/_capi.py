@@ -15,7 +15,8 @@ FA_KV_COMPACT_SPLIT_HALF, FA_KV_FLASHRT_INTERLEAVED = 0, 1
 # Every function the header declares (checked by tests/test_capi.py against include/flashact.h).
 EXPORTS = ["fa_create", "fa_pi05_load_weights", "fa_pi05_load_weights_q", "fa_ma2_load_weights", "fa_ma2_set_rope", "fa_set_modulation", "fa_bind_prefix_kv", "fa_bind_prefix_kv_masked", "fa_sample_actions",
            "fa_sync", "fa_set_stage_timing", "fa_get_stage_cycles", "fa_last_launch_count",
-           "fa_set_fault_injection", "fa_debug_trace", "fa_pi05_modulations_noalloc", "fa_last_error", "fa_destroy"]
+           "fa_set_fault_injection", "fa_debug_trace", "fa_pi05_modulations_noalloc", "fa_quantize_fp8_rows", "fa_quantize_nvfp4",
+           "fa_last_error", "fa_destroy"]
 
 
 class FaConfig(ctypes.Structure):
@@ -93,6 +94,8 @@ def load_library(path: str = None) -> ctypes.CDLL:
         "fa_set_fault_injection": (S, [H, I, ctypes.c_uint]),
         "fa_debug_trace": (S, [H, I, I, ctypes.POINTER(ctypes.c_ulonglong), I]),
         "fa_pi05_modulations_noalloc": (S, [ctypes.POINTER(FaPi05Weights), I, I, P, P, P]),
+        "fa_quantize_fp8_rows": (S, [P, I, I, I, I, P, P, P]),
+        "fa_quantize_nvfp4": (S, [P, I, I, I, I, P, P, P, P]),
         "fa_last_error": (ctypes.c_char_p, [H]),
         "fa_destroy": (None, [H]),
     }

@@ -11,7 +11,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIB_DIR, "libflashact.so")
-SOURCES = ["pi05_kernel.cu", "ma2_kernel.cu", "host_pi05.cu", "host_ma2.cu"]
+SOURCES = ["pi05_kernel.cu", "ma2_kernel.cu", "host_pi05.cu", "host_ma2.cu", "host_quant.cu"]
 DEPS = SOURCES + ["fa_pi05.cuh", "fa_ma2.cuh", "fa_ptx.cuh", "fa_engine.cuh", "fa_engine_types.cuh", "host_common.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",

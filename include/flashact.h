@@ -117,6 +117,23 @@ typedef struct fa_pi05_qscales {
   fa_qscale wq, wk, wv, wo, w_gate, w_up, w_down;
 } fa_pi05_qscales;
 
+/* On-device quantisation of GEMM weights into the codes fa_pi05_load_weights_q takes (the
+ * reference quantises on the host: FP8 branch of HybridPi05._pack_weights,
+ * src/pi05/hybrid_model.py:105-110). w: device [L][rows][K] in `dtype`; outputs are device
+ * memory; asynchronous on `stream`; bit-identical to the formulas below evaluated in fp32.
+ *  FP8: scale[l][r] = max(amax_k |w|, 1e-8) / 448; codes[l][r][k] = E4M3(clamp(w / scale,
+ *    -448, 448)), round to nearest even.
+ *  NVFP4 (K % 16 == 0, packed 8-byte aligned): tensor_scale[l] = max(amax_{r,k} |w| / 2688,
+ *    1e-12); block_scale[l][r][k/16] = E4M3(min(block amax / 6 / tensor_scale, 448));
+ *    x = w / (block_scale * tensor_scale) (/ 1 where that is 0); code = nearest E2M1 of
+ *    min(|x|, 6) (ties to the even code) with the sign of x (no negative zero); packed[l][r][k/2]
+ *    holds even k in the low nibble.
+ * Errors are read with fa_last_error(NULL). */
+FA_API fa_status fa_quantize_fp8_rows(const void* w, fa_dtype dtype, int L, int rows, int K, unsigned char* codes,
+                                      float* scale, fa_stream stream);
+FA_API fa_status fa_quantize_nvfp4(const void* w, fa_dtype dtype, int L, int rows, int K, unsigned char* packed,
+                                   unsigned char* block_scale, float* tensor_scale, fa_stream stream);
+
 /* MolmoAct2 action-expert weights (benchmarks/molmoact2/eval_numerics.py:77-100 names), stacked
  * over the L blocks, [out][in] row-major: self_attn.qkv, self_attn.out_proj, cross_attn.q_proj,
  * cross_attn.out_proj, mlp.{gate,up,down}_proj (+ biases), action_embed, final_layer.linear. */

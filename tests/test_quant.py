@@ -93,3 +93,64 @@ def test_c4_quantisation_error(require_gpu):
               f"vs bf16 max_abs={res[fmt][1][0]:.4g} cos={res[fmt][1][1]:.6f}")
     assert res["fp8"][0][0] < TOL_FP8_VS_FP32
     assert res["nvfp4"][0][0] < TOL_NVFP4_VS_FP32
+
+
+def _edge_weights(dtype):
+    """Two layers [2][48][256]: random rows, an all-zero row, a zero block, and (layer 1, whose
+    amax is 2688 so its tensor scale is exactly 1) a block of 6 with the E2M1 midpoints, signs and
+    negative zero, a block that saturates the E4M3 block scale at 448 and a tiny block whose
+    block scale underflows to 0."""
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(2, 48, 256, generator=g) * 0.02
+    w[0, 3] = 0.0
+    w[0, 5, 32:48] = 0.0
+    w[1] = torch.randn(48, 256, generator=g) * 0.5
+    w[1, 0, :16] = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, -0.25, -0.75, -2.5, -5.0, 0.0, -0.0,
+                                 0.5, -6.0])
+    w[1, 1, :16] = 2688.0
+    w[1, 2, :16] = 1e-4
+    return w.to(dtype)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_device_fp8_quantiser_bit_exact(require_gpu, dtype):
+    from flashact_b200.quant import quantize_fp8_rows
+    w = _edge_weights(dtype)
+    codes, scale = quantize_fp8_rows(w.cuda())
+    rc, rs = Q.fp8_rowwise(w.float())
+    assert torch.equal(scale.cpu(), rs)
+    assert torch.equal(codes.cpu(), rc)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_device_nvfp4_quantiser_bit_exact(require_gpu, dtype):
+    from flashact_b200.quant import quantize_nvfp4
+    w = _edge_weights(dtype)
+    packed, bs, ts = quantize_nvfp4(w.cuda())
+    rp, rbs, rts = Q.nvfp4(w.float())
+    assert rts[1].item() == 1.0 and rbs[1, 1, 0].item() == torch.tensor(448.0).to(torch.float8_e4m3fn).view(torch.uint8)
+    assert torch.equal(ts.cpu(), rts)
+    assert torch.equal(bs.cpu(), rbs)
+    assert torch.equal(packed.cpu(), rp)
+
+
+@pytest.mark.gpu
+def test_device_quantised_weights_load(require_gpu):
+    """Codes from the device quantisers drive fa_pi05_load_weights_q like the host ones."""
+    from flashact_b200 import Pi05ActionExpert
+    from flashact_b200.quant import quantize_fp8_rows
+    c = O.make_case(seed=62, L=2, T=50, AD=32, Lp=300, B=1, num_steps=3)
+    w = dict(c.w)
+    qs, deq = {}, {}
+    for n in GEMM:
+        codes, s = quantize_fp8_rows(c.w[n].cuda())
+        w[n], qs[n], deq[n] = codes, s, Q.fp8_dequant(codes.cpu(), s.cpu())
+    eng = Pi05ActionExpert(w, num_layers=c.L, horizon=c.T, action_dim=c.AD, max_prefix=c.Lp, max_batch=c.B,
+                           num_steps=c.num_steps, wfmt="fp8", qscales=qs)
+    eng.bind_prefix_kv(c.k.to(torch.bfloat16).cuda(), c.v.to(torch.bfloat16).cuda(), c.valid_len)
+    out = eng.sample_actions(c.noise.cuda()).cpu()
+    eng.close()
+    mx, cos = err(out, _oracle(c, deq))
+    assert mx < 2e-2 and cos > 0.9999, (mx, cos)
