@@ -2,10 +2,12 @@
 action chunks/s at bs=64 across 1-8 B200).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--model pi05|molmoact2]
-                  [--impl ours|reference]
+                  [--impl ours|reference] [--wfmt bf16|fp8] [--prefix P]
 
 Default workload: pi0.5 C1. --model molmoact2 runs C3 (configs[3]: 36 DiT
 blocks, width 768, T=30 with 6 valid action dims, 493 context tokens, 10 steps, seed 1).
+--wfmt fp8 streams the pi0.5 GEMM weights as E4M3 codes with per-row scales (
+C4, with --prefix 1736); the codes are made on the GPU by flashact_b200.quant.
 
 One "step" = one call of the public API that runs the whole 10-step x 18-layer Euler loop for
 the rank's batch (fa_sample_actions). Synthetic inputs follow BASELINE.json configs[1]
@@ -33,6 +35,8 @@ sys.path.insert(0, ROOT)
 
 L, T, AD, LP, NSTEPS = 18, 50, 32, 968, 10
 W_BYTES_BF16 = 622_854_144            # expert GEMM weights streamed per Euler step (bf16)
+PI05_ROWS = 2560 + 1024 + 8192 + 1024  # packed GEMM rows per layer (QKV, O, gate/up, down)
+W_BYTES_FP8 = W_BYTES_BF16 // 2 + L * PI05_ROWS * 4  # E4M3 codes + fp32 row scales: 312,348,672
 KV_BYTES = 2 * L * LP * 256 * 2       # prefix K+V read per Euler step per observation (bf16)
 GEMM_PARAMS = W_BYTES_BF16 // 2
 # MolmoAct2 C3: 36 blocks x (qkv 2304x768 + 3 x 768x768 + gate/up 2x3072x768 + down 768x3072) bf16
@@ -49,11 +53,17 @@ MA2_KV_BYTES = 2 * MA2_L * MA2_LK * 768 * 2  # cross-attention K+V per Euler ste
 NCU_TRAFFIC = {("pi05", 1): 6_252_512_512 + 5_673_216, ("molmoact2", 1): 7_739_515_904 + 3_610_112}
 
 
-def set_shape(layers, euler_steps):
-    """Smaller cases for profiling (--layers / --euler-steps); the defaults are the BASELINE ones."""
-    global L, NSTEPS, W_BYTES_BF16, KV_BYTES, GEMM_PARAMS, MA2_L, MA2_W_BYTES, MA2_BIAS_BYTES, MA2_KV_BYTES
+def set_shape(layers, euler_steps, prefix=0):
+    """Smaller cases for profiling (--layers / --euler-steps) and the pi0.5 prefix length
+    (--prefix); the defaults are the BASELINE ones."""
+    global L, NSTEPS, W_BYTES_BF16, W_BYTES_FP8, KV_BYTES, GEMM_PARAMS, MA2_L, MA2_W_BYTES, MA2_BIAS_BYTES, MA2_KV_BYTES
+    global LP
+    if prefix:
+        KV_BYTES = KV_BYTES // LP * prefix
+        LP = prefix
     if layers:
         W_BYTES_BF16 = W_BYTES_BF16 // L * layers
+        W_BYTES_FP8 = W_BYTES_FP8 // L * layers
         KV_BYTES = KV_BYTES // L * layers
         GEMM_PARAMS = W_BYTES_BF16 // 2
         MA2_W_BYTES = MA2_W_BYTES // MA2_L * layers
@@ -64,10 +74,10 @@ def set_shape(layers, euler_steps):
         NSTEPS = euler_steps
 
 
-def algorithmic_bytes(batch, model="pi05"):
+def algorithmic_bytes(batch, model="pi05", wfmt="bf16"):
     if model == "molmoact2":
         return NSTEPS * (MA2_W_BYTES + MA2_BIAS_BYTES + batch * MA2_KV_BYTES)
-    return NSTEPS * (W_BYTES_BF16 + batch * KV_BYTES)
+    return NSTEPS * ((W_BYTES_FP8 if wfmt == "fp8" else W_BYTES_BF16) + batch * KV_BYTES)
 
 
 def algorithmic_flops(batch):
@@ -257,8 +267,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: fewer expert layers than the config")
     ap.add_argument("--euler-steps", type=int, default=0, help="profiling only: fewer Euler steps than the config")
+    ap.add_argument("--wfmt", default="bf16", choices=["bf16", "fp8"],
+                    help="pi0.5 weight stream: bf16, or E4M3 codes + per-row scales (BASELINE C4)")
+    ap.add_argument("--prefix", type=int, default=0, help="pi0.5 prefix tokens (default 968; C4 uses 1736)")
     args = ap.parse_args()
-    set_shape(args.layers, args.euler_steps)
+    if args.model == "molmoact2" and (args.wfmt != "bf16" or args.prefix):
+        ap.error("--wfmt / --prefix apply to pi0.5 only")
+    set_shape(args.layers, args.euler_steps, args.prefix)
     if args.impl == "reference":  # host-CPU arm: rank 0 alone works, no process group needed
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
@@ -281,6 +296,12 @@ def main():
                                     valid_action_dim=case.adim, max_context=MA2_LK, max_batch=B, num_steps=NSTEPS,
                                     device=local, rope_cos=case.rope_cos, rope_sin=case.rope_sin)
         eng.bind_context(case.kctx, case.vctx, [MA2_LK] * B)
+    elif args.wfmt == "fp8":  # E4M3 codes + row scales made on the GPU (flashact_b200.quant)
+        from flashact_b200.pi05 import quantized_weights
+        w, qs = quantized_weights(case.w, dev)
+        eng = Pi05ActionExpert(w, num_layers=L, horizon=T, action_dim=AD, max_prefix=LP, max_batch=B,
+                               num_steps=NSTEPS, device=local, wfmt="fp8", qscales=qs)
+        eng.bind_prefix_kv(case.k.to(torch.bfloat16).to(dev), case.v.to(torch.bfloat16).to(dev), case.valid_len)
     else:
         eng = Pi05ActionExpert(case.w, num_layers=L, horizon=T, action_dim=AD, max_prefix=LP, max_batch=B,
                                num_steps=NSTEPS, device=local)
@@ -340,13 +361,19 @@ def main():
         gathered = gather_actions(out_d, args.global_batch)
         assert gathered.shape[0] == args.global_batch
     peak, peak_kind = measured_peaks()
-    achieved = algorithmic_bytes(B, args.model) / (ms_step * 1e-3) / 1e9
+    achieved = algorithmic_bytes(B, args.model, args.wfmt) / (ms_step * 1e-3) / 1e9
+    workload = WORKLOAD[args.model]
+    if args.prefix:
+        workload = workload.replace("prefix 968", f"prefix {LP}")
+    if args.wfmt == "fp8":
+        workload = workload.replace("configs[1] (C1)", "configs[4] (C4, FP8 E4M3 weights with per-row scales)")
     line = {
         "metric": METRICS[args.model], "value": value, "unit": "chunks/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "p50_ms": p50, "min_ms": per[0],
         "higher_is_better": True, "scaling": "strong" if args.global_batch > 0 else "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) prefix KV and noise)",
-        "config": {"workload": WORKLOAD[args.model] + (f" [profiling case: {L} layers, {NSTEPS} Euler steps]"
+        "dtype": "bf16" if args.wfmt == "bf16" else "e4m3 weights x bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) prefix KV and noise)",
+        "config": {"workload": workload + (f" [profiling case: {L} layers, {NSTEPS} Euler steps]"
                                                        if args.layers or args.euler_steps else ""),
                    "batch_per_gpu": B, "global_batch": total_batch, "parallelism": f"batch shards x{world}",
                    "l2": "no flush: the bf16 weight stream per Euler step (623 MB pi0.5, 764 MB MolmoAct2) exceeds "
@@ -356,9 +383,10 @@ def main():
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": (NCU_TRAFFIC.get((args.model, B)) if not (args.layers or args.euler_steps) else None),
-                     "algorithmic_bytes_per_launch": algorithmic_bytes(B, args.model),
-                     "note": "achieved = N x (bf16 weights + B x prefix KV) per launch / mean launch time"},
+                     "traffic": (NCU_TRAFFIC.get((args.model, B)) if not (args.layers or args.euler_steps or args.prefix
+                                                                           or args.wfmt != "bf16") else None),
+                     "algorithmic_bytes_per_launch": algorithmic_bytes(B, args.model, args.wfmt),
+                     "note": f"achieved = N x ({args.wfmt} weights + B x prefix KV) per launch / mean launch time"},
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -11,6 +11,8 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "fa_engine_types.cuh"
 #include "fa_ptx.cuh"
@@ -149,12 +151,15 @@ __device__ __forceinline__ bool leader() { return (threadIdx.x & 31) == 0; }
 // ------------------------------------------------------------------ CTA context
 struct Bars {
   uint64_t wfull[kMaxRing], wempty[kMaxRing];
+  uint64_t cfull[kMaxConv], cempty[kMaxConv];  // FP8 streaming: conversion slot written / read by the MMAs
   uint64_t bfull, bempty;  // activation batch loaded / consumed
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
 };
 struct Ctx {
-  uint8_t* ring;  // ring_slots x (wg x 16 KB)
+  uint8_t* ring;  // ring_slots x (wg x 16 KB); FP8 streaming: ring_slots x (wg x 8 KB) of E4M3 codes
+  uint8_t* conv;  // FP8 streaming: conv_slots x (wg x 16 KB) of bf16 atoms (null otherwise)
+  int conv_slots;
   uint8_t* work;  // activation atoms (GEMM) or Q | K/V | P (attention)
   Bars* bars;
   uint32_t tmem;
@@ -185,7 +190,10 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
   // re-read each weight tile shortly after one another (keep it in L2)
   const uint64_t pol = p.ngroups > 1 ? policy_evict_normal() : policy_evict_first();
   const int R = c.ring_slots, nsteps = p.nsteps, L = p.L, wg = p.wg;
-  const uint32_t slot_bytes = (uint32_t)wg * kAtomBytes;
+  // FP8 streaming: a slot holds the same K range in E4M3 (half the bytes); boxes are 128-byte
+  // rows of 128 K-values, so the K coordinate counts pairs of bf16 atoms
+  constexpr bool F8 = Model::kF8;
+  const uint32_t slot_bytes = F8 ? (uint32_t)wg * kAtomBytes / 2 : (uint32_t)wg * kAtomBytes;
   uint8_t* const ring = c.ring;
   Bars* const bars = c.bars;
   int* const err = p.err;
@@ -226,7 +234,8 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
                 }
 #endif
                 mbar_expect_tx(&bars->wfull[slot], slot_bytes);
-                tma_load_3d(ring + (size_t)slot * slot_bytes, maps + map, &bars->wfull[slot], 0, row0, gu.katom0 + j, pol);
+                tma_load_3d(ring + (size_t)slot * slot_bytes, maps + map, &bars->wfull[slot], 0, row0,
+                            F8 ? (gu.katom0 + j) >> 1 : gu.katom0 + j, pol);
               }
               __syncwarp();
             }
@@ -235,6 +244,87 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
   // Drain: never leave a TMA write into shared memory in flight at exit.
   const uint32_t first = it > (uint32_t)R ? it - R : 0;
   for (uint32_t k = first; k < it; ++k) mbar_wait(&bars->wfull[k % R], (k / R) & 1, err, KERR_PRODUCER);
+}
+
+// ------------------------------------------------------------------ warps 6, 7: FP8 -> bf16 conversion
+// Two E4M3 codes -> two bf16 (the bytes that `sel` picks from w: 0x1404 = bytes 0, 1; 0x3424 =
+// bytes 2, 3; the lower byte lands in the lower half). Exact, on the integer and bf16x2 pipes:
+// prmt places byte b at bits 8..15 of its half; sign | magnitude >> 4 is the bf16 whose value
+// is the E4M3 value x 2^-120 (E4M3 subnormals become bf16 subnormals, the same 2^-120 apart);
+// the bf16x2 multiply by 2^120 (0x7B80) rescales both exactly.
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t w, uint32_t sel) {
+  uint32_t t, out;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(t) : "r"(w), "r"(sel));
+  const uint32_t bits = ((t >> 4) & 0x07F007F0u) | (t & 0x80008000u);
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(out) : "r"(bits), "r"(0x7B807B80u));
+  return out;
+}
+
+// Walks the producer's schedule slot by slot: waits for the E4M3 slot, expands it into bf16
+// atoms of a conversion slot in the 128B-swizzled layout the MMA descriptors read, hands the
+// conversion slot to the MMA lane (cfull, one arrival per converter thread) and the E4M3 slot back to the producer
+// (wempty, likewise). The per-row scale is applied by the epilogue.
+// Slot layout: a 128-row unit's E4M3 slot is wg/2 boxes of 128 rows x 128 B (128 K each); a
+// 64-row unit's is wg boxes of 64 rows x 128 B; both expand to atoms of rows x 128 B (64 K),
+// box d -> atoms 2d (K 0..63) and 2d + 1 (K 64..127). Swizzle: 16-byte chunk c of line r sits at
+// r * 128 + ((c ^ (r & 7)) << 4) in both (1024-byte aligned boxes).
+template <class Model>
+__device__ __forceinline__ void run_converter(const typename Model::Params& p, const Ctx& c) {
+  const int t = threadIdx.x - kThreads;  // 0 .. kConvThreads - 1
+  const int R = c.ring_slots, RC = c.conv_slots, nsteps = p.nsteps, L = p.L, wg = p.wg;
+  const uint32_t fbytes = (uint32_t)wg * kAtomBytes / 2, cbytes = (uint32_t)wg * kAtomBytes;
+  const uint8_t* const ring = c.ring;
+  uint8_t* const conv = c.conv;
+  Bars* const bars = c.bars;
+  int* const err = p.err;
+  const GemmUnit* gul[Model::kMats];
+  int gcnt[Model::kMats];
+#pragma unroll
+  for (int m = 0; m < Model::kMats; ++m) { gul[m] = c.gu[m]; gcnt[m] = c.gcnt[m]; }
+  uint32_t it = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int step = 0; ok && step < nsteps; ++step)
+#pragma unroll 1
+    for (int l = 0; ok && l < L; ++l)
+#pragma unroll 1
+      for (int m = 0; ok && m < Model::kMats; ++m) {
+#pragma unroll 1
+        for (int u = 0; ok && u < gcnt[m]; ++u) {
+          const GemmUnit gu = gul[m][u];
+          const int aps = gu.half ? 2 * wg : wg;
+          const int lsh = gu.half ? 9 : 10;  // log2 of the 16-byte chunks in one box of rows x 128 B
+          const uint32_t abytes = gu.half ? 64 * 128 : 128 * 128;
+#pragma unroll 1
+          for (int j = 0; j < gu.natoms; j += aps, ++it) {
+            const int fslot = it % R, cslot = it % RC;
+            if (!mbar_wait(&bars->wfull[fslot], (it / R) & 1, err, KERR_CONV)) { ok = false; break; }
+            if (it >= (uint32_t)RC && !mbar_wait(&bars->cempty[cslot], ((it / RC) - 1) & 1, err, KERR_CONV)) {
+              ok = false;
+              break;
+            }
+            const uint8_t* src = ring + (size_t)fslot * fbytes;
+            uint8_t* dst = conv + (size_t)cslot * cbytes;
+#pragma unroll 2
+            for (int i = 0; i < wg * 512 / kConvThreads; ++i) {  // fbytes / 16 chunks over the converter threads
+              const int q = i * kConvThreads + t;
+              const int d = q >> lsh, rem = q & ((1 << lsh) - 1), r = rem >> 3, cc = rem & 7;
+              const uint4 raw = *reinterpret_cast<const uint4*>(src + d * abytes + r * 128 + ((cc ^ (r & 7)) << 4));
+              const uint4 lo = make_uint4(e4m3x2_to_bf16x2(raw.x, 0x1404), e4m3x2_to_bf16x2(raw.x, 0x3424),
+                                          e4m3x2_to_bf16x2(raw.y, 0x1404), e4m3x2_to_bf16x2(raw.y, 0x3424));
+              const uint4 hi = make_uint4(e4m3x2_to_bf16x2(raw.z, 0x1404), e4m3x2_to_bf16x2(raw.z, 0x3424),
+                                          e4m3x2_to_bf16x2(raw.w, 0x1404), e4m3x2_to_bf16x2(raw.w, 0x3424));
+              uint8_t* ab = dst + (2 * d + (cc >> 2)) * abytes + r * 128;
+              const int c0 = (cc & 3) * 2;
+              *reinterpret_cast<uint4*>(ab + ((c0 ^ (r & 7)) << 4)) = lo;
+              *reinterpret_cast<uint4*>(ab + (((c0 + 1) ^ (r & 7)) << 4)) = hi;
+            }
+            fence_proxy_async_shared();  // these generic-proxy stores feed tcgen05.mma reads
+            mbar_arrive(&bars->cfull[cslot]);
+            mbar_arrive(&bars->wempty[fslot]);
+          }
+        }
+      }
 }
 
 // ------------------------------------------------------------------ warp 1 lane 0: GEMM MMAs
@@ -286,8 +376,9 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
   FA_ONE(trace_mark(12));
   MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
   MmaCtx k;
-  k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[Model::act_map(m)];
-  k.tmem = c.tmem; k.R = c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG;
+  constexpr bool F8 = Model::kF8;
+  k.ring = F8 ? c.conv : c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[Model::act_map(m)];
+  k.tmem = c.tmem; k.R = F8 ? c.conv_slots : c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG;
   k.tiles = p.NPAD / p.NTILE;
   k.box_atoms = p.box_atoms;
   k.wg = p.wg;
@@ -296,6 +387,8 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
   const uint32_t idesc = idesc_bf16(128, k.NTILE);
   const uint32_t tile = k.NTILE * 128;
   Bars* const bars = k.bars;
+  uint64_t* const wfull = F8 ? bars->cfull : bars->wfull;  // weight slots the MMAs read
+  uint64_t* const wempty = F8 ? bars->cempty : bars->wempty;
   #pragma unroll 1
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
@@ -326,7 +419,7 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
 #pragma unroll 1
         for (int j = j0; j < j1; j += aps) {  // one ring slot = aps weight atoms
           const int wslot = st.wit % k.R;
-          if (!mbar_wait(&bars->wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
+          if (!mbar_wait(&wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
           if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(kTrMmaW0));
           if (u == 0 && g == 0 && j == 4) FA_ONE(trace_mark(9));
           if (u == 0 && g == 0 && j == 8) FA_ONE(trace_mark(10));
@@ -343,7 +436,7 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
                   tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, ((j + jj) | s) != 0);
               }
             }
-            tc_commit(&bars->wempty[wslot]);
+            tc_commit(&wempty[wslot]);
           }
           __syncwarp();
           ++st.wit;
@@ -398,6 +491,9 @@ __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, co
     const bool active = gu.half == 0 || qd < 2;
     const int qd_e = gu.half == 2 ? qd + 2 : qd;
     const int row_e = qd_e * 32 + lane;
+    // FP8 streaming: the weight row's scale (the MMAs ran on the E4M3 codes)
+    // (active rows only: an idle quadrant's row_e can lie past the matrix)
+    const float wsc = (Model::kF8 && active) ? Model::row_scale(p, m, l, gu.mtile, row_e) : 1.0f;
     {
       const int g = gu.grp;
       const int nchunks = min(TG, tiles - g * TG) * NTILE / 16;
@@ -413,6 +509,10 @@ __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, co
           float v[16];
           tmem_ld16(taddr + a * 256 + q * 16, v);
           tc_wait_ld();
+          if (Model::kF8) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) v[k] *= wsc;
+          }
           Model::epi_tile(e, gu, m, qd_e, lane, row_e, tok0 + q * 16, nb0, v);
         }
         if (staged) {

@@ -16,6 +16,16 @@ constexpr int kSmemDyn = kSmemUse + 1024;  // + alignment slack
 // in flight).
 constexpr int kMaxWG = 4;
 constexpr int kMaxRing = 12;               // weight-ring slots
+// FP8 weight streaming (pi0.5): the ring holds E4M3 tiles (half the bytes) and the converter warps (6, 7) expand
+// each slot into bf16 atoms in a second, small ring ("conversion slots") that the MMA reads.
+#ifndef FA_CONV_WARPS
+#define FA_CONV_WARPS 2
+#endif
+// Converter warps 6, 7: a 10-warp CTA would put 3 warps on one SM sub-partition and cap every
+// thread at 168 registers (spills); 8 warps keep 2 per sub-partition.
+constexpr int kConvThreads = 32 * FA_CONV_WARPS;
+constexpr int kThreadsF8 = kThreads + kConvThreads;
+constexpr int kMaxConv = 4;                // conversion slots
 constexpr int kMaxBBytes = 128 * 1024;     // activation (B operand) area of a GEMM CTA, upper bound
 constexpr int kMaxBAtoms = 16;             // activation atoms resident at once
 constexpr int kMaxGU = 48;                 // GEMM units per CTA per layer (all matrices)
@@ -44,6 +54,7 @@ struct CtaPlan {
   int g_off[kMaxMats], g_cnt[kMaxMats];  // GEMM units of this CTA per matrix, same for every layer
   int a_off, a_cnt;                      // attention units of this CTA
   int ring_slots;                        // weight-ring depth
+  int conv_slots;                        // FP8 streaming: bf16 conversion slots (0 otherwise)
   int b_bytes;                           // activation area of this CTA
 };
 
@@ -61,6 +72,6 @@ enum TraceSlot : int {
 };
 
 // Error codes written to the launch's error word.
-enum KernelError : int { KERR_BARRIER = 1, KERR_PRODUCER = 2, KERR_MMA = 3, KERR_EPI = 4, KERR_ATTN = 5 };
+enum KernelError : int { KERR_BARRIER = 1, KERR_PRODUCER = 2, KERR_MMA = 3, KERR_EPI = 4, KERR_ATTN = 5, KERR_CONV = 6 };
 
 }  // namespace fa

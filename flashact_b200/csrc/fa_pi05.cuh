@@ -76,6 +76,9 @@ struct Params {
   unsigned int* bar;             // grid-barrier counter, zeroed before each launch
   int* err;                      // 0 = ok; otherwise the first failure code
   int wg;  // weight atoms per ring slot / TMA box
+  // FP8 weight streaming: per packed weight row, its E4M3 scale, [L][rows] per matrix (QKV, O,
+  // gate/up, down); unused by the bf16 kernel
+  const float* wscale[4];
   unsigned long long* stage_ns;  // [NUM_STAGES] or null
   // host-side fault injection for tests: CTA 0 skips arriving at grid barrier number
   // `inject_barrier` (-1 = off); every grid-barrier spin gives up after `spin_limit` polls.

@@ -41,6 +41,12 @@ struct fa_handle {
   int ring_max = 12;           // weight-ring depth cap
   int wg = 4;                  // weight atoms per ring slot (bound batch)
   bool half_units = true;      // 64-row QKV / gate-up units at one token tile
+  // FP8 weight streaming (pi0.5 weights loaded as FP8 codes): E4M3 codes and per-row scales of
+  // QKV, O, gate/up, down in the packed row order; the FP8 kernel streams them
+  bool fp8_stream = false;
+  int conv_max = 3;  // FP8 streaming: cap on the bf16 conversion slots per CTA
+  unsigned char* w8[4] = {nullptr, nullptr, nullptr, nullptr};
+  float* ws8[4] = {nullptr, nullptr, nullptr, nullptr};
   // bound batch
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LPAD = 0;
   std::vector<int> valid_len;
@@ -229,6 +235,23 @@ static __global__ void pack_rows_kernel(PackSrc s, const int2* rowmap, bf16* dst
     dst[i] = __float2bfloat16(v);
   }
 }
+// FP8 streaming pack: codes dst[l][r][:] = src_{sel(r)}[l][row(r)][:] (16-byte copies) and the
+// row scales dscale[l][r] alongside.
+static __global__ void pack_codes_kernel(PackSrc s, const int2* rowmap, unsigned char* dst, float* dscale, int R, int K,
+                                         int L) {
+  const int kv = K / 16;
+  const size_t total = (size_t)L * R * kv;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int v = (int)(i % kv);
+    const size_t lr = i / kv;
+    const int r = (int)(lr % R), l = (int)(lr / R);
+    const int2 m = rowmap[r];
+    const size_t srow = (size_t)l * s.rows[m.x] + m.y;
+    *reinterpret_cast<uint4*>(dst + lr * K + v * 16) =
+        *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(s.ptr[m.x]) + srow * K + v * 16);
+    if (v == 0) dscale[lr] = reinterpret_cast<const float*>(s.scale[m.x])[srow];
+  }
+}
 static __global__ void to_f32_kernel(const void* src, int dt, float* dst, size_t n) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     dst[i] = load_as_float(src, i, dt);
@@ -280,6 +303,23 @@ static fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint6
   return FA_OK;
 }
 
+// 3D E4M3 map viewing a row-major [rows][K] byte array as [K/128][rows][128]: one box
+// {128, box_rows, box_n} lands as box_n consecutive 128B-swizzled boxes of box_rows x 128 bytes.
+static fa_status make_map3_u8(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
+                              uint32_t box_rows, uint32_t box_n) {
+  auto enc = get_encode();
+  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {128, rows, K / 128};
+  cuuint64_t strides[2] = {K, 128};
+  cuuint32_t box[3] = {128, box_rows, box_n};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled (3D, u8) failed (%d)", (int)r);
+  return FA_OK;
+}
+
 // Returns a device pointer holding `bytes` of `p` (staging host data into `tmp` when needed).
 static fa_status stage_bytes(fa_handle* h, const void* p, size_t bytes, const char* name, const void** dptr,
                              std::vector<void*>& tmp) {
@@ -306,6 +346,17 @@ static fa_status stage_tensor(fa_handle* h, const fa_tensor& t, size_t count, co
   tmp.push_back(d);
   FA_CUDA(h, cudaMemcpy(d, t.ptr, bytes, cudaMemcpyHostToDevice));
   *dptr = d;
+  return FA_OK;
+}
+
+static fa_status pack_codes(fa_handle* h, const std::vector<int2>& rowmap, PackSrc src, unsigned char* dst, float* dscale,
+                            int K, std::vector<void*>& tmp) {
+  int2* d_map = nullptr;
+  FA_CUDA(h, cudaMalloc(&d_map, rowmap.size() * sizeof(int2)));
+  tmp.push_back(d_map);
+  FA_CUDA(h, cudaMemcpy(d_map, rowmap.data(), rowmap.size() * sizeof(int2), cudaMemcpyHostToDevice));
+  pack_codes_kernel<<<h->num_sms * 8, 256>>>(src, d_map, dst, dscale, (int)rowmap.size(), K, h->cfg.num_layers);
+  FA_CUDA(h, cudaGetLastError());
   return FA_OK;
 }
 

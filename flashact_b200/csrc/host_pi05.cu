@@ -10,6 +10,7 @@ thread_local std::string g_create_err;
 namespace fa {
 namespace pi05 {
 __global__ void pi05_denoise_kernel(const __grid_constant__ Params p);
+__global__ void pi05_denoise_kernel_f8(const __grid_constant__ Params p);
 }
 }  // namespace fa
 
@@ -175,6 +176,7 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   if (const char* e = getenv("FA_HALF_UNITS")) h->half_units = atoi(e) != 0;
   if (const char* e = getenv("FA_BMAX_KB")) h->bmax_bytes = std::max(8, std::min(128, atoi(e))) * 1024;
   if (const char* e = getenv("FA_ATTN_PENALTY")) h->attn_penalty = std::max(0, atoi(e));
+  if (const char* e = getenv("FA_CONV_SLOTS")) h->conv_max = std::max(1, std::min(kMaxConv, atoi(e)));
   auto bad = [&](fa_status st) { g_create_err = h->err; fa_destroy(h); return st; };
   if (cudaSetDevice(device) != cudaSuccess) return bad(fail(h, FA_ERR_CUDA, "cudaSetDevice(%d) failed", device));
 
@@ -214,12 +216,15 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   ALLOC(stage_ns, kMaxStages);
   ALLOC(d_plans, h->num_sms);
 #undef ALLOC
-  if (cudaFuncSetAttribute(fa::pi05::pi05_denoise_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDyn) != cudaSuccess)
-    return bad(fail(h, FA_ERR_CUDA, "cannot reserve %d bytes of shared memory", kSmemDyn));
-  int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fa::pi05::pi05_denoise_kernel, kThreads, kSmemDyn) != cudaSuccess ||
-      occ < 1)
-    return bad(fail(h, FA_ERR_UNSUPPORTED, "megakernel does not fit on an SM (occupancy %d)", occ));
+  const void* kernels[2] = {(const void*)fa::pi05::pi05_denoise_kernel, (const void*)fa::pi05::pi05_denoise_kernel_f8};
+  const int threads[2] = {kThreads, kThreadsF8};
+  for (int i = 0; i < 2; ++i) {
+    if (cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDyn) != cudaSuccess)
+      return bad(fail(h, FA_ERR_CUDA, "cannot reserve %d bytes of shared memory", kSmemDyn));
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernels[i], threads[i], kSmemDyn) != cudaSuccess || occ < 1)
+      return bad(fail(h, FA_ERR_UNSUPPORTED, "megakernel %d does not fit on an SM (occupancy %d)", i, occ));
+  }
   *out = h;
   return FA_OK;
 }
@@ -246,6 +251,17 @@ static fa_status run_linear(fa_handle* h, const void* W, fa_dtype wdt, const voi
 }
 
 static fa_status load_weights_impl(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt, const fa_pi05_qscales* q);
+static fa_status build_plan(fa_handle* h);
+static fa_status build_params(fa_handle* h);
+
+// The plan and tensor maps depend on the weight format (FP8 streaming or bf16): a bound batch
+// is re-planned when weights are (re)loaded after the bind.
+static fa_status weights_loaded(fa_handle* h) {
+  h->weights_ready = true;
+  if (!h->kv_ready) return FA_OK;
+  fa_status st = build_plan(h);
+  return st != FA_OK ? st : build_params(h);
+}
 
 extern "C" fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt) {
   if (!h || !w) return fail(h, FA_ERR_INVALID, "null argument");
@@ -346,12 +362,34 @@ static fa_status load_weights_impl(fa_handle* h, const fa_pi05_weights* w, fa_wf
     }
   PackSrc s1 = {{wq, wk, wv}, {w->wq.dtype, w->wk.dtype, w->wv.dtype}, {QD, HD, HD}, qmode, {qs[0], qs[1], qs[2]},
                 {qt[0], qt[1], qt[2]}};
-  if ((st = pack_matrix(h, m1, s1, h->w_qkv, D, tmp)) != FA_OK) return st;
+  // FP8 codes are streamed as they are (the FP8 kernel; FA_FP8_STREAM=0 dequantises to bf16
+  // instead); the other formats are dequantised once into the bf16 layout.
+  const char* fs = getenv("FA_FP8_STREAM");
+  h->fp8_stream = qmode == 1 && !(fs && atoi(fs) == 0);
+  if (h->fp8_stream) {
+    const void* codes[7] = {wq, wk, wv, wo, wg, wu, wd};
+    for (const void* cp : codes)
+      if (reinterpret_cast<uintptr_t>(cp) % 16) return fail(h, FA_ERR_INVALID, "FP8 codes must be 16-byte aligned");
+    const size_t rows4[4] = {(size_t)QKV_ROWS, (size_t)D, (size_t)2 * F, (size_t)D}, k4[4] = {D, QD, D, F};
+    for (int m = 0; m < 4; ++m) {
+      if (!h->w8[m] && (st = dalloc(h, &h->w8[m], (size_t)L * rows4[m] * k4[m])) != FA_OK) return st;
+      if (!h->ws8[m] && (st = dalloc(h, &h->ws8[m], (size_t)L * rows4[m])) != FA_OK) return st;
+    }
+  }
+  if (h->fp8_stream) {
+    if ((st = pack_codes(h, m1, s1, h->w8[0], h->ws8[0], D, tmp)) != FA_OK) return st;
+  } else if ((st = pack_matrix(h, m1, s1, h->w_qkv, D, tmp)) != FA_OK) {
+    return st;
+  }
   std::vector<int2> mo(D);
   for (int r = 0; r < D; ++r) mo[r] = make_int2(0, r);
   PackSrc so = {{wo, wo, wo}, {w->wo.dtype, w->wo.dtype, w->wo.dtype}, {D, D, D}, qmode, {qs[3], qs[3], qs[3]},
                 {qt[3], qt[3], qt[3]}};
-  if ((st = pack_matrix(h, mo, so, h->w_o, QD, tmp)) != FA_OK) return st;
+  if (h->fp8_stream) {
+    if ((st = pack_codes(h, mo, so, h->w8[1], h->ws8[1], QD, tmp)) != FA_OK) return st;
+  } else if ((st = pack_matrix(h, mo, so, h->w_o, QD, tmp)) != FA_OK) {
+    return st;
+  }
   // gate/up rows: tile mt, row 32*q + lane -> feature 64*mt + 16*q + (lane & 15); lanes < 16 gate.
   std::vector<int2> m2(2 * F);
   for (int mt = 0; mt < 64; ++mt)
@@ -361,10 +399,18 @@ static fa_status load_weights_impl(fa_handle* h, const fa_pi05_weights* w, fa_wf
     }
   PackSrc s2 = {{wg, wu, wu}, {w->w_gate.dtype, w->w_up.dtype, w->w_up.dtype}, {F, F, F}, qmode, {qs[4], qs[5], qs[5]},
                 {qt[4], qt[5], qt[5]}};
-  if ((st = pack_matrix(h, m2, s2, h->w_gu, D, tmp)) != FA_OK) return st;
+  if (h->fp8_stream) {
+    if ((st = pack_codes(h, m2, s2, h->w8[2], h->ws8[2], D, tmp)) != FA_OK) return st;
+  } else if ((st = pack_matrix(h, m2, s2, h->w_gu, D, tmp)) != FA_OK) {
+    return st;
+  }
   PackSrc s3 = {{wd, wd, wd}, {w->w_down.dtype, w->w_down.dtype, w->w_down.dtype}, {D, D, D}, qmode,
                 {qs[6], qs[6], qs[6]}, {qt[6], qt[6], qt[6]}};
-  if ((st = pack_matrix(h, mo, s3, h->w_dn, F, tmp)) != FA_OK) return st;
+  if (h->fp8_stream) {
+    if ((st = pack_codes(h, mo, s3, h->w8[3], h->ws8[3], F, tmp)) != FA_OK) return st;
+  } else if ((st = pack_matrix(h, mo, s3, h->w_dn, F, tmp)) != FA_OK) {
+    return st;
+  }
 
   to_f32_kernel<<<64, 256>>>(aiw, w->ain_w.dtype, h->w_ain, (size_t)D * AD);
   to_f32_kernel<<<4, 256>>>(aib, w->ain_b.dtype, h->b_ain, D);
@@ -374,8 +420,7 @@ static fa_status load_weights_impl(fa_handle* h, const fa_pi05_weights* w, fa_wf
 
   if (!with_cond) {  // modulations come from fa_set_modulation
     FA_CUDA(h, cudaDeviceSynchronize());
-    h->weights_ready = true;
-    return FA_OK;
+    return weights_loaded(h);
   }
   // Conditioning for the fixed schedule t_s = 1 - s/N (src/pi05/hybrid_model.py:111-128):
   // cond = silu(W_out silu(W_in emb + b_in) + b_out); mods = Dense_{in,post}(cond); final = Dense_norm(cond).
@@ -405,8 +450,7 @@ static fa_status load_weights_impl(fa_handle* h, const fa_pi05_weights* w, fa_wf
   }
   if ((st = run_linear(h, nw, w->norm_w.dtype, nb, w->norm_b.dtype, cond, S, D, MOD, h->mod_final, MOD, 0)) != FA_OK) return st;
   FA_CUDA(h, cudaDeviceSynchronize());
-  h->weights_ready = true;
-  return FA_OK;
+  return weights_loaded(h);
 }
 
 extern "C" fa_status fa_set_modulation(fa_handle* h, const float* mods, const float* mod_final) {
@@ -471,6 +515,8 @@ static fa_status build_plan(fa_handle* h) {
   // more than divides every unit's K range.
   h->wg = h->NTILE == 64 ? kMaxWG : 2;
   if (const char* e = getenv("FA_WG")) h->wg = std::max(1, std::min(h->wg, atoi(e)));
+  // FP8 streaming: 2 atoms per slot (one 128 x 128-byte E4M3 box, expanded to 32 KB of bf16)
+  if (h->fp8_stream) h->wg = 2;
   for (int m = 0; m < 4; ++m)
     while ((spec[m].katoms / spec[m].split) % h->wg != 0) h->wg >>= 1;
   std::vector<std::vector<GemmUnit>> per(nblk * 4);
@@ -516,7 +562,15 @@ static fa_status build_plan(fa_handle* h) {
     // Attention CTAs keep their activation area inside the Q region (first 64 KB) so that the
     // prefix-K prefetch into the K/V area survives the GEMM stages in between.
     plans[i].b_bytes = plans[i].a_cnt > 0 ? std::max(tile, std::min(bb, 64 * 1024)) : bb;
+    plans[i].conv_slots = 0;
     plans[i].ring_slots = std::min(std::min(kMaxRing, h->ring_max), (kSmemUse - work) / (h->wg * kAtomBytes));
+    if (h->fp8_stream) {  // E4M3 slots (wg x 8 KB) + bf16 conversion slots (wg x 16 KB)
+      const int avail = kSmemUse - work, fb = h->wg * kAtomBytes / 2, cb = h->wg * kAtomBytes;
+      // as many conversion slots as leave two E4M3 slots (the converter runs ahead into idle
+      // time: slots converted before a stage starts cost the stage nothing)
+      plans[i].conv_slots = std::max(1, std::min(std::min(kMaxConv, h->conv_max), (avail - 2 * fb) / cb));
+      plans[i].ring_slots = std::min(std::min(kMaxRing, h->ring_max), (avail - plans[i].conv_slots * cb) / fb);
+    }
     if (plans[i].ring_slots < 1) return fail(h, FA_ERR_INVALID, "shared-memory plan leaves no weight ring");
     for (int m = 0; m < 4; ++m) {
       plans[i].g_off[m] = (int)gu.size();
@@ -546,15 +600,27 @@ static fa_status build_params(fa_handle* h) {
   const int L = h->cfg.num_layers, B = h->B;
   fa_status st;
   // weights: 3D boxes of wg K-atoms x 128 rows (one ring slot per load)
+  if (h->fp8_stream) {  // E4M3 boxes of 128 K-values: wg / 2 per 128-row slot, wg per 64-row slot
+#define MAPW8(i, base, K, rows, br, bn) if ((st = make_map3_u8(h, &p.maps[i], base, K, rows, br, bn)) != FA_OK) return st
+    MAPW8(MAP_W_QKV, h->w8[0], D, (uint64_t)L * QKV_ROWS, 128, h->wg / 2);
+    MAPW8(MAP_W_O, h->w8[1], QD, (uint64_t)L * D, 128, h->wg / 2);
+    MAPW8(MAP_W_GU, h->w8[2], D, (uint64_t)L * 2 * F, 128, h->wg / 2);
+    MAPW8(MAP_W_DN, h->w8[3], F, (uint64_t)L * D, 128, h->wg / 2);
+    MAPW8(MAP_W_QKV_H, h->w8[0], D, (uint64_t)L * QKV_ROWS, 64, h->wg);
+    MAPW8(MAP_W_GU_H, h->w8[2], D, (uint64_t)L * 2 * F, 64, h->wg);
+#undef MAPW8
+    for (int m = 0; m < 4; ++m) p.wscale[m] = h->ws8[m];
+  } else {
 #define MAPW(i, base, K, rows) if ((st = make_map3(h, &p.maps[i], base, K, rows, 128, h->wg)) != FA_OK) return st
-  MAPW(MAP_W_QKV, h->w_qkv, D, (uint64_t)L * QKV_ROWS);
-  MAPW(MAP_W_O, h->w_o, QD, (uint64_t)L * D);
-  MAPW(MAP_W_GU, h->w_gu, D, (uint64_t)L * 2 * F);
-  MAPW(MAP_W_DN, h->w_dn, F, (uint64_t)L * D);
+    MAPW(MAP_W_QKV, h->w_qkv, D, (uint64_t)L * QKV_ROWS);
+    MAPW(MAP_W_O, h->w_o, QD, (uint64_t)L * D);
+    MAPW(MAP_W_GU, h->w_gu, D, (uint64_t)L * 2 * F);
+    MAPW(MAP_W_DN, h->w_dn, F, (uint64_t)L * D);
 #undef MAPW
-  // half-row units: 64-row boxes of 2 x wg atoms (one ring slot)
-  if ((st = make_map3(h, &p.maps[MAP_W_QKV_H], h->w_qkv, D, (uint64_t)L * QKV_ROWS, 64, 2 * h->wg)) != FA_OK) return st;
-  if ((st = make_map3(h, &p.maps[MAP_W_GU_H], h->w_gu, D, (uint64_t)L * 2 * F, 64, 2 * h->wg)) != FA_OK) return st;
+    // half-row units: 64-row boxes of 2 x wg atoms (one ring slot)
+    if ((st = make_map3(h, &p.maps[MAP_W_QKV_H], h->w_qkv, D, (uint64_t)L * QKV_ROWS, 64, 2 * h->wg)) != FA_OK) return st;
+    if ((st = make_map3(h, &p.maps[MAP_W_GU_H], h->w_gu, D, (uint64_t)L * 2 * F, 64, 2 * h->wg)) != FA_OK) return st;
+  }
   const uint32_t ba = (uint32_t)act_box_atoms(h);
 #define MAP3(i, base, K, rows, br, bat) if ((st = make_map3(h, &p.maps[i], base, K, rows, br, bat)) != FA_OK) return st
   MAP3(MAP_XN, h->xn, D, h->NPAD, h->NTILE, ba);
@@ -688,8 +754,12 @@ extern "C" fa_status fa_sample_actions(fa_handle* h, int batch, const float* noi
   if (h->timing) FA_CUDA(h, cudaMemsetAsync(h->stage_ns, 0, NUM_STAGES * sizeof(unsigned long long), s));
   FA_CUDA(h, cudaMemcpyAsync(h->x_t, noise, bytes, cudaMemcpyDefault, s));
   void* args[] = {&p};
-  FA_CUDA(h, cudaLaunchCooperativeKernel((const void*)fa::pi05::pi05_denoise_kernel, dim3(h->num_sms), dim3(kThreads), args,
-                                         kSmemDyn, s));
+  if (h->fp8_stream)
+    FA_CUDA(h, cudaLaunchCooperativeKernel((const void*)fa::pi05::pi05_denoise_kernel_f8, dim3(h->num_sms), dim3(kThreadsF8),
+                                           args, kSmemDyn, s));
+  else
+    FA_CUDA(h, cudaLaunchCooperativeKernel((const void*)fa::pi05::pi05_denoise_kernel, dim3(h->num_sms), dim3(kThreads), args,
+                                           kSmemDyn, s));
   FA_CUDA(h, cudaMemcpyAsync(actions_out, h->x_t, bytes, cudaMemcpyDefault, s));
   h->last_launches = 1;
   return FA_OK;

@@ -468,6 +468,8 @@ struct Ma2Model {
   using Params = ma2::Params;
   using Epi = Ma2Epi;
   static constexpr int kMats = NUM_MATS;  // QKV, self-out, cross-q, cross-out, gate/up, down
+  static constexpr bool kF8 = false;       // bf16 weight stream only
+  __device__ static float row_scale(const Params&, int, int, int, int) { return 1.0f; }
   __device__ static int rows(int m) { return mat_rows(m); }
   __device__ static int wmap(int m) { return MAP_W_QKV + m; }
   __device__ static int wmap_half(int m) { return MAP_W_QKV + m; }  // no half-row units here

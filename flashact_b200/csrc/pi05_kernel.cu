@@ -363,6 +363,9 @@ struct Pi05Model {
   using Params = pi05::Params;
   using Epi = EpiCtx;
   static constexpr int kMats = 4;  // per layer, in consumption order: QKV, O, gate/up, down
+  static constexpr bool kF8 = false;
+  static constexpr int kCtaThreads = kThreads;
+  __device__ static float row_scale(const Params&, int, int, int, int) { return 1.0f; }
   __device__ static int rows(int m) { return m == MAT_QKV ? QKV_ROWS : (m == MAT_GU ? 2 * F : D); }
   __device__ static int wmap(int m) { return MAP_W_QKV + m; }
   __device__ static int wmap_half(int m) { return m == MAT_QKV ? MAP_W_QKV_H : MAP_W_GU_H; }
@@ -381,6 +384,16 @@ struct Pi05Model {
   }
   __device__ static void epi_copy_out(const Epi& e, const GemmUnit& gu, int m, int nb0, int r0, int r1) {
     pi05::epi_copy_out(e, gu, m, nb0, r0, r1);
+  }
+};
+
+// FP8 weight streaming: E4M3 tiles in the ring, expanded to bf16 by warps 6 and 7, row scales in the
+// epilogue (the reference's W8A16 scheme, src/pi05/mk6.cu:90-94,204-205,219-220).
+struct Pi05ModelF8 : Pi05Model {
+  static constexpr bool kF8 = true;
+  static constexpr int kCtaThreads = kThreadsF8;
+  __device__ static float row_scale(const Params& p, int m, int l, int mtile, int row) {
+    return __ldg(p.wscale[m] + (size_t)l * rows(m) + mtile * 128 + row);
   }
 };
 
@@ -604,7 +617,8 @@ __device__ __forceinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint
 }
 
 // ------------------------------------------------------------------ kernel
-__global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_constant__ Params p) {
+template <class Model>
+__device__ __forceinline__ void denoise_body(const Params& p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Bars bars;
   __shared__ uint32_t s_tmem;
@@ -642,8 +656,15 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   c.acnt = s_plan.a_cnt;
   c.batoms = min(kMaxBAtoms, s_plan.b_bytes / (p.NTILE * 128));
   c.ring_slots = s_plan.ring_slots;
+  c.conv_slots = s_plan.conv_slots;
   c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  c.work = c.ring + (size_t)c.ring_slots * p.wg * kAtomBytes;
+  if (Model::kF8) {  // E4M3 ring | bf16 conversion slots | work area
+    c.conv = c.ring + (size_t)c.ring_slots * p.wg * kAtomBytes / 2;
+    c.work = c.conv + (size_t)c.conv_slots * p.wg * kAtomBytes;
+  } else {
+    c.conv = nullptr;
+    c.work = c.ring + (size_t)c.ring_slots * p.wg * kAtomBytes;
+  }
   // epilogue staging: the P area on attention CTAs (idle outside the attention stage), else the
   // 16 KB after the activation area
   c.stage = s_plan.a_cnt > 0 ? c.work + kPOff : c.work + s_plan.b_bytes;
@@ -651,7 +672,9 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   }
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], 1); }
+    // E4M3 slots are released by the converter threads, bf16 slots by an MMA commit
+    for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], Model::kF8 ? kConvThreads : 1); }
+    for (int i = 0; i < kMaxConv; ++i) { mbar_init(&bars.cfull[i], kConvThreads); mbar_init(&bars.cempty[i], 1); }
     mbar_init(&bars.bfull, 1);
     mbar_init(&bars.bempty, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&bars.acc_full[i], 1); mbar_init(&bars.acc_empty[i], 128); }
@@ -673,8 +696,10 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
   __syncthreads();
 
   if (warp == 0) {
-    run_producer<Pi05Model>(p, c);
+    run_producer<Model>(p, c);
     __syncwarp();
+  } else if (warp >= 6) {  // FP8 streaming only (the bf16 kernel has 6 warps)
+    if constexpr (Model::kF8) run_converter<Model>(p, c);
   } else {
     const bool is_mma = (warp == 1);
     const bool is_epi = warp >= 2;
@@ -722,8 +747,8 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
         for (int s = 0; s < 8; ++s) {
           const int m = gemm_of(s);
           if (m >= 0) {
-            if (is_mma) mma_gemm<Pi05Model>(p, c, st, m);
-            if (is_epi) ecnt = epi_gemm<Pi05Model>(p, c, ecnt, m, l);
+            if (is_mma) mma_gemm<Model>(p, c, st, m);
+            if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l);
           } else if (s == 1) {
             if (is_mma) {
               if (leader()) st.last_q = -1;
@@ -767,6 +792,13 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
     tc_fence_after();
     tmem_dealloc(s_tmem, 512);
   }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_constant__ Params p) {
+  denoise_body<Pi05Model>(p);
+}
+__global__ void __launch_bounds__(kThreadsF8, 1) pi05_denoise_kernel_f8(const __grid_constant__ Params p) {
+  denoise_body<Pi05ModelF8>(p);
 }
 
 }  // namespace pi05

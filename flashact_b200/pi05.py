@@ -141,3 +141,17 @@ class Pi05ActionExpert:
             self.close()
         except Exception:
             pass
+
+
+QUANT_FIELDS = ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")
+
+
+def quantized_weights(weights: dict, device):
+    """The seven GEMM weights of `weights` quantised to FP8 on the GPU (flashact_b200.quant):
+    returns (weights with codes in place of those seven, qscales) for
+    Pi05ActionExpert(..., wfmt="fp8", qscales=...)."""
+    from .quant import quantize_fp8_rows
+    w, qs = dict(weights), {}
+    for n in QUANT_FIELDS:
+        w[n], qs[n] = quantize_fp8_rows(weights[n].to(device))
+    return w, qs

@@ -162,10 +162,14 @@ FA_API fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa
 
 /* Quantised pi0.5 GEMM weights (fmt FA_WFMT_FP8 or FA_WFMT_NVFP4; see fa_qscale): the seven
  * GEMM tensors of `w` carry the codes (their dtype field is ignored), `s` their scales; the other
- * fields as for fa_pi05_load_weights. The engine dequantises them once, on the device, into its
- * bf16 streaming layout (value = code x scale, exact for FP8 and for the E2M1 x E4M3 product),
- * so a quantised model runs the bf16 kernel with the quantised model's numerics; the weight
- * stream itself stays bf16. Replaces the FP8 branch of HybridPi05._pack_weights. */
+ * fields as for fa_pi05_load_weights. FP8: the codes are packed as they are and the FP8 kernel
+ * streams them (half the bytes of bf16): each E4M3 tile is expanded to bf16 in shared memory
+ * (exact) for the tensor cores and the row scale multiplies the fp32 accumulator, the
+ * reference's W8A16 scheme (src/pi05/mk6.cu:90-94,204-205,219-220); codes must be 16-byte
+ * aligned. (Environment FA_FP8_STREAM=0 at load time dequantises them into the bf16 layout
+ * instead.) NVFP4: dequantised once on the device into the bf16 layout (value = code x block
+ * scale x tensor scale, exact), so the model runs the bf16 kernel with the NVFP4 numerics.
+ * Replaces the FP8 branch of HybridPi05._pack_weights. */
 FA_API fa_status fa_pi05_load_weights_q(fa_handle* h, const fa_pi05_weights* w, fa_wfmt fmt, const fa_pi05_qscales* s);
 
 /* MolmoAct2: packs the weights (bf16 GEMM weights, fp32 biases). Synchronous. The

@@ -1,8 +1,9 @@
 """Quantised pi0.5 weights (FP8 per-row E4M3, NVFP4 E2M1 with E4M3 block scales).
 
 CPU: the quantisers in oracle/quant.py round-trip within the formats' resolution.
-GPU: the engine loaded through fa_pi05_load_weights_q must match the fp32 oracle run on the
-DEQUANTISED weights at the bf16 bar (max-abs 2e-2); the quantisation error itself (against the
+GPU: the engine loaded through fa_pi05_load_weights_q (FP8: the FP8-streaming kernel; NVFP4:
+dequantised at load) must match the fp32 oracle run on the DEQUANTISED weights at the bf16 bar
+(max-abs 2e-2); the quantisation error itself (against the
 unquantised fp32 and bf16 references) is measured on BASELINE config C4 (prefix 1736, bs=1) and
 bounded by the stated tolerances below (FP8 0.1, NVFP4 0.3 max-abs on the action chunk)."""
 import pytest
@@ -154,3 +155,22 @@ def test_device_quantised_weights_load(require_gpu):
     eng.close()
     mx, cos = err(out, _oracle(c, deq))
     assert mx < 2e-2 and cos > 0.9999, (mx, cos)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [1, 3])
+def test_fp8_stream_matches_dequantised_path(require_gpu, monkeypatch, B):
+    """The FP8-streaming kernel (E4M3 tiles expanded in shared memory, row scales in the epilogue)
+    against the same codes dequantised at load into the bf16 kernel (FA_FP8_STREAM=0) and against
+    the fp32 oracle: 64-row units at bs=1, 128-row units over two token tiles at bs=3."""
+    c = O.make_case(seed=63, L=2, T=50, AD=32, Lp=300, B=B, num_steps=2)
+    out_s, deq = _run(c, "fp8")
+    monkeypatch.setenv("FA_FP8_STREAM", "0")
+    out_d, _ = _run(c, "fp8")
+    ref = _oracle(c, deq)
+    for name, out in (("stream", out_s), ("dequant", out_d)):
+        mx, cos = err(out, ref)
+        print(f"B={B} fp8 {name}: max_abs={mx:.4g} cos={cos:.7f}")
+        assert mx < 2e-2 and cos > 0.9999, (name, mx, cos)
+    assert not torch.equal(out_s, out_d)  # two kernels (scale before vs after the MMAs)
+    assert (out_s - out_d).abs().max() < 2e-2
