@@ -78,10 +78,17 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 // Grid barrier among warps 1-5 of every CTA. `gen` counts barriers passed by this launch; the
 // counter only grows, so barrier k completes when it reaches (k+1) * gridDim.x. Bounded: on
 // timeout (or when another CTA already failed) it raises *err and returns false.
-template <class P>
-__device__ __forceinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned long long* next_tr) {
+// `overlap` runs on the epilogue warps (threads 64..191) between this CTA's arrival and the
+// end of the wait: work that depends on no other CTA, hidden behind the barrier latency.
+struct NoOverlap {
+  __device__ void operator()() const {}
+};
+template <class P, class F = NoOverlap>
+__device__ __forceinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned long long* next_tr,
+                                             const F& overlap = F()) {
   __shared__ int s_ok;
   sync_main();
+  if (threadIdx.x >= 64) overlap();
   if (threadIdx.x == 32) {
     trace_mark(kTrBarArrive);
     int ok = 1;
@@ -151,15 +158,13 @@ __device__ __forceinline__ bool leader() { return (threadIdx.x & 31) == 0; }
 // ------------------------------------------------------------------ CTA context
 struct Bars {
   uint64_t wfull[kMaxRing], wempty[kMaxRing];
-  uint64_t cfull[kMaxConv], cempty[kMaxConv];  // FP8 streaming: conversion slot written / read by the MMAs
+  uint64_t afull[kASlotsF8], aempty[kASlotsF8];  // FP8 streaming: TMEM A slot written / read by the MMAs
   uint64_t bfull, bempty;  // activation batch loaded / consumed
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
 };
 struct Ctx {
   uint8_t* ring;  // ring_slots x (wg x 16 KB); FP8 streaming: ring_slots x (wg x 8 KB) of E4M3 codes
-  uint8_t* conv;  // FP8 streaming: conv_slots x (wg x 16 KB) of bf16 atoms (null otherwise)
-  int conv_slots;
   uint8_t* work;  // activation atoms (GEMM) or Q | K/V | P (attention)
   Bars* bars;
   uint32_t tmem;
@@ -246,7 +251,7 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
   for (uint32_t k = first; k < it; ++k) mbar_wait(&bars->wfull[k % R], (k / R) & 1, err, KERR_PRODUCER);
 }
 
-// ------------------------------------------------------------------ warps 6, 7: FP8 -> bf16 conversion
+// ------------------------------------------------------------------ FP8 -> bf16 conversion (epilogue warps)
 // Two E4M3 codes -> two bf16 (the bytes that `sel` picks from w: 0x1404 = bytes 0, 1; 0x3424 =
 // bytes 2, 3; the lower byte lands in the lower half). Exact, on the integer and bf16x2 pipes:
 // prmt places byte b at bits 8..15 of its half; sign | magnitude >> 4 is the bf16 whose value
@@ -258,73 +263,6 @@ __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t w, uint32_t sel) {
   const uint32_t bits = ((t >> 4) & 0x07F007F0u) | (t & 0x80008000u);
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(out) : "r"(bits), "r"(0x7B807B80u));
   return out;
-}
-
-// Walks the producer's schedule slot by slot: waits for the E4M3 slot, expands it into bf16
-// atoms of a conversion slot in the 128B-swizzled layout the MMA descriptors read, hands the
-// conversion slot to the MMA lane (cfull, one arrival per converter thread) and the E4M3 slot back to the producer
-// (wempty, likewise). The per-row scale is applied by the epilogue.
-// Slot layout: a 128-row unit's E4M3 slot is wg/2 boxes of 128 rows x 128 B (128 K each); a
-// 64-row unit's is wg boxes of 64 rows x 128 B; both expand to atoms of rows x 128 B (64 K),
-// box d -> atoms 2d (K 0..63) and 2d + 1 (K 64..127). Swizzle: 16-byte chunk c of line r sits at
-// r * 128 + ((c ^ (r & 7)) << 4) in both (1024-byte aligned boxes).
-template <class Model>
-__device__ __forceinline__ void run_converter(const typename Model::Params& p, const Ctx& c) {
-  const int t = threadIdx.x - kThreads;  // 0 .. kConvThreads - 1
-  const int R = c.ring_slots, RC = c.conv_slots, nsteps = p.nsteps, L = p.L, wg = p.wg;
-  const uint32_t fbytes = (uint32_t)wg * kAtomBytes / 2, cbytes = (uint32_t)wg * kAtomBytes;
-  const uint8_t* const ring = c.ring;
-  uint8_t* const conv = c.conv;
-  Bars* const bars = c.bars;
-  int* const err = p.err;
-  const GemmUnit* gul[Model::kMats];
-  int gcnt[Model::kMats];
-#pragma unroll
-  for (int m = 0; m < Model::kMats; ++m) { gul[m] = c.gu[m]; gcnt[m] = c.gcnt[m]; }
-  uint32_t it = 0;
-  bool ok = true;
-#pragma unroll 1
-  for (int step = 0; ok && step < nsteps; ++step)
-#pragma unroll 1
-    for (int l = 0; ok && l < L; ++l)
-#pragma unroll 1
-      for (int m = 0; ok && m < Model::kMats; ++m) {
-#pragma unroll 1
-        for (int u = 0; ok && u < gcnt[m]; ++u) {
-          const GemmUnit gu = gul[m][u];
-          const int aps = gu.half ? 2 * wg : wg;
-          const int lsh = gu.half ? 9 : 10;  // log2 of the 16-byte chunks in one box of rows x 128 B
-          const uint32_t abytes = gu.half ? 64 * 128 : 128 * 128;
-#pragma unroll 1
-          for (int j = 0; j < gu.natoms; j += aps, ++it) {
-            const int fslot = it % R, cslot = it % RC;
-            if (!mbar_wait(&bars->wfull[fslot], (it / R) & 1, err, KERR_CONV)) { ok = false; break; }
-            if (it >= (uint32_t)RC && !mbar_wait(&bars->cempty[cslot], ((it / RC) - 1) & 1, err, KERR_CONV)) {
-              ok = false;
-              break;
-            }
-            const uint8_t* src = ring + (size_t)fslot * fbytes;
-            uint8_t* dst = conv + (size_t)cslot * cbytes;
-#pragma unroll 2
-            for (int i = 0; i < wg * 512 / kConvThreads; ++i) {  // fbytes / 16 chunks over the converter threads
-              const int q = i * kConvThreads + t;
-              const int d = q >> lsh, rem = q & ((1 << lsh) - 1), r = rem >> 3, cc = rem & 7;
-              const uint4 raw = *reinterpret_cast<const uint4*>(src + d * abytes + r * 128 + ((cc ^ (r & 7)) << 4));
-              const uint4 lo = make_uint4(e4m3x2_to_bf16x2(raw.x, 0x1404), e4m3x2_to_bf16x2(raw.x, 0x3424),
-                                          e4m3x2_to_bf16x2(raw.y, 0x1404), e4m3x2_to_bf16x2(raw.y, 0x3424));
-              const uint4 hi = make_uint4(e4m3x2_to_bf16x2(raw.z, 0x1404), e4m3x2_to_bf16x2(raw.z, 0x3424),
-                                          e4m3x2_to_bf16x2(raw.w, 0x1404), e4m3x2_to_bf16x2(raw.w, 0x3424));
-              uint8_t* ab = dst + (2 * d + (cc >> 2)) * abytes + r * 128;
-              const int c0 = (cc & 3) * 2;
-              *reinterpret_cast<uint4*>(ab + ((c0 ^ (r & 7)) << 4)) = lo;
-              *reinterpret_cast<uint4*>(ab + (((c0 + 1) ^ (r & 7)) << 4)) = hi;
-            }
-            fence_proxy_async_shared();  // these generic-proxy stores feed tcgen05.mma reads
-            mbar_arrive(&bars->cfull[cslot]);
-            mbar_arrive(&bars->wempty[fslot]);
-          }
-        }
-      }
 }
 
 // ------------------------------------------------------------------ warp 1 lane 0: GEMM MMAs
@@ -376,9 +314,9 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
   FA_ONE(trace_mark(12));
   MmaState st = st_shared;  // identical copy in every lane; lane 0 writes it back
   MmaCtx k;
-  constexpr bool F8 = Model::kF8;
-  k.ring = F8 ? c.conv : c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[Model::act_map(m)];
-  k.tmem = c.tmem; k.R = F8 ? c.conv_slots : c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG;
+  constexpr bool F8 = Model::kF8;  // A from the TMEM slots the epilogue warps fill
+  k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[Model::act_map(m)];
+  k.tmem = c.tmem; k.R = F8 ? kASlotsF8 : c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG;
   k.tiles = p.NPAD / p.NTILE;
   k.box_atoms = p.box_atoms;
   k.wg = p.wg;
@@ -387,8 +325,8 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
   const uint32_t idesc = idesc_bf16(128, k.NTILE);
   const uint32_t tile = k.NTILE * 128;
   Bars* const bars = k.bars;
-  uint64_t* const wfull = F8 ? bars->cfull : bars->wfull;  // weight slots the MMAs read
-  uint64_t* const wempty = F8 ? bars->cempty : bars->wempty;
+  uint64_t* const wfull = F8 ? bars->afull : bars->wfull;  // weight slots the MMAs read
+  uint64_t* const wempty = F8 ? bars->aempty : bars->wempty;
   #pragma unroll 1
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
@@ -407,7 +345,7 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
       const int a = st.acc & 1;
       if (st.acc >= 2 && !mbar_wait(&bars->acc_empty[a], ((st.acc >> 1) - 1) & 1, k.err, KERR_MMA)) return false;
       tc_fence_after();
-      const uint32_t tacc = k.tmem + a * 256;
+      const uint32_t tacc = k.tmem + a * (F8 ? kAccColsF8 : 256);
       #pragma unroll 1
       for (int j0 = 0; j0 < gu.natoms;) {
         if (!mbar_wait(&bars->bfull, st.bload & 1, k.err, KERR_MMA)) return false;
@@ -420,6 +358,7 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
         for (int j = j0; j < j1; j += aps) {  // one ring slot = aps weight atoms
           const int wslot = st.wit % k.R;
           if (!mbar_wait(&wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
+          if (F8) tc_fence_after();  // the slot's tcgen05.st writes precede these MMAs
           if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(kTrMmaW0));
           if (u == 0 && g == 0 && j == 4) FA_ONE(trace_mark(9));
           if (u == 0 && g == 0 && j == 8) FA_ONE(trace_mark(10));
@@ -428,12 +367,18 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
             #pragma unroll 1
             for (int jj = 0; jj < aps; ++jj) {
               const uint64_t da = sdesc_sw128(k.ring + (size_t)wslot * k.wg * kAtomBytes + (size_t)jj * astride);
+              // FP8: atom jj of the slot = 32 TMEM columns (64 K), K16 step s = 8 columns
+              const uint32_t ta = k.tmem + kAColF8 + wslot * kASlotColsF8 + jj * 32;
               #pragma unroll 1
               for (int i = 0; i < nt; ++i) {
                 const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j + jj - j0)) * tile);
 #pragma unroll
-                for (int s = 0; s < 4; ++s)
-                  tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, ((j + jj) | s) != 0);
+                for (int s = 0; s < 4; ++s) {
+                  if (F8)
+                    tc_mma_bf16_ts(tacc + i * k.NTILE, ta + 8 * s, db + 2 * s, idesc, ((j + jj) | s) != 0);
+                  else
+                    tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, ((j + jj) | s) != 0);
+                }
               }
             }
             tc_commit(&wempty[wslot]);
@@ -472,8 +417,87 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
 // (A K-split of the RoPE / GeGLU matrices with an in-stage reduction through L2 was measured
 // slower than full-K tiles at bs=1: its extra dependent L2 round trips outweigh the shorter MMA
 // chains.)
+// FP8 streaming: the epilogue warps expand one unit's E4M3 slots into the TMEM A slots, in the
+// producer's order. Thread = TMEM lane = row r of the slot's boxes (64-row units: warps of lane
+// quadrants 0, 1 only); it reads its row's 16-byte chunks (chunk c of line r at r * 128 +
+// ((c ^ (r & 7)) << 4): the 128-byte swizzle), converts 16 codes per chunk and stores a bf16 atom
+// (64 K = 32 columns) per tcgen05.st. Every thread, active or not, waits and arrives in order, so
+// the barrier phases never run ahead: wfull (slot landed) -> aempty (MMAs done with the A slot)
+// -> convert -> wempty (E4M3 slot free) -> afull (A slot written; one arrival per thread).
+struct ConvState {
+  uint32_t cit;  // E4M3 slots converted so far (the producer's slot sequence)
+  int ahead;     // slots of the coming GEMM stage converted ahead, during the barrier before it
+};
+// Converts slots [s0, s1) of unit gu.
+__device__ __forceinline__ bool convert_range(const Ctx& c, int* err, int wg, const GemmUnit& gu, int s0, int s1,
+                                              uint32_t& cit) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
+  const int R = c.ring_slots;
+  Bars* const bars = c.bars;
+  const int aps = gu.half ? 2 * wg : wg;
+  const int nbox = gu.half ? wg : wg / 2;                    // E4M3 boxes per slot (128 K each)
+  const uint32_t abytes = gu.half ? 64 * 128 : 128 * 128;    // one box of rows x 128 bytes
+  const bool active = gu.half == 0 || qd < 2;
+  const int r = qd * 32 + lane;
+  const uint32_t fbytes = (uint32_t)wg * kAtomBytes / 2;
+  const uint32_t tq = c.tmem + ((uint32_t)(qd * 32) << 16) + kAColF8;
+  (void)aps;
+#pragma unroll 1
+  for (int sl = s0; sl < s1; ++sl, ++cit) {
+    const int fslot = cit % R, aslot = cit % kASlotsF8;
+    if (!mbar_wait(&bars->wfull[fslot], (cit / R) & 1, err, KERR_EPI)) return false;
+    if (cit >= (uint32_t)kASlotsF8 && !mbar_wait(&bars->aempty[aslot], ((cit / kASlotsF8) - 1) & 1, err, KERR_EPI))
+      return false;
+    tc_fence_after();
+    if (active) {
+      const uint8_t* src = c.ring + (size_t)fslot * fbytes + r * 128;
+#pragma unroll 1
+      for (int a = 0; a < 2 * nbox; ++a) {  // bf16 atom a = box a / 2, chunks 4 (a & 1) .. + 3
+        uint32_t w[32];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int ch = 4 * (a & 1) + cc;
+          const uint4 raw = *reinterpret_cast<const uint4*>(src + (a >> 1) * abytes + ((ch ^ (r & 7)) << 4));
+          w[cc * 8 + 0] = e4m3x2_to_bf16x2(raw.x, 0x1404); w[cc * 8 + 1] = e4m3x2_to_bf16x2(raw.x, 0x3424);
+          w[cc * 8 + 2] = e4m3x2_to_bf16x2(raw.y, 0x1404); w[cc * 8 + 3] = e4m3x2_to_bf16x2(raw.y, 0x3424);
+          w[cc * 8 + 4] = e4m3x2_to_bf16x2(raw.z, 0x1404); w[cc * 8 + 5] = e4m3x2_to_bf16x2(raw.z, 0x3424);
+          w[cc * 8 + 6] = e4m3x2_to_bf16x2(raw.w, 0x1404); w[cc * 8 + 7] = e4m3x2_to_bf16x2(raw.w, 0x3424);
+        }
+        tmem_st32(tq + aslot * kASlotColsF8 + a * 32, w);
+      }
+    }
+    mbar_arrive(&bars->wempty[fslot]);
+    if (active) tc_wait_st();
+    tc_fence_before();
+    mbar_arrive(&bars->afull[aslot]);
+  }
+  return true;
+}
+
+// Converts the first slots of matrix m's units (the next GEMM stage) into the free A slots,
+// during the grid barrier before that stage. Every MMA of the stages before has completed by
+// then (their accumulators were drained), so the aempty waits do not block.
+__device__ __forceinline__ bool convert_ahead(const Ctx& c, int* err, int wg, int m, ConvState& cs) {
+  int done = cs.ahead;  // slots of this matrix already converted, from its first unit on
+#pragma unroll 1
+  for (int u = 0; u < c.gcnt[m] && cs.ahead < kASlotsF8; ++u) {
+    const GemmUnit gu = c.gu[m][u];
+    const int aps = gu.half ? 2 * wg : wg, ns = (gu.natoms + aps - 1) / aps;
+    if (done >= ns) {
+      done -= ns;
+      continue;
+    }
+    const int s1 = min(ns, done + (kASlotsF8 - cs.ahead));
+    if (!convert_range(c, err, wg, gu, done, s1, cs.cit)) return false;
+    cs.ahead += s1 - done;
+    done = 0;
+  }
+  return true;
+}
+
 template <class Model>
-__device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l) {
+__device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l,
+                                             ConvState& cs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int NTILE = p.NTILE, TG = p.TG, tiles = p.NPAD / p.NTILE;
   int* const err = p.err;
@@ -494,6 +518,12 @@ __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, co
     // FP8 streaming: the weight row's scale (the MMAs ran on the E4M3 codes)
     // (active rows only: an idle quadrant's row_e can lie past the matrix)
     const float wsc = (Model::kF8 && active) ? Model::row_scale(p, m, l, gu.mtile, row_e) : 1.0f;
+    if constexpr (Model::kF8) {  // this unit's slots not already converted ahead
+      const int aps = gu.half ? 2 * p.wg : p.wg, ns = (gu.natoms + aps - 1) / aps;
+      const int skip = min(cs.ahead, ns);
+      cs.ahead -= skip;
+      if (!convert_range(c, err, p.wg, gu, skip, ns, cs.cit)) return ecnt;
+    }
     {
       const int g = gu.grp;
       const int nchunks = min(TG, tiles - g * TG) * NTILE / 16;
@@ -507,7 +537,7 @@ __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, co
 #pragma unroll 1
         for (int q = c0; q < c1 && active; ++q) {
           float v[16];
-          tmem_ld16(taddr + a * 256 + q * 16, v);
+          tmem_ld16(taddr + a * (Model::kF8 ? kAccColsF8 : 256) + q * 16, v);
           tc_wait_ld();
           if (Model::kF8) {
 #pragma unroll

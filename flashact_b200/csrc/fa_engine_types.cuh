@@ -16,16 +16,14 @@ constexpr int kSmemDyn = kSmemUse + 1024;  // + alignment slack
 // in flight).
 constexpr int kMaxWG = 4;
 constexpr int kMaxRing = 12;               // weight-ring slots
-// FP8 weight streaming (pi0.5): the ring holds E4M3 tiles (half the bytes) and the converter warps (6, 7) expand
-// each slot into bf16 atoms in a second, small ring ("conversion slots") that the MMA reads.
-#ifndef FA_CONV_WARPS
-#define FA_CONV_WARPS 2
-#endif
-// Converter warps 6, 7: a 10-warp CTA would put 3 warps on one SM sub-partition and cap every
-// thread at 168 registers (spills); 8 warps keep 2 per sub-partition.
-constexpr int kConvThreads = 32 * FA_CONV_WARPS;
-constexpr int kThreadsF8 = kThreads + kConvThreads;
-constexpr int kMaxConv = 4;                // conversion slots
+// FP8 weight streaming (pi0.5): the ring holds E4M3 tiles (half the bytes); the epilogue warps
+// expand each slot to bf16 straight into tensor memory, where the MMAs read their A operand
+// (TMEM columns [kAColF8, 512): kASlotsF8 slots of kASlotColsF8 columns; accumulators in
+// [0, 2 x kAccColsF8)).
+constexpr int kAccColsF8 = 128;            // accumulator columns per buffer (token columns <= 128)
+constexpr int kAColF8 = 256;               // first TMEM column of the A slots
+constexpr int kASlotsF8 = 2;
+constexpr int kASlotColsF8 = 128;          // 256 K-values of bf16 (2 per 32-bit column)
 constexpr int kMaxBBytes = 128 * 1024;     // activation (B operand) area of a GEMM CTA, upper bound
 constexpr int kMaxBAtoms = 16;             // activation atoms resident at once
 constexpr int kMaxGU = 48;                 // GEMM units per CTA per layer (all matrices)
@@ -54,7 +52,6 @@ struct CtaPlan {
   int g_off[kMaxMats], g_cnt[kMaxMats];  // GEMM units of this CTA per matrix, same for every layer
   int a_off, a_cnt;                      // attention units of this CTA
   int ring_slots;                        // weight-ring depth
-  int conv_slots;                        // FP8 streaming: bf16 conversion slots (0 otherwise)
   int b_bytes;                           // activation area of this CTA
 };
 

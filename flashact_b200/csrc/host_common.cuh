@@ -44,7 +44,6 @@ struct fa_handle {
   // FP8 weight streaming (pi0.5 weights loaded as FP8 codes): E4M3 codes and per-row scales of
   // QKV, O, gate/up, down in the packed row order; the FP8 kernel streams them
   bool fp8_stream = false;
-  int conv_max = 3;  // FP8 streaming: cap on the bf16 conversion slots per CTA
   unsigned char* w8[4] = {nullptr, nullptr, nullptr, nullptr};
   float* ws8[4] = {nullptr, nullptr, nullptr, nullptr};
   // bound batch

@@ -176,7 +176,6 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   if (const char* e = getenv("FA_HALF_UNITS")) h->half_units = atoi(e) != 0;
   if (const char* e = getenv("FA_BMAX_KB")) h->bmax_bytes = std::max(8, std::min(128, atoi(e))) * 1024;
   if (const char* e = getenv("FA_ATTN_PENALTY")) h->attn_penalty = std::max(0, atoi(e));
-  if (const char* e = getenv("FA_CONV_SLOTS")) h->conv_max = std::max(1, std::min(kMaxConv, atoi(e)));
   auto bad = [&](fa_status st) { g_create_err = h->err; fa_destroy(h); return st; };
   if (cudaSetDevice(device) != cudaSuccess) return bad(fail(h, FA_ERR_CUDA, "cudaSetDevice(%d) failed", device));
 
@@ -217,7 +216,7 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   ALLOC(d_plans, h->num_sms);
 #undef ALLOC
   const void* kernels[2] = {(const void*)fa::pi05::pi05_denoise_kernel, (const void*)fa::pi05::pi05_denoise_kernel_f8};
-  const int threads[2] = {kThreads, kThreadsF8};
+  const int threads[2] = {kThreads, kThreads};
   for (int i = 0; i < 2; ++i) {
     if (cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDyn) != cudaSuccess)
       return bad(fail(h, FA_ERR_CUDA, "cannot reserve %d bytes of shared memory", kSmemDyn));
@@ -482,6 +481,10 @@ static bool use_half_units(const fa_handle* h) { return h->half_units && h->NTIL
 
 static fa_status build_plan(fa_handle* h) {
   const int nblk = h->num_sms;
+  // token tiles per group = per TMEM accumulator: 256 columns, or 128 with FP8 streaming (the
+  // upper half of TMEM holds the expanded weight slots)
+  h->TG = (h->fp8_stream ? kAccColsF8 : 256) / h->NTILE;
+  h->ngroups = (h->NPAD / h->NTILE + h->TG - 1) / h->TG;
   std::vector<AttnUnit> au;
   for (int b = 0; b < h->B; ++b) {
     const int npc = (h->valid_len[b] + KCH - 1) / KCH;
@@ -562,15 +565,9 @@ static fa_status build_plan(fa_handle* h) {
     // Attention CTAs keep their activation area inside the Q region (first 64 KB) so that the
     // prefix-K prefetch into the K/V area survives the GEMM stages in between.
     plans[i].b_bytes = plans[i].a_cnt > 0 ? std::max(tile, std::min(bb, 64 * 1024)) : bb;
-    plans[i].conv_slots = 0;
-    plans[i].ring_slots = std::min(std::min(kMaxRing, h->ring_max), (kSmemUse - work) / (h->wg * kAtomBytes));
-    if (h->fp8_stream) {  // E4M3 slots (wg x 8 KB) + bf16 conversion slots (wg x 16 KB)
-      const int avail = kSmemUse - work, fb = h->wg * kAtomBytes / 2, cb = h->wg * kAtomBytes;
-      // as many conversion slots as leave two E4M3 slots (the converter runs ahead into idle
-      // time: slots converted before a stage starts cost the stage nothing)
-      plans[i].conv_slots = std::max(1, std::min(std::min(kMaxConv, h->conv_max), (avail - 2 * fb) / cb));
-      plans[i].ring_slots = std::min(std::min(kMaxRing, h->ring_max), (avail - plans[i].conv_slots * cb) / fb);
-    }
+    // ring slots of wg atoms: bf16 (wg x 16 KB) or E4M3 (wg x 8 KB)
+    const int slot_bytes = h->fp8_stream ? h->wg * kAtomBytes / 2 : h->wg * kAtomBytes;
+    plans[i].ring_slots = std::min(std::min(kMaxRing, h->ring_max), (kSmemUse - work) / slot_bytes);
     if (plans[i].ring_slots < 1) return fail(h, FA_ERR_INVALID, "shared-memory plan leaves no weight ring");
     for (int m = 0; m < 4; ++m) {
       plans[i].g_off[m] = (int)gu.size();
@@ -610,6 +607,8 @@ static fa_status build_params(fa_handle* h) {
     MAPW8(MAP_W_GU_H, h->w8[2], D, (uint64_t)L * 2 * F, 64, h->wg);
 #undef MAPW8
     for (int m = 0; m < 4; ++m) p.wscale[m] = h->ws8[m];
+    const char* ea = getenv("FA_F8_AHEAD");
+    p.f8_ahead = !(ea && atoi(ea) == 0);
   } else {
 #define MAPW(i, base, K, rows) if ((st = make_map3(h, &p.maps[i], base, K, rows, 128, h->wg)) != FA_OK) return st
     MAPW(MAP_W_QKV, h->w_qkv, D, (uint64_t)L * QKV_ROWS);
@@ -754,12 +753,8 @@ extern "C" fa_status fa_sample_actions(fa_handle* h, int batch, const float* noi
   if (h->timing) FA_CUDA(h, cudaMemsetAsync(h->stage_ns, 0, NUM_STAGES * sizeof(unsigned long long), s));
   FA_CUDA(h, cudaMemcpyAsync(h->x_t, noise, bytes, cudaMemcpyDefault, s));
   void* args[] = {&p};
-  if (h->fp8_stream)
-    FA_CUDA(h, cudaLaunchCooperativeKernel((const void*)fa::pi05::pi05_denoise_kernel_f8, dim3(h->num_sms), dim3(kThreadsF8),
-                                           args, kSmemDyn, s));
-  else
-    FA_CUDA(h, cudaLaunchCooperativeKernel((const void*)fa::pi05::pi05_denoise_kernel, dim3(h->num_sms), dim3(kThreads), args,
-                                           kSmemDyn, s));
+  const void* kern = h->fp8_stream ? (const void*)fa::pi05::pi05_denoise_kernel_f8 : (const void*)fa::pi05::pi05_denoise_kernel;
+  FA_CUDA(h, cudaLaunchCooperativeKernel(kern, dim3(h->num_sms), dim3(kThreads), args, kSmemDyn, s));
   FA_CUDA(h, cudaMemcpyAsync(actions_out, h->x_t, bytes, cudaMemcpyDefault, s));
   h->last_launches = 1;
   return FA_OK;

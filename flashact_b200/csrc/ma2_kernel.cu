@@ -606,6 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     const bool is_epi = warp >= 2;
     MmaState& st = s_st;
     uint32_t ecnt = 0, gen = 0;
+    ConvState cs{0, 0};  // FP8 conversion state (unused by this bf16 kernel)
     uint64_t t_prev = globaltimer();
     const bool timing = p.stage_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 32;
     auto mark = [&](int s) {
@@ -650,7 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
           const int m = gemm_of(s);
           if (m >= 0) {
             if (is_mma) mma_gemm<Ma2Model>(p, c, st, m);
-            if (is_epi) ecnt = epi_gemm<Ma2Model>(p, c, ecnt, m, l);
+            if (is_epi) ecnt = epi_gemm<Ma2Model>(p, c, ecnt, m, l, cs);
           } else if (s == 1) {
             if (is_epi) stage_self_attn(p, vsm);
           } else if (s == 5) {

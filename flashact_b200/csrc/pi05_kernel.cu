@@ -364,7 +364,6 @@ struct Pi05Model {
   using Epi = EpiCtx;
   static constexpr int kMats = 4;  // per layer, in consumption order: QKV, O, gate/up, down
   static constexpr bool kF8 = false;
-  static constexpr int kCtaThreads = kThreads;
   __device__ static float row_scale(const Params&, int, int, int, int) { return 1.0f; }
   __device__ static int rows(int m) { return m == MAT_QKV ? QKV_ROWS : (m == MAT_GU ? 2 * F : D); }
   __device__ static int wmap(int m) { return MAP_W_QKV + m; }
@@ -387,11 +386,10 @@ struct Pi05Model {
   }
 };
 
-// FP8 weight streaming: E4M3 tiles in the ring, expanded to bf16 by warps 6 and 7, row scales in the
-// epilogue (the reference's W8A16 scheme, src/pi05/mk6.cu:90-94,204-205,219-220).
+// FP8 weight streaming: E4M3 tiles in the ring, expanded to bf16 in tensor memory by the epilogue
+// warps (the MMAs read A from there), row scales in the epilogue (the reference's W8A16 scheme, src/pi05/mk6.cu:90-94,204-205,219-220).
 struct Pi05ModelF8 : Pi05Model {
   static constexpr bool kF8 = true;
-  static constexpr int kCtaThreads = kThreadsF8;
   __device__ static float row_scale(const Params& p, int m, int l, int mtile, int row) {
     return __ldg(p.wscale[m] + (size_t)l * rows(m) + mtile * 128 + row);
   }
@@ -656,15 +654,9 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
   c.acnt = s_plan.a_cnt;
   c.batoms = min(kMaxBAtoms, s_plan.b_bytes / (p.NTILE * 128));
   c.ring_slots = s_plan.ring_slots;
-  c.conv_slots = s_plan.conv_slots;
   c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  if (Model::kF8) {  // E4M3 ring | bf16 conversion slots | work area
-    c.conv = c.ring + (size_t)c.ring_slots * p.wg * kAtomBytes / 2;
-    c.work = c.conv + (size_t)c.conv_slots * p.wg * kAtomBytes;
-  } else {
-    c.conv = nullptr;
-    c.work = c.ring + (size_t)c.ring_slots * p.wg * kAtomBytes;
-  }
+  // ring slots: wg bf16 atoms, or (FP8 streaming) the same K range of E4M3 codes, half the bytes
+  c.work = c.ring + (size_t)c.ring_slots * p.wg * (Model::kF8 ? kAtomBytes / 2 : kAtomBytes);
   // epilogue staging: the P area on attention CTAs (idle outside the attention stage), else the
   // 16 KB after the activation area
   c.stage = s_plan.a_cnt > 0 ? c.work + kPOff : c.work + s_plan.b_bytes;
@@ -672,9 +664,10 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
   }
 
   if (threadIdx.x == 0) {
-    // E4M3 slots are released by the converter threads, bf16 slots by an MMA commit
-    for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], Model::kF8 ? kConvThreads : 1); }
-    for (int i = 0; i < kMaxConv; ++i) { mbar_init(&bars.cfull[i], kConvThreads); mbar_init(&bars.cempty[i], 1); }
+    // E4M3 slots are released by the 128 epilogue threads that convert them, bf16 slots by an
+    // MMA commit; TMEM A slots are filled by those threads and released by an MMA commit
+    for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], Model::kF8 ? 128 : 1); }
+    for (int i = 0; i < kASlotsF8; ++i) { mbar_init(&bars.afull[i], 128); mbar_init(&bars.aempty[i], 1); }
     mbar_init(&bars.bfull, 1);
     mbar_init(&bars.bempty, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&bars.acc_full[i], 1); mbar_init(&bars.acc_empty[i], 128); }
@@ -698,13 +691,12 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
   if (warp == 0) {
     run_producer<Model>(p, c);
     __syncwarp();
-  } else if (warp >= 6) {  // FP8 streaming only (the bf16 kernel has 6 warps)
-    if constexpr (Model::kF8) run_converter<Model>(p, c);
   } else {
     const bool is_mma = (warp == 1);
     const bool is_epi = warp >= 2;
     MmaState& st = s_st;
     uint32_t ecnt = 0, anu = 0, gen = 0;
+    ConvState cs{0, 0};  // FP8 kernel: E4M3 slots converted (epilogue warps)
     uint64_t t_prev = globaltimer();
     const bool timing = p.stage_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 32;
     auto mark = [&](int s) {
@@ -723,8 +715,18 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     auto epi_done = [&]() {
       if (threadIdx.x == 64) trace_mark(kTrEpiDone);
     };
+    // FP8 kernel: the barrier before a GEMM stage also expands that stage's first weight slots
+    // into tensor memory (not before the O projection's stage follows attention, whose TMEM
+    // columns overlap the A slots: its slots are expanded during the merge barrier)
+    auto ahead = [&](int m) {
+      return [&, m]() {
+        if constexpr (Model::kF8) {
+          if (m >= 0 && p.f8_ahead) convert_ahead(c, p.err, p.wg, m, cs);
+        }
+      };
+    };
     if (is_epi) stage_embed(p, s_xt, s_red);
-    ok = grid_barrier(p, gen++, tr(ST_QKV, 0, 0));
+    ok = grid_barrier(p, gen++, tr(ST_QKV, 0, 0), ahead(MAT_QKV));
     mark(ST_NORM1);
     // One pass of the loop body per stage, each role function reached from ONE call site so
     // that it is inlined: no ABI calls (and no register save / restore through local memory,
@@ -748,7 +750,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
           const int m = gemm_of(s);
           if (m >= 0) {
             if (is_mma) mma_gemm<Model>(p, c, st, m);
-            if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l);
+            if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l, cs);
           } else if (s == 1) {
             if (is_mma) {
               if (leader()) st.last_q = -1;
@@ -774,7 +776,11 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
           const int nxt = s < 7 ? timed(s + 1) : ST_QKV;
           const int nstep = s < 7 ? step : (last_layer ? step + 1 : step);
           const int nl = s < 7 ? l : (last_layer ? 0 : l + 1);
-          if (!(ok = grid_barrier(p, gen++, tr(nxt == ST_NORM1 && last_layer ? ST_FINAL : nxt, nstep, nl)))) break;
+          // the GEMM of the next stage, when its expansion may start now
+          const int pre = s == 2 ? MAT_O : s == 4 ? MAT_GU : s == 5 ? MAT_DN
+                        : (s == 7 && !(last_layer && step + 1 == p.nsteps)) ? MAT_QKV : -1;
+          if (!(ok = grid_barrier(p, gen++, tr(nxt == ST_NORM1 && last_layer ? ST_FINAL : nxt, nstep, nl), ahead(pre))))
+            break;
           mark(s == 7 && last_layer ? ST_FINAL : timed(s));
         }
       }
@@ -797,7 +803,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
 __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_constant__ Params p) {
   denoise_body<Pi05Model>(p);
 }
-__global__ void __launch_bounds__(kThreadsF8, 1) pi05_denoise_kernel_f8(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel_f8(const __grid_constant__ Params p) {
   denoise_body<Pi05ModelF8>(p);
 }
 
