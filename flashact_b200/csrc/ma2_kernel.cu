@@ -369,9 +369,11 @@ __device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, 
       }
     }
     sync_epi();
-    // O = P V over the chunk: thread = (3 tokens, 8 dims), 24 accumulators
-    if (e < 12 * ((T + 2) / 3)) {
-      const int d8 = e % 12, tg = (e / 12) * 3;
+    // O = P V over the chunk: work item = (3 tokens, 8 dims), 24 accumulators; 12 x 11 = 132
+    // items for 31 or 32 tokens, so the 128 threads loop
+#pragma unroll 1
+    for (int wi = e; wi < 12 * ((T + 2) / 3); wi += 128) {
+      const int d8 = wi % 12, tg = (wi / 12) * 3;
       float acc[3][8] = {};
 #pragma unroll 4
       for (int j = 0; j < KC; ++j) {

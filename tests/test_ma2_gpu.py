@@ -79,3 +79,21 @@ def test_ma2_masked_context_equals_host_compaction(require_gpu):
     eng.bind_context(kc, vc, counts)
     out_compact = eng.sample_actions(c.noise.cuda()).cpu()
     assert torch.equal(out_masked, out_compact)
+
+
+def test_ma2_max_context_and_horizon(require_gpu):
+    """Capacity edges: 4096 context tokens (128 chunks of 32 keys, the merge's maximum) and 32
+    action tokens (the padded horizon), all 32 action dims integrated."""
+    c = M.make_case(seed=53, L=1, T=32, Lk=4096, B=1, num_steps=1, adim=32)
+    out, _ = run(c)
+    mx, cos = err(out, oracle_bf16(c))
+    assert mx < TOL and cos > 0.9999, (mx, cos)
+
+
+def test_ma2_many_token_groups(require_gpu):
+    """20 observations = 600 tokens: 128-token tiles over several token groups and several GEMM
+    units per CTA (the large-batch plan)."""
+    c = M.make_case(seed=54, L=1, T=30, Lk=64, B=20, num_steps=1)
+    out, _ = run(c)
+    mx, cos = err(out[..., :c.adim], oracle_bf16(c)[..., :c.adim])
+    assert mx < TOL and cos > 0.9999, (mx, cos)

@@ -98,3 +98,40 @@ def test_masked_bind_equals_host_compaction(require_gpu):
     eng.bind_prefix_kv(kc.cuda(), vc.cuda(), counts)
     out_compact = eng.sample_actions(c.noise.cuda()).cpu()
     assert torch.equal(out_masked, out_compact)
+
+
+def test_max_prefix_and_horizon(require_gpu):
+    """Capacity edges: the longest prefix the engine binds (31 full 128-key chunks = 3968 keys)
+    and the longest horizon (64 action tokens, one whole 64-token tile)."""
+    c = O.make_case(seed=9, L=1, T=64, AD=32, Lp=3968, B=1, num_steps=1)
+    out, _ = run_engine(c)
+    mx, cos = err(out, oracle_bf16_kv(c))
+    assert mx < TOL and cos > 0.9999, (mx, cos)
+
+
+def test_many_token_groups(require_gpu):
+    """12 observations = 600 tokens: 128-token tiles in 3 token groups, several GEMM units per
+    CTA and stage, K-splits stepped down (the large-batch plan), ragged prefixes."""
+    c = O.make_case(seed=11, L=1, T=50, AD=32, Lp=256, B=12, num_steps=1,
+                    valid_len=[256, 200, 129, 128, 127, 64, 1, 0, 256, 255, 100, 33])
+    out, _ = run_engine(c)
+    mx, cos = err(out, oracle_bf16_kv(c))
+    assert mx < TOL and cos > 0.9999, (mx, cos)
+
+
+def test_batch_permutation_full_size(require_gpu):
+    """Full C1 geometry (18 layers, T=50, prefix 968, 10 steps) at 8 observations: permuting the
+    observations permutes the action chunks bit for bit (every token column, chunk and split is
+    computed the same way wherever it sits), and each chunk matches its bs=1 run at the bf16 bar."""
+    c = O.make_case(seed=10, B=8)
+    out, eng = run_engine(c)
+    perm = [3, 0, 7, 1, 6, 2, 5, 4]
+    eng.bind_prefix_kv(c.k[perm].to(torch.bfloat16).cuda(), c.v[perm].to(torch.bfloat16).cuda(),
+                       [c.valid_len[i] for i in perm])
+    out_p = eng.sample_actions(c.noise[perm].cuda()).cpu()
+    assert torch.equal(out_p, out[perm])
+    one = O.Pi05Case(**{**c.__dict__})
+    one.B, one.noise, one.k, one.v, one.valid_len = 1, c.noise[5:6], c.k[5:6], c.v[5:6], c.valid_len[5:6]
+    out1, _ = run_engine(one)
+    mx, cos = err(out1, out[5:6])
+    assert mx < TOL and cos > 0.9999, (mx, cos)

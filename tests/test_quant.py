@@ -158,7 +158,7 @@ def test_device_quantised_weights_load(require_gpu):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B", [1, 3])
+@pytest.mark.parametrize("B", [1, 3, 12])
 def test_fp8_stream_matches_dequantised_path(require_gpu, monkeypatch, B):
     """The FP8-streaming kernel (E4M3 tiles expanded in shared memory, row scales in the epilogue)
     against the same codes dequantised at load into the bf16 kernel (FA_FP8_STREAM=0) and against
