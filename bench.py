@@ -50,7 +50,8 @@ MA2_KV_BYTES = 2 * MA2_L * MA2_LK * 768 * 2  # cross-attention K+V per Euler ste
 # of `bench.py [--model molmoact2] --steps 1 --warmup 3 --no-cpu-baseline` (metrics
 # dram__bytes_read.sum and dram__bytes_write.sum, -k regex:<kernel> -s 3 -c 1; summaries kept
 # under profiles/).
-NCU_TRAFFIC = {("pi05", 1): 6_252_512_512 + 5_673_216, ("molmoact2", 1): 7_739_515_904 + 3_610_112}
+NCU_TRAFFIC = {("pi05", 1): 6_252_512_512 + 5_673_216, ("molmoact2", 1): 7_739_515_904 + 3_610_112,
+               ("pi05-fp8", 1): 3_134_528_512 + 3_190_016}
 
 
 def set_shape(layers, euler_steps, prefix=0):
@@ -383,8 +384,8 @@ def main():
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": (NCU_TRAFFIC.get((args.model, B)) if not (args.layers or args.euler_steps or args.prefix
-                                                                           or args.wfmt != "bf16") else None),
+                     "traffic": (NCU_TRAFFIC.get((args.model + ("-fp8" if args.wfmt == "fp8" else ""), B))
+                                 if not (args.layers or args.euler_steps or args.prefix) else None),
                      "algorithmic_bytes_per_launch": algorithmic_bytes(B, args.model, args.wfmt),
                      "note": f"achieved = N x ({args.wfmt} weights + B x prefix KV) per launch / mean launch time"},
         "clocks": clk.summary(),

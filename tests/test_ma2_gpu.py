@@ -97,3 +97,13 @@ def test_ma2_many_token_groups(require_gpu):
     out, _ = run(c)
     mx, cos = err(out[..., :c.adim], oracle_bf16(c)[..., :c.adim])
     assert mx < TOL and cos > 0.9999, (mx, cos)
+
+
+@pytest.mark.parametrize("T,adim,Lk,B", [(1, 1, 1, 2), (7, 6, 33, 3), (30, 6, 4064, 1)])
+def test_ma2_odd_shapes(require_gpu, T, adim, Lk, B):
+    """One action token and one context token, partial 32-key chunks, and 127 context chunks."""
+    c = M.make_case(seed=55 + T, L=1, T=T, Lk=Lk, B=B, num_steps=2, adim=adim)
+    out, _ = run(c)
+    mx, cos = err(out[..., :adim], oracle_bf16(c)[..., :adim])
+    assert mx < TOL and cos > 0.9999, (mx, cos)
+    assert torch.equal(out[..., adim:], c.noise[..., adim:])

@@ -135,3 +135,13 @@ def test_batch_permutation_full_size(require_gpu):
     out1, _ = run_engine(one)
     mx, cos = err(out1, out[5:6])
     assert mx < TOL and cos > 0.9999, (mx, cos)
+
+
+@pytest.mark.parametrize("T,AD,B,num_steps", [(1, 1, 3, 2), (17, 5, 2, 1), (63, 32, 1, 1), (50, 32, 1, 50)])
+def test_odd_shapes(require_gpu, T, AD, B, num_steps):
+    """Horizons 1 / 17 / 63 (partial 16-token chunks, the scalar V-transpose path), action dims
+    1 / 5, and the longest schedule (50 Euler steps)."""
+    c = O.make_case(seed=12 + T, L=1, T=T, AD=AD, Lp=130, B=B, num_steps=num_steps)
+    out, _ = run_engine(c)
+    mx, cos = err(out, oracle_bf16_kv(c))
+    assert mx < TOL and cos > 0.9999, (mx, cos)
