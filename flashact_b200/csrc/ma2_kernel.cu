@@ -415,6 +415,15 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
     const int b = tok_b(p, n), t = n - b * p.T;
     const int nch = (p.ctx_len[b] + KC - 1) / KC;
     const size_t base = (size_t)(b * H + h) * MAX_CH;
+    // the first 16 chunks' rows are loaded together with the (max, sum) pairs: one round trip
+    // per item for contexts up to 512 tokens
+    unsigned short rv[16][3];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const unsigned short* src = reinterpret_cast<const unsigned short*>(p.opart) + ((base + j) * TMAX + t) * HD + lane;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) rv[j][k] = j < nch ? __ldcg(src + 32 * k) : (unsigned short)0;
+    }
     float2 ml[kPer];
     float mloc = -INFINITY;
 #pragma unroll
@@ -434,10 +443,16 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
     const float wsum = warp_sum(wloc);
     float acc[3] = {0.f, 0.f, 0.f};
 #pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float wgt = __shfl_sync(0xffffffffu, w_own[0], j);
+#pragma unroll
+      for (int k = 0; k < 3; ++k) acc[k] += wgt * __bfloat162float(__ushort_as_bfloat16(rv[j][k]));
+    }
+#pragma unroll
     for (int g = 0; g < kPer; ++g) {
       if (32 * g >= nch) break;
 #pragma unroll 8
-      for (int j = 0; j < 32; ++j) {
+      for (int j = g == 0 ? 16 : 0; j < 32; ++j) {
         const int cidx = 32 * g + j;
         const float wgt = __shfl_sync(0xffffffffu, w_own[g], j);
         if (cidx < nch) {

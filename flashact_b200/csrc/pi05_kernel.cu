@@ -202,6 +202,14 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
     const int npc = p_nchunks[b];
     const size_t base = (size_t)(b * 4 + hp) * (MAX_CH + 1);
     const int nc = npc + 1;  // prefix chunks + the action-token chunk (stored at MAX_CH); <= 32
+    // every load of the item in one round trip: the partial rows of the first 16 chunks are
+    // issued with the (max, sum) pairs, before the weights that need the maximum
+    uint4 raw[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int cc = j < npc ? j : MAX_CH;
+      if (j < nc) raw[j] = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base + cc) * 128 + r) * HD + lane * 8));
+    }
     float2 ml = make_float2(-INFINITY, 0.f);
     if (lane < nc) {
       const int cc = lane < npc ? lane : MAX_CH;
@@ -211,9 +219,21 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
     const float wgt_own = (lane < nc && ml.y > 0.f) ? exp2f(ml.x - M) * ml.y : 0.f;
     const float wsum = warp_sum(wgt_own);
     float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+    auto accumulate = [&](const uint4& q, float wgt) {
+      const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+      const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+      const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.z));
+      const float2 f3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.w));
+      acc0.x += wgt * f0.x; acc0.y += wgt * f0.y; acc0.z += wgt * f1.x; acc0.w += wgt * f1.y;
+      acc1.x += wgt * f2.x; acc1.y += wgt * f2.y; acc1.z += wgt * f3.x; acc1.w += wgt * f3.y;
+    };
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float wgt = __shfl_sync(0xffffffffu, wgt_own, j);
+      if (j < nc) accumulate(raw[j], wgt);
+    }
 #pragma unroll 1
-    for (int c0 = 0; c0 < nc; c0 += 8) {  // 8 chunks' partial rows in flight at once
-      uint4 raw[8];
+    for (int c0 = 16; c0 < nc; c0 += 8) {  // prefixes over 15 chunks (1920 keys): 8 more rows per round trip
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = c0 + j, cc = c < npc ? c : MAX_CH;
@@ -222,14 +242,7 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float wgt = __shfl_sync(0xffffffffu, wgt_own, (c0 + j) & 31);
-        if (c0 + j < nc) {
-          const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[j].x));
-          const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[j].y));
-          const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[j].z));
-          const float2 f3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[j].w));
-          acc0.x += wgt * f0.x; acc0.y += wgt * f0.y; acc0.z += wgt * f1.x; acc0.w += wgt * f1.y;
-          acc1.x += wgt * f2.x; acc1.y += wgt * f2.y; acc1.z += wgt * f3.x; acc1.w += wgt * f3.y;
-        }
+        if (c0 + j < nc) accumulate(raw[j], wgt);
       }
     }
     const float inv = 1.f / wsum;
