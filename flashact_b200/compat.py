@@ -15,7 +15,10 @@ engine (cached on the weights' data pointers), every call binds the prefix KV / 
 Argument handling:
   * pi0.5 weights arrive FP8 E4M3 with per-row scales in the reference's packed row order
     (W1 = [Q rope-pair interleaved | K interleaved | V], W2 = gate/up interleaved,
-    src/pi05/hybrid_model.py:100-110); they are dequantised (q * scale) once and loaded as bf16.
+    src/pi05/hybrid_model.py:100-110); the codes and scales are put back in model row order and
+    loaded as FP8, so the engine streams E4M3 with the row scales applied to the fp32
+    accumulators, the reference's own W8A16 scheme (FA_FP8_STREAM=0 dequantises them at load
+    into the bf16 kernel instead).
   * mods / mod_final are used as given (the reference precomputes them on the host).
   * RoPE tables: the engine derives the action tokens' rotation from the prefix length with
     theta = 10000 (src/pi05/pack_weights.py:54-58), which is what the reference's callers pass;
@@ -39,26 +42,30 @@ def _dev_index(t: torch.Tensor) -> int:
     return t.device.index if t.device.index is not None else torch.cuda.current_device()
 
 
-def _deq(q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
-    """uint8 E4M3 codes [..., rows, cols] x per-row fp32 scales [..., rows] -> bf16."""
-    return (q.view(torch.float8_e4m3fn).float() * s.float()[..., None]).to(torch.bfloat16)
-
-
 def _pi05_weights(w1, wo, w2, w3, s1, so_, s2, s3, w_ain, b_ain, w_aout, b_aout):
+    """The reference's packed FP8 tensors -> (weights with codes in model row order, qscales)."""
     L = w1.shape[0]
-    W1 = _deq(w1, s1)  # [L][2560][1024]
-    p = torch.arange(1024, device=w1.device)
+    dev = w1.device
+    p = torch.arange(1024, device=dev)
     qsrc = torch.stack([p // 128 * 256 + p % 128, p // 128 * 256 + p % 128 + 128], 1).reshape(-1)
-    jk = torch.arange(128, device=w1.device)
+    jk = torch.arange(128, device=dev)
     ksrc = torch.stack([jk, jk + 128], 1).reshape(-1)
-    wq = torch.empty(L, 2048, 1024, dtype=torch.bfloat16, device=w1.device)
-    wk = torch.empty(L, 256, 1024, dtype=torch.bfloat16, device=w1.device)
-    wq[:, qsrc] = W1[:, :2048]
-    wk[:, ksrc] = W1[:, 2048:2304]
-    W2 = _deq(w2, s2).view(L, 4096, 2, 1024)
-    return {"wq": wq, "wk": wk, "wv": W1[:, 2304:].contiguous(), "wo": _deq(wo, so_),
-            "w_gate": W2[:, :, 0].contiguous(), "w_up": W2[:, :, 1].contiguous(), "w_down": _deq(w3, s3),
-            "ain_w": w_ain, "ain_b": b_ain, "aout_w": w_aout, "aout_b": b_aout}
+
+    def unpermute(x, src, rows):  # packed row i holds model row src[i]
+        out = torch.empty((L, rows) + tuple(x.shape[2:]), dtype=x.dtype, device=dev)
+        out[:, src] = x
+        return out.contiguous()
+
+    c1, sc1 = w1.view(torch.uint8), s1.float()
+    c2, sc2 = w2.view(torch.uint8).view(L, 4096, 2, 1024), s2.float().view(L, 4096, 2)
+    codes = {"wq": unpermute(c1[:, :2048], qsrc, 2048), "wk": unpermute(c1[:, 2048:2304], ksrc, 256),
+             "wv": c1[:, 2304:].contiguous(), "wo": wo.view(torch.uint8).contiguous(),
+             "w_gate": c2[:, :, 0].contiguous(), "w_up": c2[:, :, 1].contiguous(),
+             "w_down": w3.view(torch.uint8).contiguous()}
+    scales = {"wq": unpermute(sc1[:, :2048], qsrc, 2048), "wk": unpermute(sc1[:, 2048:2304], ksrc, 256),
+              "wv": sc1[:, 2304:].contiguous(), "wo": so_.float().contiguous(),
+              "w_gate": sc2[:, :, 0].contiguous(), "w_up": sc2[:, :, 1].contiguous(), "w_down": s3.float().contiguous()}
+    return {**codes, "ain_w": w_ain, "ain_b": b_ain, "aout_w": w_aout, "aout_b": b_aout}, scales
 
 
 def _write_stage_times(eng, stage_cycles):
@@ -82,10 +89,10 @@ def pi05_launch(w1, wo, w2, w3, s1, so_, s2, s3, mods, mod_final, rope_cos, rope
            int(num_steps), int(Lmax))
     eng = _engines.get(key)
     if eng is None:
-        weights = _pi05_weights(w1, wo, w2, w3, s1, so_, s2, s3, w_ain, b_ain, w_aout, b_aout)
+        weights, qscales = _pi05_weights(w1, wo, w2, w3, s1, so_, s2, s3, w_ain, b_ain, w_aout, b_aout)
         eng = Pi05ActionExpert(weights, num_layers=L, horizon=int(Tv), action_dim=int(x_t.shape[1]),
                                max_prefix=max(int(Lmax), int(srows)), max_batch=1, num_steps=int(num_steps),
-                               device=dev, mods=mods, mod_final=mod_final)
+                               device=dev, mods=mods, mod_final=mod_final, wfmt="fp8", qscales=qscales)
         _engines[key] = eng
     if stage_cycles is not None and stage_cycles.numel() > 0:
         eng.set_stage_timing(True)
