@@ -93,15 +93,10 @@ __device__ __forceinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned 
     trace_mark(kTrBarArrive);
     int ok = 1;
     fence_proxy_async_global();
-#ifdef FA_BAR_FENCE
-    __threadfence();
-    if (!(blockIdx.x == 0 && (int)gen == p.inject_barrier)) atomicAdd(p.bar, 1u);
-#else
     // release-add: orders this CTA's earlier writes (made visible to this thread by the CTA
     // barrier above) before the arrival, without a separate full fence
     if (!(blockIdx.x == 0 && (int)gen == p.inject_barrier))
       asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
-#endif
     const uint32_t target = (gen + 1) * gridDim.x;
     uint32_t i = 0;
     for (;; ++i) {
@@ -112,9 +107,6 @@ __device__ __forceinline__ bool grid_barrier(const P& p, uint32_t gen, unsigned 
       if (i > p.spin_limit) { atomicCAS(p.err, 0, KERR_BARRIER); ok = 0; break; }
       if (i > 64) __nanosleep(32);
     }
-#ifdef FA_BAR_FENCE
-    __threadfence();
-#endif
     fence_proxy_async_global();
     s_ok = ok;
 #ifdef FA_TRACE

@@ -31,9 +31,7 @@ constexpr int kMaxAU = 64;                 // attention units per CTA per layer
 constexpr int kMaxMats = 6;                // GEMM matrices per layer
 constexpr int kStageBytes = 16 * 1024;     // epilogue staging area
 constexpr int kMaxStages = 16;             // traced stage kinds
-constexpr int kMaxGroupCtr = 256;          // K-split group counters (one per 128-row tile of a grouped matrix)
-constexpr int kGroupMaxTokens = 256;       // K-split groups only for batches of at most this many padded tokens
-constexpr int kCtrlWords = 2 + kMaxGroupCtr;  // launch control words: barrier, error, group counters
+constexpr int kCtrlWords = 2;  // launch control words, zeroed before each launch: grid-barrier counter, error word
 
 struct GemmUnit {
   uint16_t mtile;   // 128-row tile of the packed weight

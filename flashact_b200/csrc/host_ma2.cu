@@ -109,7 +109,7 @@ fa_status ma2_create(const fa_config& c, int device, fa_handle* h) {
   ALLOC(s->vctx, (size_t)MB * L * LKm * M::D);
   ALLOC(s->d_ctx, MB);
   ALLOC(s->d_plans, h->num_sms);
-  ALLOC(h->ctrl, 2);
+  ALLOC(h->ctrl, fa::kCtrlWords);
   ALLOC(h->stage_ns, fa::kMaxStages);
 #undef ALLOC
   // default RoPE tables: theta 10000 over the 96 head dims, positions 0..T-1
@@ -417,7 +417,7 @@ fa_status ma2_sample(fa_handle* h, int batch, const float* noise, float* out, cu
   M::Params& p = s->params;
   ma2_set_debug(h);
   p.stage_ns = h->timing ? h->stage_ns : nullptr;
-  FA_CUDA(h, cudaMemsetAsync(h->ctrl, 0, 2 * sizeof(unsigned int), stream));
+  FA_CUDA(h, cudaMemsetAsync(h->ctrl, 0, fa::kCtrlWords * sizeof(unsigned int), stream));
   if (h->timing) FA_CUDA(h, cudaMemsetAsync(h->stage_ns, 0, fa::kMaxStages * sizeof(unsigned long long), stream));
   FA_CUDA(h, cudaMemcpyAsync(s->x_t, noise, bytes, cudaMemcpyDefault, stream));
   void* args[] = {&p};
