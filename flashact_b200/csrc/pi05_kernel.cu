@@ -196,63 +196,84 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
   const float p_invT = p.invT;
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   const int total = p_NT * H;
-  for (int item = blockIdx.x * 4 + wq; item < total; item += gridDim.x * 4) {
-    const int n = item / H, h = item % H;
-    const int b = tok_bi(p_invT, n), t = n - b * p_T, hp = h >> 1, r = (h & 1) * TPAD + t;
-    const int npc = p_nchunks[b];
-    const size_t base = (size_t)(b * 4 + hp) * (MAX_CH + 1);
-    const int nc = npc + 1;  // prefix chunks + the action-token chunk (stored at MAX_CH); <= 32
-    // every load of the item in one round trip: the partial rows of the first 16 chunks are
-    // issued with the (max, sum) pairs, before the weights that need the maximum
-    uint4 raw[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int cc = j < npc ? j : MAX_CH;
-      if (j < nc) raw[j] = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base + cc) * 128 + r) * HD + lane * 8));
-    }
-    float2 ml = make_float2(-INFINITY, 0.f);
-    if (lane < nc) {
-      const int cc = lane < npc ? lane : MAX_CH;
-      ml = __ldcg(reinterpret_cast<const float2*>(p_oml + ((base + cc) * 128 + r) * 2));
-    }
-    const float M = warp_max(ml.x);
-    const float wgt_own = (lane < nc && ml.y > 0.f) ? exp2f(ml.x - M) * ml.y : 0.f;
-    const float wsum = warp_sum(wgt_own);
-    float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-    auto accumulate = [&](const uint4& q, float wgt) {
-      const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
-      const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
-      const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.z));
-      const float2 f3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.w));
-      acc0.x += wgt * f0.x; acc0.y += wgt * f0.y; acc0.z += wgt * f1.x; acc0.w += wgt * f1.y;
-      acc1.x += wgt * f2.x; acc1.y += wgt * f2.y; acc1.z += wgt * f3.x; acc1.w += wgt * f3.y;
-    };
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float wgt = __shfl_sync(0xffffffffu, wgt_own, j);
-      if (j < nc) accumulate(raw[j], wgt);
-    }
+  constexpr int kFirst = 12;  // chunks per item loaded up front (prefixes up to 1408 keys)
+  // Two items per warp per pass: both items' loads (the first kFirst partial rows and the
+  // (max, sum) pairs) are in flight together, one round trip for the pair; at large batch a warp
+  // merges tens of items one after another.
+  const int stride = gridDim.x * 4;
 #pragma unroll 1
-    for (int c0 = 16; c0 < nc; c0 += 8) {  // prefixes over 15 chunks (1920 keys): 8 more rows per round trip
+  for (int item0 = blockIdx.x * 4 + wq; item0 < total; item0 += 2 * stride) {
+    int nc[2], npc[2], r[2], n_[2], h_[2];
+    size_t base[2];
+    uint4 raw[2][kFirst];
+    float2 ml[2];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = c0 + j, cc = c < npc ? c : MAX_CH;
-        if (c < nc) raw[j] = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base + cc) * 128 + r) * HD + lane * 8));
+    for (int s = 0; s < 2; ++s) {
+      const int item = item0 + s * stride;
+      const bool live = item < total;
+      const int n = live ? item / H : 0, h = live ? item % H : 0;
+      const int b = tok_bi(p_invT, n), t = n - b * p_T, hp = h >> 1;
+      n_[s] = n; h_[s] = h;
+      r[s] = (h & 1) * TPAD + t;
+      npc[s] = p_nchunks[b];
+      nc[s] = live ? npc[s] + 1 : 0;  // prefix chunks + the action-token chunk (stored at MAX_CH)
+      base[s] = (size_t)(b * 4 + hp) * (MAX_CH + 1);
+#pragma unroll
+      for (int j = 0; j < kFirst; ++j) {
+        const int cc = j < npc[s] ? j : MAX_CH;
+        if (j < nc[s])
+          raw[s][j] = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base[s] + cc) * 128 + r[s]) * HD + lane * 8));
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float wgt = __shfl_sync(0xffffffffu, wgt_own, (c0 + j) & 31);
-        if (c0 + j < nc) accumulate(raw[j], wgt);
+      ml[s] = make_float2(-INFINITY, 0.f);
+      if (lane < nc[s]) {
+        const int cc = lane < npc[s] ? lane : MAX_CH;
+        ml[s] = __ldcg(reinterpret_cast<const float2*>(p_oml + ((base[s] + cc) * 128 + r[s]) * 2));
       }
     }
-    const float inv = 1.f / wsum;
-    __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0.x * inv, acc0.y * inv);
-    __nv_bfloat162 b1 = __floats2bfloat162_rn(acc0.z * inv, acc0.w * inv);
-    __nv_bfloat162 b2 = __floats2bfloat162_rn(acc1.x * inv, acc1.y * inv);
-    __nv_bfloat162 b3 = __floats2bfloat162_rn(acc1.z * inv, acc1.w * inv);
-    *reinterpret_cast<uint4*>(p_attn + (size_t)n * QD + h * HD + lane * 8) =
-        make_uint4(*reinterpret_cast<uint32_t*>(&b0), *reinterpret_cast<uint32_t*>(&b1),
-                   *reinterpret_cast<uint32_t*>(&b2), *reinterpret_cast<uint32_t*>(&b3));
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      if (nc[s] == 0) continue;
+      const float M = warp_max(ml[s].x);
+      const float wgt_own = (lane < nc[s] && ml[s].y > 0.f) ? exp2f(ml[s].x - M) * ml[s].y : 0.f;
+      const float wsum = warp_sum(wgt_own);
+      float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+      auto accumulate = [&](const uint4& q, float wgt) {
+        const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+        const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+        const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.z));
+        const float2 f3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.w));
+        acc0.x += wgt * f0.x; acc0.y += wgt * f0.y; acc0.z += wgt * f1.x; acc0.w += wgt * f1.y;
+        acc1.x += wgt * f2.x; acc1.y += wgt * f2.y; acc1.z += wgt * f3.x; acc1.w += wgt * f3.y;
+      };
+#pragma unroll
+      for (int j = 0; j < kFirst; ++j) {
+        const float wgt = __shfl_sync(0xffffffffu, wgt_own, j);
+        if (j < nc[s]) accumulate(raw[s][j], wgt);
+      }
+#pragma unroll 1
+      for (int c0 = kFirst; c0 < nc[s]; c0 += 8) {  // longer prefixes: 8 more rows per round trip
+        uint4 more[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = c0 + j, cc = c < npc[s] ? c : MAX_CH;
+          if (c < nc[s])
+            more[j] = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base[s] + cc) * 128 + r[s]) * HD + lane * 8));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float wgt = __shfl_sync(0xffffffffu, wgt_own, (c0 + j) & 31);
+          if (c0 + j < nc[s]) accumulate(more[j], wgt);
+        }
+      }
+      const float inv = 1.f / wsum;
+      __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0.x * inv, acc0.y * inv);
+      __nv_bfloat162 b1 = __floats2bfloat162_rn(acc0.z * inv, acc0.w * inv);
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(acc1.x * inv, acc1.y * inv);
+      __nv_bfloat162 b3 = __floats2bfloat162_rn(acc1.z * inv, acc1.w * inv);
+      *reinterpret_cast<uint4*>(p_attn + (size_t)n_[s] * QD + h_[s] * HD + lane * 8) =
+          make_uint4(*reinterpret_cast<uint32_t*>(&b0), *reinterpret_cast<uint32_t*>(&b1),
+                     *reinterpret_cast<uint32_t*>(&b2), *reinterpret_cast<uint32_t*>(&b3));
+    }
   }
 }
 
