@@ -522,6 +522,14 @@ static fa_status build_plan(fa_handle* h) {
   if (h->fp8_stream) h->wg = 2;
   for (int m = 0; m < 4; ++m)
     while ((spec[m].katoms / spec[m].split) % h->wg != 0) h->wg >>= 1;
+  // QKV also runs as 64-row units while its 128-row units would leave most SMs idle (20 tiles per
+  // token group: at a few observations per GPU the stage is otherwise carried by 20 x groups
+  // CTAs), provided every CTA that can receive one has room for its activation batch: an
+  // attention CTA's area is 64 KB, and the planner fills the CTAs without attention units first.
+  const int ntg_max = std::min(h->TG, h->NPAD / h->NTILE);
+  const bool half_fits_attn = h->NTILE * 128 * ntg_max * std::max(act_box_atoms(h), 2 * h->wg) <= 64 * 1024;
+  const bool qkv_half = use_half_units(h) ||
+                        (h->half_units && 40 * h->ngroups <= (half_fits_attn ? nblk : nblk - acta));
   std::vector<std::vector<GemmUnit>> per(nblk * 4);
   const int order[4] = {MAT_QKV, MAT_GU, MAT_DN, MAT_O};
   for (int oi = 0; oi < 4; ++oi) {
@@ -530,7 +538,7 @@ static fa_status build_plan(fa_handle* h) {
     const int per_split = s.katoms / s.split;
     // QKV and gate/up at one 64-token tile: 64-row units (each SM streams half a tile, which its
     // weight ring holds whole; RoPE / GeGLU partners stay in one unit)
-    const int halves = (use_half_units(h) && (m == MAT_QKV || m == MAT_GU)) ? 2 : 1;
+    const int halves = ((m == MAT_QKV && qkv_half) || (m == MAT_GU && use_half_units(h))) ? 2 : 1;
     std::vector<int> cnt(nblk, 0);
     for (int g = 0; g < h->ngroups; ++g)
       for (int mt = 0; mt < s.mtiles; ++mt)
@@ -560,7 +568,7 @@ static fa_status build_plan(fa_handle* h) {
                   plans[i].a_cnt);
     // Capped so that the weight ring stays deep (larger K ranges load in several batches).
     bb = std::min(bb, std::min(std::min(kMaxBBytes, h->bmax_bytes), kMaxBAtoms * tile));
-    bb = std::max(bb, tile * ntg * std::max(act_box_atoms(h), use_half_units(h) ? 2 * h->wg : h->wg));  // one activation box and weight slot per token tile
+    bb = std::max(bb, tile * ntg * std::max(act_box_atoms(h), qkv_half ? 2 * h->wg : h->wg));  // one activation box and weight slot per token tile
     const int work = plans[i].a_cnt > 0 ? kAttnWork : bb + 16 * 1024;  // + epilogue staging
     // Attention CTAs keep their activation area inside the Q region (first 64 KB) so that the
     // prefix-K prefetch into the K/V area survives the GEMM stages in between.
@@ -569,6 +577,16 @@ static fa_status build_plan(fa_handle* h) {
     const int slot_bytes = h->fp8_stream ? h->wg * kAtomBytes / 2 : h->wg * kAtomBytes;
     plans[i].ring_slots = std::min(std::min(kMaxRing, h->ring_max), (kSmemUse - work) / slot_bytes);
     if (plans[i].ring_slots < 1) return fail(h, FA_ERR_INVALID, "shared-memory plan leaves no weight ring");
+    // every unit's smallest activation batch (whole boxes and weight slots, all its token tiles)
+    // must fit this CTA's activation area: the MMA lane never splits below that granule
+    for (int m = 0; m < 4; ++m)
+      for (const GemmUnit& x : per[i * 4 + m]) {
+        const int aps = x.half ? 2 * h->wg : h->wg, gran = std::max(act_box_atoms(h), aps);
+        const int nt = std::min(h->TG, h->NPAD / h->NTILE - x.grp * h->TG);
+        if (gran * nt * tile > plans[i].b_bytes)
+          return fail(h, FA_ERR_INVALID, "plan error: a %d-atom activation batch of %d token tiles exceeds CTA %d's %d-byte area",
+                      gran, nt, i, plans[i].b_bytes);
+      }
     for (int m = 0; m < 4; ++m) {
       plans[i].g_off[m] = (int)gu.size();
       plans[i].g_cnt[m] = (int)per[i * 4 + m].size();
