@@ -347,8 +347,13 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
         // 8 KB apart, so rows 64..127 of each MMA read the next atom (results ignored)
         const uint32_t astride = gu.half ? kAtomBytes / 2 : kAtomBytes;
 #pragma unroll 1
+        int deferred = -1;
         for (int j = j0; j < j1; j += aps) {  // one ring slot = aps weight atoms
           const int wslot = st.wit % k.R;
+          // The last slot before a further activation batch is released only after that batch's
+          // loads are issued: otherwise the producer's refill of the slot (the next stage's
+          // weights, from HBM) goes out first and the activation batch queues behind it.
+          const bool defer = j + aps >= j1 && j1 < gu.natoms;
           if (!mbar_wait(&wfull[wslot], (st.wit / k.R) & 1, k.err, KERR_MMA)) return false;
           if (F8) tc_fence_after();  // the slot's tcgen05.st writes precede these MMAs
           if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(kTrMmaW0));
@@ -373,9 +378,10 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
                 }
               }
             }
-            tc_commit(&wempty[wslot]);
+            if (!defer) tc_commit(&wempty[wslot]);
           }
           __syncwarp();
+          if (defer) deferred = wslot;
           ++st.wit;
         }
         j0 = j1;
@@ -386,6 +392,8 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
           if (u == 0 && g == 0) FA_ONE(trace_mark(14));
           j1 = min((int)gu.natoms, j0 + per_batch);
           load_b_batch(k, gu, g, nt, j0, j1);
+          // the deferred slot's MMAs are complete (bempty above covers them)
+          if (deferred >= 0) FA_ONE(mbar_arrive(&wempty[deferred]));
         }
       }
       FA_ONE(tc_commit(&bars->acc_full[a]));
