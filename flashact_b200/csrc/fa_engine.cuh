@@ -343,11 +343,11 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
         if (!mbar_wait(&bars->bfull, st.bload & 1, k.err, KERR_MMA)) return false;
         ++st.bload;
         if (u == 0 && g == 0 && j0 == 0) FA_ONE(trace_mark(kTrMmaB0));
-                // A operand of atom jj: a 128-row SW128 tile (16 KB); a half-row unit's 64-row atoms are
+        // A operand of atom jj: a 128-row SW128 tile (16 KB); a half-row unit's 64-row atoms are
         // 8 KB apart, so rows 64..127 of each MMA read the next atom (results ignored)
         const uint32_t astride = gu.half ? kAtomBytes / 2 : kAtomBytes;
-#pragma unroll 1
         int deferred = -1;
+#pragma unroll 1
         for (int j = j0; j < j1; j += aps) {  // one ring slot = aps weight atoms
           const int wslot = st.wit % k.R;
           // The last slot before a further activation batch is released only after that batch's

@@ -94,7 +94,7 @@ static inline fa_status fail(fa_handle* h, fa_status st, const char* fmt, ...) {
   } while (0)
 
 template <class T>
-static fa_status dalloc(fa_handle* h, T** out, size_t count) {
+static inline fa_status dalloc(fa_handle* h, T** out, size_t count) {
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, count * sizeof(T) + 16);
   if (e != cudaSuccess) return fail(h, FA_ERR_OOM, "cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
@@ -141,7 +141,7 @@ static __global__ void rowmap_kernel(const unsigned char* keep, int src_rows, in
 
 // Builds the row map of a masked bind on `stream` (into the handle's reusable buffers) and
 // returns the kept-row counts on the host (the bind plans its attention work from them).
-static fa_status masked_rows(fa_handle* h, int batch, int src_rows, const unsigned char* keep, cudaStream_t stream,
+static inline fa_status masked_rows(fa_handle* h, int batch, int src_rows, const unsigned char* keep, cudaStream_t stream,
                              std::vector<int>& counts) {
   if (!keep || batch < 1 || src_rows < 1) return fail(h, FA_ERR_INVALID, "masked bind: bad mask arguments");
   cudaPointerAttributes a;
@@ -171,7 +171,7 @@ static fa_status masked_rows(fa_handle* h, int batch, int src_rows, const unsign
   return FA_OK;
 }
 
-static bool is_device_ptr(const void* p) {
+static inline bool is_device_ptr(const void* p) {
   cudaPointerAttributes a;
   if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
     cudaGetLastError();
@@ -258,7 +258,7 @@ static __global__ void to_f32_kernel(const void* src, int dt, float* dst, size_t
 static inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
 
 // ------------------------------------------------------------------ TMA descriptors
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+static inline PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     void* ptr = nullptr;
@@ -269,25 +269,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   }
   return fn;
 }
-// 2D bf16 map over a row-major [outer][inner] array, 128-byte swizzle, box {box_inner, box_outer}.
-static fa_status make_map(fa_handle* h, CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
-                          uint32_t box_inner, uint32_t box_outer) {
-  auto enc = get_encode();
-  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * 2};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return FA_OK;
-}
-
 // 3D bf16 map viewing a row-major [rows][K] array as [K/64 atoms][rows][64]: one box
 // {64, box_rows, box_atoms} lands in shared memory as box_atoms consecutive 128B-swizzled atoms.
-static fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
+static inline fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
                            uint32_t box_rows, uint32_t box_atoms) {
   auto enc = get_encode();
   if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -304,7 +288,7 @@ static fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint6
 
 // 3D E4M3 map viewing a row-major [rows][K] byte array as [K/128][rows][128]: one box
 // {128, box_rows, box_n} lands as box_n consecutive 128B-swizzled boxes of box_rows x 128 bytes.
-static fa_status make_map3_u8(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
+static inline fa_status make_map3_u8(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
                               uint32_t box_rows, uint32_t box_n) {
   auto enc = get_encode();
   if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -320,7 +304,7 @@ static fa_status make_map3_u8(fa_handle* h, CUtensorMap* m, const void* base, ui
 }
 
 // Returns a device pointer holding `bytes` of `p` (staging host data into `tmp` when needed).
-static fa_status stage_bytes(fa_handle* h, const void* p, size_t bytes, const char* name, const void** dptr,
+static inline fa_status stage_bytes(fa_handle* h, const void* p, size_t bytes, const char* name, const void** dptr,
                              std::vector<void*>& tmp) {
   if (!p) return fail(h, FA_ERR_INVALID, "'%s' is null", name);
   if (is_device_ptr(p)) { *dptr = p; return FA_OK; }
@@ -333,7 +317,7 @@ static fa_status stage_bytes(fa_handle* h, const void* p, size_t bytes, const ch
 }
 
 // Returns a device pointer holding `t` (staging host data into `tmp` when needed).
-static fa_status stage_tensor(fa_handle* h, const fa_tensor& t, size_t count, const char* name, const void** dptr,
+static inline fa_status stage_tensor(fa_handle* h, const fa_tensor& t, size_t count, const char* name, const void** dptr,
                               std::vector<void*>& tmp) {
   if (!t.ptr) return fail(h, FA_ERR_INVALID, "weight '%s' is null", name);
   if (t.dtype != FA_DT_F32 && t.dtype != FA_DT_BF16 && t.dtype != FA_DT_F16)
@@ -348,7 +332,7 @@ static fa_status stage_tensor(fa_handle* h, const fa_tensor& t, size_t count, co
   return FA_OK;
 }
 
-static fa_status pack_codes(fa_handle* h, const std::vector<int2>& rowmap, PackSrc src, unsigned char* dst, float* dscale,
+static inline fa_status pack_codes(fa_handle* h, const std::vector<int2>& rowmap, PackSrc src, unsigned char* dst, float* dscale,
                             int K, std::vector<void*>& tmp) {
   int2* d_map = nullptr;
   FA_CUDA(h, cudaMalloc(&d_map, rowmap.size() * sizeof(int2)));
@@ -359,7 +343,7 @@ static fa_status pack_codes(fa_handle* h, const std::vector<int2>& rowmap, PackS
   return FA_OK;
 }
 
-static fa_status pack_matrix(fa_handle* h, const std::vector<int2>& rowmap, PackSrc src, bf16* dst, int K,
+static inline fa_status pack_matrix(fa_handle* h, const std::vector<int2>& rowmap, PackSrc src, bf16* dst, int K,
                              std::vector<void*>& tmp) {
   int2* d_map = nullptr;
   FA_CUDA(h, cudaMalloc(&d_map, rowmap.size() * sizeof(int2)));

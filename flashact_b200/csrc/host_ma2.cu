@@ -156,12 +156,12 @@ extern "C" fa_status fa_ma2_load_weights(fa_handle* h, const fa_ma2_weights* w) 
   const char* names[M::NUM_MATS] = {"w_qkv", "w_so", "w_cq", "w_co", "w_gate", "w_down"};
   for (int m = 0; m < M::NUM_MATS; ++m) {
     const int rows = m == M::MAT_GU ? M::F : kMatRows[m];
-    const void *dw, *db;
+    const void *dw = nullptr, *db = nullptr;
     if ((st = stage_tensor(h, *mats[m], (size_t)L * rows * kMatK[m], names[m], &dw, tmp)) != FA_OK) return st;
     if ((st = stage_tensor(h, *biases[m], (size_t)L * rows, names[m], &db, tmp)) != FA_OK) return st;
     to_f32_kernel<<<64, 256>>>(db, biases[m]->dtype, s->bias[m], (size_t)L * rows);
     if (m == M::MAT_GU) {
-      const void *du, *dub;
+      const void *du = nullptr, *dub = nullptr;
       if ((st = stage_tensor(h, w->w_up, (size_t)L * M::F * M::D, "w_up", &du, tmp)) != FA_OK) return st;
       if ((st = stage_tensor(h, w->b_up, (size_t)L * M::F, "b_up", &dub, tmp)) != FA_OK) return st;
       to_f32_kernel<<<64, 256>>>(dub, w->b_up.dtype, s->b_up, (size_t)L * M::F);
@@ -181,7 +181,7 @@ extern "C" fa_status fa_ma2_load_weights(fa_handle* h, const fa_ma2_weights* w) 
       if ((st = pack_matrix(h, map, src, s->w[m], kMatK[m], tmp)) != FA_OK) return st;
     }
   }
-  const void *aiw, *aib, *aow, *aob;
+  const void *aiw = nullptr, *aib = nullptr, *aow = nullptr, *aob = nullptr;
   if ((st = stage_tensor(h, w->ain_w, (size_t)M::D * AD, "ain_w", &aiw, tmp)) != FA_OK) return st;
   if ((st = stage_tensor(h, w->ain_b, M::D, "ain_b", &aib, tmp)) != FA_OK) return st;
   if ((st = stage_tensor(h, w->aout_w, (size_t)AD * M::D, "aout_w", &aow, tmp)) != FA_OK) return st;

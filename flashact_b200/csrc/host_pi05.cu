@@ -286,9 +286,10 @@ static fa_status load_weights_impl(fa_handle* h, const fa_pi05_weights* w, fa_wf
     ~Cleanup() { for (void* p : t) cudaFree(p); }
   } cleanup{tmp};
   fa_status st;
-  const void *wq, *wk, *wv, *wo, *wg, *wu, *wd, *lniw = nullptr, *lnib = nullptr, *lnpw = nullptr, *lnpb = nullptr,
-             *nw = nullptr, *nb = nullptr, *tiw = nullptr, *tib = nullptr, *tow = nullptr, *tob = nullptr, *aiw, *aib,
-             *aow, *aob;
+  const void *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *wg = nullptr, *wu = nullptr, *wd = nullptr,
+             *lniw = nullptr, *lnib = nullptr, *lnpw = nullptr, *lnpb = nullptr, *nw = nullptr, *nb = nullptr,
+             *tiw = nullptr, *tib = nullptr, *tow = nullptr, *tob = nullptr, *aiw = nullptr, *aib = nullptr,
+             *aow = nullptr, *aob = nullptr;
   // The conditioning weights (time MLP, adaRMS denses) are optional as a group: without them the
   // caller supplies the modulations with fa_set_modulation, as the reference's launch() takes them.
   const fa_tensor* cond_w[10] = {&w->ln_in_w, &w->ln_in_b, &w->ln_post_w, &w->ln_post_b, &w->norm_w,

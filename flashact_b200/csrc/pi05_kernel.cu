@@ -662,7 +662,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
 
   __shared__ Ctx s_c;        // per-CTA constants, shared so that no role keeps them on its stack
   __shared__ MmaState s_st;  // MMA-lane state
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   Ctx& c = s_c;
   if (threadIdx.x == 0) {
     s_plan = p.plans[blockIdx.x];
