@@ -155,3 +155,48 @@ def quantized_weights(weights: dict, device):
     for n in QUANT_FIELDS:
         w[n], qs[n] = quantize_fp8_rows(weights[n].to(device))
     return w, qs
+
+
+OPENPI_EXPERT = "paligemma_with_expert.gemma_expert.model."
+
+
+def weights_from_openpi(source, num_layers: int = 18) -> dict:
+    """The engine's weight dict (keys of flashact_b200._capi.PI05_WEIGHT_FIELDS) from an openpi
+    pi0.5 checkpoint: a state dict, or the path of a .safetensors file (read lazily, tensor by
+    tensor) or of a torch checkpoint. Key names as the reference reads them
+    (src/pi05/hybrid_model.py:76-133): `paligemma_with_expert.gemma_expert.model.layers.{i}.`
+    `self_attn.{q,k,v,o}_proj.weight`, `mlp.{gate,up,down}_proj.weight`,
+    `{input,post_attention}_layernorm.dense.{weight,bias}`, `...model.norm.dense.{weight,bias}`,
+    `time_mlp_{in,out}.{weight,bias}`, `action_{in,out}_proj.{weight,bias}`. Per-layer tensors are
+    stacked over the layers; dtypes are kept (the engine packs bf16 / fp16 / fp32 on the device)."""
+    if isinstance(source, (str, bytes)) or hasattr(source, "__fspath__"):
+        import os
+        path = os.fspath(source)
+        if str(path).endswith(".safetensors"):
+            from safetensors import safe_open
+            handle = safe_open(str(path), framework="pt", device="cpu")
+            get = handle.get_tensor
+        else:
+            sd = torch.load(path, map_location="cpu", mmap=True, weights_only=True)
+            get = sd.__getitem__
+    else:
+        get = source.__getitem__
+    layer = OPENPI_EXPERT + "layers.{}."
+
+    def stack(name):
+        return torch.stack([get(layer.format(i) + name) for i in range(num_layers)])
+
+    return {
+        "wq": stack("self_attn.q_proj.weight"), "wk": stack("self_attn.k_proj.weight"),
+        "wv": stack("self_attn.v_proj.weight"), "wo": stack("self_attn.o_proj.weight"),
+        "w_gate": stack("mlp.gate_proj.weight"), "w_up": stack("mlp.up_proj.weight"),
+        "w_down": stack("mlp.down_proj.weight"),
+        "ln_in_w": stack("input_layernorm.dense.weight"), "ln_in_b": stack("input_layernorm.dense.bias"),
+        "ln_post_w": stack("post_attention_layernorm.dense.weight"),
+        "ln_post_b": stack("post_attention_layernorm.dense.bias"),
+        "norm_w": get(OPENPI_EXPERT + "norm.dense.weight"), "norm_b": get(OPENPI_EXPERT + "norm.dense.bias"),
+        "time_in_w": get("time_mlp_in.weight"), "time_in_b": get("time_mlp_in.bias"),
+        "time_out_w": get("time_mlp_out.weight"), "time_out_b": get("time_mlp_out.bias"),
+        "ain_w": get("action_in_proj.weight"), "ain_b": get("action_in_proj.bias"),
+        "aout_w": get("action_out_proj.weight"), "aout_b": get("action_out_proj.bias"),
+    }
