@@ -17,7 +17,7 @@ inter-rank traffic is the barrier around the timed region and the max-over-ranks
 the measured times (no collective in the loop).
 
 --impl reference times the reference's CPU path on the host cores: openpi's PyTorch model is
-not available, so the CPU fp32 restatement in oracle/ stands in for it (see DESIGN.md).
+not available, so the CPU fp32 restatement in oracle/ stands in for it.
 """
 import argparse
 import json
