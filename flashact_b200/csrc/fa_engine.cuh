@@ -152,6 +152,7 @@ struct Bars {
   uint64_t wfull[kMaxRing], wempty[kMaxRing];
   uint64_t afull[kASlotsF8], aempty[kASlotsF8];  // FP8 streaming: TMEM A slot written / read by the MMAs
   uint64_t bfull, bempty;  // activation batch loaded / consumed
+  uint64_t sfull[4];       // token-major GEMMs: activation K-chunk landed in staging slot 0..3
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
 };
@@ -161,6 +162,7 @@ struct Ctx {
   Bars* bars;
   uint32_t tmem;
   int ring_slots;
+  int tm_slots;             // token-major GEMMs: activation staging slots (2..4 chunks of 32 KB)
   int batoms;               // activation atoms that fit in the work area at once
   uint8_t* stage;           // 16 KB epilogue staging area (coalesced bf16 output writes)
   const GemmUnit* gu[kMaxMats];  // this CTA's units per matrix (shared-memory copy of the plan)
@@ -203,10 +205,40 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
   for (int m = 0; m < Model::kMats; ++m) { gul[m] = c.gu[m]; gcnt[m] = c.gcnt[m]; }
   uint32_t it = 0;
   bool ok = true;
+  // L2 prefetch of the weight stream, `ahead` layer-steps in front of the ring: HBM keeps
+  // streaming while the dependent chain of a layer (attention, norms, barriers) runs, and the
+  // GEMM stages then read their weights from L2. Each CTA prefetches exactly the boxes it will
+  // load itself, in the same (matrix, unit, K) order.
+  const int ahead = p.l2_ahead, total_layers = nsteps * L;
+  const uint64_t pol_pf = policy_evict_normal();
+  auto prefetch_layer = [&](int g) {
+    if (g >= total_layers || !leader()) return;
+    const int lp = g % L;
+#pragma unroll 1
+    for (int m = 0; m < Model::kMats; ++m) {
+      const int rows = Model::rows(m);
+#pragma unroll 1
+      for (int u = 0; u < gcnt[m]; ++u) {
+        const GemmUnit gu = gul[m][u];
+        const int aps = gu.half ? 2 * wg : wg;
+        const int map = gu.half ? Model::wmap_half(m) : Model::wmap(m);
+        const int row0 = lp * rows + gu.mtile * 128 + (gu.half == 2 ? 64 : 0);
+        // (several token groups share a weight tile: prefetch it once)
+        if (gu.grp != 0) continue;
+#pragma unroll 1
+        for (int j = 0; j < gu.natoms; j += aps)
+          tma_prefetch_l2_3d(maps + map, 0, row0, F8 ? (gu.katom0 + j) >> 1 : gu.katom0 + j, pol_pf);
+      }
+    }
+  };
+  if (ahead > 0)
+    for (int g = 0; g < ahead && g < total_layers; ++g) prefetch_layer(g);
 #pragma unroll 1
   for (int step = 0; ok && step < nsteps; ++step)
 #pragma unroll 1
-    for (int l = 0; ok && l < L; ++l)
+    for (int l = 0; ok && l < L; ++l) {
+      if (ahead > 0) prefetch_layer(step * L + l + ahead);
+      __syncwarp();
 #pragma unroll 1
       for (int m = 0; ok && m < Model::kMats; ++m) {
         const int rows = Model::rows(m);
@@ -238,6 +270,7 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
             }
         }
       }
+    }
   // Drain: never leave a TMA write into shared memory in flight at exit.
   const uint32_t first = it > (uint32_t)R ? it - R : 0;
   for (uint32_t k = first; k < it; ++k) mbar_wait(&bars->wfull[k % R], (k / R) & 1, err, KERR_PRODUCER);
@@ -267,6 +300,7 @@ struct MmaState {
   uint32_t nq, nu;       // attention: Q loads, units
   int last_q;
   int k_pre;             // the next attention unit's prefix K is already loading (prefetched)
+  uint32_t qtm;          // token-major GEMMs: activation K-chunks consumed (staging / TMEM A slot phases)
 };
 
 // Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
@@ -380,6 +414,7 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
             }
             if (!defer) tc_commit(&wempty[wslot]);
           }
+          if (u == 0 && g == 0 && j == 0) FA_ONE(trace_mark(15));
           __syncwarp();
           if (defer) deferred = wslot;
           ++st.wit;
@@ -408,6 +443,180 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
   if (leader()) st_shared = st;
   __syncwarp();
   return true;
+}
+
+// ------------------------------------------------------------------ token-major GEMMs (one 64-token tile)
+// While the bound batch is a single tile of at most 64 tokens, the GEMMs run "token-major": the
+// activation tile is the A operand, held in tensor memory (M = 128 lanes, tokens in lanes 0..63),
+// and the weights are the B operand straight from the ring (N = 64 or 128 weight rows, K-major,
+// 128-byte swizzle). Each weight byte is then read from shared memory once per MMA (2 KB per M128
+// N64 K16 instruction, against 6 KB when the weights are the 128-row A operand and half of them
+// belong to another unit), which keeps the MMAs clear of the ring's TMA writes.
+//
+// Activation K-chunks of kTmChunkAtoms atoms (256 K) flow: TMA into a staging slot (MMA lane) ->
+// the epilogue warps of TMEM lane quadrants 0 and 1 (one token per thread) copy their row into a
+// TMEM A slot -> MMAs -> the slot is released by an MMA commit. Staging slot q & 1 is free again
+// once the fill of chunk q has been signalled (afull), so the MMA lane refills it right after.
+// TMEM: accumulators at columns [0, 256) (two buffers of N <= 128), A slots at [256, 512).
+// (kTmChunkAtoms, kTmChunkBytes, kTmACol, kTmASlotCols: fa_engine_types.cuh)
+
+// The whole role runs on lane 0 of the MMA warp (lanes 1..31 wait at the warp sync after it):
+// no warp-level synchronisation between consecutive MMAs.
+template <class Model>
+__device__ __noinline__ bool mma_gemm_tm_lane(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
+  trace_mark(12);
+  MmaState st = st_shared;
+  uint8_t* const ring = c.ring;
+  uint8_t* const work = c.work;
+  Bars* const bars = c.bars;
+  int* const err = p.err;
+  const CUtensorMap* const amap = &p.maps[Model::act_map(m)];
+  const uint32_t tmem = c.tmem;
+  const int R = c.ring_slots, wg = p.wg;
+  const uint32_t slot_bytes = (uint32_t)wg * kAtomBytes;
+  const GemmUnit* const units = c.gu[m];
+  const int nunits = c.gcnt[m];
+  const uint64_t pol = policy_evict_last();
+  const uint32_t nst = (uint32_t)c.tm_slots;
+  uint32_t wslot = st.wit % R, wphase = (st.wit / R) & 1;
+#pragma unroll 1
+  for (int u = 0; u < nunits; ++u) {
+    const GemmUnit gu = units[u];
+    const int natoms = gu.natoms, nch = natoms / kTmChunkAtoms;
+    const int aps = gu.half ? 2 * wg : wg;                       // weight atoms per ring slot
+    const uint32_t wst = gu.half ? kAtomBytes / 2 : kAtomBytes;  // weight atom stride inside a slot
+    const uint32_t idesc = idesc_bf16(128, gu.half ? 64 : 128);
+    const uint32_t q0 = st.qtm;
+#pragma unroll 1
+    for (int ch = 0; ch < nst && ch < nch; ++ch) {  // the unit's first K-chunks, one per staging slot
+      const int sl = (int)((q0 + ch) % nst);
+      uint64_t* b = &bars->sfull[sl];
+      mbar_expect_tx(b, kTmChunkBytes);
+      tma_load_3d(work + sl * kTmChunkBytes, amap, b, 0, 0, gu.katom0 + ch * kTmChunkAtoms, pol);
+    }
+    const int a = st.acc & 1;
+    if (st.acc >= 2 && !mbar_wait(&bars->acc_empty[a], ((st.acc >> 1) - 1) & 1, err, KERR_MMA)) return false;
+    const uint32_t tacc = tmem + a * 128;
+    int js = 0;  // atom within the current ring slot
+    uint64_t db = 0;
+#pragma unroll 1
+    for (int ch = 0; ch < nch; ++ch) {
+      const uint32_t q = q0 + ch;
+      if (!mbar_wait(&bars->afull[q & 1], (q >> 1) & 1, err, KERR_MMA)) return false;
+      tc_fence_after();
+      if (u == 0) trace_mark(ch == 0 ? 9 : ch == 1 ? 10 : ch == 2 ? 11 : 13);
+      if (ch + nst < nch) {  // the fill has read this chunk's staging slot: refill it
+        const int sl = (int)(q % nst);
+        uint64_t* b = &bars->sfull[sl];
+        mbar_expect_tx(b, kTmChunkBytes);
+        tma_load_3d(work + sl * kTmChunkBytes, amap, b, 0, 0, gu.katom0 + (ch + nst) * kTmChunkAtoms, pol);
+      }
+      const uint32_t ta = tmem + kTmACol + (q & 1) * kTmASlotCols;
+#pragma unroll
+      for (int jj = 0; jj < kTmChunkAtoms; ++jj) {
+        if (js == 0) {
+          if (!mbar_wait(&bars->wfull[wslot], wphase, err, KERR_MMA)) return false;
+          db = sdesc_sw128(ring + (size_t)wslot * slot_bytes);
+          if (u == 0) trace_mark(ch == 0 ? 1 : 14);
+        }
+        const uint64_t dbj = db + (uint64_t)((js * wst) >> 4);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) tc_mma_bf16_ts(tacc, ta + jj * 32 + 8 * s, dbj + 2 * s, idesc, (ch | jj | s) != 0);
+        if (++js == aps || ch * kTmChunkAtoms + jj == natoms - 1) {
+          tc_commit(&bars->wempty[wslot]);
+          js = 0;
+          ++st.wit;
+          if (++wslot == (uint32_t)R) { wslot = 0; wphase ^= 1; }
+        }
+      }
+      tc_commit(&bars->aempty[q & 1]);
+      if (u == 0) trace_mark(ch == 0 ? 15 : ch == 1 ? 2 : ch == 2 ? 3 : 8);
+    }
+    st.qtm = q0 + nch;
+    tc_commit(&bars->acc_full[a]);
+    ++st.acc;
+  }
+  st_shared = st;
+  return true;
+}
+
+template <class Model>
+__device__ __forceinline__ bool mma_gemm_tm(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
+  bool ok = true;
+  if (leader()) ok = mma_gemm_tm_lane<Model>(p, c, st_shared, m);
+  __syncwarp();
+  return __shfl_sync(0xffffffffu, ok, 0);
+}
+
+// Epilogue warps of a token-major GEMM stage: per unit, fill its K-chunks into the TMEM A slots
+// (threads of lane quadrants 0 and 1: thread = token; rows read from the 128-byte-swizzled staging
+// tile, 16-byte chunk c of row r at r * 128 + ((c ^ (r & 7)) << 4)), then drain the accumulator
+// (token row, 32 weight-row columns at a time) through Model::epi_tm. Quadrants 2 and 3 (lanes of
+// padding rows) only take part in the accumulator hand-back.
+template <class Model>
+__device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m,
+                                                uint32_t& qtm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
+  const bool active = qd < 2;
+  const int tok = qd * 32 + lane;
+  int* const err = p.err;
+  Bars* const bars = c.bars;
+  const uint8_t* const work = c.work;
+  const uint32_t tl = c.tmem + ((uint32_t)(qd * 32) << 16);
+  const GemmUnit* const units = c.gu[m];
+  const int nunits = c.gcnt[m];
+  const uint32_t nst = (uint32_t)c.tm_slots;
+  typename Model::Epi e;
+  Model::epi_load(e, p, c, 0);
+#pragma unroll 1
+  for (int u = 0; u < nunits; ++u) {
+    const GemmUnit gu = units[u];
+    const int nch = gu.natoms / kTmChunkAtoms;
+    if (active) {
+#pragma unroll 1
+      for (int ch = 0; ch < nch; ++ch) {
+        const uint32_t q = qtm + ch;
+        if (!mbar_wait(&bars->sfull[q % nst], (q / nst) & 1, err, KERR_EPI)) return ecnt;
+        if (q >= 2 && !mbar_wait(&bars->aempty[q & 1], ((q >> 1) - 1) & 1, err, KERR_EPI)) return ecnt;
+        tc_fence_after();
+        const uint8_t* row = work + (q % nst) * kTmChunkBytes + tok * 128;
+        const int sw = tok & 7;
+#pragma unroll 1
+        for (int at = 0; at < kTmChunkAtoms; ++at) {
+          uint32_t w[32];
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            const uint4 v = *reinterpret_cast<const uint4*>(row + at * (64 * 128) + ((cc ^ sw) << 4));
+            w[4 * cc] = v.x; w[4 * cc + 1] = v.y; w[4 * cc + 2] = v.z; w[4 * cc + 3] = v.w;
+          }
+          tmem_st32(tl + kTmACol + (q & 1) * kTmASlotCols + at * 32, w);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars->afull[q & 1]);
+      }
+    }
+    qtm += nch;
+    const int a = ecnt & 1;
+    if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;
+    tc_fence_after();
+    if (u == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
+    if (active) {
+      const int ncols = gu.half ? 64 : 128;
+#pragma unroll 1
+      for (int c0 = 0; c0 < ncols; c0 += 32) {
+        float v[32];
+        tmem_ld16(tl + a * 128 + c0, v);
+        tmem_ld16(tl + a * 128 + c0 + 16, v + 16);
+        tc_wait_ld();
+        Model::epi_tm(e, gu, m, tok, c0, v);
+      }
+    }
+    tc_fence_before();
+    mbar_arrive(&bars->acc_empty[a]);
+    ++ecnt;
+  }
+  return ecnt;
 }
 
 // GEMM epilogue driver (warps 2-5): waits for each accumulator, walks it in 16-token chunks
@@ -530,6 +739,7 @@ __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, co
       const int a = ecnt & 1;
       if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;
       tc_fence_after();
+      if (u == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
       const int tok0 = g * TG * NTILE;
       for (int sub = 0; sub < (nchunks + 3) >> 2; ++sub) {  // 64-token sub-tiles
         const int c0 = sub * 4, c1 = min(nchunks, sub * 4 + 4);

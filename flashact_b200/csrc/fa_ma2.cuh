@@ -77,6 +77,9 @@ struct Params {
   unsigned int* bar;
   int* err;
   int wg;  // weight atoms per ring slot / TMA box
+  // L2 prefetch distance of the weight stream, in layers (0 = off): the producer warp brings
+  // this CTA's weight boxes of layer-step g + l2_ahead into L2 when it starts layer-step g.
+  int l2_ahead;
   unsigned long long* stage_ns;
   int inject_barrier;
   unsigned int spin_limit;

@@ -76,6 +76,9 @@ struct Params {
   unsigned int* bar;             // grid-barrier counter, zeroed before each launch
   int* err;                      // 0 = ok; otherwise the first failure code
   int wg;  // weight atoms per ring slot / TMA box
+  // L2 prefetch distance of the weight stream, in layers (0 = off): the producer warp brings
+  // this CTA's weight boxes of layer-step g + l2_ahead into L2 when it starts layer-step g.
+  int l2_ahead;
   // FP8 weight streaming: per packed weight row, its E4M3 scale, [L][rows] per matrix (QKV, O,
   // gate/up, down); unused by the bf16 kernel
   const float* wscale[4];

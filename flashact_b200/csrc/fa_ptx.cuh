@@ -116,6 +116,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, uint64_t
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
       : "memory");
 }
+// 3D tiled prefetch into L2 (no shared-memory destination, no completion signal): the box the
+// matching tma_load_3d would fetch is brought into L2 ahead of its load.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* map, int x, int y, int z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.3d.L2.global.tile.L2::cache_hint [%0, {%1, %2, %3}], %4;" ::"l"(map), "r"(x),
+      "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

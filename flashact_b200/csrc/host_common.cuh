@@ -44,6 +44,7 @@ struct fa_handle {
   // FP8 weight streaming (pi0.5 weights loaded as FP8 codes): E4M3 codes and per-row scales of
   // QKV, O, gate/up, down in the packed row order; the FP8 kernel streams them
   bool fp8_stream = false;
+  bool tm = false;             // token-major GEMM kernel (bound batch = one tile of <= 64 tokens)
   unsigned char* w8[4] = {nullptr, nullptr, nullptr, nullptr};
   float* ws8[4] = {nullptr, nullptr, nullptr, nullptr};
   // bound batch
@@ -178,6 +179,13 @@ static inline bool is_device_ptr(const void* p) {
     return false;
   }
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// Layers of weights the producer warps prefetch into L2 ahead of their loads (FA_L2_AHEAD, 0..4;
+// default 0).
+static inline int l2_ahead_layers() {
+  const char* e = getenv("FA_L2_AHEAD");
+  return e ? std::max(0, std::min(4, atoi(e))) : 0;
 }
 
 static size_t dtype_size(fa_dtype t) { return t == FA_DT_F32 ? 4 : 2; }

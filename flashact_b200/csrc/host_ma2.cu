@@ -367,6 +367,7 @@ void ma2_set_debug(fa_handle* h) {
   M::Params& p = h->ma2->params;
   p.inject_barrier = h->params.inject_barrier;
   p.spin_limit = h->params.spin_limit ? h->params.spin_limit : (1u << 24);
+  p.l2_ahead = l2_ahead_layers();
   p.trace = h->trace;
   p.trace_step = h->trace_step;
   p.trace_layer = h->trace_layer;

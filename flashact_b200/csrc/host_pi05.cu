@@ -11,6 +11,7 @@ namespace fa {
 namespace pi05 {
 __global__ void pi05_denoise_kernel(const __grid_constant__ Params p);
 __global__ void pi05_denoise_kernel_f8(const __grid_constant__ Params p);
+__global__ void pi05_denoise_kernel_tm(const __grid_constant__ Params p);
 }
 }  // namespace fa
 
@@ -215,9 +216,10 @@ extern "C" fa_status fa_create(fa_model_kind kind, const fa_config* cfg, int dev
   ALLOC(stage_ns, kMaxStages);
   ALLOC(d_plans, h->num_sms);
 #undef ALLOC
-  const void* kernels[2] = {(const void*)fa::pi05::pi05_denoise_kernel, (const void*)fa::pi05::pi05_denoise_kernel_f8};
-  const int threads[2] = {kThreads, kThreads};
-  for (int i = 0; i < 2; ++i) {
+  const void* kernels[3] = {(const void*)fa::pi05::pi05_denoise_kernel, (const void*)fa::pi05::pi05_denoise_kernel_f8,
+                            (const void*)fa::pi05::pi05_denoise_kernel_tm};
+  const int threads[3] = {kThreads, kThreads, kThreads};
+  for (int i = 0; i < 3; ++i) {
     if (cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDyn) != cudaSuccess)
       return bad(fail(h, FA_ERR_CUDA, "cannot reserve %d bytes of shared memory", kSmemDyn));
     int occ = 0;
@@ -517,7 +519,17 @@ static fa_status build_plan(fa_handle* h) {
   // Weight atoms per ring slot: 64 KB boxes when one token tile is in flight, 32 KB otherwise
   // (keeps an attention CTA's activation batch, which must hold whole slots, inside 64 KB); never
   // more than divides every unit's K range.
-  h->wg = h->NTILE == 64 ? kMaxWG : 2;
+  // Token-major GEMMs (pi05_denoise_kernel_tm) while the batch is one tile of <= 64 tokens with
+  // bf16 weights and every unit's K range is whole 4-atom chunks (FA_TM=0 keeps the weight-major
+  // kernel). Their CTAs stage a unit's activation K-chunks (32 KB each, four on CTAs without
+  // attention units) beside the weight ring, which then holds 32 KB boxes.
+  {
+    const char* e = getenv("FA_TM");
+    bool tm = !(e && atoi(e) == 0) && !h->fp8_stream && use_half_units(h) && act_box_atoms(h) == kTmChunkAtoms;
+    for (int m = 0; m < 4; ++m) tm = tm && (spec[m].katoms / spec[m].split) % kTmChunkAtoms == 0;
+    h->tm = tm;
+  }
+  h->wg = h->tm ? 2 : h->NTILE == 64 ? kMaxWG : 2;
   if (const char* e = getenv("FA_WG")) h->wg = std::max(1, std::min(h->wg, atoi(e)));
   // FP8 streaming: 2 atoms per slot (one 128 x 128-byte E4M3 box, expanded to 32 KB of bf16)
   if (h->fp8_stream) h->wg = 2;
@@ -570,7 +582,9 @@ static fa_status build_plan(fa_handle* h) {
     // Capped so that the weight ring stays deep (larger K ranges load in several batches).
     bb = std::min(bb, std::min(std::min(kMaxBBytes, h->bmax_bytes), kMaxBAtoms * tile));
     bb = std::max(bb, tile * ntg * std::max(act_box_atoms(h), qkv_half ? 2 * h->wg : h->wg));  // one activation box and weight slot per token tile
-    const int work = plans[i].a_cnt > 0 ? kAttnWork : bb + 16 * 1024;  // + epilogue staging
+    if (h->tm) bb = 4 * (int)kTmChunkBytes;
+    // + the epilogue staging area (the token-major epilogues store straight from registers)
+    const int work = plans[i].a_cnt > 0 ? kAttnWork : bb + (h->tm ? 0 : 16 * 1024);
     // Attention CTAs keep their activation area inside the Q region (first 64 KB) so that the
     // prefix-K prefetch into the K/V area survives the GEMM stages in between.
     plans[i].b_bytes = plans[i].a_cnt > 0 ? std::max(tile, std::min(bb, 64 * 1024)) : bb;
@@ -594,6 +608,10 @@ static fa_status build_plan(fa_handle* h) {
       gu.insert(gu.end(), per[i * 4 + m].begin(), per[i * 4 + m].end());
     }
   }
+  if (h->tm)
+    for (int i = 0; i < nblk; ++i)
+      if (plans[i].b_bytes < 2 * (int)kTmChunkBytes)
+        return fail(h, FA_ERR_INVALID, "plan error: CTA %d has room for fewer than two activation chunks", i);
   if (gu.size() > h->n_gunits_cap) {
     if (h->d_gunits) cudaFree(h->d_gunits);
     FA_CUDA(h, cudaMalloc(&h->d_gunits, gu.size() * sizeof(GemmUnit)));
@@ -670,6 +688,7 @@ static fa_status build_params(fa_handle* h) {
   p.trace_step = h->trace_step;
   p.trace_layer = h->trace_layer;
   p.spin_limit = 1u << 24;
+  p.l2_ahead = l2_ahead_layers();
   return FA_OK;
 }
 
@@ -772,7 +791,9 @@ extern "C" fa_status fa_sample_actions(fa_handle* h, int batch, const float* noi
   if (h->timing) FA_CUDA(h, cudaMemsetAsync(h->stage_ns, 0, NUM_STAGES * sizeof(unsigned long long), s));
   FA_CUDA(h, cudaMemcpyAsync(h->x_t, noise, bytes, cudaMemcpyDefault, s));
   void* args[] = {&p};
-  const void* kern = h->fp8_stream ? (const void*)fa::pi05::pi05_denoise_kernel_f8 : (const void*)fa::pi05::pi05_denoise_kernel;
+  const void* kern = h->fp8_stream ? (const void*)fa::pi05::pi05_denoise_kernel_f8
+                     : h->tm       ? (const void*)fa::pi05::pi05_denoise_kernel_tm
+                                   : (const void*)fa::pi05::pi05_denoise_kernel;
   FA_CUDA(h, cudaLaunchCooperativeKernel(kern, dim3(h->num_sms), dim3(kThreads), args, kSmemDyn, s));
   FA_CUDA(h, cudaMemcpyAsync(actions_out, h->x_t, bytes, cudaMemcpyDefault, s));
   h->last_launches = 1;
@@ -836,23 +857,28 @@ extern "C" fa_status fa_set_fault_injection(fa_handle* h, int barrier_index, uns
 constexpr int kNoAllocMaxSteps = 50;
 static __device__ __align__(256) float g_cond_scratch[3 * kNoAllocMaxSteps * D];
 
-// Device address of g_cond_scratch, looked up once per device (the host-side symbol is only a
-// stand-in and must never be handed to a kernel).
-static float* g_cond_scratch_dev[64];
-static std::mutex g_cond_scratch_mu;
-
-static fa_status cond_scratch_address(int device, float** out) {
-  std::lock_guard<std::mutex> lock(g_cond_scratch_mu);
-  if (device < 0 || device >= 64) return fail(nullptr, FA_ERR_INVALID, "device %d out of range", device);
-  if (!g_cond_scratch_dev[device]) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_cond_scratch);
-    if (e != cudaSuccess)
-      return fail(nullptr, FA_ERR_CUDA, "cudaGetSymbolAddress(g_cond_scratch): %s", cudaGetErrorString(e));
-    g_cond_scratch_dev[device] = reinterpret_cast<float*>(ptr);
-  }
-  *out = g_cond_scratch_dev[device];
+// Device address of g_cond_scratch on the current device. The host-side symbol is only a
+// stand-in and must never be handed to a kernel. The lookup is repeated on every call (a host-side
+// table lookup once the module is loaded), so the address stays right after a cudaDeviceReset,
+// which reloads the module at a new address.
+static fa_status cond_scratch_address(float** out) {
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_cond_scratch);
+  if (e != cudaSuccess)
+    return fail(nullptr, FA_ERR_CUDA, "cudaGetSymbolAddress(g_cond_scratch): %s", cudaGetErrorString(e));
+  *out = reinterpret_cast<float*>(ptr);
   return FA_OK;
+}
+
+// True when `p` is device (or managed) memory that kernels on `device` may use directly.
+static bool on_device(const void* p, int device) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (a.type == cudaMemoryTypeManaged) return true;
+  return a.type == cudaMemoryTypeDevice && a.device == device;
 }
 
 extern "C" fa_status fa_pi05_modulations_noalloc(const fa_pi05_weights* w, int num_layers, int num_steps,
@@ -862,20 +888,27 @@ extern "C" fa_status fa_pi05_modulations_noalloc(const fa_pi05_weights* w, int n
     return fail(nullptr, FA_ERR_INVALID, "num_steps %d outside 1..%d (the static scratch holds %d steps)", num_steps,
                 kNoAllocMaxSteps, kNoAllocMaxSteps);
   if (num_layers < 1 || num_layers > 64) return fail(nullptr, FA_ERR_INVALID, "num_layers %d outside 1..64", num_layers);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return fail(nullptr, FA_ERR_CUDA, "cudaGetDevice failed");
+  // An error left pending by the caller's earlier work would otherwise be reported (and cleared)
+  // as if one of these launches had failed: refuse to start instead and leave it in place.
+  const cudaError_t pending = cudaPeekAtLastError();
+  if (pending != cudaSuccess)
+    return fail(nullptr, FA_ERR_CUDA, "a CUDA error is pending from earlier work on this thread: %s",
+                cudaGetErrorString(pending));
   const fa_tensor* need[] = {&w->ln_in_w, &w->ln_in_b, &w->ln_post_w, &w->ln_post_b, &w->norm_w,
                              &w->norm_b, &w->time_in_w, &w->time_in_b, &w->time_out_w, &w->time_out_b};
   for (const fa_tensor* t : need) {
-    if (!t->ptr || !is_device_ptr(t->ptr))
-      return fail(nullptr, FA_ERR_INVALID, "every conditioning weight must be a device pointer (none is staged here)");
+    if (!t->ptr || !on_device(t->ptr, device))
+      return fail(nullptr, FA_ERR_INVALID,
+                  "every conditioning weight must be memory of the current device %d (none is staged here)", device);
     if (t->dtype != FA_DT_F32 && t->dtype != FA_DT_BF16 && t->dtype != FA_DT_F16)
       return fail(nullptr, FA_ERR_INVALID, "unsupported weight dtype %d", (int)t->dtype);
   }
-  if (!is_device_ptr(mods_out) || !is_device_ptr(mod_final_out))
-    return fail(nullptr, FA_ERR_INVALID, "mods_out / mod_final_out must be device pointers");
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return fail(nullptr, FA_ERR_CUDA, "cudaGetDevice failed");
+  if (!on_device(mods_out, device) || !on_device(mod_final_out, device))
+    return fail(nullptr, FA_ERR_INVALID, "mods_out / mod_final_out must be memory of the current device %d", device);
   float* scratch = nullptr;
-  fa_status st = cond_scratch_address(device, &scratch);
+  fa_status st = cond_scratch_address(&scratch);
   if (st != FA_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int S = num_steps, L = num_layers;
@@ -887,27 +920,39 @@ extern "C" fa_status fa_pi05_modulations_noalloc(const fa_pi05_weights* w, int n
       cudaFuncSetAttribute(linear_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return fail(nullptr, FA_ERR_CUDA, "cannot reserve %zu bytes of shared memory", smem);
   int sms = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  const int grid = std::max(1, sms * 2);
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms < 1)
+    return fail(nullptr, FA_ERR_CUDA, "cudaDeviceGetAttribute(multiProcessorCount) failed on device %d", device);
+  const int grid = sms * 2;
+  // every launch is checked at once: nothing was pending on entry, so an error here is ours
+#define NOALLOC_CHECK(what)                                                                        \
+  do {                                                                                             \
+    const cudaError_t e_ = cudaGetLastError();                                                     \
+    if (e_ != cudaSuccess) return fail(nullptr, FA_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e_)); \
+  } while (0)
   time_embed_kernel<<<8, 256, 0, s>>>(emb, S, D);
+  NOALLOC_CHECK("time embedding");
   linear_f32_kernel<<<grid, 256, smem, s>>>(w->time_in_w.ptr, w->time_in_w.dtype, w->time_in_b.ptr, w->time_in_b.dtype,
                                             emb, S, D, D, h1, D, 1);
+  NOALLOC_CHECK("time MLP in");
   linear_f32_kernel<<<grid, 256, smem, s>>>(w->time_out_w.ptr, w->time_out_w.dtype, w->time_out_b.ptr,
                                             w->time_out_b.dtype, h1, S, D, D, cond, D, 1);
+  NOALLOC_CHECK("time MLP out");
   const size_t sstride = (size_t)L * 2 * MOD;
   for (int l = 0; l < L; ++l) {
     linear_f32_kernel<<<grid, 256, smem, s>>>(
         (const char*)w->ln_in_w.ptr + (size_t)l * MOD * D * dtype_size(w->ln_in_w.dtype), w->ln_in_w.dtype,
         (const char*)w->ln_in_b.ptr + (size_t)l * MOD * dtype_size(w->ln_in_b.dtype), w->ln_in_b.dtype, cond, S, D, MOD,
         mods_out + (size_t)l * 2 * MOD, sstride, 0);
+    NOALLOC_CHECK("input adaRMS dense");
     linear_f32_kernel<<<grid, 256, smem, s>>>(
         (const char*)w->ln_post_w.ptr + (size_t)l * MOD * D * dtype_size(w->ln_post_w.dtype), w->ln_post_w.dtype,
         (const char*)w->ln_post_b.ptr + (size_t)l * MOD * dtype_size(w->ln_post_b.dtype), w->ln_post_b.dtype, cond, S, D,
         MOD, mods_out + (size_t)l * 2 * MOD + MOD, sstride, 0);
+    NOALLOC_CHECK("post-attention adaRMS dense");
   }
-  linear_f32_kernel<<<grid, 256, smem, s>>>(w->norm_w.ptr, w->norm_w.dtype, w->norm_b.ptr, w->norm_b.dtype, cond, S, D,
-                                            MOD, mod_final_out, MOD, 0);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(nullptr, FA_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
+  linear_f32_kernel<<<grid, 256, smem, s>>>(w->norm_w.ptr, w->norm_w.dtype, w->norm_b.ptr,
+                                            w->norm_b.dtype, cond, S, D, MOD, mod_final_out, MOD, 0);
+  NOALLOC_CHECK("final adaRMS dense");
+#undef NOALLOC_CHECK
   return FA_OK;
 }

@@ -392,12 +392,73 @@ __device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu
   }
 }
 
+// Token-major epilogue (bound batch = one tile of <= 64 tokens): thread = token n, v = 32
+// consecutive columns c0.. of its accumulator row, i.e. 32 consecutive packed weight rows of the
+// unit. In the packed QKV and gate/up tiles, row 32 q + i (i < 16) and row 32 q + 16 + i are
+// rotary / GeGLU partners, so both halves of a 32-column group sit in this thread's registers.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b2);
+}
+__device__ __forceinline__ void epi_tm(const EpiCtx& p, const GemmUnit& gu, int m, int n, int c0, const float* v) {
+  if (n >= p.NT) return;
+  const int q = 2 * (gu.half ? gu.half - 1 : 0) + (c0 >> 5);  // row quadrant of the 128-row packed tile
+  if (m == MAT_QKV) {
+    const int mt = gu.mtile;
+    const int b = tok_bi(p.invT, n), t = n - b * p.T;
+    if (mt < 18) {  // Q heads / K: split-half RoPE, pair dims p0 + i and p0 + 128 + i
+      const int pb = mt < 16 ? (mt & 1) : mt - 16;
+      const int p0 = 64 * pb + 16 * q;
+      float cs[16], sn[16];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.rope_cos + (size_t)n * 128 + p0) + k);
+        const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.rope_sin + (size_t)n * 128 + p0) + k);
+        cs[4 * k] = c4.x; cs[4 * k + 1] = c4.y; cs[4 * k + 2] = c4.z; cs[4 * k + 3] = c4.w;
+        sn[4 * k] = s4.x; sn[4 * k + 1] = s4.y; sn[4 * k + 2] = s4.z; sn[4 * k + 3] = s4.w;
+      }
+      uint32_t lo[8], hi[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i0 = 2 * k, i1 = 2 * k + 1;
+        lo[k] = pack_bf16x2(fmaf(v[i0], cs[i0], -v[16 + i0] * sn[i0]), fmaf(v[i1], cs[i1], -v[16 + i1] * sn[i1]));
+        hi[k] = pack_bf16x2(fmaf(v[16 + i0], cs[i0], v[i0] * sn[i0]), fmaf(v[16 + i1], cs[i1], v[i1] * sn[i1]));
+      }
+      __nv_bfloat16* dst = mt < 16 ? p.q + ((size_t)(b * H + (mt >> 1)) * TPAD + t) * HD : p.sk + ((size_t)b * TPAD + t) * HD;
+      uint4* d0 = reinterpret_cast<uint4*>(dst + p0);
+      uint4* d1 = reinterpret_cast<uint4*>(dst + p0 + 128);
+      d0[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      d0[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+      d1[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      d1[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+    } else {  // V: natural row order, stored transposed [dim][token]
+      const int dim0 = (mt - 18) * 128 + 32 * q;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) p.svt[((size_t)b * HD + dim0 + i) * TPAD + t] = __float2bfloat16(v[i]);
+    }
+  } else if (m == MAT_GU) {  // GeGLU: columns i < 16 gate, 16 + i up of feature f0 + i
+    const int f0 = 64 * gu.mtile + 16 * q;
+    uint32_t hv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      hv[k] = pack_bf16x2(gelu_tanh(v[2 * k]) * v[16 + 2 * k], gelu_tanh(v[2 * k + 1]) * v[17 + 2 * k]);
+    uint4* d = reinterpret_cast<uint4*>(p.hbuf + (size_t)n * F + f0);
+    d[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    d[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+  } else {  // O / down: fp32 K-split partial of rows 32 q .. 32 q + 31 of the tile
+    float4* d = reinterpret_cast<float4*>(p.part + ((size_t)gu.split * p.NPAD + n) * D + gu.mtile * 128 + 32 * q);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) d[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  }
+}
+
 // ------------------------------------------------------------------ model traits for the engine
 struct Pi05Model {
   using Params = pi05::Params;
   using Epi = EpiCtx;
   static constexpr int kMats = 4;  // per layer, in consumption order: QKV, O, gate/up, down
   static constexpr bool kF8 = false;
+  static constexpr bool kTM = false;  // token-major GEMMs (one tile of <= 64 tokens)
   __device__ static float row_scale(const Params&, int, int, int, int) { return 1.0f; }
   __device__ static int rows(int m) { return m == MAT_QKV ? QKV_ROWS : (m == MAT_GU ? 2 * F : D); }
   __device__ static int wmap(int m) { return MAP_W_QKV + m; }
@@ -418,6 +479,15 @@ struct Pi05Model {
   __device__ static void epi_copy_out(const Epi& e, const GemmUnit& gu, int m, int nb0, int r0, int r1) {
     pi05::epi_copy_out(e, gu, m, nb0, r0, r1);
   }
+  __device__ static void epi_tm(const Epi& e, const GemmUnit& gu, int m, int n, int c0, const float* v) {
+    pi05::epi_tm(e, gu, m, n, c0, v);
+  }
+};
+
+// One tile of <= 64 tokens (bs=1 at T <= 64): token-major GEMMs (activations in tensor memory,
+// weights as the B operand).
+struct Pi05ModelTM : Pi05Model {
+  static constexpr bool kTM = true;
 };
 
 // FP8 weight streaming: E4M3 tiles in the ring, expanded to bf16 in tensor memory by the epilogue
@@ -670,6 +740,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = 0;
     s_st.last_q = -1;
     s_st.k_pre = 0;
+    s_st.qtm = 0;
   }
   __syncthreads();
   {  // this CTA's work lists, read once from global memory
@@ -688,6 +759,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
   c.acnt = s_plan.a_cnt;
   c.batoms = min(kMaxBAtoms, s_plan.b_bytes / (p.NTILE * 128));
   c.ring_slots = s_plan.ring_slots;
+  c.tm_slots = min(4, s_plan.b_bytes / (int)kTmChunkBytes);
   c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   // ring slots: wg bf16 atoms, or (FP8 streaming) the same K range of E4M3 codes, half the bytes
   c.work = c.ring + (size_t)c.ring_slots * p.wg * (Model::kF8 ? kAtomBytes / 2 : kAtomBytes);
@@ -701,7 +773,9 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     // E4M3 slots are released by the 128 epilogue threads that convert them, bf16 slots by an
     // MMA commit; TMEM A slots are filled by those threads and released by an MMA commit
     for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], Model::kF8 ? 128 : 1); }
-    for (int i = 0; i < kASlotsF8; ++i) { mbar_init(&bars.afull[i], 128); mbar_init(&bars.aempty[i], 1); }
+    // A slots: filled by the 128 converting threads (FP8) or by the 64 token threads (token-major)
+    for (int i = 0; i < kASlotsF8; ++i) { mbar_init(&bars.afull[i], Model::kTM ? 64 : 128); mbar_init(&bars.aempty[i], 1); }
+    for (int i = 0; i < 4; ++i) mbar_init(&bars.sfull[i], 1);
     mbar_init(&bars.bfull, 1);
     mbar_init(&bars.bempty, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&bars.acc_full[i], 1); mbar_init(&bars.acc_empty[i], 128); }
@@ -729,7 +803,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     const bool is_mma = (warp == 1);
     const bool is_epi = warp >= 2;
     MmaState& st = s_st;
-    uint32_t ecnt = 0, anu = 0, gen = 0;
+    uint32_t ecnt = 0, anu = 0, gen = 0, qtm = 0;
     ConvState cs{0, 0};  // FP8 kernel: E4M3 slots converted (epilogue warps)
     uint64_t t_prev = globaltimer();
     const bool timing = p.stage_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 32;
@@ -783,8 +857,13 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
         for (int s = 0; s < 8; ++s) {
           const int m = gemm_of(s);
           if (m >= 0) {
-            if (is_mma) mma_gemm<Model>(p, c, st, m);
-            if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l, cs);
+            if constexpr (Model::kTM) {
+              if (is_mma) mma_gemm_tm<Model>(p, c, st, m);
+              if (is_epi) ecnt = epi_gemm_tm<Model>(p, c, ecnt, m, qtm);
+            } else {
+              if (is_mma) mma_gemm<Model>(p, c, st, m);
+              if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l, cs);
+            }
           } else if (s == 1) {
             if (is_mma) {
               if (leader()) st.last_q = -1;
@@ -839,6 +918,9 @@ __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel(const __grid_
 }
 __global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel_f8(const __grid_constant__ Params p) {
   denoise_body<Pi05ModelF8>(p);
+}
+__global__ void __launch_bounds__(kThreads, 1) pi05_denoise_kernel_tm(const __grid_constant__ Params p) {
+  denoise_body<Pi05ModelTM>(p);
 }
 
 }  // namespace pi05

@@ -163,8 +163,8 @@ FA_API fa_status fa_pi05_load_weights(fa_handle* h, const fa_pi05_weights* w, fa
 /* Quantised pi0.5 GEMM weights (fmt FA_WFMT_FP8 or FA_WFMT_NVFP4; see fa_qscale): the seven
  * GEMM tensors of `w` carry the codes (their dtype field is ignored), `s` their scales; the other
  * fields as for fa_pi05_load_weights. FP8: the codes are packed as they are and the FP8 kernel
- * streams them (half the bytes of bf16): each E4M3 tile is expanded to bf16 in shared memory
- * (exact) for the tensor cores and the row scale multiplies the fp32 accumulator, the
+ * streams them (half the bytes of bf16): each E4M3 tile is expanded exactly to bf16 in tensor
+ * memory, where the MMAs read it as their A operand, and the row scale multiplies the fp32 accumulator, the
  * reference's W8A16 scheme (src/pi05/mk6.cu:90-94,204-205,219-220); codes must be 16-byte
  * aligned. (Environment FA_FP8_STREAM=0 at load time dequantises them into the bf16 layout
  * instead.) NVFP4: dequantised once on the device into the bf16 layout (value = code x block
@@ -257,10 +257,15 @@ FA_API fa_status fa_debug_trace(fa_handle* h, int step, int layer, unsigned long
  * the layout fa_set_modulation takes) on `stream`, asynchronously. Only the conditioning fields of
  * `w` are read (ln_*, norm_*, time_*), and they must already be in device memory.
  * Scratch: a static 600 KB device array inside the library (at most 50 steps), held by every GPU
- * that loads the library until exit; the call allocates nothing. The first call on each device
- * looks the array up (cudaGetSymbolAddress) with that device current, so make that first call
- * before any stream capture. All calls share the array: calls that overlap on the GPU race. The
- * last error message is read with fa_last_error(NULL). Rejects num_steps > 50. */
+ * that loads the library until exit; the call allocates nothing itself. Under CUDA's lazy module
+ * loading, the library's device module (and with it that array) is loaded on a device the first
+ * time the library touches it there, and that load takes device memory: make the first call on
+ * each device at start-up, before the memory budget is fixed and before any stream capture. Every
+ * call looks the array up (cudaGetSymbolAddress) on the current device, so it keeps working after
+ * a cudaDeviceReset. Weights and outputs must be memory of the current device (or managed).
+ * A CUDA error already pending on the thread is reported (FA_ERR_CUDA) and left in place; nothing
+ * is launched then. All calls share the array: calls that overlap on the GPU race. The last error
+ * message is read with fa_last_error(NULL). Rejects num_steps > 50. */
 FA_API fa_status fa_pi05_modulations_noalloc(const fa_pi05_weights* w, int num_layers, int num_steps,
                                              float* mods_out, float* mod_final_out, fa_stream stream);
 

@@ -14,7 +14,9 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-REF = os.environ.get("FA_REFERENCE_ROOT", "/root/reference")
+# The reference checkout: $FA_REFERENCE_ROOT, else a directory named "reference" beside this
+# repository (the layout of the build machine); absent on GPU boxes, which use the prebuilt .so files.
+REF = os.environ.get("FA_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 KERNELS = {
     "mk_v6_ref": ["src/pi05/binding.cpp", "src/pi05/mk6.cu"],
     "mk_ma2_ref": ["src/molmoact2/binding.cpp", "src/molmoact2/mk_ma2.cu"],

@@ -160,7 +160,7 @@ def test_device_quantised_weights_load(require_gpu):
 @pytest.mark.gpu
 @pytest.mark.parametrize("B", [1, 3, 12])
 def test_fp8_stream_matches_dequantised_path(require_gpu, monkeypatch, B):
-    """The FP8-streaming kernel (E4M3 tiles expanded in shared memory, row scales in the epilogue)
+    """The FP8-streaming kernel (E4M3 tiles expanded into tensor memory, row scales in the epilogue)
     against the same codes dequantised at load into the bf16 kernel (FA_FP8_STREAM=0) and against
     the fp32 oracle: 64-row units at bs=1, 128-row units over two token tiles at bs=3."""
     c = O.make_case(seed=63, L=2, T=50, AD=32, Lp=300, B=B, num_steps=2)
