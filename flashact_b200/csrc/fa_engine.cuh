@@ -150,7 +150,7 @@ __device__ __forceinline__ bool leader() { return (threadIdx.x & 31) == 0; }
 // ------------------------------------------------------------------ CTA context
 struct Bars {
   uint64_t wfull[kMaxRing], wempty[kMaxRing];
-  uint64_t afull[kASlotsF8], aempty[kASlotsF8];  // FP8 streaming: TMEM A slot written / read by the MMAs
+  uint64_t afull[kTmASlots], aempty[kTmASlots];  // TMEM A slot written / read by the MMAs (FP8: 2, token-major: 3)
   uint64_t bfull, bempty;  // activation batch loaded / consumed
   uint64_t sfull[4];       // token-major GEMMs: activation K-chunk landed in staging slot 0..3
   uint64_t acc_full[2], acc_empty[2];
@@ -207,27 +207,33 @@ __device__ __forceinline__ void run_producer(const typename Model::Params& p, co
   bool ok = true;
   // L2 prefetch of the weight stream, `ahead` layer-steps in front of the ring: HBM keeps
   // streaming while the dependent chain of a layer (attention, norms, barriers) runs, and the
-  // GEMM stages then read their weights from L2. Each CTA prefetches exactly the boxes it will
-  // load itself, in the same (matrix, unit, K) order.
+  // GEMM stages then read their weights from L2. Each CTA prefetches exactly the rows and K
+  // ranges of its own units, with all 32 lanes issuing line prefetches (prefetch.global.L2 goes
+  // through the load/store path, so the TMA queue, which carries the ring and activation loads,
+  // stays clear).
   const int ahead = p.l2_ahead, total_layers = nsteps * L;
-  const uint64_t pol_pf = policy_evict_normal();
   auto prefetch_layer = [&](int g) {
-    if (g >= total_layers || !leader()) return;
+    if (g >= total_layers) return;
     const int lp = g % L;
 #pragma unroll 1
     for (int m = 0; m < Model::kMats; ++m) {
       const int rows = Model::rows(m);
+      const uint8_t* const wb = p.wraw[m];
+      const size_t rb = (size_t)p.wrow_bytes[m];
+      const int esz = F8 ? 1 : 2;
 #pragma unroll 1
       for (int u = 0; u < gcnt[m]; ++u) {
         const GemmUnit gu = gul[m][u];
-        const int aps = gu.half ? 2 * wg : wg;
-        const int map = gu.half ? Model::wmap_half(m) : Model::wmap(m);
-        const int row0 = lp * rows + gu.mtile * 128 + (gu.half == 2 ? 64 : 0);
-        // (several token groups share a weight tile: prefetch it once)
-        if (gu.grp != 0) continue;
-#pragma unroll 1
-        for (int j = 0; j < gu.natoms; j += aps)
-          tma_prefetch_l2_3d(maps + map, 0, row0, F8 ? (gu.katom0 + j) >> 1 : gu.katom0 + j, pol_pf);
+        if (gu.grp != 0) continue;  // token groups share a weight tile: prefetch it once
+        const int nr = gu.half ? 64 : 128;
+        const size_t r0 = (size_t)lp * rows + gu.mtile * 128 + (gu.half == 2 ? 64 : 0);
+        const int lpr = gu.natoms * 64 * esz / 128;  // 128-byte lines per row segment
+        const uint8_t* base = wb + r0 * rb + (size_t)gu.katom0 * 64 * esz;
+#pragma unroll 4
+        for (int i = lane_id(); i < nr * lpr; i += 32) {
+          const int r = i / lpr, cidx = i - r * lpr;
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (size_t)r * rb + cidx * 128));
+        }
       }
     }
   };
@@ -455,85 +461,111 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
 //
 // Activation K-chunks of kTmChunkAtoms atoms (256 K) flow: TMA into a staging slot (MMA lane) ->
 // the epilogue warps of TMEM lane quadrants 0 and 1 (one token per thread) copy their row into a
-// TMEM A slot -> MMAs -> the slot is released by an MMA commit. Staging slot q & 1 is free again
-// once the fill of chunk q has been signalled (afull), so the MMA lane refills it right after.
-// TMEM: accumulators at columns [0, 256) (two buffers of N <= 128), A slots at [256, 512).
+// TMEM A slot -> MMAs -> the slot is released by an MMA commit. A unit's first chunks go out at
+// once, one per staging slot (four on CTAs without attention units); a staging slot is free again
+// once the fill of its chunk has been signalled (afull), and the MMA lane refills it right after.
+// (Per-thread cp.async staging, which keeps the activation loads out of the TMA queue, was measured
+// slower: 10.3 against 8.8 ms per chunk.)
+// TMEM: one accumulator at columns [0, 128) (N <= 128), three A slots at [128, 512).
 // (kTmChunkAtoms, kTmChunkBytes, kTmACol, kTmASlotCols: fa_engine_types.cuh)
 
+// MMAs of NA consecutive weight atoms of one ring slot against the matching A columns, fully
+// unrolled with compile-time descriptor offsets: the issuing thread then spends a few independent
+// integer adds per MMA. (A rolled loop that recomputes the descriptors per MMA made the single
+// issuing thread latency-bound at 110-260 cycles per MMA, against ~48 for M128 N64 K16.)
+// `first`: this is the unit's first slot (its first MMA overwrites the accumulator).
+template <int NA, uint32_t WST16>
+__device__ __forceinline__ void tm_issue(uint32_t tacc, uint32_t ta, uint64_t db, uint32_t idesc, bool first) {
+#pragma unroll
+  for (int jj = 0; jj < NA; ++jj)
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+      tc_mma_bf16_ts(tacc, ta + jj * 32 + 8 * s, db + (uint64_t)(jj * WST16 + 2 * s), idesc,
+                     (jj | s) != 0 || !first);
+}
+
 // The whole role runs on lane 0 of the MMA warp (lanes 1..31 wait at the warp sync after it):
-// no warp-level synchronisation between consecutive MMAs.
+// no warp-level synchronisation between consecutive MMAs. Ring slots hold 32 KB boxes (wg = 2):
+// one K-chunk of a 64-row unit is one slot of 4 atoms, one K-chunk of a 128-row unit two slots of
+// 2 atoms.
 template <class Model>
 __device__ __noinline__ bool mma_gemm_tm_lane(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
-  trace_mark(12);
+  trace_mark(14);
   MmaState st = st_shared;
   uint8_t* const ring = c.ring;
-  uint8_t* const work = c.work;
   Bars* const bars = c.bars;
   int* const err = p.err;
-  const CUtensorMap* const amap = &p.maps[Model::act_map(m)];
   const uint32_t tmem = c.tmem;
-  const int R = c.ring_slots, wg = p.wg;
-  const uint32_t slot_bytes = (uint32_t)wg * kAtomBytes;
-  const GemmUnit* const units = c.gu[m];
-  const int nunits = c.gcnt[m];
+  const int R = c.ring_slots;
+  constexpr uint32_t kSlotBytes = 2 * kAtomBytes;
+  constexpr uint32_t kHalfAtom16 = kAtomBytes / 2 / 16, kFullAtom16 = kAtomBytes / 16;  // atom strides, 16-byte units
+  uint8_t* const work = c.work;
+  const CUtensorMap* const amap = &p.maps[Model::act_map(m)];
   const uint64_t pol = policy_evict_last();
   const uint32_t nst = (uint32_t)c.tm_slots;
+  const GemmUnit* const units = c.gu[m];
+  const int nunits = c.gcnt[m];
+  const uint64_t ring_desc = sdesc_sw128(ring);
   uint32_t wslot = st.wit % R, wphase = (st.wit / R) & 1;
+  // next ring slot: wait for it, return its descriptor
+  auto take_slot = [&](uint64_t& db) -> bool {
+    if (!mbar_wait(&bars->wfull[wslot], wphase, err, KERR_MMA)) return false;
+    db = ring_desc + (uint64_t)((wslot * kSlotBytes) >> 4);
+    return true;
+  };
+  auto release_slot = [&]() {
+    tc_commit(&bars->wempty[wslot]);
+    ++st.wit;
+    if (++wslot == (uint32_t)R) { wslot = 0; wphase ^= 1; }
+  };
 #pragma unroll 1
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
-    const int natoms = gu.natoms, nch = natoms / kTmChunkAtoms;
-    const int aps = gu.half ? 2 * wg : wg;                       // weight atoms per ring slot
-    const uint32_t wst = gu.half ? kAtomBytes / 2 : kAtomBytes;  // weight atom stride inside a slot
-    const uint32_t idesc = idesc_bf16(128, gu.half ? 64 : 128);
+    const int nch = gu.natoms / kTmChunkAtoms;
     const uint32_t q0 = st.qtm;
 #pragma unroll 1
-    for (int ch = 0; ch < nst && ch < nch; ++ch) {  // the unit's first K-chunks, one per staging slot
+    for (int ch = 0; ch < (int)nst && ch < nch; ++ch) {  // the unit's first K-chunks, one per staging slot
       const int sl = (int)((q0 + ch) % nst);
       uint64_t* b = &bars->sfull[sl];
       mbar_expect_tx(b, kTmChunkBytes);
       tma_load_3d(work + sl * kTmChunkBytes, amap, b, 0, 0, gu.katom0 + ch * kTmChunkAtoms, pol);
     }
-    const int a = st.acc & 1;
-    if (st.acc >= 2 && !mbar_wait(&bars->acc_empty[a], ((st.acc >> 1) - 1) & 1, err, KERR_MMA)) return false;
-    const uint32_t tacc = tmem + a * 128;
-    int js = 0;  // atom within the current ring slot
-    uint64_t db = 0;
+    // one accumulator: the previous unit's must have been drained
+    if (st.acc >= 1 && !mbar_wait(&bars->acc_empty[0], (st.acc - 1) & 1, err, KERR_MMA)) return false;
+    const uint32_t tacc = tmem;
 #pragma unroll 1
     for (int ch = 0; ch < nch; ++ch) {
       const uint32_t q = q0 + ch;
-      if (!mbar_wait(&bars->afull[q & 1], (q >> 1) & 1, err, KERR_MMA)) return false;
+      const uint32_t qa = q % kTmASlots;
+      if (!mbar_wait(&bars->afull[qa], (q / kTmASlots) & 1, err, KERR_MMA)) return false;
       tc_fence_after();
-      if (u == 0) trace_mark(ch == 0 ? 9 : ch == 1 ? 10 : ch == 2 ? 11 : 13);
-      if (ch + nst < nch) {  // the fill has read this chunk's staging slot: refill it
+      if (u == 0) trace_mark(ch == 0 ? 9 : ch == 1 ? 10 : 11);
+      if (ch + (int)nst < nch) {  // the fill has read this chunk's staging slot: refill it
         const int sl = (int)(q % nst);
         uint64_t* b = &bars->sfull[sl];
         mbar_expect_tx(b, kTmChunkBytes);
         tma_load_3d(work + sl * kTmChunkBytes, amap, b, 0, 0, gu.katom0 + (ch + nst) * kTmChunkAtoms, pol);
       }
-      const uint32_t ta = tmem + kTmACol + (q & 1) * kTmASlotCols;
-#pragma unroll
-      for (int jj = 0; jj < kTmChunkAtoms; ++jj) {
-        if (js == 0) {
-          if (!mbar_wait(&bars->wfull[wslot], wphase, err, KERR_MMA)) return false;
-          db = sdesc_sw128(ring + (size_t)wslot * slot_bytes);
-          if (u == 0) trace_mark(ch == 0 ? 1 : 14);
-        }
-        const uint64_t dbj = db + (uint64_t)((js * wst) >> 4);
-#pragma unroll
-        for (int s = 0; s < 4; ++s) tc_mma_bf16_ts(tacc, ta + jj * 32 + 8 * s, dbj + 2 * s, idesc, (ch | jj | s) != 0);
-        if (++js == aps || ch * kTmChunkAtoms + jj == natoms - 1) {
-          tc_commit(&bars->wempty[wslot]);
-          js = 0;
-          ++st.wit;
-          if (++wslot == (uint32_t)R) { wslot = 0; wphase ^= 1; }
-        }
+      const uint32_t ta = tmem + kTmACol + qa * kTmASlotCols;
+      uint64_t db;
+      if (gu.half) {  // N = 64: 64-row atoms of 8 KB, one slot per chunk
+        if (!take_slot(db)) return false;
+        if (u == 0) trace_mark(ch == 0 ? 1 : ch == 1 ? 4 : 13);
+        tm_issue<4, kHalfAtom16>(tacc, ta, db, idesc_bf16(128, 64), ch == 0);
+        release_slot();
+      } else {  // N = 128: 128-row atoms of 16 KB, two slots per chunk
+        if (!take_slot(db)) return false;
+        tm_issue<2, kFullAtom16>(tacc, ta, db, idesc_bf16(128, 128), ch == 0);
+        release_slot();
+        if (!take_slot(db)) return false;
+        tm_issue<2, kFullAtom16>(tacc, ta + 64, db, idesc_bf16(128, 128), false);
+        release_slot();
       }
-      tc_commit(&bars->aempty[q & 1]);
-      if (u == 0) trace_mark(ch == 0 ? 15 : ch == 1 ? 2 : ch == 2 ? 3 : 8);
+      tc_commit(&bars->aempty[qa]);
+      if (u == 0) trace_mark(ch == 0 ? 15 : ch == 1 ? 6 : ch == 2 ? 3 : 8);
     }
     st.qtm = q0 + nch;
-    tc_commit(&bars->acc_full[a]);
+    tc_commit(&bars->acc_full[0]);
     ++st.acc;
   }
   st_shared = st;
@@ -561,7 +593,8 @@ __device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p,
   const int tok = qd * 32 + lane;
   int* const err = p.err;
   Bars* const bars = c.bars;
-  const uint8_t* const work = c.work;
+  uint8_t* const stage_base = c.work;
+  const int sw = tok & 7;  // 128-byte swizzle of this thread's staging rows (conflict-free)
   const uint32_t tl = c.tmem + ((uint32_t)(qd * 32) << 16);
   const GemmUnit* const units = c.gu[m];
   const int nunits = c.gcnt[m];
@@ -577,10 +610,10 @@ __device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p,
       for (int ch = 0; ch < nch; ++ch) {
         const uint32_t q = qtm + ch;
         if (!mbar_wait(&bars->sfull[q % nst], (q / nst) & 1, err, KERR_EPI)) return ecnt;
-        if (q >= 2 && !mbar_wait(&bars->aempty[q & 1], ((q >> 1) - 1) & 1, err, KERR_EPI)) return ecnt;
+        const uint32_t qa = q % kTmASlots;
+        if (q >= kTmASlots && !mbar_wait(&bars->aempty[qa], ((q / kTmASlots) - 1) & 1, err, KERR_EPI)) return ecnt;
         tc_fence_after();
-        const uint8_t* row = work + (q % nst) * kTmChunkBytes + tok * 128;
-        const int sw = tok & 7;
+        const uint8_t* row = stage_base + (q % nst) * kTmChunkBytes + tok * 128;
 #pragma unroll 1
         for (int at = 0; at < kTmChunkAtoms; ++at) {
           uint32_t w[32];
@@ -589,31 +622,29 @@ __device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p,
             const uint4 v = *reinterpret_cast<const uint4*>(row + at * (64 * 128) + ((cc ^ sw) << 4));
             w[4 * cc] = v.x; w[4 * cc + 1] = v.y; w[4 * cc + 2] = v.z; w[4 * cc + 3] = v.w;
           }
-          tmem_st32(tl + kTmACol + (q & 1) * kTmASlotCols + at * 32, w);
+          tmem_st32(tl + kTmACol + qa * kTmASlotCols + at * 32, w);
         }
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(&bars->afull[q & 1]);
+        mbar_arrive(&bars->afull[qa]);
       }
     }
     qtm += nch;
-    const int a = ecnt & 1;
-    if (!mbar_wait(&bars->acc_full[a], (ecnt >> 1) & 1, err, KERR_EPI)) return ecnt;
+    if (!mbar_wait(&bars->acc_full[0], ecnt & 1, err, KERR_EPI)) return ecnt;
     tc_fence_after();
-    if (u == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);
     if (active) {
       const int ncols = gu.half ? 64 : 128;
 #pragma unroll 1
       for (int c0 = 0; c0 < ncols; c0 += 32) {
         float v[32];
-        tmem_ld16(tl + a * 128 + c0, v);
-        tmem_ld16(tl + a * 128 + c0 + 16, v + 16);
+        tmem_ld16(tl + c0, v);
+        tmem_ld16(tl + c0 + 16, v + 16);
         tc_wait_ld();
         Model::epi_tm(e, gu, m, tok, c0, v);
       }
     }
     tc_fence_before();
-    mbar_arrive(&bars->acc_empty[a]);
+    mbar_arrive(&bars->acc_empty[0]);
     ++ecnt;
   }
   return ecnt;

@@ -80,6 +80,8 @@ struct Params {
   // L2 prefetch distance of the weight stream, in layers (0 = off): the producer warp brings
   // this CTA's weight boxes of layer-step g + l2_ahead into L2 when it starts layer-step g.
   int l2_ahead;
+  const uint8_t* wraw[kMaxMats];  // streamed weight matrices (bf16, or E4M3 codes), row-major [L * rows][K]
+  int wrow_bytes[kMaxMats];        // bytes per weight row
   unsigned long long* stage_ns;
   int inject_barrier;
   unsigned int spin_limit;

@@ -79,6 +79,8 @@ struct Params {
   // L2 prefetch distance of the weight stream, in layers (0 = off): the producer warp brings
   // this CTA's weight boxes of layer-step g + l2_ahead into L2 when it starts layer-step g.
   int l2_ahead;
+  const uint8_t* wraw[kMaxMats];  // streamed weight matrices (bf16, or E4M3 codes), row-major [L * rows][K]
+  int wrow_bytes[kMaxMats];        // bytes per weight row
   // FP8 weight streaming: per packed weight row, its E4M3 scale, [L][rows] per matrix (QKV, O,
   // gate/up, down); unused by the bf16 kernel
   const float* wscale[4];

@@ -352,6 +352,10 @@ static fa_status ma2_params(fa_handle* h) {
   p.gunits = s->d_gunits; p.aunits = s->d_aunits; p.plans = s->d_plans; p.ctx_len = s->d_ctx;
   p.mods = s->mods; p.mod_final = s->mod_final; p.rope_cos = s->rope_cos; p.rope_sin = s->rope_sin;
   for (int m = 0; m < M::NUM_MATS; ++m) p.bias[m] = s->bias[m];
+  for (int m = 0; m < M::NUM_MATS; ++m) {
+    p.wraw[m] = reinterpret_cast<const uint8_t*>(s->w[m]);
+    p.wrow_bytes[m] = kMatK[m] * 2;
+  }
   p.b_up = s->b_up;
   p.w_ain = s->w_ain; p.b_ain = s->b_ain; p.w_aout = s->w_aout; p.b_aout = s->b_aout;
   p.kctx = s->kctx; p.vctx = s->vctx;

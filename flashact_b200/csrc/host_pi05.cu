@@ -529,12 +529,13 @@ static fa_status build_plan(fa_handle* h) {
     for (int m = 0; m < 4; ++m) tm = tm && (spec[m].katoms / spec[m].split) % kTmChunkAtoms == 0;
     h->tm = tm;
   }
-  h->wg = h->tm ? 2 : h->NTILE == 64 ? kMaxWG : 2;
-  if (const char* e = getenv("FA_WG")) h->wg = std::max(1, std::min(h->wg, atoi(e)));
+  h->wg = h->tm ? 2 : h->NTILE == 64 ? kMaxWG : 2;  // token-major: 32 KB boxes (its MMA issue assumes 2 atoms)
+  if (const char* e = getenv("FA_WG"); e && !h->tm) h->wg = std::max(1, std::min(h->wg, atoi(e)));
   // FP8 streaming: 2 atoms per slot (one 128 x 128-byte E4M3 box, expanded to 32 KB of bf16)
   if (h->fp8_stream) h->wg = 2;
   for (int m = 0; m < 4; ++m)
     while ((spec[m].katoms / spec[m].split) % h->wg != 0) h->wg >>= 1;
+  if (h->tm && h->wg != 2) return fail(h, FA_ERR_INVALID, "plan error: token-major GEMMs need 2-atom weight boxes");
   // QKV also runs as 64-row units while its 128-row units would leave most SMs idle (20 tiles per
   // token group: at a few observations per GPU the stage is otherwise carried by 20 x groups
   // CTAs), provided every CTA that can receive one has room for its activation batch: an
@@ -689,6 +690,14 @@ static fa_status build_params(fa_handle* h) {
   p.trace_layer = h->trace_layer;
   p.spin_limit = 1u << 24;
   p.l2_ahead = l2_ahead_layers();
+  {
+    const int K4[4] = {D, QD, D, F};
+    const void* w16[4] = {h->w_qkv, h->w_o, h->w_gu, h->w_dn};
+    for (int m = 0; m < 4; ++m) {
+      p.wraw[m] = reinterpret_cast<const uint8_t*>(h->fp8_stream ? h->w8[m] : w16[m]);
+      p.wrow_bytes[m] = h->fp8_stream ? K4[m] : 2 * K4[m];
+    }
+  }
   return FA_OK;
 }
 

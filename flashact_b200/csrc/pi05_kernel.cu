@@ -482,6 +482,11 @@ struct Pi05Model {
   __device__ static void epi_tm(const Epi& e, const GemmUnit& gu, int m, int n, int c0, const float* v) {
     pi05::epi_tm(e, gu, m, n, c0, v);
   }
+  // activation operand of matrix m, row-major [NPAD][act_ld(m)] bf16
+  __device__ static const __nv_bfloat16* act_src(const Params& p, int m) {
+    return m == MAT_O ? p.attn : m == MAT_DN ? p.hbuf : p.xn;
+  }
+  __device__ static int act_ld(int m) { return m == MAT_O ? QD : m == MAT_DN ? F : D; }
 };
 
 // One tile of <= 64 tokens (bs=1 at T <= 64): token-major GEMMs (activations in tensor memory,
@@ -774,7 +779,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     // MMA commit; TMEM A slots are filled by those threads and released by an MMA commit
     for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], Model::kF8 ? 128 : 1); }
     // A slots: filled by the 128 converting threads (FP8) or by the 64 token threads (token-major)
-    for (int i = 0; i < kASlotsF8; ++i) { mbar_init(&bars.afull[i], Model::kTM ? 64 : 128); mbar_init(&bars.aempty[i], 1); }
+    for (int i = 0; i < (int)kTmASlots; ++i) { mbar_init(&bars.afull[i], Model::kTM ? 64 : 128); mbar_init(&bars.aempty[i], 1); }
     for (int i = 0; i < 4; ++i) mbar_init(&bars.sfull[i], 1);
     mbar_init(&bars.bfull, 1);
     mbar_init(&bars.bempty, 1);
