@@ -356,6 +356,9 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
   const int nunits = c.gcnt[m];
   const uint32_t idesc = idesc_bf16(128, k.NTILE);
   const uint32_t tile = k.NTILE * 128;
+  const uint32_t tile16 = tile >> 4;
+  const uint32_t slot_bytes = (uint32_t)k.wg * kAtomBytes;
+  const uint64_t ring_desc = sdesc_sw128(k.ring), work_desc = sdesc_sw128(k.work);
   Bars* const bars = k.bars;
   uint64_t* const wfull = F8 ? bars->afull : bars->wfull;  // weight slots the MMAs read
   uint64_t* const wempty = F8 ? bars->aempty : bars->wempty;
@@ -385,7 +388,7 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
         if (u == 0 && g == 0 && j0 == 0) FA_ONE(trace_mark(kTrMmaB0));
         // A operand of atom jj: a 128-row SW128 tile (16 KB); a half-row unit's 64-row atoms are
         // 8 KB apart, so rows 64..127 of each MMA read the next atom (results ignored)
-        const uint32_t astride = gu.half ? kAtomBytes / 2 : kAtomBytes;
+        const uint32_t astride16 = (gu.half ? kAtomBytes / 2 : kAtomBytes) >> 4;
         int deferred = -1;
 #pragma unroll 1
         for (int j = j0; j < j1; j += aps) {  // one ring slot = aps weight atoms
@@ -401,20 +404,29 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
           if (u == 0 && g == 0 && j == 8) FA_ONE(trace_mark(10));
           if (u == 0 && g == 0 && j == 12) FA_ONE(trace_mark(11));
           if (leader()) {
+            // Descriptors advance by plain adds from per-slot bases (16-byte units): a per-MMA
+            // recomputation leaves the single issuing thread latency-bound, far below the MMA rate.
+            const uint64_t da0 = ring_desc + (uint64_t)((wslot * slot_bytes) >> 4);
+            const uint32_t ta0 = k.tmem + kAColF8 + wslot * kASlotColsF8;  // FP8: atom = 32 TMEM columns
+            const uint64_t db0 = work_desc + (uint64_t)((uint32_t)(j - j0) * tile16);
+            const uint32_t bstride16 = (uint32_t)(j1 - j0) * tile16;  // next token tile of the batch
             #pragma unroll 1
             for (int jj = 0; jj < aps; ++jj) {
-              const uint64_t da = sdesc_sw128(k.ring + (size_t)wslot * k.wg * kAtomBytes + (size_t)jj * astride);
-              // FP8: atom jj of the slot = 32 TMEM columns (64 K), K16 step s = 8 columns
-              const uint32_t ta = k.tmem + kAColF8 + wslot * kASlotColsF8 + jj * 32;
-              #pragma unroll 1
-              for (int i = 0; i < nt; ++i) {
-                const uint64_t db = sdesc_sw128(k.work + (size_t)(i * (j1 - j0) + (j + jj - j0)) * tile);
+              const uint64_t da = da0 + (uint64_t)(jj * astride16);
+              const uint32_t ta = ta0 + jj * 32;
+              const uint64_t dbj = db0 + (uint64_t)(jj * tile16);
+              const bool acc0 = (j + jj) != 0;
 #pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                  if (F8)
-                    tc_mma_bf16_ts(tacc + i * k.NTILE, ta + 8 * s, db + 2 * s, idesc, ((j + jj) | s) != 0);
-                  else
-                    tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, ((j + jj) | s) != 0);
+              for (int i = 0; i < 2; ++i) {
+                if (i < nt) {
+                  const uint64_t db = dbj + (uint64_t)(i * bstride16);
+#pragma unroll
+                  for (int s = 0; s < 4; ++s) {
+                    if (F8)
+                      tc_mma_bf16_ts(tacc + i * k.NTILE, ta + 8 * s, db + 2 * s, idesc, acc0 || s != 0);
+                    else
+                      tc_mma_bf16(tacc + i * k.NTILE, da + 2 * s, db + 2 * s, idesc, acc0 || s != 0);
+                  }
                 }
               }
             }
