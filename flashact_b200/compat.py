@@ -30,6 +30,8 @@ Errors raise flashact_b200.FlashActError (the reference raises on launch failure
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from .molmoact2 import MolmoAct2ActionExpert
@@ -69,10 +71,17 @@ def _pi05_weights(w1, wo, w2, w3, s1, so_, s2, s3, w_ain, b_ain, w_aout, b_aout)
 
 
 def _write_stage_times(eng, stage_cycles):
-    if stage_cycles is not None and stage_cycles.numel() > 0:
-        t = eng.stage_times_ns()
-        vals = torch.tensor(list(t.values())[: stage_cycles.numel()], dtype=torch.int64)
-        stage_cycles.view(-1)[: vals.numel()].copy_(vals.to(stage_cycles.device).to(stage_cycles.dtype))
+    """Per-stage nanoseconds into stage_cycles, asynchronously on the launch stream when it is a
+    contiguous 64-bit device tensor (the reference fills it from inside its kernel)."""
+    if stage_cycles is None or stage_cycles.numel() == 0:
+        return
+    if stage_cycles.is_cuda and stage_cycles.dtype in (torch.int64, torch.uint64) and stage_cycles.is_contiguous():
+        eng._check(eng.lib.fa_get_stage_cycles(eng.h, ctypes.cast(stage_cycles.data_ptr(), ctypes.POINTER(ctypes.c_uint64)),
+                                               min(stage_cycles.numel(), 16)))
+        return
+    t = eng.stage_times_ns()
+    vals = torch.tensor(list(t.values())[: stage_cycles.numel()], dtype=torch.int64)
+    stage_cycles.view(-1)[: vals.numel()].copy_(vals.to(stage_cycles.device).to(stage_cycles.dtype))
 
 
 def pi05_launch(w1, wo, w2, w3, s1, so_, s2, s3, mods, mod_final, rope_cos, rope_sin,

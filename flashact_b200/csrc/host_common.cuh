@@ -35,6 +35,7 @@ struct fa_handle {
   std::string err;
   bool weights_ready = false, kv_ready = false, timing = false;
   int last_launches = 0;
+  cudaStream_t last_stream = nullptr;  // stream of the last fa_sample_actions
   int split_o = 8, split_dn = 8, attn_penalty = 8;
   int split_o_eff = 4, split_dn_eff = 8;  // K-splits used for the bound batch
   int bmax_bytes = 64 * 1024;  // activation-area cap of a GEMM CTA

@@ -388,6 +388,17 @@ fa_status ma2_bind(fa_handle* h, int batch, const void* k, const void* v, int sr
                   src_rows, h->cfg.max_prefix);
   if (!is_device_ptr(k) || !is_device_ptr(v)) return fail(h, FA_ERR_INVALID, "k/v must be device pointers");
   FA_CUDA(h, cudaSetDevice(h->device));
+  if (s->bound && !rowmap && batch == s->B && (int)s->ctx.size() == batch &&
+      std::equal(ctx_len, ctx_len + batch, s->ctx.begin())) {
+    // Same batch and context lengths: plan and parameters stay; the context is re-copied
+    // asynchronously on `stream` (ordered after earlier launches on that stream).
+    const int L_ = h->cfg.num_layers;
+    const dim3 grid(std::max(1, s->LKPAD * M::D / 8 / 256 / 4), L_, batch);
+    ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)k, src_rows, s->d_ctx, nullptr, L_, s->LKPAD, s->kctx);
+    ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)v, src_rows, s->d_ctx, nullptr, L_, s->LKPAD, s->vctx);
+    FA_CUDA(h, cudaGetLastError());
+    return FA_OK;
+  }
   FA_CUDA(h, cudaStreamSynchronize(stream));
   const int T = h->cfg.horizon, L = h->cfg.num_layers;
   s->B = batch;
@@ -430,5 +441,6 @@ fa_status ma2_sample(fa_handle* h, int batch, const float* noise, float* out, cu
                                          fa::kSmemDyn, stream));
   FA_CUDA(h, cudaMemcpyAsync(out, s->x_t, bytes, cudaMemcpyDefault, stream));
   h->last_launches = 1;
+  h->last_stream = stream;
   return FA_OK;
 }

@@ -739,6 +739,22 @@ static fa_status bind_impl(fa_handle* h, int batch, const void* k, const void* v
   if (maxvl > 0 && (!is_device_ptr(k) || !is_device_ptr(v))) return fail(h, FA_ERR_INVALID, "k/v must be device pointers");
   FA_CUDA(h, cudaSetDevice(h->device));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int L_ = h->cfg.num_layers;
+  if (h->kv_ready && !rowmap && batch == h->B && (int)h->valid_len.size() == batch &&
+      std::equal(valid_len, valid_len + batch, h->valid_len.begin())) {
+    // Same batch and valid lengths: the work plan, tensor maps, valid lengths and RoPE tables on the
+    // device all stay; only the cache contents are rewritten, asynchronously on `stream` (ordered
+    // after earlier launches on that stream, like the reference's in-launch KV handoff,
+    // src/pi05/mk6.cu:258-277).
+    const int sr = std::max(src_rows, 1);
+    bind_k_kernel<<<dim3(std::max(1, h->LPAD * HD / 256 / 4), L_, batch), 256, 0, s>>>(
+        (const bf16*)k, sr, h->d_valid, nullptr, L_, h->LPAD, layout == FA_KV_FLASHRT_INTERLEAVED, h->kcache);
+    FA_CUDA(h, cudaGetLastError());
+    bind_vt_kernel<<<dim3(h->LPAD / 32, HD / 32, batch * L_), dim3(32, 8), 0, s>>>((const bf16*)v, sr, h->d_valid, nullptr,
+                                                                                 L_, h->LPAD, h->vtcache);
+    FA_CUDA(h, cudaGetLastError());
+    return FA_OK;
+  }
   FA_CUDA(h, cudaStreamSynchronize(s));  // previous launches may still read the cache and plan
   const int T = h->cfg.horizon, L = h->cfg.num_layers;
   h->B = batch;
@@ -779,6 +795,11 @@ extern "C" fa_status fa_set_stage_timing(fa_handle* h, int enable) {
 extern "C" fa_status fa_get_stage_cycles(fa_handle* h, uint64_t* out, int n) {
   if (!h || !out) return fail(h, FA_ERR_INVALID, "null argument");
   FA_CUDA(h, cudaSetDevice(h->device));
+  if (is_device_ptr(out)) {  // device destination: copied on the last launch's stream, no host synchronisation
+    const int m = std::max(0, std::min(n, (int)kMaxStages));
+    if (m > 0) FA_CUDA(h, cudaMemcpyAsync(out, h->stage_ns, (size_t)m * 8, cudaMemcpyDeviceToDevice, h->last_stream));
+    return FA_OK;
+  }
   unsigned long long tmp[kMaxStages];
   FA_CUDA(h, cudaMemcpy(tmp, h->stage_ns, sizeof(tmp), cudaMemcpyDeviceToHost));
   for (int i = 0; i < n; ++i) out[i] = i < kMaxStages ? tmp[i] : 0;
@@ -806,6 +827,7 @@ extern "C" fa_status fa_sample_actions(fa_handle* h, int batch, const float* noi
   FA_CUDA(h, cudaLaunchCooperativeKernel(kern, dim3(h->num_sms), dim3(kThreads), args, kSmemDyn, s));
   FA_CUDA(h, cudaMemcpyAsync(actions_out, h->x_t, bytes, cudaMemcpyDefault, s));
   h->last_launches = 1;
+  h->last_stream = s;
   return FA_OK;
 }
 

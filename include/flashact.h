@@ -198,7 +198,11 @@ FA_API fa_status fa_set_modulation(fa_handle* h, const float* mods, const float*
  * [batch][L][src_rows][256]; valid_len (host array, batch entries) gives each observation's
  * number of valid (compacted) prefix tokens, <= src_rows <= max_prefix. The action tokens'
  * RoPE positions start at valid_len (src/pi05/pack_weights.py:54-58). The copy / transpose /
- * de-interleave runs on `stream`. Replaces compact_kv + the kcache/vtcache fill. */
+ * de-interleave runs on `stream`. Replaces compact_kv + the kcache/vtcache fill.
+ * A bind that changes the batch or any valid length re-plans the work and synchronises `stream`;
+ * a rebind with the same batch and valid lengths (both models, unmasked) only re-copies the cache,
+ * asynchronously on `stream` with no host synchronisation, like the reference's KV handoff inside
+ * its launch (src/pi05/mk6.cu:258-277): issue it on the stream of the launches that read the cache. */
 FA_API fa_status fa_bind_prefix_kv(fa_handle* h, int batch, const void* k, const void* v, int src_rows,
                             const int* valid_len, fa_kv_layout layout, fa_stream stream);
 
@@ -225,7 +229,9 @@ FA_API fa_status fa_sync(fa_handle* h, fa_stream stream);
 
 /* Per-stage time of the last launch, in nanoseconds summed over the loop (block 0's view):
  * [0] embed/norm1 [1] qkv [2] attention [3] merge [4] o_proj [5] norm2 [6] gate/up [7] down
- * [8] final+euler. Enable with fa_set_stage_timing(h, 1) before sampling. n = array length. */
+ * [8] final+euler. Enable with fa_set_stage_timing(h, 1) before sampling. n = array length.
+ * A host `out` is filled synchronously; a device `out` is filled asynchronously on the stream of
+ * the last fa_sample_actions (MolmoAct2 reports its 13 stages; entries past the model's count are 0). */
 FA_API fa_status fa_set_stage_timing(fa_handle* h, int enable);
 FA_API fa_status fa_get_stage_cycles(fa_handle* h, uint64_t* out, int n);
 
