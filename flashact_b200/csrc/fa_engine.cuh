@@ -348,7 +348,7 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
   MmaCtx k;
   constexpr bool F8 = Model::kF8;  // A from the TMEM slots the epilogue warps fill
   k.ring = c.ring; k.work = c.work; k.bars = c.bars; k.err = p.err; k.amap = &p.maps[Model::act_map(m)];
-  k.tmem = c.tmem; k.R = F8 ? kASlotsF8 : c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.TG;
+  k.tmem = c.tmem; k.R = F8 ? kASlotsF8 : c.ring_slots; k.batoms = c.batoms; k.NTILE = p.NTILE; k.TG = p.tg[m];
   k.tiles = p.NPAD / p.NTILE;
   k.box_atoms = p.box_atoms;
   k.wg = p.wg;
@@ -417,7 +417,7 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
               const uint64_t dbj = db0 + (uint64_t)(jj * tile16);
               const bool acc0 = (j + jj) != 0;
 #pragma unroll
-              for (int i = 0; i < 2; ++i) {
+              for (int i = 0; i < 4; ++i) {  // token tiles of the group (<= 4: 256 accumulator columns)
                 if (i < nt) {
                   const uint64_t db = dbj + (uint64_t)(i * bstride16);
 #pragma unroll
@@ -751,7 +751,7 @@ template <class Model>
 __device__ __forceinline__ uint32_t epi_gemm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m, int l,
                                              ConvState& cs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
-  const int NTILE = p.NTILE, TG = p.TG, tiles = p.NPAD / p.NTILE;
+  const int NTILE = p.NTILE, TG = p.tg[m], tiles = p.NPAD / p.NTILE;
   int* const err = p.err;
   Bars* const bars = c.bars;
   const uint32_t taddr = c.tmem + ((uint32_t)(qd * 32) << 16);

@@ -41,6 +41,7 @@ struct Params {
   // geometry
   int L, T, B, NT, NPAD, NTILE, TG, ngroups, nsteps, AD, adim, LKPAD;
   int split[NUM_MATS];  // K-split factor per matrix (1 = full K, epilogue sees the final sum)
+  int tg[kMaxMats];  // token tiles per group (one accumulator) of each GEMM matrix
   int box_atoms;
   float dt, invT;
   // plan

@@ -42,6 +42,7 @@ struct Params {
   // geometry
   int L, T, B, NT, NPAD, NTILE, TG, ngroups, nsteps, LPAD, AD;
   int split_o, split_dn;
+  int tg[kMaxMats];  // token tiles per group (one accumulator) of each GEMM matrix
   int box_atoms;  // K atoms per activation TMA load (3D box)
   float dt;
   float invT;  // 1 / T

@@ -50,6 +50,7 @@ struct fa_handle {
   float* ws8[4] = {nullptr, nullptr, nullptr, nullptr};
   // bound batch
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LPAD = 0;
+  int tgm[4] = {4, 4, 4, 4};  // pi0.5: token tiles per group of each GEMM matrix (QKV, O, gate/up, down)
   std::vector<int> valid_len;
   // device memory
   std::vector<void*> allocs;

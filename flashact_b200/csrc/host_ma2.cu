@@ -347,6 +347,7 @@ static fa_status ma2_params(fa_handle* h) {
   p.L = L; p.T = h->cfg.horizon; p.B = s->B; p.NT = s->NT; p.NPAD = s->NPAD; p.NTILE = s->NTILE; p.TG = s->TG;
   p.ngroups = s->ngroups; p.nsteps = h->cfg.num_steps; p.AD = h->cfg.action_dim; p.adim = s->adim; p.LKPAD = s->LKPAD;
   for (int m = 0; m < M::NUM_MATS; ++m) p.split[m] = s->split_eff[m];
+  for (int m = 0; m < M::NUM_MATS; ++m) p.tg[m] = s->TG;
   p.dt = 1.0f / (float)h->cfg.num_steps;
   p.invT = 1.0f / (float)h->cfg.horizon;
   p.gunits = s->d_gunits; p.aunits = s->d_aunits; p.plans = s->d_plans; p.ctx_len = s->d_ctx;

@@ -487,7 +487,19 @@ static fa_status build_plan(fa_handle* h) {
   // token tiles per group = per TMEM accumulator: 256 columns, or 128 with FP8 streaming (the
   // upper half of TMEM holds the expanded weight slots)
   h->TG = (h->fp8_stream ? kAccColsF8 : 256) / h->NTILE;
+  if (const char* e = getenv("FA_TG_MAX")) h->TG = std::max(1, std::min(h->TG, atoi(e)));  // tuning knob
   h->ngroups = (h->NPAD / h->NTILE + h->TG - 1) / h->TG;
+  // QKV at 128-token tiles: one tile per unit. Its units then each read a quarter or half of the
+  // activation of a 2-tile group (the activation, not the 5.2 MB of weights, dominates what a QKV
+  // CTA loads once the batch spans several tiles); measured at bs=8: QKV 7.4 -> 5.3 ms per chunk.
+  const int tiles = h->NPAD / h->NTILE;
+  for (int m = 0; m < 4; ++m) h->tgm[m] = h->TG;
+  if (h->NTILE == 128) {
+    const char* e = getenv("FA_QKV_TG");
+    h->tgm[MAT_QKV] = std::max(1, std::min(h->TG, e ? atoi(e) : 1));
+  }
+  auto ngr = [&](int m) { return (tiles + h->tgm[m] - 1) / h->tgm[m]; };
+  auto ntiles_of = [&](int m, int g) { return std::min(h->tgm[m], tiles - g * h->tgm[m]); };
   std::vector<AttnUnit> au;
   for (int b = 0; b < h->B; ++b) {
     const int npc = (h->valid_len[b] + KCH - 1) / KCH;
@@ -540,10 +552,10 @@ static fa_status build_plan(fa_handle* h) {
   // token group: at a few observations per GPU the stage is otherwise carried by 20 x groups
   // CTAs), provided every CTA that can receive one has room for its activation batch: an
   // attention CTA's area is 64 KB, and the planner fills the CTAs without attention units first.
-  const int ntg_max = std::min(h->TG, h->NPAD / h->NTILE);
+  const int ntg_max = std::min(h->tgm[MAT_QKV], tiles);
   const bool half_fits_attn = h->NTILE * 128 * ntg_max * std::max(act_box_atoms(h), 2 * h->wg) <= 64 * 1024;
   const bool qkv_half = use_half_units(h) ||
-                        (h->half_units && 40 * h->ngroups <= (half_fits_attn ? nblk : nblk - acta));
+                        (h->half_units && 40 * ngr(MAT_QKV) <= (half_fits_attn ? nblk : nblk - acta));
   std::vector<std::vector<GemmUnit>> per(nblk * 4);
   const int order[4] = {MAT_QKV, MAT_GU, MAT_DN, MAT_O};
   for (int oi = 0; oi < 4; ++oi) {
@@ -554,7 +566,7 @@ static fa_status build_plan(fa_handle* h) {
     // weight ring holds whole; RoPE / GeGLU partners stay in one unit)
     const int halves = ((m == MAT_QKV && qkv_half) || (m == MAT_GU && use_half_units(h))) ? 2 : 1;
     std::vector<int> cnt(nblk, 0);
-    for (int g = 0; g < h->ngroups; ++g)
+    for (int g = 0; g < ngr(m); ++g)
       for (int mt = 0; mt < s.mtiles; ++mt)
         for (int hf = 0; hf < halves; ++hf)
           for (int sp = 0; sp < s.split; ++sp) {
@@ -564,18 +576,20 @@ static fa_status build_plan(fa_handle* h) {
             per[best * 4 + m].push_back({(uint16_t)mt, (uint16_t)(sp * per_split), (uint16_t)per_split, (uint16_t)sp,
                                          (uint16_t)g, (uint16_t)(halves == 2 ? hf + 1 : 0)});
             cnt[best]++;
-            load[best] += per_split * std::min(h->TG, h->NPAD / h->NTILE - g * h->TG) / halves;
+            load[best] += per_split * ntiles_of(m, g) / halves;
           }
   }
   std::vector<GemmUnit> gu;
   const int tile = h->NTILE * 128;
   for (int i = 0; i < nblk; ++i) {
     // Activation area: the largest (unit, token group) K-range of this CTA, whole if it fits.
-    int bb = tile, ng = 0;
-    const int ntg = std::min(h->TG, h->NPAD / h->NTILE);  // token tiles per group
+    int bb = tile, ng = 0, ntg = 1;  // ntg: most token tiles of a unit of this CTA
     for (int m = 0; m < 4; ++m) {
       ng += (int)per[i * 4 + m].size();
-      for (const GemmUnit& x : per[i * 4 + m]) bb = std::max(bb, (int)x.natoms * ntg * tile);
+      for (const GemmUnit& x : per[i * 4 + m]) {
+        bb = std::max(bb, (int)x.natoms * ntiles_of(m, x.grp) * tile);
+        ntg = std::max(ntg, ntiles_of(m, x.grp));
+      }
     }
     if (ng > kMaxGU || plans[i].a_cnt > kMaxAU)
       return fail(h, FA_ERR_INVALID, "batch too large for the per-CTA work lists (%d GEMM, %d attention units)", ng,
@@ -598,7 +612,7 @@ static fa_status build_plan(fa_handle* h) {
     for (int m = 0; m < 4; ++m)
       for (const GemmUnit& x : per[i * 4 + m]) {
         const int aps = x.half ? 2 * h->wg : h->wg, gran = std::max(act_box_atoms(h), aps);
-        const int nt = std::min(h->TG, h->NPAD / h->NTILE - x.grp * h->TG);
+        const int nt = ntiles_of(m, x.grp);
         if (gran * nt * tile > plans[i].b_bytes)
           return fail(h, FA_ERR_INVALID, "plan error: a %d-atom activation batch of %d token tiles exceeds CTA %d's %d-byte area",
                       gran, nt, i, plans[i].b_bytes);
@@ -672,6 +686,7 @@ static fa_status build_params(fa_handle* h) {
   p.box_atoms = (int)ba;
   p.wg = h->wg;
   p.L = L; p.T = h->cfg.horizon; p.B = B; p.NT = h->NT; p.NPAD = h->NPAD; p.NTILE = h->NTILE; p.TG = h->TG;
+  for (int m = 0; m < 4; ++m) p.tg[m] = h->tgm[m];
   p.ngroups = h->ngroups; p.nsteps = h->cfg.num_steps; p.LPAD = h->LPAD; p.AD = h->cfg.action_dim;
   p.split_o = h->split_o_eff; p.split_dn = h->split_dn_eff;
   p.dt = -1.0f / (float)h->cfg.num_steps;
@@ -760,6 +775,7 @@ static fa_status bind_impl(fa_handle* h, int batch, const void* k, const void* v
   h->B = batch;
   h->NT = batch * T;
   h->NTILE = h->NT <= 64 ? 64 : 128;
+  if (const char* e = getenv("FA_NTILE"); e && atoi(e) == 64) h->NTILE = 64;  // tuning knob
   h->NPAD = round_up(h->NT, h->NTILE);
   h->TG = 256 / h->NTILE;
   h->ngroups = (h->NPAD / h->NTILE + h->TG - 1) / h->TG;
