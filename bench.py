@@ -50,7 +50,7 @@ MA2_KV_BYTES = 2 * MA2_L * MA2_LK * 768 * 2  # cross-attention K+V per Euler ste
 # of `bench.py [--model molmoact2] --steps 1 --warmup 3 --no-cpu-baseline` (metrics
 # dram__bytes_read.sum and dram__bytes_write.sum, -k regex:<kernel> -s 3 -c 1; summaries kept
 # under profiles/).
-NCU_TRAFFIC = {("pi05", 1): 6_252_512_512 + 5_673_216, ("molmoact2", 1): 7_739_515_904 + 3_610_112,
+NCU_TRAFFIC = {("pi05", 1): 6_246_001_408 + 3_208_704, ("molmoact2", 1): 7_739_515_904 + 3_610_112,
                ("pi05-fp8", 1): 3_134_528_512 + 3_190_016}
 
 
