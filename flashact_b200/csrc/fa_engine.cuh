@@ -155,6 +155,7 @@ struct Bars {
   uint64_t sfull[4];       // token-major GEMMs: activation K-chunk landed in staging slot 0..3
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
+  uint64_t s_free, pv_done;  // whole-unit attention: S read by the softmax warps; P V done (P and V free)
 };
 struct Ctx {
   uint8_t* ring;  // ring_slots x (wg x 16 KB); FP8 streaming: ring_slots x (wg x 8 KB) of E4M3 codes
@@ -305,6 +306,7 @@ struct MmaState {
   uint32_t acc;          // accumulator buffers used
   uint32_t nq, nu;       // attention: Q loads, units
   int last_q;
+  uint32_t ns, npv;      // whole-unit attention: S tiles computed, P V products issued
   int k_pre;             // the next attention unit's prefix K is already loading (prefetched)
   uint32_t qtm;          // token-major GEMMs: activation K-chunks consumed (staging / TMEM A slot phases)
 };

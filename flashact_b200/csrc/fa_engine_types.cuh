@@ -53,6 +53,7 @@ struct GemmUnit {
 struct AttnUnit {
   uint16_t b, hp, chunk, is_suffix;  // observation, head (pair), key chunk, action-token chunk flag
 };
+constexpr uint16_t kWholeChunk = 0xFFFF;  // AttnUnit::chunk of a unit that covers every key chunk
 struct CtaPlan {
   int g_off[kMaxMats], g_cnt[kMaxMats];  // GEMM units of this CTA per matrix, same for every layer
   int a_off, a_cnt;                      // attention units of this CTA

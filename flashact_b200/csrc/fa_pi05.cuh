@@ -85,6 +85,7 @@ struct Params {
   // FP8 weight streaming: per packed weight row, its E4M3 scale, [L][rows] per matrix (QKV, O,
   // gate/up, down); unused by the bf16 kernel
   const float* wscale[4];
+  int attn_whole;  // attention units cover all key chunks of (observation, head pair): two-pass softmax, no merge
   int f8_ahead;  // FP8 kernel: expand the next GEMM stage's first slots during the barrier before it
   unsigned long long* stage_ns;  // [NUM_STAGES] or null
   // host-side fault injection for tests: CTA 0 skips arriving at grid barrier number

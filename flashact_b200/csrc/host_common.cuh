@@ -45,7 +45,8 @@ struct fa_handle {
   // FP8 weight streaming (pi0.5 weights loaded as FP8 codes): E4M3 codes and per-row scales of
   // QKV, O, gate/up, down in the packed row order; the FP8 kernel streams them
   bool fp8_stream = false;
-  bool tm = false;             // token-major GEMM kernel (bound batch = one tile of <= 64 tokens)
+  bool tm = false;
+  bool attn_whole = false;     // pi0.5: whole-unit attention (two-pass softmax, no merge)             // token-major GEMM kernel (bound batch = one tile of <= 64 tokens)
   unsigned char* w8[4] = {nullptr, nullptr, nullptr, nullptr};
   float* ws8[4] = {nullptr, nullptr, nullptr, nullptr};
   // bound batch

@@ -500,10 +500,21 @@ static fa_status build_plan(fa_handle* h) {
   }
   auto ngr = [&](int m) { return (tiles + h->tgm[m] - 1) / h->tgm[m]; };
   auto ntiles_of = [&](int m, int g) { return std::min(h->tgm[m], tiles - g * h->tgm[m]); };
+  // Attention units: per (observation, head pair, key chunk) with a merge stage (split-KV: the
+  // latency choice at a few observations), or per (observation, head pair) over all its chunks
+  // (two-pass softmax, no partials: the throughput choice once the units alone fill the GPU).
+  {
+    const char* e = getenv("FA_ATTN_WHOLE");
+    h->attn_whole = e ? atoi(e) != 0 : 8 * h->B >= nblk;  // measured: 32 obs 53.9 -> 46.9 ms, 16 obs 33.1 -> 34.0
+  }
   std::vector<AttnUnit> au;
   for (int b = 0; b < h->B; ++b) {
     const int npc = (h->valid_len[b] + KCH - 1) / KCH;
     for (int hp = 0; hp < 4; ++hp) {
+      if (h->attn_whole) {
+        au.push_back({(uint16_t)b, (uint16_t)hp, kWholeChunk, 0});
+        continue;
+      }
       for (int c = 0; c < npc; ++c) au.push_back({(uint16_t)b, (uint16_t)hp, (uint16_t)c, 0});
       au.push_back({(uint16_t)b, (uint16_t)hp, 0, 1});
     }
@@ -689,6 +700,7 @@ static fa_status build_params(fa_handle* h) {
   for (int m = 0; m < 4; ++m) p.tg[m] = h->tgm[m];
   p.ngroups = h->ngroups; p.nsteps = h->cfg.num_steps; p.LPAD = h->LPAD; p.AD = h->cfg.action_dim;
   p.split_o = h->split_o_eff; p.split_dn = h->split_dn_eff;
+  p.attn_whole = h->attn_whole ? 1 : 0;
   p.dt = -1.0f / (float)h->cfg.num_steps;
   p.invT = 1.0f / (float)h->cfg.horizon;
   p.gunits = h->d_gunits; p.aunits = h->d_aunits; p.plans = h->d_plans;

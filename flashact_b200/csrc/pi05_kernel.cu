@@ -723,6 +723,242 @@ __device__ __forceinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint
   return anu;
 }
 
+// ------------------------------------------------------------------ attention (whole units, large batches)
+// Unit = (observation b, head pair hp) over ALL its key chunks (prefix chunks, then the action-token
+// chunk), softmax in two passes: pass 1 computes S = Q K^T chunk by chunk and keeps each query
+// row's running maximum; pass 2 recomputes S, forms P = 2^(S - M) with the final maximum M (no
+// rescaling of O ever) and accumulates O += P V in tensor memory. The normalised output goes
+// straight to `attn`: no per-chunk partials and no merge stage. At large batches this trades one
+// extra read of the prefix K and one extra S MMA per chunk for the partial round trip through
+// memory (151 MB per layer-step at 64 observations).
+__device__ __forceinline__ int whole_chunks(const Params& p, int b) { return p.nchunks[b] + 1; }
+
+__device__ __forceinline__ bool mma_attn_whole(const Params& p, const Ctx& c, MmaState& st_shared, int l) {
+  const int c_acnt = c.acnt;
+  const AttnUnit* const c_au = c.au;
+  Bars* const br = c.bars;
+  const uint32_t c_tmem = c.tmem;
+  uint8_t* const c_work = c.work;
+  const int p_L = p.L, p_LPAD = p.LPAD;
+  int* const p_err = p.err;
+  const CUtensorMap* const p_maps = p.maps;
+  MmaState st = st_shared;
+  const uint64_t pol_kv = policy_evict_last();
+  for (int u = 0; u < c_acnt; ++u) {
+    const AttnUnit au = c_au[u];
+    const int nc = whole_chunks(p, au.b);
+    // the previous unit's output has been read out of tensor memory
+    if (st.nu > 0 && !mbar_wait(&br->o_free, (st.nu - 1) & 1, p_err, KERR_ATTN)) return false;
+    FA_ONE(mbar_expect_tx(&br->q_full, 4 * kAtomBytes));
+    FA_ONE(tma_load_3d(c_work + kQOff, &p_maps[MAP_Q], &br->q_full, 0, (au.b * H + 2 * au.hp) * TPAD, 0, pol_kv));
+    if (!mbar_wait(&br->q_full, st.nq & 1, p_err, KERR_ATTN)) return false;
+    ++st.nq;
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll 1
+      for (int ch = 0; ch < nc; ++ch) {
+        const bool suffix = ch == nc - 1;
+        const int nk = suffix ? TPAD : KCH;
+        // K into the K/V area: free once the previous S (pass 1) or P V (pass 2) has run
+        FA_ONE(mbar_expect_tx(&br->k_full, 4 * nk * 128));
+        if (suffix)
+          FA_ONE(tma_load_3d(c_work + kKVOff, &p_maps[MAP_SK], &br->k_full, 0, au.b * TPAD, 0, pol_kv));
+        else
+          FA_ONE(tma_load_3d(c_work + kKVOff, &p_maps[MAP_K], &br->k_full, 0, (au.b * p_L + l) * p_LPAD + ch * KCH, 0,
+                             pol_kv));
+        // the S tile in tensor memory has been read by the softmax warps
+        if (st.ns > 0 && !mbar_wait(&br->s_free, (st.ns - 1) & 1, p_err, KERR_ATTN)) return false;
+        if (!mbar_wait(&br->k_full, st.ns & 1, p_err, KERR_ATTN)) return false;
+        tc_fence_after();
+        const uint32_t id_s = idesc_bf16(128, nk);
+        if (leader()) {
+          const uint64_t dq0 = sdesc_sw128(c_work + kQOff), dk0 = sdesc_sw128(c_work + kKVOff);
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            const uint64_t dq = dq0 + (uint64_t)((a * kAtomBytes) >> 4);
+            const uint64_t dk = dk0 + (uint64_t)((a * nk * 128) >> 4);
+#pragma unroll
+            for (int s4 = 0; s4 < 4; ++s4) tc_mma_bf16(c_tmem, dq + 2 * s4, dk + 2 * s4, id_s, (a | s4) != 0);
+          }
+          tc_commit(&br->s_full);
+          tc_commit(&br->kv_free);
+        }
+        __syncwarp();
+        if (!mbar_wait(&br->kv_free, st.ns & 1, p_err, KERR_ATTN)) return false;  // S done: K area free
+        ++st.ns;
+        if (pass == 1) {  // V of this chunk, then O += P V once the softmax warps have written P
+          const int nka = nk / 64;
+          FA_ONE(mbar_expect_tx(&br->v_full, nka * 2 * kAtomBytes));
+          for (int hh = 0; hh < 2; ++hh) {
+            uint8_t* dst = c_work + kKVOff + hh * nka * kAtomBytes;
+            if (suffix)
+              FA_ONE(tma_load_3d(dst, &p_maps[MAP_SVT], &br->v_full, 0, au.b * HD + 128 * hh, 0, pol_kv));
+            else
+              FA_ONE(tma_load_3d(dst, &p_maps[MAP_VT], &br->v_full, 0, (au.b * p_L + l) * HD + 128 * hh, ch * 2, pol_kv));
+          }
+          if (!mbar_wait(&br->v_full, st.npv & 1, p_err, KERR_ATTN)) return false;
+          if (!mbar_wait(&br->p_full, st.npv & 1, p_err, KERR_ATTN)) return false;
+          tc_fence_after();
+          const uint32_t id_o = idesc_bf16(128, 128);
+          if (leader()) {
+            const uint64_t dp0 = sdesc_sw128(c_work + kPOff), dv0 = sdesc_sw128(c_work + kKVOff);
+            for (int kk = 0; kk < nka; ++kk)
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const uint64_t dp = dp0 + (uint64_t)((kk * kAtomBytes) >> 4);
+                const uint64_t dv = dv0 + (uint64_t)(((hh * nka + kk) * kAtomBytes) >> 4);
+#pragma unroll
+                for (int s4 = 0; s4 < 4; ++s4)
+                  tc_mma_bf16(c_tmem + 128 + 128 * hh, dp + 2 * s4, dv + 2 * s4, id_o, (ch | kk | s4) != 0);
+              }
+            tc_commit(&br->pv_done);
+          }
+          __syncwarp();
+          if (!mbar_wait(&br->pv_done, st.npv & 1, p_err, KERR_ATTN)) return false;  // K/V area and P free
+          ++st.npv;
+        }
+      }
+    }
+    FA_ONE(tc_commit(&br->o_full));
+    ++st.nu;
+  }
+  if (leader()) st_shared = st;
+  __syncwarp();
+  return true;
+}
+
+// Row maximum of one S tile over its valid keys (raw scores).
+template <int NK>
+__device__ __forceinline__ float row_max_s(uint32_t taddr, int nvalid) {
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+  for (int cc = 0; cc < NK; cc += 32) {
+    float v[32];
+    tmem_ld16(taddr + cc, v);
+    tmem_ld16(taddr + cc + 16, v + 16);
+    tc_wait_ld();
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      if (cc + k < nvalid) m4[k & 3] = fmaxf(m4[k & 3], v[k]);
+  }
+  return fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+}
+
+// P = 2^(S sl2 - mx) of one S tile as bf16 K-major atoms in shared memory (the A operand of P V);
+// returns the row sum of the stored values.
+template <int NK>
+__device__ __forceinline__ float probs_row(uint32_t taddr, int nvalid, float mx, uint8_t* prow, int r) {
+  constexpr float sl2 = 0.0625f * 1.4426950408889634f;
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int cc = 0; cc < NK; cc += 32) {
+    float v[32];
+    tmem_ld16(taddr + cc, v);
+    tmem_ld16(taddr + cc + 16, v + 16);
+    tc_wait_ld();
+    uint32_t pk[16];
+#pragma unroll
+    for (int k = 0; k < 32; k += 2) {
+      const float p0 = cc + k < nvalid ? fast_exp2(fmaf(v[k], sl2, -mx)) : 0.f;
+      const float p1 = cc + k + 1 < nvalid ? fast_exp2(fmaf(v[k + 1], sl2, -mx)) : 0.f;
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+      s4[(k >> 1) & 3] += __low2float(b2) + __high2float(b2);
+      pk[k >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    uint8_t* base = prow + (cc >> 6) * kAtomBytes;
+    const int ch0 = (cc & 63) >> 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(base + (((ch0 + q) ^ (r & 7)) << 4)) =
+          make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+  }
+  return (s4[0] + s4[1]) + (s4[2] + s4[3]);
+}
+
+struct AttnEpiState {
+  uint32_t anu, ns, npv;  // units finished, S tiles read, P V products waited for
+};
+
+__device__ __forceinline__ void epi_attn_whole(const Params& p, const Ctx& c, AttnEpiState& es) {
+  constexpr float sl2 = 0.0625f * 1.4426950408889634f;
+  const int nunits = c.acnt;
+  const AttnUnit* const units = c.au;
+  Bars* const br = c.bars;
+  const uint32_t tmem = c.tmem;
+  uint8_t* const work = c.work;
+  const int T = p.T;
+  int* const err = p.err;
+  const int* const valid_len = p.valid_len;
+  __nv_bfloat16* const attn = p.attn;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
+  const int r = qd * 32 + lane;
+  const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
+  uint8_t* const prow = work + kPOff + (r >> 3) * 1024 + (r & 7) * 128;
+  for (int u = 0; u < nunits; ++u) {
+    const AttnUnit au = units[u];
+    const int nc = whole_chunks(p, au.b);
+    const int vl = valid_len[au.b];
+    float mx = -INFINITY;
+    float sum = 0.f;
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll 1
+      for (int ch = 0; ch < nc; ++ch) {
+        const bool suffix = ch == nc - 1;
+        const int nvalid = suffix ? T : min(KCH, vl - ch * KCH);
+        if (!mbar_wait(&br->s_full, es.ns & 1, err, KERR_ATTN)) return;
+        tc_fence_after();
+        if (pass == 0) {
+          const float m = suffix ? row_max_s<TPAD>(tmem + lane_addr, nvalid) : row_max_s<KCH>(tmem + lane_addr, nvalid);
+          mx = fmaxf(mx, m);
+          tc_fence_before();
+          mbar_arrive(&br->s_free);
+        } else {
+          // P of the previous chunk has been consumed by its P V MMAs
+          if (ch > 0 && !mbar_wait(&br->pv_done, (es.npv - 1) & 1, err, KERR_ATTN)) return;
+          const float mxs = mx * sl2;
+          sum += suffix ? probs_row<TPAD>(tmem + lane_addr, nvalid, mxs, prow, r)
+                        : probs_row<KCH>(tmem + lane_addr, nvalid, mxs, prow, r);
+          fence_proxy_async_shared();
+          tc_fence_before();
+          mbar_arrive(&br->s_free);
+          mbar_arrive(&br->p_full);
+          ++es.npv;
+        }
+        ++es.ns;
+      }
+    }
+    if (!mbar_wait(&br->o_full, es.anu & 1, err, KERR_ATTN)) return;
+    tc_fence_after();
+    // row r: head 2 hp + (r >> 6), action token t = r & 63
+    const int t = r & 63;
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+    __nv_bfloat16* dst = attn + (size_t)(au.b * T + t) * QD + (2 * au.hp + (r >> 6)) * HD;
+#pragma unroll 1
+    for (int cc = 0; cc < HD; cc += 32) {
+      float v[32];
+      tmem_ld16(tmem + lane_addr + 128 + cc, v);
+      tmem_ld16(tmem + lane_addr + 128 + cc + 16, v + 16);
+      tc_wait_ld();
+      if (t < T) {
+#pragma unroll
+        for (int k = 0; k < 32; k += 8) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(v[k + 2 * q] * inv, v[k + 2 * q + 1] * inv);
+            w4[q] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          *reinterpret_cast<uint4*>(dst + cc + k) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+    }
+    tc_fence_before();
+    mbar_arrive(&br->o_free);
+    ++es.anu;
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 template <class Model>
 __device__ __forceinline__ void denoise_body(const Params& p) {
@@ -745,6 +981,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = 0;
     s_st.last_q = -1;
     s_st.k_pre = 0;
+    s_st.ns = s_st.npv = 0;
     s_st.qtm = 0;
   }
   __syncthreads();
@@ -788,6 +1025,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     mbar_init(&bars.kv_free, 1); mbar_init(&bars.v_free, 1); mbar_init(&bars.s_full, 1);
     mbar_init(&bars.p_full, 128); mbar_init(&bars.o_full, 1); mbar_init(&bars.o_free, 128);
     mbar_init(&bars.drain, 1);
+    mbar_init(&bars.s_free, 128); mbar_init(&bars.pv_done, 1);
     fence_mbar_init();
     for (int i = 0; i < NUM_MAPS; ++i) tma_prefetch_desc(&p.maps[i]);
   }
@@ -809,6 +1047,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     const bool is_epi = warp >= 2;
     MmaState& st = s_st;
     uint32_t ecnt = 0, anu = 0, gen = 0, qtm = 0;
+    AttnEpiState aes{0, 0, 0};  // whole-unit attention (epilogue warps)
     ConvState cs{0, 0};  // FP8 kernel: E4M3 slots converted (epilogue warps)
     uint64_t t_prev = globaltimer();
     const bool timing = p.stage_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 32;
@@ -870,14 +1109,19 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
               if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l, cs);
             }
           } else if (s == 1) {
-            if (is_mma) {
-              if (leader()) st.last_q = -1;
-              __syncwarp();
-              mma_attn(p, c, st, l, step + 1 == p.nsteps && last_layer);
+            if (p.attn_whole) {
+              if (is_mma) mma_attn_whole(p, c, st, l);
+              if (is_epi) epi_attn_whole(p, c, aes);
+            } else {
+              if (is_mma) {
+                if (leader()) st.last_q = -1;
+                __syncwarp();
+                mma_attn(p, c, st, l, step + 1 == p.nsteps && last_layer);
+              }
+              if (is_epi) anu = epi_attn(p, c, anu);
             }
-            if (is_epi) anu = epi_attn(p, c, anu);
           } else if (s == 2) {
-            if (is_epi) stage_merge(p);
+            if (is_epi && !p.attn_whole) stage_merge(p);  // whole units wrote attn themselves
           } else if (s == 4 || !last_layer) {  // norm2 | norm1 of the next layer
             if (is_epi) {
               const bool n2 = s == 4;

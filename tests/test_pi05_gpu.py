@@ -145,3 +145,15 @@ def test_odd_shapes(require_gpu, T, AD, B, num_steps):
     out, _ = run_engine(c)
     mx, cos = err(out, oracle_bf16_kv(c))
     assert mx < TOL and cos > 0.9999, (mx, cos)
+
+
+@pytest.mark.parametrize("B,valid", [(3, [300, 77, 0]), (12, [256, 200, 129, 128, 127, 64, 1, 0, 256, 255, 100, 33])])
+def test_whole_unit_attention(require_gpu, monkeypatch, B, valid):
+    """Whole-unit attention (one unit per observation and head pair over all its key chunks, two-pass
+    softmax, no merge stage; the plan above 36 observations) forced on small ragged batches,
+    empty and partial prefixes included, against the fp32 oracle."""
+    monkeypatch.setenv("FA_ATTN_WHOLE", "1")
+    c = O.make_case(seed=40 + B, L=2, T=50, AD=32, Lp=300, B=B, num_steps=2, valid_len=valid)
+    out, _ = run_engine(c)
+    mx, cos = err(out, oracle_bf16_kv(c))
+    assert mx < TOL and cos > 0.9999, (mx, cos)
