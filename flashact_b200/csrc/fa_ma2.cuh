@@ -42,6 +42,8 @@ struct Params {
   int L, T, B, NT, NPAD, NTILE, TG, ngroups, nsteps, AD, adim, LKPAD;
   int split[NUM_MATS];  // K-split factor per matrix (1 = full K, epilogue sees the final sum)
   int tg[kMaxMats];  // token tiles per group (one accumulator) of each GEMM matrix
+  int self_q;       // query tokens per self-attention unit (8, or 32 = all of an observation's tokens)
+  int cross_whole;  // cross-attention units cover all context chunks of (observation, head): no merge
   int box_atoms;
   float dt, invT;
   // plan

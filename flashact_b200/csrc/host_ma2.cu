@@ -27,6 +27,8 @@ struct Ma2State {
   CtaPlan* d_plans = nullptr;
   size_t gcap = 0, acap = 0;
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LKPAD = 0, adim = 0;
+  int self_q = 8;
+  bool cross_whole = false;
   int wg = 4;  // weight atoms per ring slot
   int ba = 4;  // activation atoms per TMA box
   int split[M::NUM_MATS] = {1, 3, 3, 3, 1, 6};
@@ -232,11 +234,28 @@ fa_status ma2_set_modulation(fa_handle* h, const float* mods, const float* mod_f
 static fa_status ma2_plan(fa_handle* h) {
   Ma2State* s = h->ma2;
   const int nblk = h->num_sms;
+  // Cross-attention units per (observation, head, 32-key chunk) with a merge stage, or (FA_MA2_WHOLE=1)
+  // per (observation, head) over all chunks (online softmax, no merge). Self-attention units take 8
+  // query tokens, or all of an observation's tokens once the (observation, head) pairs alone give
+  // half the SMs a unit (keys normalised once per unit: 32 observations 22.3 -> 17.0 ms per chunk).
+  {
+    const char* e = getenv("FA_MA2_WHOLE");
+    // (whole cross-attention units measured no faster on CUDA cores: 32 observations 98 -> 101 ms
+    // per chunk, so they are opt-in)
+    s->cross_whole = (e && atoi(e) != 0) && 12 * ((h->cfg.horizon + 2) / 3) <= 128;  // one work item per thread
+    const char* q = getenv("FA_MA2_SELFQ");
+    s->self_q = q ? (atoi(q) >= 32 ? 32 : 8) : (2 * s->B * M::H >= nblk ? 32 : 8);
+  }
   std::vector<AttnUnit> au;
   for (int b = 0; b < s->B; ++b) {
     const int nch = (s->ctx[b] + M::KC - 1) / M::KC;
-    for (int hh = 0; hh < M::H; ++hh)
+    for (int hh = 0; hh < M::H; ++hh) {
+      if (s->cross_whole) {
+        au.push_back({(uint16_t)b, (uint16_t)hh, fa::kWholeChunk, 0});
+        continue;
+      }
       for (int c = 0; c < nch; ++c) au.push_back({(uint16_t)b, (uint16_t)hh, (uint16_t)c, 0});
+    }
   }
   std::vector<CtaPlan> plans(nblk);
   std::vector<long> load(nblk, 0);
@@ -348,6 +367,8 @@ static fa_status ma2_params(fa_handle* h) {
   p.ngroups = s->ngroups; p.nsteps = h->cfg.num_steps; p.AD = h->cfg.action_dim; p.adim = s->adim; p.LKPAD = s->LKPAD;
   for (int m = 0; m < M::NUM_MATS; ++m) p.split[m] = s->split_eff[m];
   for (int m = 0; m < M::NUM_MATS; ++m) p.tg[m] = s->TG;
+  p.self_q = s->self_q;
+  p.cross_whole = s->cross_whole ? 1 : 0;
   p.dt = 1.0f / (float)h->cfg.num_steps;
   p.invT = 1.0f / (float)h->cfg.horizon;
   p.gunits = s->d_gunits; p.aunits = s->d_aunits; p.plans = s->d_plans; p.ctx_len = s->d_ctx;

@@ -169,7 +169,7 @@ __device__ __noinline__ void stage_final(const Params& p, int step, float* xf, f
 // tokens of the observation. q, k get a weightless RMS norm over the 96 head dims and half-split
 // RoPE (pairs i, i+48) at positions 0..T-1 from the bound tables; scale 1/sqrt(96)
 // (mk_ma2.cu:293-384). Every global load of a phase is issued before its first use.
-constexpr int kSelfQ = 8;  // query tokens per self-attention unit
+constexpr int kSelfQMax = TMAX;  // query tokens per self-attention unit: Params::self_q (8 or 32)
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& raw, float* dst) {
   const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
@@ -184,12 +184,13 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& raw, float* dst) {
 __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   const int T = p.T;
+  const int kSelfQ = p.self_q;
   const int ngroups = (T + kSelfQ - 1) / kSelfQ;
   float* ks = sm;                  // [32][97] keys (normed + rotated)
   float* vs = ks + TMAX * 97;      // [32][96]
-  float* qs = vs + TMAX * 96;      // [8][97]
-  float* ps = qs + kSelfQ * 97;    // [8][33]
-  float* rc = ps + kSelfQ * 33;    // [T][48] RoPE cos, then [T][48] sin
+  float* qs = vs + TMAX * 96;      // [self_q][97]
+  float* ps = qs + kSelfQMax * 97; // [self_q][33]
+  float* rc = ps + kSelfQMax * 33; // [T][48] RoPE cos, then [T][48] sin
   const float scale = 0.10206207261596577f;  // 1/sqrt(96)
   const int T48 = T * 48;
   for (int u = blockIdx.x; u < p.B * H * ngroups; u += gridDim.x) {
@@ -197,9 +198,9 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
     const int t0 = g * kSelfQ, nq = min(kSelfQ, T - t0);
     // rows: k (T), v (T), q (nq); 12 16-byte pieces per 96-dim row
     const int nrows = 2 * T + nq;
-    uint4 raw[8];
+    uint4 raw[9];  // up to 2 x 32 key / value rows + 32 query rows of 12 pieces
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
+    for (int it = 0; it < 9; ++it) {
       const int idx = e + it * 128;
       if (idx < nrows * 12) {
         const int row = idx / 12, seg = idx % 12;
@@ -213,7 +214,7 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
       reinterpret_cast<float4*>(rc + T48)[i] = __ldg(reinterpret_cast<const float4*>(p.rope_sin) + i);
     }
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
+    for (int it = 0; it < 9; ++it) {
       const int idx = e + it * 128;
       if (idx < nrows * 12) {
         const int row = idx / 12, seg = idx % 12;
@@ -399,6 +400,163 @@ __device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, 
         }
         *reinterpret_cast<uint4*>(p.opart + (((size_t)(b * H + h) * MAX_CH + ch) * TMAX + t) * HD + d8 * 8) =
             make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+    }
+    sync_epi();
+  }
+}
+
+// Whole-unit cross-attention (large batches): unit = (observation b, head h) over all its context
+// chunks, online softmax. The cross query is summed from its K-split partials and normalised once
+// per unit (a per-chunk unit redoes that for every 32 keys); per chunk, warp w scores tokens w,
+// w + 4, ... (lane = key), updates the token's running max m and sum l, and leaves 2^(s - m) in ps
+// and the factor 2^(m_old - m) by which the token's earlier output is rescaled; thread = (3 tokens,
+// 8 dims) work item then updates its accumulators. The normalised output goes straight to cattn:
+// no per-chunk partials and no merge stage.
+__device__ __forceinline__ void stage_cross_attn_whole(const Params& p, const Ctx& c, int l, float* sm) {
+  const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
+  const int T = p.T;
+  float* qs = sm;                        // [32][96], normed, pre-scaled
+  float* ps = qs + TMAX * HD;            // [32][33] probabilities of the chunk
+  float* mrun = ps + TMAX * 33;          // [32] running max (log2 units)
+  float* lrun = mrun + TMAX;             // [32] running sum
+  float* scl = lrun + TMAX;              // [32] rescale factor of this chunk
+  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(scl + TMAX);  // [32][96] V chunk
+  const float qscale = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 units
+  const int nitems = 12 * ((T + 2) / 3);               // (3 tokens, 8 dims) work items: <= 128 (T <= 30)
+  const int wi = e, d8 = wi % 12, tg = (wi / 12) * 3;  // this thread's item
+  for (int u = 0; u < c.acnt; ++u) {
+    const AttnUnit au = c.au[u];
+    const int b = au.b, h = au.hp;
+    const int lk = p.ctx_len[b];
+    const int nch = (lk + KC - 1) / KC;
+    const size_t kbase = (size_t)(b * p.L + l) * p.LKPAD;
+    {  // cross query: K-split partials summed in split order (bias on split 0), then per-head RMS
+      const int nsq = p.split[MAT_CQ];
+      float4 qa[6];
+#pragma unroll
+      for (int it = 0; it < 6; ++it) {
+        const int idx = e + it * 128;
+        if (idx < T * 24)
+          qa[it] = __ldcg(reinterpret_cast<const float4*>(p.part + (size_t)(b * T + idx / 24) * D + h * HD + (idx % 24) * 4));
+      }
+#pragma unroll 1
+      for (int sp = 1; sp < nsq; ++sp) {
+#pragma unroll
+        for (int it = 0; it < 6; ++it) {
+          const int idx = e + it * 128;
+          if (idx < T * 24) {
+            const float4 bq = __ldcg(reinterpret_cast<const float4*>(
+                p.part + ((size_t)sp * p.NPAD + b * T + idx / 24) * D + h * HD + (idx % 24) * 4));
+            qa[it].x += bq.x; qa[it].y += bq.y; qa[it].z += bq.z; qa[it].w += bq.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < 6; ++it) {
+        const int idx = e + it * 128;
+        if (idx < T * 24) *reinterpret_cast<float4*>(qs + (idx / 24) * HD + (idx % 24) * 4) = qa[it];
+      }
+      if (e < TMAX) { mrun[e] = -INFINITY; lrun[e] = 0.f; }
+    }
+    sync_epi();
+    for (int t = wq; t < T; t += 4) {
+      float* rp = qs + t * HD;
+      const float a0 = rp[lane], a1 = rp[lane + 32], a2 = rp[lane + 64];
+      const float r = rsqrtf(warp_sum(a0 * a0 + a1 * a1 + a2 * a2) * (1.0f / HD) + kEps) * qscale;
+      rp[lane] = a0 * r;
+      rp[lane + 32] = a1 * r;
+      rp[lane + 64] = a2 * r;
+    }
+    float acc[3][8];
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[q][k] = 0.f;
+#pragma unroll 1
+    for (int ch = 0; ch < nch; ++ch) {
+      const int nvalid = min(KC, lk - ch * KC);
+      const size_t krow0 = kbase + (size_t)ch * KC;
+      float kr[HD];
+      {
+        uint4 vraw[3], kraw[12];
+#pragma unroll
+        for (int it = 0; it < 3; ++it) {
+          const int idx = e + it * 128;
+          vraw[it] = __ldg(reinterpret_cast<const uint4*>(p.vctx + (krow0 + idx / 12) * D + h * HD) + idx % 12);
+        }
+        const uint4* ksrc = reinterpret_cast<const uint4*>(p.kctx + (krow0 + lane) * D + h * HD);
+#pragma unroll
+        for (int s8 = 0; s8 < 12; ++s8) kraw[s8] = __ldg(ksrc + s8);
+        sync_epi();  // the previous chunk's ps / vs are no longer read
+#pragma unroll
+        for (int it = 0; it < 3; ++it) {
+          const int idx = e + it * 128;
+          *reinterpret_cast<uint4*>(vs + (idx / 12) * HD + (idx % 12) * 8) = vraw[it];
+        }
+#pragma unroll
+        for (int s8 = 0; s8 < 12; ++s8) bf16x8_to_f32(kraw[s8], kr + s8 * 8);
+      }
+      const bool valid = lane < nvalid;
+#pragma unroll 1
+      for (int t = wq; t < T; t += 4) {
+        const float4* q4 = reinterpret_cast<const float4*>(qs + t * HD);
+        float a4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int d4 = 0; d4 < HD / 4; ++d4) {
+          const float4 q = q4[d4];
+          a4[d4 & 3] = fmaf(q.x, kr[4 * d4], fmaf(q.y, kr[4 * d4 + 1], fmaf(q.z, kr[4 * d4 + 2], fmaf(q.w, kr[4 * d4 + 3], a4[d4 & 3]))));
+        }
+        const float sc = valid ? (a4[0] + a4[1]) + (a4[2] + a4[3]) : -INFINITY;
+        const float mold = mrun[t];
+        const float mnew = fmaxf(mold, warp_max(sc));
+        const float pj = valid ? fast_exp2(sc - mnew) : 0.f;
+        const float sum = warp_sum(pj);
+        ps[t * 33 + lane] = pj;
+        __syncwarp();
+        if (lane == 0) {
+          const float f = mold == -INFINITY ? 0.f : fast_exp2(mold - mnew);
+          scl[t] = f;
+          lrun[t] = lrun[t] * f + sum;
+          mrun[t] = mnew;
+        }
+      }
+      sync_epi();
+      if (wi < nitems) {
+        float f[3];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) f[q] = tg + q < T ? scl[tg + q] : 0.f;
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[q][k] *= f[q];
+#pragma unroll 4
+        for (int j = 0; j < KC; ++j) {
+          float vv[8];
+          bf16x8_to_f32(*reinterpret_cast<const uint4*>(vs + j * HD + d8 * 8), vv);
+#pragma unroll
+          for (int q = 0; q < 3; ++q) {
+            const float pj = tg + q < T ? ps[(tg + q) * 33 + j] : 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[q][k] = fmaf(pj, vv[k], acc[q][k]);
+          }
+        }
+      }
+    }
+    sync_epi();
+    if (wi < nitems) {
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const int t = tg + q;
+        if (t >= T) continue;
+        const float inv = lrun[t] > 0.f ? 1.f / lrun[t] : 0.f;
+        uint32_t w4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[q][2 * k] * inv, acc[q][2 * k + 1] * inv);
+          w4[k] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(p.cattn + (size_t)(b * T + t) * D + h * HD + d8 * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
     }
     sync_epi();
@@ -672,9 +830,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
           } else if (s == 1) {
             if (is_epi) stage_self_attn(p, vsm);
           } else if (s == 5) {
-            if (is_epi) stage_cross_attn(p, c, l, vsm);
+            if (is_epi) {
+              if (p.cross_whole) stage_cross_attn_whole(p, c, l, vsm);
+              else stage_cross_attn(p, c, l, vsm);
+            }
           } else if (s == 6) {
-            if (is_epi) stage_merge(p);
+            if (is_epi && !p.cross_whole) stage_merge(p);  // whole units wrote cattn themselves
           } else if (s == 3 || s == 8 || !last_layer) {  // norm(mca) | norm(mlp) | next block's norm(msa)
             if (is_epi) {
               const float* gate = (s == 3 ? m_self : s == 8 ? m_cross : m_mlp) + 2 * D;

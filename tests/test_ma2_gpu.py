@@ -107,3 +107,17 @@ def test_ma2_odd_shapes(require_gpu, T, adim, Lk, B):
     mx, cos = err(out[..., :adim], oracle_bf16(c)[..., :adim])
     assert mx < TOL and cos > 0.9999, (mx, cos)
     assert torch.equal(out[..., adim:], c.noise[..., adim:])
+
+
+@pytest.mark.parametrize("whole,selfq", [("1", "32"), ("1", "8"), ("0", "32")])
+def test_ma2_large_batch_attention_forms(require_gpu, monkeypatch, whole, selfq):
+    """The large-batch attention forms forced on a small case: whole-unit cross-attention (one unit
+    per observation and head over every 32-key context chunk, online softmax, no merge) and
+    self-attention units over all 30 query tokens, against the fp32 oracle."""
+    monkeypatch.setenv("FA_MA2_WHOLE", whole)
+    monkeypatch.setenv("FA_MA2_SELFQ", selfq)
+    c = M.make_case(seed=54, L=2, T=30, Lk=300, B=3, num_steps=2)
+    out, _ = run(c)
+    mx, cos = err(out[..., :c.adim], oracle_bf16(c)[..., :c.adim])
+    assert mx < TOL and cos > 0.9999, (mx, cos)
+    assert torch.equal(out[..., c.adim:], c.noise[..., c.adim:])
