@@ -21,14 +21,15 @@ constexpr int F = 3072;      // SiLU-gated MLP hidden
 constexpr int QKV_ROWS = 3 * D;
 constexpr int MOD = 3 * D;   // scale | shift | gate of one norm
 constexpr int TMAX = 32;     // action tokens per observation (padded)
-constexpr int KC = 32;       // context keys per cross-attention chunk (one key per lane)
-constexpr int MAX_CH = 128;  // context chunks per observation (context <= 4096 tokens)
+constexpr int KC = 128;      // context keys per cross-attention unit (one 128-key tcgen05 tile)
+constexpr int MAX_CH = 32;   // context chunks per observation (context <= 4096 tokens)
 constexpr int kMinWork = 64 * 1024;  // every CTA keeps this much work area for the vector stages
 
 enum Mat : int { MAT_QKV = 0, MAT_SO, MAT_CQ, MAT_CO, MAT_GU, MAT_DN, NUM_MATS };
 enum Map : int {
   MAP_W_QKV = 0, MAP_W_SO, MAP_W_CQ, MAP_W_CO, MAP_W_GU, MAP_W_DN,  // weights, box {64, 128}
   MAP_XN, MAP_SATTN, MAP_CATTN, MAP_H,                              // activations, 3D boxes
+  MAP_KCTX, MAP_VTCTX,  // cross-attention context: K rows (2D, box 64 dims x 128 keys), V^T (3D, 96 dims x 128 keys)
   NUM_MAPS
 };
 enum Stage : int {
@@ -43,7 +44,6 @@ struct Params {
   int split[NUM_MATS];  // K-split factor per matrix (1 = full K, epilogue sees the final sum)
   int tg[kMaxMats];  // token tiles per group (one accumulator) of each GEMM matrix
   int self_q;       // query tokens per self-attention unit (8, or 32 = all of an observation's tokens)
-  int cross_whole;  // cross-attention units cover all context chunks of (observation, head): no merge
   int box_atoms;
   float dt, invT;
   // plan
@@ -62,7 +62,8 @@ struct Params {
   const float* b_ain;   // [768]
   const float* w_aout;  // [AD][768] (bf16 values held in fp32)
   const float* b_aout;  // [AD]
-  // cross-attention context (bound once): [B][L][LKPAD][768] bf16, rows >= ctx_len zero
+  // cross-attention context (bound once), bf16, keys >= ctx_len zero: K [B][L][LKPAD][768] and V
+  // transposed [B][L][768][LKPAD] (the K-major operand of O = P V)
   const __nv_bfloat16* kctx;
   const __nv_bfloat16* vctx;
   // state / scratch

@@ -282,6 +282,23 @@ static inline PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 // 3D bf16 map viewing a row-major [rows][K] array as [K/64 atoms][rows][64]: one box
 // {64, box_rows, box_atoms} lands in shared memory as box_atoms consecutive 128B-swizzled atoms.
+// 2D bf16 map over a row-major [rows][K] matrix: boxes of box_k x box_rows (box_k x 2 bytes = 128 for
+// the 128-byte swizzle), at any K offset that is a multiple of 8 elements.
+static inline fa_status make_map2(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
+                                  uint32_t box_k, uint32_t box_rows) {
+  auto enc = get_encode();
+  if (!enc) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {K, rows};
+  cuuint64_t strides[1] = {K * 2};
+  cuuint32_t box[2] = {box_k, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(h, FA_ERR_CUDA, "cuTensorMapEncodeTiled (2D) failed (%d)", (int)r);
+  return FA_OK;
+}
+
 static inline fa_status make_map3(fa_handle* h, CUtensorMap* m, const void* base, uint64_t K, uint64_t rows,
                            uint32_t box_rows, uint32_t box_atoms) {
   auto enc = get_encode();

@@ -28,7 +28,6 @@ struct Ma2State {
   size_t gcap = 0, acap = 0;
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LKPAD = 0, adim = 0;
   int self_q = 8;
-  bool cross_whole = false;
   int wg = 4;  // weight atoms per ring slot
   int ba = 4;  // activation atoms per TMA box
   int split[M::NUM_MATS] = {1, 3, 3, 3, 1, 6};
@@ -53,6 +52,26 @@ static __global__ void ma2_bind_ctx_kernel(const bf16* src, int src_rows, const 
     const int sr = rowmap && r < n ? rowmap[(size_t)b * src_rows + r] : r;
     if (r < n) val = *reinterpret_cast<const uint4*>(src + (((size_t)b * L + l) * src_rows + sr) * M::D + seg * 8);
     *reinterpret_cast<uint4*>(dst + (((size_t)b * L + l) * LKPAD + r) * M::D + seg * 8) = val;
+  }
+}
+
+// V^T bind: dst[b][l][d][r] = src[b][l][map(r)][d] for r < len[b], zero up to LKPAD (32 x 32 tiles
+// through shared memory).
+static __global__ void ma2_bind_vt_kernel(const bf16* src, int src_rows, const int* len, const int* rowmap, int L,
+                                          int LKPAD, bf16* dst) {
+  __shared__ bf16 tile[32][33];
+  const int b = blockIdx.z / L, l = blockIdx.z % L;
+  const int n = len[b];
+  const int r0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, d = d0 + threadIdx.x;
+    const int sr = rowmap && r < n ? rowmap[(size_t)b * src_rows + r] : r;
+    tile[i][threadIdx.x] = r < n ? src[(((size_t)b * L + l) * src_rows + sr) * M::D + d] : __float2bfloat16(0.f);
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int d = d0 + i, r = r0 + threadIdx.x;
+    dst[(((size_t)b * L + l) * M::D + d) * LKPAD + r] = tile[threadIdx.x][i];
   }
 }
 
@@ -234,28 +253,19 @@ fa_status ma2_set_modulation(fa_handle* h, const float* mods, const float* mod_f
 static fa_status ma2_plan(fa_handle* h) {
   Ma2State* s = h->ma2;
   const int nblk = h->num_sms;
-  // Cross-attention units per (observation, head, 32-key chunk) with a merge stage, or (FA_MA2_WHOLE=1)
-  // per (observation, head) over all chunks (online softmax, no merge). Self-attention units take 8
-  // query tokens, or all of an observation's tokens once the (observation, head) pairs alone give
-  // half the SMs a unit (keys normalised once per unit: 32 observations 22.3 -> 17.0 ms per chunk).
+  // Cross-attention units per (observation, head, 128-key context chunk), merged per (token, head)
+  // afterwards. Self-attention units take 8 query tokens, or all of an observation's tokens once the
+  // (observation, head) pairs alone give half the SMs a unit (keys normalised once per unit:
+  // 32 observations 22.3 -> 17.0 ms per chunk).
   {
-    const char* e = getenv("FA_MA2_WHOLE");
-    // (whole cross-attention units measured no faster on CUDA cores: 32 observations 98 -> 101 ms
-    // per chunk, so they are opt-in)
-    s->cross_whole = (e && atoi(e) != 0) && 12 * ((h->cfg.horizon + 2) / 3) <= 128;  // one work item per thread
     const char* q = getenv("FA_MA2_SELFQ");
     s->self_q = q ? (atoi(q) >= 32 ? 32 : 8) : (2 * s->B * M::H >= nblk ? 32 : 8);
   }
   std::vector<AttnUnit> au;
   for (int b = 0; b < s->B; ++b) {
     const int nch = (s->ctx[b] + M::KC - 1) / M::KC;
-    for (int hh = 0; hh < M::H; ++hh) {
-      if (s->cross_whole) {
-        au.push_back({(uint16_t)b, (uint16_t)hh, fa::kWholeChunk, 0});
-        continue;
-      }
+    for (int hh = 0; hh < M::H; ++hh)
       for (int c = 0; c < nch; ++c) au.push_back({(uint16_t)b, (uint16_t)hh, (uint16_t)c, 0});
-    }
   }
   std::vector<CtaPlan> plans(nblk);
   std::vector<long> load(nblk, 0);
@@ -361,6 +371,10 @@ static fa_status ma2_params(fa_handle* h) {
   if ((st = make_map3(h, &p.maps[M::MAP_SATTN], s->sattn, M::D, s->NPAD, s->NTILE, ba)) != FA_OK) return st;
   if ((st = make_map3(h, &p.maps[M::MAP_CATTN], s->cattn, M::D, s->NPAD, s->NTILE, ba)) != FA_OK) return st;
   if ((st = make_map3(h, &p.maps[M::MAP_H], s->hbuf, M::F, s->NPAD, s->NTILE, ba)) != FA_OK) return st;
+  // cross-attention context: K rows [B*L*LKPAD][768], 64 x 128 boxes at any 8-aligned dim offset
+  // (a head starts at 96 h); V^T [B*L*768][LKPAD], boxes of 96 dims x 2 atoms of 64 keys
+  if ((st = make_map2(h, &p.maps[M::MAP_KCTX], s->kctx, M::D, (uint64_t)s->B * L * s->LKPAD, 64, 128)) != FA_OK) return st;
+  if ((st = make_map3(h, &p.maps[M::MAP_VTCTX], s->vctx, s->LKPAD, (uint64_t)s->B * L * M::D, 96, 2)) != FA_OK) return st;
   p.box_atoms = (int)ba;
   p.wg = s->wg;
   p.L = L; p.T = h->cfg.horizon; p.B = s->B; p.NT = s->NT; p.NPAD = s->NPAD; p.NTILE = s->NTILE; p.TG = s->TG;
@@ -368,7 +382,6 @@ static fa_status ma2_params(fa_handle* h) {
   for (int m = 0; m < M::NUM_MATS; ++m) p.split[m] = s->split_eff[m];
   for (int m = 0; m < M::NUM_MATS; ++m) p.tg[m] = s->TG;
   p.self_q = s->self_q;
-  p.cross_whole = s->cross_whole ? 1 : 0;
   p.dt = 1.0f / (float)h->cfg.num_steps;
   p.invT = 1.0f / (float)h->cfg.horizon;
   p.gunits = s->d_gunits; p.aunits = s->d_aunits; p.plans = s->d_plans; p.ctx_len = s->d_ctx;
@@ -417,7 +430,8 @@ fa_status ma2_bind(fa_handle* h, int batch, const void* k, const void* v, int sr
     const int L_ = h->cfg.num_layers;
     const dim3 grid(std::max(1, s->LKPAD * M::D / 8 / 256 / 4), L_, batch);
     ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)k, src_rows, s->d_ctx, nullptr, L_, s->LKPAD, s->kctx);
-    ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)v, src_rows, s->d_ctx, nullptr, L_, s->LKPAD, s->vctx);
+    ma2_bind_vt_kernel<<<dim3(s->LKPAD / 32, M::D / 32, batch * L_), dim3(32, 8), 0, stream>>>(
+        (const bf16*)v, src_rows, s->d_ctx, nullptr, L_, s->LKPAD, s->vctx);
     FA_CUDA(h, cudaGetLastError());
     return FA_OK;
   }
@@ -437,7 +451,8 @@ fa_status ma2_bind(fa_handle* h, int batch, const void* k, const void* v, int sr
   if ((st = ma2_params(h)) != FA_OK) return st;
   const dim3 grid(std::max(1, s->LKPAD * M::D / 8 / 256 / 4), L, batch);
   ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)k, src_rows, s->d_ctx, rowmap, L, s->LKPAD, s->kctx);
-  ma2_bind_ctx_kernel<<<grid, 256, 0, stream>>>((const bf16*)v, src_rows, s->d_ctx, rowmap, L, s->LKPAD, s->vctx);
+  ma2_bind_vt_kernel<<<dim3(s->LKPAD / 32, M::D / 32, batch * L), dim3(32, 8), 0, stream>>>(
+      (const bf16*)v, src_rows, s->d_ctx, rowmap, L, s->LKPAD, s->vctx);
   FA_CUDA(h, cudaGetLastError());
   FA_CUDA(h, cudaStreamSynchronize(stream));
   s->bound = true;

@@ -272,295 +272,220 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
   }
 }
 
-// ------------------------------------------------------------------ cross-attention (warps 2-5)
-// Unit = (observation b, head h, context chunk c of 32 keys). q = RMS-normalised cross query of
-// head h (mk_ma2.cu:398-422); scores over the chunk's valid keys, scale 1/sqrt(96); the chunk's
-// normalised output and (max, sum) go to opart / oml for stage_merge. Lane j of every warp owns
-// key j (its 96-dim row in registers); warp w owns tokens w, w + 4, ...: a token's 32 scores sit
-// in one warp, so its max and sum are warp reductions.
-__device__ __forceinline__ void stage_cross_attn(const Params& p, const Ctx& c, int l, float* sm) {
-  const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
-  const int T = p.T;
-  float* qs = sm;                                                  // [32][96], normed, pre-scaled
-  float* ps = qs + TMAX * HD;                                      // [32][33] probabilities
-  float* rinv = ps + TMAX * 33;                                    // [32] 1 / row sum
-  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(rinv + TMAX);  // [32][96] V chunk
-  const float qscale = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 units
-  for (int u = 0; u < c.acnt; ++u) {
-    const AttnUnit au = c.au[u];
-    const int b = au.b, h = au.hp, ch = au.chunk;
-    const int lk = p.ctx_len[b];
-    const int nvalid = min(KC, lk - ch * KC);
-    const size_t krow0 = ((size_t)(b * p.L + l) * p.LKPAD + ch * KC);
-    float kr[HD];
-    {  // the V chunk (32 x 12 pieces), this lane's key row and the cross query (the K-split
-       // partials of the cross-q projection, bias on split 0, summed in split order): loads first
-      uint4 vraw[3], kraw[12];
+// ------------------------------------------------------------------ cross-attention (tcgen05)
+// Unit = (observation b, head h, context chunk c of 128 keys); 8 heads with their own K / V (MHA).
+// Per unit, in the 64 KB work area:
+//   epilogue warps  Q tile [0, 32 KB): row t = the RMS-normalised cross query of token t (the
+//                   K-split partials of the cross-q projection summed in split order, bias on split
+//                   0, mk_ma2.cu:398-422), dims 96..127 and rows >= T zero; 2 atoms of 64 dims.
+//   MMA lane        K tile [32, 64 KB) by TMA: 128 keys x dims [96 h, 96 h + 128) (the last 32 belong
+//                   to the next head and meet Q's zero dims); S = Q K^T (M 128, N 128, K 128) into
+//                   TMEM columns 0..127.
+//   epilogue warps  softmax of the rows (scale 1/sqrt(96), log2 units) -> P (bf16) into the K area.
+//   MMA lane        V^T tile (96 dims x 128 keys, 2 atoms) by TMA into the Q area once S is done;
+//                   O = P V (M 128, N 96, K 128) into TMEM columns 128..223.
+//   epilogue warps  normalised O rows and (max, sum) of the T valid rows -> opart / oml, merged per
+//                   (token, head) by stage_merge.
+// Each barrier completes once per unit, so unit u waits on phase u & 1 everywhere.
+constexpr int kXQOff = 0, kXKOff = 32 * 1024;
+constexpr float kXScale2 = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 units
+
+__device__ __forceinline__ bool mma_cross(const Params& p, const Ctx& c, MmaState& st_shared, int l) {
+  const int nunits = c.acnt;
+  const AttnUnit* const units = c.au;
+  Bars* const br = c.bars;
+  const uint32_t tmem = c.tmem;
+  uint8_t* const work = c.work;
+  int* const err = p.err;
+  const CUtensorMap* const maps = p.maps;
+  const int L = p.L, LKPAD = p.LKPAD;
+  MmaState st = st_shared;
+  const uint64_t pol = policy_evict_last();
+  for (int u = 0; u < nunits; ++u) {
+    const AttnUnit au = units[u];
+    const uint32_t ph = st.nu & 1;
+    const int krow = (au.b * L + l) * LKPAD + au.chunk * KC;
+    // K (the previous unit's P V has finished reading P from this area: o_full was waited by the
+    // epilogue before it built this unit's Q, which we wait for next)
+    if (!mbar_wait(&br->q_full, ph, err, KERR_ATTN)) return false;  // Q built, previous unit drained
+    FA_ONE(mbar_expect_tx(&br->k_full, 2 * kAtomBytes));
+    FA_ONE(tma_load_2d(work + kXKOff, &maps[MAP_KCTX], &br->k_full, 96 * au.hp, krow, pol));
+    FA_ONE(tma_load_2d(work + kXKOff + kAtomBytes, &maps[MAP_KCTX], &br->k_full, 96 * au.hp + 64, krow, pol));
+    if (!mbar_wait(&br->k_full, ph, err, KERR_ATTN)) return false;
+    tc_fence_after();
+    if (leader()) {
+      const uint32_t id_s = idesc_bf16(128, 128);
+      const uint64_t dq0 = sdesc_sw128(work + kXQOff), dk0 = sdesc_sw128(work + kXKOff);
 #pragma unroll
-      for (int it = 0; it < 3; ++it) {
-        const int idx = e + it * 128;
-        vraw[it] = __ldg(reinterpret_cast<const uint4*>(p.vctx + (krow0 + idx / 12) * D + h * HD) + idx % 12);
-      }
-      const uint4* ksrc = reinterpret_cast<const uint4*>(p.kctx + (krow0 + lane) * D + h * HD);
+      for (int a = 0; a < 2; ++a)
 #pragma unroll
-      for (int s8 = 0; s8 < 12; ++s8) kraw[s8] = __ldg(ksrc + s8);
-      const int nsq = p.split[MAT_CQ];
-      float4 qa[6];  // T rows x 24 float4 pieces, <= 6 per thread; one round trip per split
-#pragma unroll
-      for (int it = 0; it < 6; ++it) {
-        const int idx = e + it * 128;
-        if (idx < T * 24)
-          qa[it] = __ldcg(reinterpret_cast<const float4*>(p.part + (size_t)(b * T + idx / 24) * D + h * HD + (idx % 24) * 4));
-      }
-#pragma unroll 1
-      for (int sp = 1; sp < nsq; ++sp) {
-#pragma unroll
-        for (int it = 0; it < 6; ++it) {
-          const int idx = e + it * 128;
-          if (idx < T * 24) {
-            const float4 bq = __ldcg(reinterpret_cast<const float4*>(
-                p.part + ((size_t)sp * p.NPAD + b * T + idx / 24) * D + h * HD + (idx % 24) * 4));
-            qa[it].x += bq.x; qa[it].y += bq.y; qa[it].z += bq.z; qa[it].w += bq.w;
-          }
-        }
-      }
-#pragma unroll
-      for (int it = 0; it < 6; ++it) {
-        const int idx = e + it * 128;
-        if (idx < T * 24) *reinterpret_cast<float4*>(qs + (idx / 24) * HD + (idx % 24) * 4) = qa[it];
-      }
-#pragma unroll
-      for (int it = 0; it < 3; ++it) {
-        const int idx = e + it * 128;
-        *reinterpret_cast<uint4*>(vs + (idx / 12) * HD + (idx % 12) * 8) = vraw[it];
-      }
-#pragma unroll
-      for (int s8 = 0; s8 < 12; ++s8) bf16x8_to_f32(kraw[s8], kr + s8 * 8);
+        for (int s4 = 0; s4 < 4; ++s4)
+          tc_mma_bf16(tmem, dq0 + (uint64_t)((a * kAtomBytes) >> 4) + 2 * s4, dk0 + (uint64_t)((a * kAtomBytes) >> 4) + 2 * s4,
+                      id_s, (a | s4) != 0);
+      tc_commit(&br->s_full);
+      tc_commit(&br->kv_free);
     }
-    sync_epi();
-    for (int t = wq; t < T; t += 4) {  // per-head RMS of the query, then fold in the scale
-      float* rp = qs + t * HD;
-      const float a0 = rp[lane], a1 = rp[lane + 32], a2 = rp[lane + 64];
-      const float r = rsqrtf(warp_sum(a0 * a0 + a1 * a1 + a2 * a2) * (1.0f / HD) + kEps) * qscale;
-      rp[lane] = a0 * r;
-      rp[lane + 32] = a1 * r;
-      rp[lane + 64] = a2 * r;
+    __syncwarp();
+    if (!mbar_wait(&br->kv_free, ph, err, KERR_ATTN)) return false;  // S done: Q area free for V
+    FA_ONE(mbar_expect_tx(&br->v_full, 2 * 96 * 128));
+    FA_ONE(tma_load_3d(work + kXQOff, &maps[MAP_VTCTX], &br->v_full, 0, (au.b * L + l) * D + 96 * au.hp, au.chunk * 2, pol));
+    if (!mbar_wait(&br->v_full, ph, err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->p_full, ph, err, KERR_ATTN)) return false;
+    tc_fence_after();
+    if (leader()) {
+      const uint32_t id_o = idesc_bf16(128, 96);
+      const uint64_t dp0 = sdesc_sw128(work + kXKOff), dv0 = sdesc_sw128(work + kXQOff);
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+        for (int s4 = 0; s4 < 4; ++s4)
+          tc_mma_bf16(tmem + 128, dp0 + (uint64_t)((kk * kAtomBytes) >> 4) + 2 * s4,
+                      dv0 + (uint64_t)((kk * 96 * 128) >> 4) + 2 * s4, id_o, (kk | s4) != 0);
+      tc_commit(&br->o_full);
     }
-    sync_epi();
-    const bool valid = lane < nvalid;
-#pragma unroll 1
-    for (int t = wq; t < T; t += 4) {  // scores, max, probabilities, sum of token t (one warp)
-      const float4* q4 = reinterpret_cast<const float4*>(qs + t * HD);
-      float a4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int d4 = 0; d4 < HD / 4; ++d4) {
-        const float4 q = q4[d4];
-        a4[d4 & 3] = fmaf(q.x, kr[4 * d4], fmaf(q.y, kr[4 * d4 + 1], fmaf(q.z, kr[4 * d4 + 2], fmaf(q.w, kr[4 * d4 + 3], a4[d4 & 3]))));
-      }
-      const float s = valid ? (a4[0] + a4[1]) + (a4[2] + a4[3]) : -INFINITY;
-      const float m = warp_max(s);
-      const float pj = valid ? fast_exp2(s - m) : 0.f;
-      const float sum = warp_sum(pj);
-      ps[t * 33 + lane] = pj;
-      if (lane == 0) {
-        const size_t o = (((size_t)(b * H + h) * MAX_CH + ch) * TMAX + t) * 2;
-        p.oml[o] = nvalid > 0 ? m : -INFINITY;
-        p.oml[o + 1] = sum;
-        rinv[t] = sum > 0.f ? 1.f / sum : 0.f;
-      }
-    }
-    sync_epi();
-    // O = P V over the chunk: work item = (3 tokens, 8 dims), 24 accumulators; 12 x 11 = 132
-    // items for 31 or 32 tokens, so the 128 threads loop
-#pragma unroll 1
-    for (int wi = e; wi < 12 * ((T + 2) / 3); wi += 128) {
-      const int d8 = wi % 12, tg = (wi / 12) * 3;
-      float acc[3][8] = {};
-#pragma unroll 4
-      for (int j = 0; j < KC; ++j) {
-        float vv[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(vs + j * HD + d8 * 8), vv);
-#pragma unroll
-        for (int q = 0; q < 3; ++q) {
-          const float pj = tg + q < T ? ps[(tg + q) * 33 + j] : 0.f;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) acc[q][k] = fmaf(pj, vv[k], acc[q][k]);
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 3; ++q) {
-        const int t = tg + q;
-        if (t >= T) continue;
-        const float inv = rinv[t];
-        uint32_t w4[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[q][2 * k] * inv, acc[q][2 * k + 1] * inv);
-          w4[k] = *reinterpret_cast<uint32_t*>(&b2);
-        }
-        *reinterpret_cast<uint4*>(p.opart + (((size_t)(b * H + h) * MAX_CH + ch) * TMAX + t) * HD + d8 * 8) =
-            make_uint4(w4[0], w4[1], w4[2], w4[3]);
-      }
-    }
-    sync_epi();
+    __syncwarp();
+    ++st.nu;
   }
+  if (leader()) st_shared = st;
+  __syncwarp();
+  return true;
 }
 
-// Whole-unit cross-attention (large batches): unit = (observation b, head h) over all its context
-// chunks, online softmax. The cross query is summed from its K-split partials and normalised once
-// per unit (a per-chunk unit redoes that for every 32 keys); per chunk, warp w scores tokens w,
-// w + 4, ... (lane = key), updates the token's running max m and sum l, and leaves 2^(s - m) in ps
-// and the factor 2^(m_old - m) by which the token's earlier output is rescaled; thread = (3 tokens,
-// 8 dims) work item then updates its accumulators. The normalised output goes straight to cattn:
-// no per-chunk partials and no merge stage.
-__device__ __forceinline__ void stage_cross_attn_whole(const Params& p, const Ctx& c, int l, float* sm) {
-  const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
-  const int T = p.T;
-  float* qs = sm;                        // [32][96], normed, pre-scaled
-  float* ps = qs + TMAX * HD;            // [32][33] probabilities of the chunk
-  float* mrun = ps + TMAX * 33;          // [32] running max (log2 units)
-  float* lrun = mrun + TMAX;             // [32] running sum
-  float* scl = lrun + TMAX;              // [32] rescale factor of this chunk
-  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(scl + TMAX);  // [32][96] V chunk
-  const float qscale = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 units
-  const int nitems = 12 * ((T + 2) / 3);               // (3 tokens, 8 dims) work items: <= 128 (T <= 30)
-  const int wi = e, d8 = wi % 12, tg = (wi / 12) * 3;  // this thread's item
-  for (int u = 0; u < c.acnt; ++u) {
-    const AttnUnit au = c.au[u];
+// Epilogue side of the tcgen05 cross-attention; `nu` counts this CTA's units over the launch.
+__device__ __forceinline__ uint32_t epi_cross(const Params& p, const Ctx& c, uint32_t nu) {
+  const int nunits = c.acnt;
+  const AttnUnit* const units = c.au;
+  Bars* const br = c.bars;
+  const uint32_t tmem = c.tmem;
+  uint8_t* const work = c.work;
+  int* const err = p.err;
+  const int T = p.T, nsq = p.split[MAT_CQ];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
+  const int r = qd * 32 + lane;  // TMEM lane = query row = token
+  const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
+  for (int u = 0; u < nunits; ++u) {
+    const AttnUnit au = units[u];
+    const uint32_t ph = nu & 1;
     const int b = au.b, h = au.hp;
-    const int lk = p.ctx_len[b];
-    const int nch = (lk + KC - 1) / KC;
-    const size_t kbase = (size_t)(b * p.L + l) * p.LKPAD;
-    {  // cross query: K-split partials summed in split order (bias on split 0), then per-head RMS
-      const int nsq = p.split[MAT_CQ];
-      float4 qa[6];
+    // the previous unit's P V has run (its O was drained below): the Q area is free again
+    {  // Q row r: sum of the K-split partials, RMS over the 96 head dims, bf16, 128-byte swizzle
+      float q[96];
+      if (r < T) {
+        const float4* src = reinterpret_cast<const float4*>(p.part + (size_t)(b * T + r) * D + h * HD);
 #pragma unroll
-      for (int it = 0; it < 6; ++it) {
-        const int idx = e + it * 128;
-        if (idx < T * 24)
-          qa[it] = __ldcg(reinterpret_cast<const float4*>(p.part + (size_t)(b * T + idx / 24) * D + h * HD + (idx % 24) * 4));
-      }
+        for (int k = 0; k < 24; ++k) {
+          const float4 v = __ldcg(src + k);
+          q[4 * k] = v.x; q[4 * k + 1] = v.y; q[4 * k + 2] = v.z; q[4 * k + 3] = v.w;
+        }
 #pragma unroll 1
-      for (int sp = 1; sp < nsq; ++sp) {
+        for (int sp = 1; sp < nsq; ++sp) {
+          const float4* s2 = reinterpret_cast<const float4*>(p.part + ((size_t)sp * p.NPAD + b * T + r) * D + h * HD);
 #pragma unroll
-        for (int it = 0; it < 6; ++it) {
-          const int idx = e + it * 128;
-          if (idx < T * 24) {
-            const float4 bq = __ldcg(reinterpret_cast<const float4*>(
-                p.part + ((size_t)sp * p.NPAD + b * T + idx / 24) * D + h * HD + (idx % 24) * 4));
-            qa[it].x += bq.x; qa[it].y += bq.y; qa[it].z += bq.z; qa[it].w += bq.w;
+          for (int k = 0; k < 24; ++k) {
+            const float4 v = __ldcg(s2 + k);
+            q[4 * k] += v.x; q[4 * k + 1] += v.y; q[4 * k + 2] += v.z; q[4 * k + 3] += v.w;
           }
         }
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < 96; ++k) ss += q[k] * q[k];
+        const float rn = rsqrtf(ss * (1.0f / HD) + kEps);
+#pragma unroll
+        for (int k = 0; k < 96; ++k) q[k] *= rn;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 96; ++k) q[k] = 0.f;
       }
 #pragma unroll
-      for (int it = 0; it < 6; ++it) {
-        const int idx = e + it * 128;
-        if (idx < T * 24) *reinterpret_cast<float4*>(qs + (idx / 24) * HD + (idx % 24) * 4) = qa[it];
-      }
-      if (e < TMAX) { mrun[e] = -INFINITY; lrun[e] = 0.f; }
-    }
-    sync_epi();
-    for (int t = wq; t < T; t += 4) {
-      float* rp = qs + t * HD;
-      const float a0 = rp[lane], a1 = rp[lane + 32], a2 = rp[lane + 64];
-      const float r = rsqrtf(warp_sum(a0 * a0 + a1 * a1 + a2 * a2) * (1.0f / HD) + kEps) * qscale;
-      rp[lane] = a0 * r;
-      rp[lane + 32] = a1 * r;
-      rp[lane + 64] = a2 * r;
-    }
-    float acc[3][8];
+      for (int a = 0; a < 2; ++a) {
+        uint8_t* row = work + kXQOff + a * kAtomBytes + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-    for (int q = 0; q < 3; ++q)
+        for (int ch = 0; ch < 8; ++ch) {
+          uint32_t w4[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) acc[q][k] = 0.f;
-#pragma unroll 1
-    for (int ch = 0; ch < nch; ++ch) {
-      const int nvalid = min(KC, lk - ch * KC);
-      const size_t krow0 = kbase + (size_t)ch * KC;
-      float kr[HD];
-      {
-        uint4 vraw[3], kraw[12];
-#pragma unroll
-        for (int it = 0; it < 3; ++it) {
-          const int idx = e + it * 128;
-          vraw[it] = __ldg(reinterpret_cast<const uint4*>(p.vctx + (krow0 + idx / 12) * D + h * HD) + idx % 12);
-        }
-        const uint4* ksrc = reinterpret_cast<const uint4*>(p.kctx + (krow0 + lane) * D + h * HD);
-#pragma unroll
-        for (int s8 = 0; s8 < 12; ++s8) kraw[s8] = __ldg(ksrc + s8);
-        sync_epi();  // the previous chunk's ps / vs are no longer read
-#pragma unroll
-        for (int it = 0; it < 3; ++it) {
-          const int idx = e + it * 128;
-          *reinterpret_cast<uint4*>(vs + (idx / 12) * HD + (idx % 12) * 8) = vraw[it];
-        }
-#pragma unroll
-        for (int s8 = 0; s8 < 12; ++s8) bf16x8_to_f32(kraw[s8], kr + s8 * 8);
-      }
-      const bool valid = lane < nvalid;
-#pragma unroll 1
-      for (int t = wq; t < T; t += 4) {
-        const float4* q4 = reinterpret_cast<const float4*>(qs + t * HD);
-        float a4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int d4 = 0; d4 < HD / 4; ++d4) {
-          const float4 q = q4[d4];
-          a4[d4 & 3] = fmaf(q.x, kr[4 * d4], fmaf(q.y, kr[4 * d4 + 1], fmaf(q.z, kr[4 * d4 + 2], fmaf(q.w, kr[4 * d4 + 3], a4[d4 & 3]))));
-        }
-        const float sc = valid ? (a4[0] + a4[1]) + (a4[2] + a4[3]) : -INFINITY;
-        const float mold = mrun[t];
-        const float mnew = fmaxf(mold, warp_max(sc));
-        const float pj = valid ? fast_exp2(sc - mnew) : 0.f;
-        const float sum = warp_sum(pj);
-        ps[t * 33 + lane] = pj;
-        __syncwarp();
-        if (lane == 0) {
-          const float f = mold == -INFINITY ? 0.f : fast_exp2(mold - mnew);
-          scl[t] = f;
-          lrun[t] = lrun[t] * f + sum;
-          mrun[t] = mnew;
-        }
-      }
-      sync_epi();
-      if (wi < nitems) {
-        float f[3];
-#pragma unroll
-        for (int q = 0; q < 3; ++q) f[q] = tg + q < T ? scl[tg + q] : 0.f;
-#pragma unroll
-        for (int q = 0; q < 3; ++q)
-#pragma unroll
-          for (int k = 0; k < 8; ++k) acc[q][k] *= f[q];
-#pragma unroll 4
-        for (int j = 0; j < KC; ++j) {
-          float vv[8];
-          bf16x8_to_f32(*reinterpret_cast<const uint4*>(vs + j * HD + d8 * 8), vv);
-#pragma unroll
-          for (int q = 0; q < 3; ++q) {
-            const float pj = tg + q < T ? ps[(tg + q) * 33 + j] : 0.f;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) acc[q][k] = fmaf(pj, vv[k], acc[q][k]);
+          for (int k = 0; k < 4; ++k) {
+            const int d = a * 64 + ch * 8 + 2 * k;
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(d < 96 ? q[d] : 0.f, d + 1 < 96 ? q[d + 1] : 0.f);
+            w4[k] = *reinterpret_cast<uint32_t*>(&b2);
           }
+          *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
     }
-    sync_epi();
-    if (wi < nitems) {
+    fence_proxy_async_shared();
+    mbar_arrive(&br->q_full);
+    // softmax of S row r over the chunk's valid keys -> P into the K area
+    const int nvalid = min(KC, p.ctx_len[b] - au.chunk * KC);
+    if (!mbar_wait(&br->s_full, ph, err, KERR_ATTN)) return nu;
+    tc_fence_after();
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+    for (int cc = 0; cc < KC; cc += 32) {
+      float v[32];
+      tmem_ld16(tmem + lane_addr + cc, v);
+      tmem_ld16(tmem + lane_addr + cc + 16, v + 16);
+      tc_wait_ld();
 #pragma unroll
-      for (int q = 0; q < 3; ++q) {
-        const int t = tg + q;
-        if (t >= T) continue;
-        const float inv = lrun[t] > 0.f ? 1.f / lrun[t] : 0.f;
-        uint32_t w4[4];
+      for (int k = 0; k < 32; ++k)
+        if (cc + k < nvalid) m4[k & 3] = fmaxf(m4[k & 3], v[k]);
+    }
+    const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * kXScale2;
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+    uint8_t* prow = work + kXKOff + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll 1
+    for (int cc = 0; cc < KC; cc += 32) {
+      float v[32];
+      tmem_ld16(tmem + lane_addr + cc, v);
+      tmem_ld16(tmem + lane_addr + cc + 16, v + 16);
+      tc_wait_ld();
+      uint32_t pk[16];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[q][2 * k] * inv, acc[q][2 * k + 1] * inv);
-          w4[k] = *reinterpret_cast<uint32_t*>(&b2);
+      for (int k = 0; k < 32; k += 2) {
+        const float p0 = cc + k < nvalid ? fast_exp2(fmaf(v[k], kXScale2, -mx)) : 0.f;
+        const float p1 = cc + k + 1 < nvalid ? fast_exp2(fmaf(v[k + 1], kXScale2, -mx)) : 0.f;
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+        s4[(k >> 1) & 3] += __low2float(b2) + __high2float(b2);
+        pk[k >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      uint8_t* base = prow + (cc >> 6) * kAtomBytes;
+      const int ch0 = (cc & 63) >> 3;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(base + (((ch0 + q) ^ (r & 7)) << 4)) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    }
+    const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+    fence_proxy_async_shared();
+    tc_fence_before();
+    mbar_arrive(&br->p_full);
+    // normalised O row r and (max, sum) of the valid rows
+    if (!mbar_wait(&br->o_full, ph, err, KERR_ATTN)) return nu;
+    tc_fence_after();
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+    const size_t slot = ((size_t)(b * H + h) * MAX_CH + au.chunk) * TMAX + r;
+#pragma unroll 1
+    for (int cc = 0; cc < HD; cc += 32) {
+      float v[32];
+      tmem_ld16(tmem + lane_addr + 128 + cc, v);
+      tmem_ld16(tmem + lane_addr + 128 + cc + 16, v + 16);
+      tc_wait_ld();
+      if (r < T) {
+#pragma unroll
+        for (int k = 0; k < 32; k += 8) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(v[k + 2 * q] * inv, v[k + 2 * q + 1] * inv);
+            w4[q] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          *reinterpret_cast<uint4*>(p.opart + slot * HD + cc + k) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
-        *reinterpret_cast<uint4*>(p.cattn + (size_t)(b * T + t) * D + h * HD + d8 * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
     }
-    sync_epi();
+    if (r < T) *reinterpret_cast<float2*>(p.oml + slot * 2) = make_float2(nvalid > 0 ? mx : -INFINITY, sum);
+    tc_fence_before();
+    ++nu;
   }
+  return nu;
 }
 
 // Merge of the context chunks per (token, head): out = sum_c w_c O_c / sum_c w_c,
@@ -760,6 +685,9 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     mbar_init(&bars.bempty, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&bars.acc_full[i], 1); mbar_init(&bars.acc_empty[i], 128); }
     mbar_init(&bars.drain, 1);
+    // tcgen05 cross-attention: Q built / K / S / S done / V / P written / O, once per unit
+    mbar_init(&bars.q_full, 128); mbar_init(&bars.k_full, 1); mbar_init(&bars.s_full, 1);
+    mbar_init(&bars.kv_free, 1); mbar_init(&bars.v_full, 1); mbar_init(&bars.p_full, 128); mbar_init(&bars.o_full, 1);
     fence_mbar_init();
     for (int i = 0; i < NUM_MAPS; ++i) tma_prefetch_desc(&p.maps[i]);
   }
@@ -780,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     const bool is_mma = (warp == 1);
     const bool is_epi = warp >= 2;
     MmaState& st = s_st;
-    uint32_t ecnt = 0, gen = 0;
+    uint32_t ecnt = 0, gen = 0, xnu = 0;  // xnu: cross-attention units done (epilogue warps)
     ConvState cs{0, 0};  // FP8 conversion state (unused by this bf16 kernel)
     uint64_t t_prev = globaltimer();
     const bool timing = p.stage_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 32;
@@ -830,12 +758,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
           } else if (s == 1) {
             if (is_epi) stage_self_attn(p, vsm);
           } else if (s == 5) {
-            if (is_epi) {
-              if (p.cross_whole) stage_cross_attn_whole(p, c, l, vsm);
-              else stage_cross_attn(p, c, l, vsm);
-            }
+            if (is_mma) mma_cross(p, c, st, l);
+            if (is_epi) xnu = epi_cross(p, c, xnu);
           } else if (s == 6) {
-            if (is_epi && !p.cross_whole) stage_merge(p);  // whole units wrote cattn themselves
+            if (is_epi) stage_merge(p);
           } else if (s == 3 || s == 8 || !last_layer) {  // norm(mca) | norm(mlp) | next block's norm(msa)
             if (is_epi) {
               const float* gate = (s == 3 ? m_self : s == 8 ? m_cross : m_mlp) + 2 * D;

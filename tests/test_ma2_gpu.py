@@ -109,15 +109,38 @@ def test_ma2_odd_shapes(require_gpu, T, adim, Lk, B):
     assert torch.equal(out[..., adim:], c.noise[..., adim:])
 
 
-@pytest.mark.parametrize("whole,selfq", [("1", "32"), ("1", "8"), ("0", "32")])
-def test_ma2_large_batch_attention_forms(require_gpu, monkeypatch, whole, selfq):
-    """The large-batch attention forms forced on a small case: whole-unit cross-attention (one unit
-    per observation and head over every 32-key context chunk, online softmax, no merge) and
-    self-attention units over all 30 query tokens, against the fp32 oracle."""
-    monkeypatch.setenv("FA_MA2_WHOLE", whole)
+@pytest.mark.parametrize("selfq", ["8", "32"])
+def test_ma2_self_attention_unit_sizes(require_gpu, monkeypatch, selfq):
+    """Self-attention units of 8 query tokens (the small-batch plan) and of all 30 tokens (the
+    large-batch plan) on the same small case, against the fp32 oracle."""
     monkeypatch.setenv("FA_MA2_SELFQ", selfq)
     c = M.make_case(seed=54, L=2, T=30, Lk=300, B=3, num_steps=2)
     out, _ = run(c)
     mx, cos = err(out[..., :c.adim], oracle_bf16(c)[..., :c.adim])
     assert mx < TOL and cos > 0.9999, (mx, cos)
     assert torch.equal(out[..., c.adim:], c.noise[..., c.adim:])
+
+
+def test_ma2_ragged_context_lengths(require_gpu):
+    """Contexts of 1, 127, 128, 129 and 493 tokens in one batch: empty-but-one, partial and exact
+    128-key tensor-core chunks of the cross-attention."""
+    from flashact_b200 import MolmoAct2ActionExpert
+    c = M.make_case(seed=55, L=2, T=30, Lk=493, B=5, num_steps=2)
+    lens = [1, 127, 128, 129, 493]
+    for b, n in enumerate(lens):
+        c.kctx[b, :, n:] = 0
+        c.vctx[b, :, n:] = 0
+    eng = MolmoAct2ActionExpert(c.w, c.mods, c.mod_final, num_layers=c.L, horizon=c.T, action_dim=c.AD,
+                                valid_action_dim=c.adim, max_context=c.Lk, max_batch=c.B, num_steps=c.num_steps,
+                                rope_cos=c.rope_cos, rope_sin=c.rope_sin)
+    eng.bind_context(c.kctx, c.vctx, lens)
+    out = eng.sample_actions(c.noise.cuda()).cpu()
+    outs = []
+    for b, n in enumerate(lens):
+        sub = M.Ma2Case(**{**c.__dict__})
+        sub.B, sub.noise, sub.Lk = 1, c.noise[b:b + 1], n
+        sub.kctx, sub.vctx = c.kctx[b:b + 1, :, :n], c.vctx[b:b + 1, :, :n]
+        outs.append(oracle_bf16(sub)[0])
+    ref = torch.stack(outs)
+    mx, cos = err(out[..., :c.adim], ref[..., :c.adim])
+    assert mx < TOL and cos > 0.9999, (mx, cos)
