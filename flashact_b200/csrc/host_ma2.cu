@@ -382,6 +382,10 @@ static fa_status ma2_params(fa_handle* h) {
   for (int m = 0; m < M::NUM_MATS; ++m) p.split[m] = s->split_eff[m];
   for (int m = 0; m < M::NUM_MATS; ++m) p.tg[m] = s->TG;
   p.self_q = s->self_q;
+  {
+    const char* e = getenv("FA_MA2_SELF_TC");  // 0: CUDA-core self-attention
+    p.self_tc = !(e && atoi(e) == 0);
+  }
   p.dt = 1.0f / (float)h->cfg.num_steps;
   p.invT = 1.0f / (float)h->cfg.horizon;
   p.gunits = s->d_gunits; p.aunits = s->d_aunits; p.plans = s->d_plans; p.ctx_len = s->d_ctx;

@@ -272,6 +272,190 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
   }
 }
 
+constexpr float kXScale2 = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 units
+
+// ------------------------------------------------------------------ self-attention (tcgen05)
+// Unit = (observation b, head h): all T (<= 32) action tokens attend to each other. The epilogue
+// warps stage the operands in the work area: warp of lane quadrant 0 the Q rows (token t = lane;
+// weightless RMS over the 96 head dims, then half-split RoPE of pairs (i, i + 48) at position t,
+// mk_ma2.cu:293-384), quadrant 1 the K rows the same way, quadrant 2 V transposed (V^T[d][t]);
+// all as 128-byte-swizzled K-major atoms. S = Q K^T (M 128, N 32, K 128: dims 96..127 zero) ->
+// softmax of the T rows on quadrant 0 (scale 1/sqrt(96)) -> P -> O = P V (M 128, N 96, K 32) ->
+// the T normalised rows straight into sattn (one key chunk: no merge).
+// Work area: Q [0, 32 KB) | K [32, 40 KB) | V^T [40, 52 KB) | P [52 KB, ...): the MMAs read 128
+// rows of P, of which only the first 32 (4 KB) are written; the rest lie in the epilogue staging
+// area that follows the 64 KB work area and feed result rows that are never read.
+constexpr int kSQOff = 0, kSKOff = 32 * 1024, kSVOff = 40 * 1024, kSPOff = 52 * 1024;
+
+// Row `t` (96 bf16 from qkv) -> RMS -> optional RoPE -> bf16 into a 2-atom K-major tile row `r`
+// (dims 96..127 zero). `atom_rows`: rows per atom (128 for Q, 32 for K).
+__device__ __forceinline__ void self_stage_row(const __nv_bfloat16* src, const float* cs, const float* sn,
+                                               uint8_t* tile, int r, int atom_rows) {
+  float x[96];
+#pragma unroll
+  for (int k = 0; k < 12; ++k) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(src) + k), x + 8 * k);
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < 96; ++k) ss += x[k] * x[k];
+  const float rn = rsqrtf(ss * (1.0f / HD) + kEps);
+#pragma unroll
+  for (int i = 0; i < 48; ++i) {
+    const float x1 = x[i] * rn, x2 = x[i + 48] * rn;
+    x[i] = x1 * cs[i] - x2 * sn[i];
+    x[i + 48] = x1 * sn[i] + x2 * cs[i];
+  }
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+    uint8_t* row = tile + a * atom_rows * 128 + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      uint32_t w4[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int d = a * 64 + ch * 8 + 2 * k;
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(d < 96 ? x[d] : 0.f, d + 1 < 96 ? x[d + 1] : 0.f);
+        w4[k] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+  }
+}
+
+__device__ __forceinline__ bool mma_self(const Params& p, const Ctx& c, MmaState& st_shared) {
+  Bars* const br = c.bars;
+  const uint32_t tmem = c.tmem;
+  uint8_t* const work = c.work;
+  int* const err = p.err;
+  MmaState st = st_shared;
+  const int nunits = p.B * H;
+  for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+    const uint32_t ph = st.nu & 1;
+    if (!mbar_wait(&br->q_full, ph, err, KERR_ATTN)) return false;  // Q, K, V^T staged
+    tc_fence_after();
+    if (leader()) {
+      const uint64_t dq = sdesc_sw128(work + kSQOff), dk = sdesc_sw128(work + kSKOff);
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int s4 = 0; s4 < 4; ++s4)
+          tc_mma_bf16(tmem, dq + (uint64_t)((a * kAtomBytes) >> 4) + 2 * s4, dk + (uint64_t)((a * 32 * 128) >> 4) + 2 * s4,
+                      idesc_bf16(128, 32), (a | s4) != 0);
+      tc_commit(&br->s_full);
+    }
+    __syncwarp();
+    if (!mbar_wait(&br->p_full, ph, err, KERR_ATTN)) return false;
+    tc_fence_after();
+    if (leader()) {
+      const uint64_t dp = sdesc_sw128(work + kSPOff), dv = sdesc_sw128(work + kSVOff);
+#pragma unroll
+      for (int s4 = 0; s4 < 2; ++s4) tc_mma_bf16(tmem + 128, dp + 2 * s4, dv + 2 * s4, idesc_bf16(128, 96), s4 != 0);
+      tc_commit(&br->o_full);
+    }
+    __syncwarp();
+    ++st.nu;
+  }
+  if (leader()) st_shared = st;
+  __syncwarp();
+  return true;
+}
+
+__device__ __forceinline__ uint32_t epi_self(const Params& p, const Ctx& c, uint32_t nu) {
+  Bars* const br = c.bars;
+  const uint32_t tmem = c.tmem;
+  uint8_t* const work = c.work;
+  int* const err = p.err;
+  const int T = p.T;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
+  const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
+  const int nunits = p.B * H;
+  for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+    const int b = u / H, h = u % H;
+    const uint32_t ph = nu & 1;
+    // stage the operands (the previous unit's O has been drained: its MMAs are done)
+    if (lane < T && qd < 2) {
+      const int sec = qd == 0 ? 0 : 1;  // q | k section of the qkv row
+      self_stage_row(p.qkv + (size_t)(b * T + lane) * QKV_ROWS + sec * D + h * HD, p.rope_cos + lane * 48,
+                     p.rope_sin + lane * 48, work + (qd == 0 ? kSQOff : kSKOff), lane, qd == 0 ? 128 : 32);
+    } else if (qd < 2) {  // rows of missing tokens: zero (they meet valid rows as keys)
+      for (int a = 0; a < 2; ++a) {
+        uint8_t* row = work + (qd == 0 ? kSQOff : kSKOff) + a * (qd == 0 ? 128 : 32) * 128 + (lane >> 3) * 1024 + (lane & 7) * 128;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) *reinterpret_cast<uint4*>(row + (ch << 4)) = make_uint4(0, 0, 0, 0);
+      }
+    } else if (qd == 2) {  // V^T[d][t] for token t = lane: 96 two-byte stores into the swizzled rows
+      const unsigned short* src = reinterpret_cast<const unsigned short*>(p.qkv + (size_t)(b * T + lane) * QKV_ROWS + 2 * D + h * HD);
+      const int t = lane, chunk = t >> 3;
+      uint8_t* vt = work + kSVOff;
+#pragma unroll 4
+      for (int d = 0; d < 96; ++d) {
+        const unsigned short v = lane < T ? __ldg(src + d) : (unsigned short)0;
+        *reinterpret_cast<unsigned short*>(vt + (d >> 3) * 1024 + (d & 7) * 128 + ((chunk ^ (d & 7)) << 4) + (t & 7) * 2) = v;
+      }
+    }
+    fence_proxy_async_shared();
+    mbar_arrive(&br->q_full);
+    if (qd == 0) {  // softmax of the T rows (row = lane), P into the work area
+      if (!mbar_wait(&br->s_full, ph, err, KERR_ATTN)) return nu;
+      tc_fence_after();
+      float v[32];
+      tmem_ld16(tmem + lane_addr, v);
+      tmem_ld16(tmem + lane_addr + 16, v + 16);
+      tc_wait_ld();
+      float m = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (k < T) m = fmaxf(m, v[k]);
+      m *= kXScale2;
+      float sum = 0.f;
+      uint32_t pk[16];
+#pragma unroll
+      for (int k = 0; k < 32; k += 2) {
+        const float p0 = k < T ? fast_exp2(fmaf(v[k], kXScale2, -m)) : 0.f;
+        const float p1 = k + 1 < T ? fast_exp2(fmaf(v[k + 1], kXScale2, -m)) : 0.f;
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+        sum += __low2float(b2) + __high2float(b2);
+        pk[k >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      uint8_t* prow = work + kSPOff + (lane >> 3) * 1024 + (lane & 7) * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(prow + ((q ^ (lane & 7)) << 4)) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+      fence_proxy_async_shared();
+      tc_fence_before();
+      mbar_arrive(&br->p_full);
+      if (!mbar_wait(&br->o_full, ph, err, KERR_ATTN)) return nu;
+      tc_fence_after();
+      const float inv = sum > 0.f ? 1.f / sum : 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < HD; cc += 32) {
+        float o[32];
+        tmem_ld16(tmem + lane_addr + 128 + cc, o);
+        tmem_ld16(tmem + lane_addr + 128 + cc + 16, o + 16);
+        tc_wait_ld();
+        if (lane < T) {
+#pragma unroll
+          for (int k = 0; k < 32; k += 8) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(o[k + 2 * q] * inv, o[k + 2 * q + 1] * inv);
+              w4[q] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+            *reinterpret_cast<uint4*>(p.sattn + (size_t)(b * T + lane) * D + h * HD + cc + k) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+        }
+      }
+      tc_fence_before();
+    } else {  // the others: p_full counts all 128 epilogue threads; then wait for the unit's MMAs
+      mbar_arrive(&br->p_full);
+      if (!mbar_wait(&br->o_full, ph, err, KERR_ATTN)) return nu;
+    }
+    sync_epi();  // quadrant 0 has drained O before anyone restages the operands
+    ++nu;
+  }
+  return nu;
+}
+
 // ------------------------------------------------------------------ cross-attention (tcgen05)
 // Unit = (observation b, head h, context chunk c of 128 keys); 8 heads with their own K / V (MHA).
 // Per unit, in the 64 KB work area:
@@ -286,9 +470,9 @@ __device__ __forceinline__ void stage_self_attn(const Params& p, float* sm) {
 //                   O = P V (M 128, N 96, K 128) into TMEM columns 128..223.
 //   epilogue warps  normalised O rows and (max, sum) of the T valid rows -> opart / oml, merged per
 //                   (token, head) by stage_merge.
-// Each barrier completes once per unit, so unit u waits on phase u & 1 everywhere.
+// q_full, s_full, p_full and o_full complete once per unit of this stage and of the self-attention
+// stage (phase = all units so far & 1); k_full, kv_free and v_full once per cross unit only.
 constexpr int kXQOff = 0, kXKOff = 32 * 1024;
-constexpr float kXScale2 = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 units
 
 __device__ __forceinline__ bool mma_cross(const Params& p, const Ctx& c, MmaState& st_shared, int l) {
   const int nunits = c.acnt;
@@ -303,7 +487,8 @@ __device__ __forceinline__ bool mma_cross(const Params& p, const Ctx& c, MmaStat
   const uint64_t pol = policy_evict_last();
   for (int u = 0; u < nunits; ++u) {
     const AttnUnit au = units[u];
-    const uint32_t ph = st.nu & 1;
+    const uint32_t ph = st.nu & 1;   // barriers shared with the self-attention units
+    const uint32_t phx = st.nq & 1;  // k_full, kv_free, v_full: completed by cross units only
     const int krow = (au.b * L + l) * LKPAD + au.chunk * KC;
     // K (the previous unit's P V has finished reading P from this area: o_full was waited by the
     // epilogue before it built this unit's Q, which we wait for next)
@@ -311,7 +496,7 @@ __device__ __forceinline__ bool mma_cross(const Params& p, const Ctx& c, MmaStat
     FA_ONE(mbar_expect_tx(&br->k_full, 2 * kAtomBytes));
     FA_ONE(tma_load_2d(work + kXKOff, &maps[MAP_KCTX], &br->k_full, 96 * au.hp, krow, pol));
     FA_ONE(tma_load_2d(work + kXKOff + kAtomBytes, &maps[MAP_KCTX], &br->k_full, 96 * au.hp + 64, krow, pol));
-    if (!mbar_wait(&br->k_full, ph, err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->k_full, phx, err, KERR_ATTN)) return false;
     tc_fence_after();
     if (leader()) {
       const uint32_t id_s = idesc_bf16(128, 128);
@@ -326,10 +511,10 @@ __device__ __forceinline__ bool mma_cross(const Params& p, const Ctx& c, MmaStat
       tc_commit(&br->kv_free);
     }
     __syncwarp();
-    if (!mbar_wait(&br->kv_free, ph, err, KERR_ATTN)) return false;  // S done: Q area free for V
+    if (!mbar_wait(&br->kv_free, phx, err, KERR_ATTN)) return false;  // S done: Q area free for V
     FA_ONE(mbar_expect_tx(&br->v_full, 2 * 96 * 128));
     FA_ONE(tma_load_3d(work + kXQOff, &maps[MAP_VTCTX], &br->v_full, 0, (au.b * L + l) * D + 96 * au.hp, au.chunk * 2, pol));
-    if (!mbar_wait(&br->v_full, ph, err, KERR_ATTN)) return false;
+    if (!mbar_wait(&br->v_full, phx, err, KERR_ATTN)) return false;
     if (!mbar_wait(&br->p_full, ph, err, KERR_ATTN)) return false;
     tc_fence_after();
     if (leader()) {
@@ -345,6 +530,7 @@ __device__ __forceinline__ bool mma_cross(const Params& p, const Ctx& c, MmaStat
     }
     __syncwarp();
     ++st.nu;
+    ++st.nq;
   }
   if (leader()) st_shared = st;
   __syncwarp();
@@ -756,7 +942,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
             if (is_mma) mma_gemm<Ma2Model>(p, c, st, m);
             if (is_epi) ecnt = epi_gemm<Ma2Model>(p, c, ecnt, m, l, cs);
           } else if (s == 1) {
-            if (is_epi) stage_self_attn(p, vsm);
+            if (p.self_tc) {
+              if (is_mma) mma_self(p, c, st);
+              if (is_epi) xnu = epi_self(p, c, xnu);
+            } else if (is_epi) {
+              stage_self_attn(p, vsm);
+            }
           } else if (s == 5) {
             if (is_mma) mma_cross(p, c, st, l);
             if (is_epi) xnu = epi_cross(p, c, xnu);
