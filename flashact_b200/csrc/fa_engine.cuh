@@ -156,6 +156,8 @@ struct Bars {
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
   uint64_t s_free, pv_done;  // whole-unit attention: S read by the softmax warps; P V done (P and V free)
+  // MolmoAct2 whole-unit cross-attention (double-buffered S / P / O per 128-key chunk)
+  uint64_t xq_full, xs_full[2], xs_free[2], xp_full[2], xo_full[2], xo_free[2];
 };
 struct Ctx {
   uint8_t* ring;  // ring_slots x (wg x 16 KB); FP8 streaming: ring_slots x (wg x 8 KB) of E4M3 codes
@@ -308,6 +310,7 @@ struct MmaState {
   int last_q;
   uint32_t ns, npv;      // whole-unit attention: S tiles computed, P V products issued
   int k_pre;             // the next attention unit's prefix K is already loading (prefetched)
+  uint32_t xu, xc;       // MolmoAct2 whole-unit cross-attention: units, key chunks
   uint32_t qtm;          // token-major GEMMs: activation K-chunks consumed (staging / TMEM A slot phases)
 };
 

@@ -44,6 +44,7 @@ struct Params {
   int split[NUM_MATS];  // K-split factor per matrix (1 = full K, epilogue sees the final sum)
   int tg[kMaxMats];  // token tiles per group (one accumulator) of each GEMM matrix
   int self_tc;      // self-attention on tcgen05 (one unit per observation and head)
+  int cross_whole;  // cross-attention units cover all context chunks of one (observation, head); no merge
   int self_q;       // query tokens per self-attention unit (8, or 32 = all of an observation's tokens)
   int box_atoms;
   float dt, invT;

@@ -28,6 +28,7 @@ struct Ma2State {
   size_t gcap = 0, acap = 0;
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LKPAD = 0, adim = 0;
   int self_q = 8;
+  bool cross_whole = false;
   int wg = 4;  // weight atoms per ring slot
   int ba = 4;  // activation atoms per TMA box
   int split[M::NUM_MATS] = {1, 3, 3, 3, 1, 6};
@@ -261,11 +262,24 @@ static fa_status ma2_plan(fa_handle* h) {
     const char* q = getenv("FA_MA2_SELFQ");
     s->self_q = q ? (atoi(q) >= 32 ? 32 : 8) : (2 * s->B * M::H >= nblk ? 32 : 8);
   }
+  // Whole units (every chunk of one (observation, head), online softmax, no merge stage) once the
+  // (observation, head) pairs give a quarter of the SMs a unit (B200, context 493: 32 observations
+  // 92.3 -> 74.6 ms per chunk, 8 observations 54.2 -> 48.5 ms; 1 observation 29.5 -> 31.0 ms, so
+  // small batches keep the per-chunk units).
+  {
+    const char* w = getenv("FA_MA2_XWHOLE");
+    s->cross_whole = w ? atoi(w) != 0 : 4 * s->B * M::H >= nblk;
+  }
   std::vector<AttnUnit> au;
   for (int b = 0; b < s->B; ++b) {
     const int nch = (s->ctx[b] + M::KC - 1) / M::KC;
-    for (int hh = 0; hh < M::H; ++hh)
+    for (int hh = 0; hh < M::H; ++hh) {
+      if (s->cross_whole) {
+        au.push_back({(uint16_t)b, (uint16_t)hh, fa::kWholeChunk, 0});
+        continue;
+      }
       for (int c = 0; c < nch; ++c) au.push_back({(uint16_t)b, (uint16_t)hh, (uint16_t)c, 0});
+    }
   }
   std::vector<CtaPlan> plans(nblk);
   std::vector<long> load(nblk, 0);
@@ -274,7 +288,9 @@ static fa_status ma2_plan(fa_handle* h) {
     const int lo = i < acta ? (int)((long)na * i / acta) : 0, hi = i < acta ? (int)((long)na * (i + 1) / acta) : 0;
     plans[i].a_off = lo;
     plans[i].a_cnt = hi - lo;
-    load[i] = (long)plans[i].a_cnt * 8;
+    load[i] = 0;
+    for (int k = lo; k < hi; ++k)  // a chunk's worth of work per unit, or every chunk of a whole unit
+      load[i] += 8L * (au[k].chunk == fa::kWholeChunk ? (s->ctx[au[k].b] + M::KC - 1) / M::KC : 1);
   }
   std::vector<std::vector<GemmUnit>> per((size_t)nblk * M::NUM_MATS);
   const int order[M::NUM_MATS] = {M::MAT_GU, M::MAT_QKV, M::MAT_DN, M::MAT_SO, M::MAT_CQ, M::MAT_CO};
@@ -385,6 +401,7 @@ static fa_status ma2_params(fa_handle* h) {
   {
     const char* e = getenv("FA_MA2_SELF_TC");  // 0: CUDA-core self-attention
     p.self_tc = !(e && atoi(e) == 0);
+    p.cross_whole = s->cross_whole;
   }
   p.dt = 1.0f / (float)h->cfg.num_steps;
   p.invT = 1.0f / (float)h->cfg.horizon;

@@ -287,6 +287,58 @@ constexpr float kXScale2 = 0.10206207261596577f * kLog2e;  // 1/sqrt(96), log2 u
 // area that follows the 64 KB work area and feed result rows that are never read.
 constexpr int kSQOff = 0, kSKOff = 32 * 1024, kSVOff = 40 * 1024, kSPOff = 52 * 1024;
 
+// 96 floats -> bf16 row `r` of a 2-atom K-major tile with 128-byte swizzle (dims 96..127 zero);
+// the atoms lie `atom_bytes` apart (16 KB for 128-row atoms; less when only the first rows are
+// stored and the MMA's other rows may read anything).
+__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int r, int atom_bytes, const float* x) {
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+    uint8_t* row = tile + a * atom_bytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      uint32_t w4[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int d = a * 64 + ch * 8 + 2 * k;
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(d < 96 ? x[d] : 0.f, d + 1 < 96 ? x[d + 1] : 0.f);
+        w4[k] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+  }
+}
+
+// Cross-attention query row of token r, head h: the sum of the cross-q GEMM's K-split partials,
+// weightless RMS over the 96 head dims (mk_ma2.cu:293-384); zeros for r >= T.
+__device__ __forceinline__ void cross_q_row(const Params& p, int b, int h, int r, float* q) {
+  if (r >= p.T) {
+#pragma unroll
+    for (int k = 0; k < 96; ++k) q[k] = 0.f;
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(p.part + (size_t)(b * p.T + r) * D + h * HD);
+#pragma unroll
+  for (int k = 0; k < 24; ++k) {
+    const float4 v = __ldcg(src + k);
+    q[4 * k] = v.x; q[4 * k + 1] = v.y; q[4 * k + 2] = v.z; q[4 * k + 3] = v.w;
+  }
+#pragma unroll 1
+  for (int sp = 1; sp < p.split[MAT_CQ]; ++sp) {
+    const float4* s2 = reinterpret_cast<const float4*>(p.part + ((size_t)sp * p.NPAD + b * p.T + r) * D + h * HD);
+#pragma unroll
+    for (int k = 0; k < 24; ++k) {
+      const float4 v = __ldcg(s2 + k);
+      q[4 * k] += v.x; q[4 * k + 1] += v.y; q[4 * k + 2] += v.z; q[4 * k + 3] += v.w;
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < 96; ++k) ss += q[k] * q[k];
+  const float rn = rsqrtf(ss * (1.0f / HD) + kEps);
+#pragma unroll
+  for (int k = 0; k < 96; ++k) q[k] *= rn;
+}
+
 // Row `t` (96 bf16 from qkv) -> RMS -> optional RoPE -> bf16 into a 2-atom K-major tile row `r`
 // (dims 96..127 zero). `atom_rows`: rows per atom (128 for Q, 32 for K).
 __device__ __forceinline__ void self_stage_row(const __nv_bfloat16* src, const float* cs, const float* sn,
@@ -304,21 +356,7 @@ __device__ __forceinline__ void self_stage_row(const __nv_bfloat16* src, const f
     x[i] = x1 * cs[i] - x2 * sn[i];
     x[i + 48] = x1 * sn[i] + x2 * cs[i];
   }
-#pragma unroll
-  for (int a = 0; a < 2; ++a) {
-    uint8_t* row = tile + a * atom_rows * 128 + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      uint32_t w4[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int d = a * 64 + ch * 8 + 2 * k;
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(d < 96 ? x[d] : 0.f, d + 1 < 96 ? x[d + 1] : 0.f);
-        w4[k] = *reinterpret_cast<uint32_t*>(&b2);
-      }
-      *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-    }
-  }
+  store_row_sw128(tile, r, atom_rows * 128, x);
 }
 
 __device__ __forceinline__ bool mma_self(const Params& p, const Ctx& c, MmaState& st_shared) {
@@ -545,7 +583,7 @@ __device__ __forceinline__ uint32_t epi_cross(const Params& p, const Ctx& c, uin
   const uint32_t tmem = c.tmem;
   uint8_t* const work = c.work;
   int* const err = p.err;
-  const int T = p.T, nsq = p.split[MAT_CQ];
+  const int T = p.T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const int r = qd * 32 + lane;  // TMEM lane = query row = token
   const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
@@ -554,49 +592,10 @@ __device__ __forceinline__ uint32_t epi_cross(const Params& p, const Ctx& c, uin
     const uint32_t ph = nu & 1;
     const int b = au.b, h = au.hp;
     // the previous unit's P V has run (its O was drained below): the Q area is free again
-    {  // Q row r: sum of the K-split partials, RMS over the 96 head dims, bf16, 128-byte swizzle
+    {  // Q row r: K-split partials summed, RMS, bf16 into the 128-row Q tile
       float q[96];
-      if (r < T) {
-        const float4* src = reinterpret_cast<const float4*>(p.part + (size_t)(b * T + r) * D + h * HD);
-#pragma unroll
-        for (int k = 0; k < 24; ++k) {
-          const float4 v = __ldcg(src + k);
-          q[4 * k] = v.x; q[4 * k + 1] = v.y; q[4 * k + 2] = v.z; q[4 * k + 3] = v.w;
-        }
-#pragma unroll 1
-        for (int sp = 1; sp < nsq; ++sp) {
-          const float4* s2 = reinterpret_cast<const float4*>(p.part + ((size_t)sp * p.NPAD + b * T + r) * D + h * HD);
-#pragma unroll
-          for (int k = 0; k < 24; ++k) {
-            const float4 v = __ldcg(s2 + k);
-            q[4 * k] += v.x; q[4 * k + 1] += v.y; q[4 * k + 2] += v.z; q[4 * k + 3] += v.w;
-          }
-        }
-        float ss = 0.f;
-#pragma unroll
-        for (int k = 0; k < 96; ++k) ss += q[k] * q[k];
-        const float rn = rsqrtf(ss * (1.0f / HD) + kEps);
-#pragma unroll
-        for (int k = 0; k < 96; ++k) q[k] *= rn;
-      } else {
-#pragma unroll
-        for (int k = 0; k < 96; ++k) q[k] = 0.f;
-      }
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        uint8_t* row = work + kXQOff + a * kAtomBytes + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          uint32_t w4[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int d = a * 64 + ch * 8 + 2 * k;
-            __nv_bfloat162 b2 = __floats2bfloat162_rn(d < 96 ? q[d] : 0.f, d + 1 < 96 ? q[d + 1] : 0.f);
-            w4[k] = *reinterpret_cast<uint32_t*>(&b2);
-          }
-          *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-        }
-      }
+      cross_q_row(p, b, h, r, q);
+      store_row_sw128(work + kXQOff, r, kAtomBytes, q);
     }
     fence_proxy_async_shared();
     mbar_arrive(&br->q_full);
@@ -672,6 +671,215 @@ __device__ __forceinline__ uint32_t epi_cross(const Params& p, const Ctx& c, uin
     ++nu;
   }
   return nu;
+}
+
+// ------------------------------------------------------------------ cross-attention, whole units
+// Unit = (observation b, head h) over all of b's 128-key context chunks, for batches that give
+// every SM such a unit: Q is built once per unit, the chunks run as an online softmax (running
+// max and sum per query row; the un-normalised O of each chunk is rescaled into registers), and
+// the normalised rows go straight to cattn: no per-chunk partials, no merge stage.
+// Only the T <= 32 query rows are real, so Q and P keep just rows 0..31 of their two 64-dim
+// atoms (atoms 4 KB apart); the MMA's rows 32..127 read whatever follows and produce S / O rows
+// that are never read. Work area (64 KB + the 16 KB staging area that follows it):
+//   Q [0, 8 KB) | P0 [8, 16 KB) | P1 [16, 24 KB) | K [24, 56 KB) | V^T [56, 80 KB)
+// TMEM: S of chunk n in columns (n & 1) * 128, its O in 256 + (n & 1) * 128.
+// The MMA lane computes S of chunk c + 1 before P V of chunk c, so the softmax warp finds the next
+// S ready; K of chunk c + 2 loads once S of c + 1 is done, V of chunk c + 1 once P V of c is done.
+constexpr int kWQOff = 0, kWPOff = 8 * 1024, kWKOff = 24 * 1024, kWVOff = 56 * 1024, kWRowAtom = 4096;
+
+__device__ __forceinline__ bool mma_cross_whole(const Params& p, const Ctx& c, MmaState& st_shared, int l) {
+  Bars* const br = c.bars;
+  const uint32_t tmem = c.tmem;
+  uint8_t* const work = c.work;
+  int* const err = p.err;
+  const CUtensorMap* const maps = p.maps;
+  const int L = p.L, LKPAD = p.LKPAD;
+  MmaState st = st_shared;
+  const uint64_t pol = policy_evict_last();
+  const uint32_t id_s = idesc_bf16(128, 128), id_o = idesc_bf16(128, 96);
+  for (int u = 0; u < c.acnt; ++u) {
+    const AttnUnit au = c.au[u];
+    const int nch = (p.ctx_len[au.b] + KC - 1) / KC;
+    const int krow0 = (au.b * L + l) * LKPAD, vrow = (au.b * L + l) * D + 96 * au.hp;
+    const uint32_t n0 = st.xc;
+    auto load_k = [&](int ch) {
+      FA_ONE(mbar_expect_tx(&br->k_full, 2 * kAtomBytes));
+      FA_ONE(tma_load_2d(work + kWKOff, &maps[MAP_KCTX], &br->k_full, 96 * au.hp, krow0 + ch * KC, pol));
+      FA_ONE(tma_load_2d(work + kWKOff + kAtomBytes, &maps[MAP_KCTX], &br->k_full, 96 * au.hp + 64, krow0 + ch * KC, pol));
+    };
+    auto load_v = [&](int ch) {
+      FA_ONE(mbar_expect_tx(&br->v_full, 2 * 96 * 128));
+      FA_ONE(tma_load_3d(work + kWVOff, &maps[MAP_VTCTX], &br->v_full, 0, vrow, ch * 2, pol));
+    };
+    // S of chunk ch (global chunk index n) into TMEM buffer n & 1; then K of chunk ch + 1
+    auto do_s = [&](int ch) -> bool {
+      const uint32_t n = n0 + ch, j = n & 1;
+      if (!mbar_wait(&br->k_full, n & 1, err, KERR_ATTN)) return false;
+      if (!mbar_wait(&br->xs_free[j], ((n >> 1) & 1) ^ 1, err, KERR_ATTN)) return false;
+      tc_fence_after();
+      if (leader()) {
+        const uint64_t dq = sdesc_sw128(work + kWQOff), dk = sdesc_sw128(work + kWKOff);
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+          for (int s4 = 0; s4 < 4; ++s4)
+            tc_mma_bf16(tmem + j * 128, dq + (uint64_t)((a * kWRowAtom) >> 4) + 2 * s4,
+                        dk + (uint64_t)((a * kAtomBytes) >> 4) + 2 * s4, id_s, (a | s4) != 0);
+        tc_commit(&br->xs_full[j]);
+        tc_commit(&br->kv_free);
+      }
+      __syncwarp();
+      if (!mbar_wait(&br->kv_free, n & 1, err, KERR_ATTN)) return false;  // K area free
+      if (ch + 1 < nch) load_k(ch + 1);
+      return true;
+    };
+    // K and V of the first chunk: both areas are free (the previous unit's last S and P V were
+    // waited for below)
+    load_k(0);
+    load_v(0);
+    if (!mbar_wait(&br->xq_full, st.xu & 1, err, KERR_ATTN)) return false;
+    if (!do_s(0)) return false;
+    for (int ch = 0; ch < nch; ++ch) {
+      if (ch + 1 < nch && !do_s(ch + 1)) return false;
+      const uint32_t n = n0 + ch, j = n & 1;
+      if (!mbar_wait(&br->v_full, n & 1, err, KERR_ATTN)) return false;
+      if (!mbar_wait(&br->xp_full[j], (n >> 1) & 1, err, KERR_ATTN)) return false;
+      if (!mbar_wait(&br->xo_free[j], ((n >> 1) & 1) ^ 1, err, KERR_ATTN)) return false;
+      tc_fence_after();
+      if (leader()) {
+        const uint64_t dp = sdesc_sw128(work + kWPOff + j * 2 * kWRowAtom), dv = sdesc_sw128(work + kWVOff);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+          for (int s4 = 0; s4 < 4; ++s4)
+            tc_mma_bf16(tmem + 256 + j * 128, dp + (uint64_t)((kk * kWRowAtom) >> 4) + 2 * s4,
+                        dv + (uint64_t)((kk * 96 * 128) >> 4) + 2 * s4, id_o, (kk | s4) != 0);
+        tc_commit(&br->xo_full[j]);
+        tc_commit(&br->v_free);
+      }
+      __syncwarp();
+      if (!mbar_wait(&br->v_free, n & 1, err, KERR_ATTN)) return false;  // V area free
+      if (ch + 1 < nch) load_v(ch + 1);
+    }
+    st.xc = n0 + nch;
+    ++st.xu;
+  }
+  if (leader()) st_shared = st;
+  __syncwarp();
+  return true;
+}
+
+// Epilogue side of the whole-unit cross-attention: the warp of TMEM lane quadrant 0 (query row =
+// lane) alone; `xu` / `xc` count this CTA's units / chunks over the launch.
+__device__ __forceinline__ void epi_cross_whole(const Params& p, const Ctx& c, uint32_t& xu, uint32_t& xc) {
+  Bars* const br = c.bars;
+  const uint32_t tmem = c.tmem;
+  uint8_t* const work = c.work;
+  int* const err = p.err;
+  const int T = p.T, lane = threadIdx.x & 31;
+  for (int u = 0; u < c.acnt; ++u) {
+    const AttnUnit au = c.au[u];
+    const int b = au.b, h = au.hp;
+    const int len = p.ctx_len[b], nch = (len + KC - 1) / KC;
+    {  // Q: the previous unit's S products have all been waited for below
+      float q[96];
+      cross_q_row(p, b, h, lane, q);
+      store_row_sw128(work + kWQOff, lane, kWRowAtom, q);
+    }
+    fence_proxy_async_shared();
+    mbar_arrive(&br->xq_full);
+    float acc[96];
+#pragma unroll
+    for (int k = 0; k < 96; ++k) acc[k] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, m_acc = -INFINITY, m_last = -INFINITY;
+    // O of chunk n (computed against running max m_n) folded into acc
+    auto fold = [&](uint32_t n, float m_n) -> bool {
+      const uint32_t j = n & 1;
+      if (!mbar_wait(&br->xo_full[j], (n >> 1) & 1, err, KERR_ATTN)) return false;
+      tc_fence_after();
+      const float alpha = fast_exp2(m_acc - m_n);
+#pragma unroll
+      for (int cc = 0; cc < HD; cc += 32) {
+        float o[32];
+        tmem_ld16(tmem + 256 + j * 128 + cc, o);
+        tmem_ld16(tmem + 256 + j * 128 + cc + 16, o + 16);
+        tc_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 32; ++k) acc[cc + k] = fmaf(acc[cc + k], alpha, o[k]);
+      }
+      m_acc = m_n;
+      tc_fence_before();
+      mbar_arrive(&br->xo_free[j]);
+      return true;
+    };
+    for (int ch = 0; ch < nch; ++ch) {
+      const uint32_t n = xc + ch, j = n & 1;
+      const int nvalid = min(KC, len - ch * KC);
+      if (!mbar_wait(&br->xs_full[j], (n >> 1) & 1, err, KERR_ATTN)) return;
+      tc_fence_after();
+      const uint32_t scol = tmem + j * 128;
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+      for (int cc = 0; cc < KC; cc += 32) {
+        float v[32];
+        tmem_ld16(scol + cc, v);
+        tmem_ld16(scol + cc + 16, v + 16);
+        tc_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (cc + k < nvalid) m4[k & 3] = fmaxf(m4[k & 3], v[k]);
+      }
+      const float m_new = fmaxf(m_run, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * kXScale2);
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint8_t* prow = work + kWPOff + j * 2 * kWRowAtom + (lane >> 3) * 1024 + (lane & 7) * 128;
+#pragma unroll 1
+      for (int cc = 0; cc < KC; cc += 32) {
+        float v[32];
+        tmem_ld16(scol + cc, v);
+        tmem_ld16(scol + cc + 16, v + 16);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          const float p0 = cc + k < nvalid ? fast_exp2(fmaf(v[k], kXScale2, -m_new)) : 0.f;
+          const float p1 = cc + k + 1 < nvalid ? fast_exp2(fmaf(v[k + 1], kXScale2, -m_new)) : 0.f;
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+          s4[(k >> 1) & 3] += __low2float(b2) + __high2float(b2);
+          pk[k >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        uint8_t* base = prow + (cc >> 6) * kWRowAtom;
+        const int ch0 = (cc & 63) >> 3;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(base + (((ch0 + q) ^ (lane & 7)) << 4)) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+      }
+      tc_fence_before();
+      mbar_arrive(&br->xs_free[j]);
+      l_run = fmaf(l_run, fast_exp2(m_run - m_new), (s4[0] + s4[1]) + (s4[2] + s4[3]));
+      m_run = m_new;
+      fence_proxy_async_shared();
+      mbar_arrive(&br->xp_full[j]);
+      if (ch > 0 && !fold(n - 1, m_last)) return;
+      m_last = m_new;
+    }
+    if (!fold(xc + nch - 1, m_last)) return;
+    xc += nch;
+    ++xu;
+    if (lane < T) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(p.cattn + (size_t)(b * T + lane) * D + h * HD);
+#pragma unroll
+      for (int k = 0; k < 96; k += 8) {
+        uint32_t w4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[k + 2 * q] * inv, acc[k + 2 * q + 1] * inv);
+          w4[q] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        dst[k / 8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+    }
+  }
 }
 
 // Merge of the context chunks per (token, head): out = sum_c w_c O_c / sum_c w_c,
@@ -841,7 +1049,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
   if (threadIdx.x == 0) {
     s_plan = p.plans[blockIdx.x];
     g_trp = nullptr;
-    s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = 0;
+    s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = s_st.xu = s_st.xc = 0;
     s_st.last_q = -1;
     s_st.k_pre = 0;
   }
@@ -874,6 +1082,11 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     // tcgen05 cross-attention: Q built / K / S / S done / V / P written / O, once per unit
     mbar_init(&bars.q_full, 128); mbar_init(&bars.k_full, 1); mbar_init(&bars.s_full, 1);
     mbar_init(&bars.kv_free, 1); mbar_init(&bars.v_full, 1); mbar_init(&bars.p_full, 128); mbar_init(&bars.o_full, 1);
+    mbar_init(&bars.v_free, 1); mbar_init(&bars.xq_full, 32);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.xs_full[i], 1); mbar_init(&bars.xs_free[i], 32); mbar_init(&bars.xp_full[i], 32);
+      mbar_init(&bars.xo_full[i], 1); mbar_init(&bars.xo_free[i], 32);
+    }
     fence_mbar_init();
     for (int i = 0; i < NUM_MAPS; ++i) tma_prefetch_desc(&p.maps[i]);
   }
@@ -894,7 +1107,8 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     const bool is_mma = (warp == 1);
     const bool is_epi = warp >= 2;
     MmaState& st = s_st;
-    uint32_t ecnt = 0, gen = 0, xnu = 0;  // xnu: cross-attention units done (epilogue warps)
+    uint32_t ecnt = 0, gen = 0, xnu = 0;  // xnu: attention units done (epilogue warps)
+    uint32_t xwu = 0, xwc = 0;             // whole-unit cross-attention: units, key chunks (lane quadrant 0)
     ConvState cs{0, 0};  // FP8 conversion state (unused by this bf16 kernel)
     uint64_t t_prev = globaltimer();
     const bool timing = p.stage_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 32;
@@ -949,10 +1163,15 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
               stage_self_attn(p, vsm);
             }
           } else if (s == 5) {
-            if (is_mma) mma_cross(p, c, st, l);
-            if (is_epi) xnu = epi_cross(p, c, xnu);
+            if (p.cross_whole) {
+              if (is_mma) mma_cross_whole(p, c, st, l);
+              if (is_epi && (warp & 3) == 0) epi_cross_whole(p, c, xwu, xwc);
+            } else {
+              if (is_mma) mma_cross(p, c, st, l);
+              if (is_epi) xnu = epi_cross(p, c, xnu);
+            }
           } else if (s == 6) {
-            if (is_epi) stage_merge(p);
+            if (is_epi && !p.cross_whole) stage_merge(p);
           } else if (s == 3 || s == 8 || !last_layer) {  // norm(mca) | norm(mlp) | next block's norm(msa)
             if (is_epi) {
               const float* gate = (s == 3 ? m_self : s == 8 ? m_cross : m_mlp) + 2 * D;

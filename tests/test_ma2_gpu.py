@@ -121,10 +121,13 @@ def test_ma2_self_attention_unit_sizes(require_gpu, monkeypatch, selfq):
     assert torch.equal(out[..., c.adim:], c.noise[..., c.adim:])
 
 
-def test_ma2_ragged_context_lengths(require_gpu):
+@pytest.mark.parametrize("whole", ["0", "1"])
+def test_ma2_ragged_context_lengths(require_gpu, monkeypatch, whole):
     """Contexts of 1, 127, 128, 129 and 493 tokens in one batch: empty-but-one, partial and exact
-    128-key tensor-core chunks of the cross-attention."""
+    128-key tensor-core chunks of the cross-attention, with per-chunk units and a merge ("0") and
+    with whole (observation, head) units and an online softmax over the chunks ("1")."""
     from flashact_b200 import MolmoAct2ActionExpert
+    monkeypatch.setenv("FA_MA2_XWHOLE", whole)
     c = M.make_case(seed=55, L=2, T=30, Lk=493, B=5, num_steps=2)
     lens = [1, 127, 128, 129, 493]
     for b, n in enumerate(lens):
