@@ -150,9 +150,10 @@ __device__ __forceinline__ bool leader() { return (threadIdx.x & 31) == 0; }
 // ------------------------------------------------------------------ CTA context
 struct Bars {
   uint64_t wfull[kMaxRing], wempty[kMaxRing];
-  uint64_t afull[kTmASlots], aempty[kTmASlots];  // TMEM A slot written / read by the MMAs (FP8: 2, token-major: 3)
+  uint64_t afull[kTmASlots], aempty[kTmASlots];  // FP8: TMEM A slot written / read by the MMAs
   uint64_t bfull, bempty;  // activation batch loaded / consumed
   uint64_t sfull[4];       // token-major GEMMs: activation K-chunk landed in staging slot 0..3
+  uint64_t sempty[4];      // token-major GEMMs: the MMAs reading staging slot 0..3 have completed
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_full, k_full, v_full, kv_free, v_free, s_full, p_full, o_full, o_free, drain;
   uint64_t s_free, pv_done;  // whole-unit attention: S read by the softmax warps; P V done (P and V free)
@@ -311,7 +312,7 @@ struct MmaState {
   uint32_t ns, npv;      // whole-unit attention: S tiles computed, P V products issued
   int k_pre;             // the next attention unit's prefix K is already loading (prefetched)
   uint32_t xu, xc;       // MolmoAct2 whole-unit cross-attention: units, key chunks
-  uint32_t qtm;          // token-major GEMMs: activation K-chunks consumed (staging / TMEM A slot phases)
+  uint32_t qtm;          // token-major GEMMs: activation K-chunks consumed (staging slot phases)
 };
 
 // Activation operand of one (unit, token group): atoms [j0, j1) of K x nt token tiles, all
@@ -470,44 +471,42 @@ __device__ __forceinline__ bool mma_gemm(const typename Model::Params& p, const 
 
 // ------------------------------------------------------------------ token-major GEMMs (one 64-token tile)
 // While the bound batch is a single tile of at most 64 tokens, the GEMMs run "token-major": the
-// activation tile is the A operand, held in tensor memory (M = 128 lanes, tokens in lanes 0..63),
-// and the weights are the B operand straight from the ring (N = 64 or 128 weight rows, K-major,
-// 128-byte swizzle). Each weight byte is then read from shared memory once per MMA (2 KB per M128
-// N64 K16 instruction, against 6 KB when the weights are the 128-row A operand and half of them
-// belong to another unit), which keeps the MMAs clear of the ring's TMA writes.
+// activation tile is the A operand (M = 64: the tokens), the weights the B operand straight from
+// the ring (N = 64 or 128 weight rows), both read from shared memory by the MMA (K-major, 128-byte
+// swizzle). Per M64 N64 K16 instruction that is 2 KB of activation and 2 KB of weights.
 //
-// Activation K-chunks of kTmChunkAtoms atoms (256 K) flow: TMA into a staging slot (MMA lane) ->
-// the epilogue warps of TMEM lane quadrants 0 and 1 (one token per thread) copy their row into a
-// TMEM A slot -> MMAs -> the slot is released by an MMA commit. A unit's first chunks go out at
-// once, one per staging slot (four on CTAs without attention units); a staging slot is free again
-// once the fill of its chunk has been signalled (afull), and the MMA lane refills it right after.
-// (Per-thread cp.async staging, which keeps the activation loads out of the TMA queue, was measured
-// slower: 10.3 against 8.8 ms per chunk.)
-// TMEM: one accumulator at columns [0, 128) (N <= 128), three A slots at [128, 512).
-// (kTmChunkAtoms, kTmChunkBytes, kTmACol, kTmASlotCols: fa_engine_types.cuh)
+// Activation K-chunks of kTmChunkAtoms atoms (256 K, 64 rows x 128 bytes per atom) are loaded by
+// TMA into up to four staging slots and read there by the MMAs; an MMA commit releases a slot. A
+// unit's first chunks go out at once, one per slot; a later chunk reuses the slot of the chunk
+// before last once that chunk's MMAs have completed.
+// (Copying each chunk into tensor memory first and reading A from there was measured slower: the
+// epilogue warps' tcgen05.st traffic and the MMAs' tensor-memory reads slowed each other to ~96
+// cycles per M128 N64 K16 MMA and ~2,200 cycles per 32 KB chunk.)
+// M = 64 accumulator layout: row r in TMEM lane 32 (r >> 4) + (r & 15), one column per weight row.
+// TMEM: one accumulator at columns [0, 128) (N <= 128).
+// (kTmChunkAtoms, kTmChunkBytes: fa_engine_types.cuh)
 
-// MMAs of NA consecutive weight atoms of one ring slot against the matching A columns, fully
-// unrolled with compile-time descriptor offsets: the issuing thread then spends a few independent
-// integer adds per MMA. (A rolled loop that recomputes the descriptors per MMA made the single
-// issuing thread latency-bound at 110-260 cycles per MMA, against ~48 for M128 N64 K16.)
-// `first`: this is the unit's first slot (its first MMA overwrites the accumulator).
+// MMAs of NA consecutive weight atoms of one ring slot against the matching activation atoms of a
+// staging slot, fully unrolled with compile-time descriptor offsets and issued by one elected lane
+// of the converged MMA warp. `first`: the unit's first slot (its first MMA overwrites the
+// accumulator).
 template <int NA, uint32_t WST16>
-__device__ __forceinline__ void tm_issue(uint32_t tacc, uint32_t ta, uint64_t db, uint32_t idesc, bool first) {
+__device__ __forceinline__ void tm_issue(uint32_t tacc, uint64_t da, uint64_t db, uint32_t idesc, bool first) {
+  constexpr uint32_t kAst16 = 64 * 128 / 16;  // activation atom stride, 16-byte units
 #pragma unroll
   for (int jj = 0; jj < NA; ++jj)
 #pragma unroll
     for (int s = 0; s < 4; ++s)
-      tc_mma_bf16_ts(tacc, ta + jj * 32 + 8 * s, db + (uint64_t)(jj * WST16 + 2 * s), idesc,
-                     (jj | s) != 0 || !first);
+      tc_mma_bf16_elect(tacc, da + (uint64_t)(jj * kAst16 + 2 * s), db + (uint64_t)(jj * WST16 + 2 * s), idesc,
+                        (jj | s) != 0 || !first);
 }
 
-// The whole role runs on lane 0 of the MMA warp (lanes 1..31 wait at the warp sync after it):
-// no warp-level synchronisation between consecutive MMAs. Ring slots hold 32 KB boxes (wg = 2):
-// one K-chunk of a 64-row unit is one slot of 4 atoms, one K-chunk of a 128-row unit two slots of
-// 2 atoms.
+// The MMA warp of a token-major GEMM stage (all 32 lanes: waits on every lane, TMA issue on lane 0,
+// MMAs and commits on the elected lane). Ring slots hold 32 KB boxes (wg = 2): one K-chunk of a
+// 64-row unit is one slot of 4 atoms, one K-chunk of a 128-row unit two slots of 2 atoms.
 template <class Model>
-__device__ __noinline__ bool mma_gemm_tm_lane(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
-  trace_mark(14);
+__device__ __forceinline__ bool mma_gemm_tm(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
+  FA_ONE(trace_mark(12));  // entry
   MmaState st = st_shared;
   uint8_t* const ring = c.ring;
   Bars* const bars = c.bars;
@@ -515,25 +514,33 @@ __device__ __noinline__ bool mma_gemm_tm_lane(const typename Model::Params& p, c
   const uint32_t tmem = c.tmem;
   const int R = c.ring_slots;
   constexpr uint32_t kSlotBytes = 2 * kAtomBytes;
-  constexpr uint32_t kHalfAtom16 = kAtomBytes / 2 / 16, kFullAtom16 = kAtomBytes / 16;  // atom strides, 16-byte units
+  constexpr uint32_t kHalfAtom16 = kAtomBytes / 2 / 16, kFullAtom16 = kAtomBytes / 16;  // weight atom strides
   uint8_t* const work = c.work;
   const CUtensorMap* const amap = &p.maps[Model::act_map(m)];
   const uint64_t pol = policy_evict_last();
   const uint32_t nst = (uint32_t)c.tm_slots;
   const GemmUnit* const units = c.gu[m];
   const int nunits = c.gcnt[m];
-  const uint64_t ring_desc = sdesc_sw128(ring);
+  const uint64_t ring_desc = sdesc_sw128(ring), work_desc = sdesc_sw128(work);
   uint32_t wslot = st.wit % R, wphase = (st.wit / R) & 1;
-  // next ring slot: wait for it, return its descriptor
   auto take_slot = [&](uint64_t& db) -> bool {
     if (!mbar_wait(&bars->wfull[wslot], wphase, err, KERR_MMA)) return false;
     db = ring_desc + (uint64_t)((wslot * kSlotBytes) >> 4);
     return true;
   };
   auto release_slot = [&]() {
-    tc_commit(&bars->wempty[wslot]);
+    tc_commit_elect(&bars->wempty[wslot]);
     ++st.wit;
     if (++wslot == (uint32_t)R) { wslot = 0; wphase ^= 1; }
+  };
+  // activation chunk q (count over the launch) into staging slot q % nst, once the MMAs of the
+  // chunk that used the slot before have completed
+  auto load_chunk = [&](uint32_t q, int katom) -> bool {
+    const uint32_t sl = q % nst;
+    if (q >= nst && !mbar_wait(&bars->sempty[sl], ((q / nst) - 1) & 1, err, KERR_MMA)) return false;
+    FA_ONE(mbar_expect_tx(&bars->sfull[sl], kTmChunkBytes));
+    FA_ONE(tma_load_3d(work + sl * kTmChunkBytes, amap, &bars->sfull[sl], 0, 0, katom, pol));
+    return true;
   };
 #pragma unroll 1
   for (int u = 0; u < nunits; ++u) {
@@ -541,124 +548,74 @@ __device__ __noinline__ bool mma_gemm_tm_lane(const typename Model::Params& p, c
     const int nch = gu.natoms / kTmChunkAtoms;
     const uint32_t q0 = st.qtm;
 #pragma unroll 1
-    for (int ch = 0; ch < (int)nst && ch < nch; ++ch) {  // the unit's first K-chunks, one per staging slot
-      const int sl = (int)((q0 + ch) % nst);
-      uint64_t* b = &bars->sfull[sl];
-      mbar_expect_tx(b, kTmChunkBytes);
-      tma_load_3d(work + sl * kTmChunkBytes, amap, b, 0, 0, gu.katom0 + ch * kTmChunkAtoms, pol);
-    }
+    for (int ch = 0; ch < (int)nst && ch < nch; ++ch)
+      if (!load_chunk(q0 + ch, gu.katom0 + ch * kTmChunkAtoms)) return false;
     // one accumulator: the previous unit's must have been drained
     if (st.acc >= 1 && !mbar_wait(&bars->acc_empty[0], (st.acc - 1) & 1, err, KERR_MMA)) return false;
-    const uint32_t tacc = tmem;
 #pragma unroll 1
     for (int ch = 0; ch < nch; ++ch) {
-      const uint32_t q = q0 + ch;
-      const uint32_t qa = q % kTmASlots;
-      if (!mbar_wait(&bars->afull[qa], (q / kTmASlots) & 1, err, KERR_MMA)) return false;
+      const uint32_t q = q0 + ch, sl = q % nst;
+      if (!mbar_wait(&bars->sfull[sl], (q / nst) & 1, err, KERR_MMA)) return false;
       tc_fence_after();
-      if (u == 0) trace_mark(ch == 0 ? 9 : ch == 1 ? 10 : 11);
-      if (ch + (int)nst < nch) {  // the fill has read this chunk's staging slot: refill it
-        const int sl = (int)(q % nst);
-        uint64_t* b = &bars->sfull[sl];
-        mbar_expect_tx(b, kTmChunkBytes);
-        tma_load_3d(work + sl * kTmChunkBytes, amap, b, 0, 0, gu.katom0 + (ch + nst) * kTmChunkAtoms, pol);
-      }
-      const uint32_t ta = tmem + kTmACol + qa * kTmASlotCols;
+      if (u == 0 && ch < 4) FA_ONE(trace_mark(1 + ch));  // chunk ch landed
+      const uint64_t da = work_desc + (uint64_t)((sl * kTmChunkBytes) >> 4);
       uint64_t db;
-      if (gu.half) {  // N = 64: 64-row atoms of 8 KB, one slot per chunk
+      if (gu.half) {  // N = 64: 64-row weight atoms of 8 KB, one ring slot per chunk
         if (!take_slot(db)) return false;
-        if (u == 0) trace_mark(ch == 0 ? 1 : ch == 1 ? 4 : 13);
-        tm_issue<4, kHalfAtom16>(tacc, ta, db, idesc_bf16(128, 64), ch == 0);
+        if (u == 0 && ch < 4) FA_ONE(trace_mark(8 + ch));  // its weight slot ready
+        tm_issue<4, kHalfAtom16>(tmem, da, db, idesc_bf16(64, 64), ch == 0);
         release_slot();
-      } else {  // N = 128: 128-row atoms of 16 KB, two slots per chunk
+      } else {  // N = 128: 128-row weight atoms of 16 KB, two ring slots per chunk
         if (!take_slot(db)) return false;
-        tm_issue<2, kFullAtom16>(tacc, ta, db, idesc_bf16(128, 128), ch == 0);
+        tm_issue<2, kFullAtom16>(tmem, da, db, idesc_bf16(64, 128), ch == 0);
         release_slot();
         if (!take_slot(db)) return false;
-        tm_issue<2, kFullAtom16>(tacc, ta + 64, db, idesc_bf16(128, 128), false);
+        tm_issue<2, kFullAtom16>(tmem, da + (uint64_t)(2 * 64 * 128 / 16), db, idesc_bf16(64, 128), false);
         release_slot();
       }
-      tc_commit(&bars->aempty[qa]);
-      if (u == 0) trace_mark(ch == 0 ? 15 : ch == 1 ? 6 : ch == 2 ? 3 : 8);
+      tc_commit_elect(&bars->sempty[sl]);
+      if (u == 0 && ch < 3) FA_ONE(trace_mark(13 + ch));  // its MMAs issued
+      // the chunk before this one is done with its slot soon: refill it while these MMAs run
+      if (ch >= 1 && ch - 1 + (int)nst < nch && !load_chunk(q - 1 + nst, gu.katom0 + (ch - 1 + nst) * kTmChunkAtoms))
+        return false;
     }
     st.qtm = q0 + nch;
-    tc_commit(&bars->acc_full[0]);
+    tc_commit_elect(&bars->acc_full[0]);
     ++st.acc;
   }
-  st_shared = st;
+  if (leader()) st_shared = st;
+  __syncwarp();
   return true;
 }
 
+// Epilogue warps of a token-major GEMM stage: per unit, drain the accumulator through
+// Model::epi_tm (thread = token: lanes 0..15 of each warp hold the 16 rows of its lane quadrant;
+// 32 weight-row columns at a time).
 template <class Model>
-__device__ __forceinline__ bool mma_gemm_tm(const typename Model::Params& p, const Ctx& c, MmaState& st_shared, int m) {
-  bool ok = true;
-  if (leader()) ok = mma_gemm_tm_lane<Model>(p, c, st_shared, m);
-  __syncwarp();
-  return __shfl_sync(0xffffffffu, ok, 0);
-}
-
-// Epilogue warps of a token-major GEMM stage: per unit, fill its K-chunks into the TMEM A slots
-// (threads of lane quadrants 0 and 1: thread = token; rows read from the 128-byte-swizzled staging
-// tile, 16-byte chunk c of row r at r * 128 + ((c ^ (r & 7)) << 4)), then drain the accumulator
-// (token row, 32 weight-row columns at a time) through Model::epi_tm. Quadrants 2 and 3 (lanes of
-// padding rows) only take part in the accumulator hand-back.
-template <class Model>
-__device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m,
-                                                uint32_t& qtm) {
+__device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
-  const bool active = qd < 2;
-  const int tok = qd * 32 + lane;
+  const bool active = lane < 16;
+  const int tok = qd * 16 + lane;
   int* const err = p.err;
   Bars* const bars = c.bars;
-  uint8_t* const stage_base = c.work;
-  const int sw = tok & 7;  // 128-byte swizzle of this thread's staging rows (conflict-free)
   const uint32_t tl = c.tmem + ((uint32_t)(qd * 32) << 16);
   const GemmUnit* const units = c.gu[m];
   const int nunits = c.gcnt[m];
-  const uint32_t nst = (uint32_t)c.tm_slots;
   typename Model::Epi e;
   Model::epi_load(e, p, c, 0);
 #pragma unroll 1
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];
-    const int nch = gu.natoms / kTmChunkAtoms;
-    if (active) {
-#pragma unroll 1
-      for (int ch = 0; ch < nch; ++ch) {
-        const uint32_t q = qtm + ch;
-        if (!mbar_wait(&bars->sfull[q % nst], (q / nst) & 1, err, KERR_EPI)) return ecnt;
-        const uint32_t qa = q % kTmASlots;
-        if (q >= kTmASlots && !mbar_wait(&bars->aempty[qa], ((q / kTmASlots) - 1) & 1, err, KERR_EPI)) return ecnt;
-        tc_fence_after();
-        const uint8_t* row = stage_base + (q % nst) * kTmChunkBytes + tok * 128;
-#pragma unroll 1
-        for (int at = 0; at < kTmChunkAtoms; ++at) {
-          uint32_t w[32];
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            const uint4 v = *reinterpret_cast<const uint4*>(row + at * (64 * 128) + ((cc ^ sw) << 4));
-            w[4 * cc] = v.x; w[4 * cc + 1] = v.y; w[4 * cc + 2] = v.z; w[4 * cc + 3] = v.w;
-          }
-          tmem_st32(tl + kTmACol + qa * kTmASlotCols + at * 32, w);
-        }
-        tc_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bars->afull[qa]);
-      }
-    }
-    qtm += nch;
     if (!mbar_wait(&bars->acc_full[0], ecnt & 1, err, KERR_EPI)) return ecnt;
     tc_fence_after();
-    if (active) {
-      const int ncols = gu.half ? 64 : 128;
+    const int ncols = gu.half ? 64 : 128;
 #pragma unroll 1
-      for (int c0 = 0; c0 < ncols; c0 += 32) {
-        float v[32];
-        tmem_ld16(tl + c0, v);
-        tmem_ld16(tl + c0 + 16, v + 16);
-        tc_wait_ld();
-        Model::epi_tm(e, gu, m, tok, c0, v);
-      }
+    for (int c0 = 0; c0 < ncols; c0 += 32) {
+      float v[32];
+      tmem_ld16(tl + c0, v);
+      tmem_ld16(tl + c0 + 16, v + 16);
+      tc_wait_ld();
+      if (active) Model::epi_tm(e, gu, m, tok, c0, v);
     }
     tc_fence_before();
     mbar_arrive(&bars->acc_empty[0]);

@@ -25,16 +25,14 @@ constexpr int kAColF8 = 256;               // first TMEM column of the A slots
 constexpr int kASlotsF8 = 2;
 constexpr int kASlotColsF8 = 128;          // 256 K-values of bf16 (2 per 32-bit column)
 // Token-major GEMMs (one tile of <= 64 tokens): activation K-chunks of 4 atoms (256 K) staged in up
-// to four 32 KB slots and copied into three TMEM A slots of 128 columns at [kTmACol, 512); one
-// accumulator of <= 128 columns at [0, 128).
+// to four 32 KB slots, read there by the MMAs; one accumulator of <= 128 columns at [0, 128).
 constexpr int kTmChunkAtoms = 4;
 constexpr uint32_t kTmChunkBytes = 64 * 128 * kTmChunkAtoms;
-constexpr uint32_t kTmACol = 128, kTmASlotCols = 128;
-constexpr uint32_t kTmASlots = 3;
+constexpr uint32_t kTmASlots = 3;  // A-slot barriers (FP8 expansion uses 2)
 constexpr int kMaxBBytes = 128 * 1024;     // activation (B operand) area of a GEMM CTA, upper bound
 constexpr int kMaxBAtoms = 16;             // activation atoms resident at once
 constexpr int kMaxGU = 48;                 // GEMM units per CTA per layer (all matrices)
-constexpr int kMaxAU = 64;                 // attention units per CTA per layer
+constexpr int kMaxAU = 48;                 // attention units per CTA per layer
 constexpr int kMaxMats = 6;                // GEMM matrices per layer
 constexpr int kStageBytes = 16 * 1024;     // epilogue staging area
 constexpr int kMaxStages = 16;             // traced stage kinds

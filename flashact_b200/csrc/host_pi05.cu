@@ -636,8 +636,8 @@ static fa_status build_plan(fa_handle* h) {
   }
   if (h->tm)
     for (int i = 0; i < nblk; ++i)
-      if (plans[i].b_bytes < 2 * (int)kTmChunkBytes)
-        return fail(h, FA_ERR_INVALID, "plan error: CTA %d has room for fewer than two activation chunks", i);
+      if (plans[i].b_bytes < 2 * (int)kTmChunkBytes || plans[i].ring_slots < 2)  // a 128-row chunk takes 2 ring slots
+        return fail(h, FA_ERR_INVALID, "plan error: CTA %d has room for fewer than two activation chunks or ring slots", i);
   if (gu.size() > h->n_gunits_cap) {
     if (h->d_gunits) cudaFree(h->d_gunits);
     FA_CUDA(h, cudaMalloc(&h->d_gunits, gu.size() * sizeof(GemmUnit)));

@@ -197,83 +197,67 @@ __device__ __forceinline__ void stage_merge(const Params& p) {
   const int e = threadIdx.x - 64, lane = e & 31, wq = e >> 5;
   const int total = p_NT * H;
   constexpr int kFirst = 12;  // chunks per item loaded up front (prefixes up to 1408 keys)
-  // Two items per warp per pass: both items' loads (the first kFirst partial rows and the
-  // (max, sum) pairs) are in flight together, one round trip for the pair; at large batch a warp
-  // merges tens of items one after another.
-  const int stride = gridDim.x * 4;
+  // One item per warp per pass, its first kFirst partial rows and the (max, sum) pairs in flight
+  // together (one round trip). The code is kept small on purpose: every layer runs this stage,
+  // and instruction fetches that miss the SM's instruction cache cost an L2 round trip each.
 #pragma unroll 1
-  for (int item0 = blockIdx.x * 4 + wq; item0 < total; item0 += 2 * stride) {
-    int nc[2], npc[2], r[2], n_[2], h_[2];
-    size_t base[2];
-    uint4 raw[2][kFirst];
-    float2 ml[2];
+  for (int item = blockIdx.x * 4 + wq; item < total; item += gridDim.x * 4) {
+    const int n = item / H, h = item % H;
+    const int b = tok_bi(p_invT, n), t = n - b * p_T, hp = h >> 1;
+    const int r = (h & 1) * TPAD + t;
+    const int npc = p_nchunks[b], nc = npc + 1;  // prefix chunks + the action-token chunk (stored at MAX_CH)
+    const size_t base = (size_t)(b * 4 + hp) * (MAX_CH + 1);
+    auto row = [&](int c) {
+      const int cc = c < npc ? c : MAX_CH;
+      return reinterpret_cast<const uint4*>(p_opart + ((base + cc) * 128 + r) * HD + lane * 8);
+    };
+    uint4 raw[kFirst];
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      const int item = item0 + s * stride;
-      const bool live = item < total;
-      const int n = live ? item / H : 0, h = live ? item % H : 0;
-      const int b = tok_bi(p_invT, n), t = n - b * p_T, hp = h >> 1;
-      n_[s] = n; h_[s] = h;
-      r[s] = (h & 1) * TPAD + t;
-      npc[s] = p_nchunks[b];
-      nc[s] = live ? npc[s] + 1 : 0;  // prefix chunks + the action-token chunk (stored at MAX_CH)
-      base[s] = (size_t)(b * 4 + hp) * (MAX_CH + 1);
+    for (int j = 0; j < kFirst; ++j)
+      if (j < nc) raw[j] = __ldcg(row(j));
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (lane < nc) {
+      const int cc = lane < npc ? lane : MAX_CH;
+      ml = __ldcg(reinterpret_cast<const float2*>(p_oml + ((base + cc) * 128 + r) * 2));
+    }
+    const float M = warp_max(ml.x);
+    const float wgt_own = (lane < nc && ml.y > 0.f) ? exp2f(ml.x - M) * ml.y : 0.f;
+    const float wsum = warp_sum(wgt_own);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    auto accumulate = [&](const uint4& q, float wgt) {
+      const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int j = 0; j < kFirst; ++j) {
-        const int cc = j < npc[s] ? j : MAX_CH;
-        if (j < nc[s])
-          raw[s][j] = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base[s] + cc) * 128 + r[s]) * HD + lane * 8));
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
+        acc[2 * k] = fmaf(wgt, f.x, acc[2 * k]);
+        acc[2 * k + 1] = fmaf(wgt, f.y, acc[2 * k + 1]);
       }
-      ml[s] = make_float2(-INFINITY, 0.f);
-      if (lane < nc[s]) {
-        const int cc = lane < npc[s] ? lane : MAX_CH;
-        ml[s] = __ldcg(reinterpret_cast<const float2*>(p_oml + ((base[s] + cc) * 128 + r[s]) * 2));
+    };
+#pragma unroll
+    for (int j = 0; j < kFirst; ++j) {
+      const float wgt = __shfl_sync(0xffffffffu, wgt_own, j);
+      if (j < nc) accumulate(raw[j], wgt);
+    }
+#pragma unroll 1
+    for (int c0 = kFirst; c0 < nc; c0 += 4) {  // longer prefixes: 4 more rows per round trip
+      uint4 more[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (c0 + j < nc) more[j] = __ldcg(row(c0 + j));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float wgt = __shfl_sync(0xffffffffu, wgt_own, (c0 + j) & 31);
+        if (c0 + j < nc) accumulate(more[j], wgt);
       }
     }
+    const float inv = 1.f / wsum;
+    uint32_t o4[4];
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      if (nc[s] == 0) continue;
-      const float M = warp_max(ml[s].x);
-      const float wgt_own = (lane < nc[s] && ml[s].y > 0.f) ? exp2f(ml[s].x - M) * ml[s].y : 0.f;
-      const float wsum = warp_sum(wgt_own);
-      float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-      auto accumulate = [&](const uint4& q, float wgt) {
-        const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
-        const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
-        const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.z));
-        const float2 f3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.w));
-        acc0.x += wgt * f0.x; acc0.y += wgt * f0.y; acc0.z += wgt * f1.x; acc0.w += wgt * f1.y;
-        acc1.x += wgt * f2.x; acc1.y += wgt * f2.y; acc1.z += wgt * f3.x; acc1.w += wgt * f3.y;
-      };
-#pragma unroll
-      for (int j = 0; j < kFirst; ++j) {
-        const float wgt = __shfl_sync(0xffffffffu, wgt_own, j);
-        if (j < nc[s]) accumulate(raw[s][j], wgt);
-      }
-#pragma unroll 1
-      for (int c0 = kFirst; c0 < nc[s]; c0 += 8) {  // longer prefixes: 8 more rows per round trip
-        uint4 more[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int c = c0 + j, cc = c < npc[s] ? c : MAX_CH;
-          if (c < nc[s])
-            more[j] = __ldcg(reinterpret_cast<const uint4*>(p_opart + ((base[s] + cc) * 128 + r[s]) * HD + lane * 8));
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float wgt = __shfl_sync(0xffffffffu, wgt_own, (c0 + j) & 31);
-          if (c0 + j < nc[s]) accumulate(more[j], wgt);
-        }
-      }
-      const float inv = 1.f / wsum;
-      __nv_bfloat162 b0 = __floats2bfloat162_rn(acc0.x * inv, acc0.y * inv);
-      __nv_bfloat162 b1 = __floats2bfloat162_rn(acc0.z * inv, acc0.w * inv);
-      __nv_bfloat162 b2 = __floats2bfloat162_rn(acc1.x * inv, acc1.y * inv);
-      __nv_bfloat162 b3 = __floats2bfloat162_rn(acc1.z * inv, acc1.w * inv);
-      *reinterpret_cast<uint4*>(p_attn + (size_t)n_[s] * QD + h_[s] * HD + lane * 8) =
-          make_uint4(*reinterpret_cast<uint32_t*>(&b0), *reinterpret_cast<uint32_t*>(&b1),
-                     *reinterpret_cast<uint32_t*>(&b2), *reinterpret_cast<uint32_t*>(&b3));
+    for (int k = 0; k < 4; ++k) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[2 * k] * inv, acc[2 * k + 1] * inv);
+      o4[k] = *reinterpret_cast<uint32_t*>(&b2);
     }
+    *reinterpret_cast<uint4*>(p_attn + (size_t)n * QD + h * HD + lane * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
   }
 }
 
@@ -610,11 +594,11 @@ __device__ __forceinline__ bool mma_attn(const Params& p, const Ctx& c, MmaState
   return true;
 }
 
-// Softmax of one 128-query-row tile over NK keys, all in one TMEM round trip: thread r owns
+// Softmax of one 128-query-row tile over NK keys (one code copy for every NK: each layer runs it,
+// and instruction-cache space is a first-order cost), all in one TMEM round trip: thread r owns
 // row r (its NK scores in registers), writes the bf16 probabilities as the A operand of O = P V
 // (128-byte-swizzled K-major atoms of 64 keys) and returns (max in log2 units, sum).
-template <int NK>
-__device__ __forceinline__ float2 softmax_row(uint32_t taddr, int nvalid, uint8_t* prow, int r) {
+__device__ __forceinline__ float2 softmax_row(uint32_t taddr, int NK, int nvalid, uint8_t* prow, int r) {
   constexpr float sl2 = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2 units
   float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
@@ -680,8 +664,7 @@ __device__ __forceinline__ uint32_t epi_attn(const Params& p, const Ctx& c, uint
     tc_fence_after();
     if (u == 0 && threadIdx.x == 64) trace_mark(kTrEpiAcc0);  // S in TMEM
     uint8_t* prow = work + kPOff + (r >> 3) * 1024 + (r & 7) * 128;
-    const float2 ms = au.is_suffix ? softmax_row<TPAD>(tmem + lane_addr, nvalid, prow, r)
-                                   : softmax_row<KCH>(tmem + lane_addr, nvalid, prow, r);
+    const float2 ms = softmax_row(tmem + lane_addr, au.is_suffix ? TPAD : KCH, nvalid, prow, r);
     fence_proxy_async_shared();
     tc_fence_before();
     mbar_arrive(&br->p_full);
@@ -1015,9 +998,9 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     // E4M3 slots are released by the 128 epilogue threads that convert them, bf16 slots by an
     // MMA commit; TMEM A slots are filled by those threads and released by an MMA commit
     for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], Model::kF8 ? 128 : 1); }
-    // A slots: filled by the 128 converting threads (FP8) or by the 64 token threads (token-major)
-    for (int i = 0; i < (int)kTmASlots; ++i) { mbar_init(&bars.afull[i], Model::kTM ? 64 : 128); mbar_init(&bars.aempty[i], 1); }
-    for (int i = 0; i < 4; ++i) mbar_init(&bars.sfull[i], 1);
+    // A slots: filled by the 128 converting threads (FP8)
+    for (int i = 0; i < (int)kTmASlots; ++i) { mbar_init(&bars.afull[i], 128); mbar_init(&bars.aempty[i], 1); }
+    for (int i = 0; i < 4; ++i) { mbar_init(&bars.sfull[i], 1); mbar_init(&bars.sempty[i], 1); }
     mbar_init(&bars.bfull, 1);
     mbar_init(&bars.bempty, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&bars.acc_full[i], 1); mbar_init(&bars.acc_empty[i], 128); }
@@ -1046,7 +1029,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
     const bool is_mma = (warp == 1);
     const bool is_epi = warp >= 2;
     MmaState& st = s_st;
-    uint32_t ecnt = 0, anu = 0, gen = 0, qtm = 0;
+    uint32_t ecnt = 0, anu = 0, gen = 0;
     AttnEpiState aes{0, 0, 0};  // whole-unit attention (epilogue warps)
     ConvState cs{0, 0};  // FP8 kernel: E4M3 slots converted (epilogue warps)
     uint64_t t_prev = globaltimer();
@@ -1103,7 +1086,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
           if (m >= 0) {
             if constexpr (Model::kTM) {
               if (is_mma) mma_gemm_tm<Model>(p, c, st, m);
-              if (is_epi) ecnt = epi_gemm_tm<Model>(p, c, ecnt, m, qtm);
+              if (is_epi) ecnt = epi_gemm_tm<Model>(p, c, ecnt, m);
             } else {
               if (is_mma) mma_gemm<Model>(p, c, st, m);
               if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l, cs);
