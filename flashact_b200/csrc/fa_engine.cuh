@@ -592,7 +592,8 @@ __device__ __forceinline__ bool mma_gemm_tm(const typename Model::Params& p, con
 // Model::epi_tm (thread = token: lanes 0..15 of each warp hold the 16 rows of its lane quadrant;
 // 32 weight-row columns at a time).
 template <class Model>
-__device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m) {
+__device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p, const Ctx& c, uint32_t ecnt, int m,
+                                                int l) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3;
   const bool active = lane < 16;
   const int tok = qd * 16 + lane;
@@ -602,7 +603,7 @@ __device__ __forceinline__ uint32_t epi_gemm_tm(const typename Model::Params& p,
   const GemmUnit* const units = c.gu[m];
   const int nunits = c.gcnt[m];
   typename Model::Epi e;
-  Model::epi_load(e, p, c, 0);
+  Model::epi_load(e, p, c, l);
 #pragma unroll 1
   for (int u = 0; u < nunits; ++u) {
     const GemmUnit gu = units[u];

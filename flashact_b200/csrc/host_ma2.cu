@@ -6,6 +6,7 @@
 namespace fa {
 namespace ma2 {
 __global__ void ma2_denoise_kernel(const __grid_constant__ Params p);
+__global__ void ma2_denoise_kernel_tm(const __grid_constant__ Params p);
 }
 }  // namespace fa
 
@@ -29,6 +30,7 @@ struct Ma2State {
   int B = 0, NT = 0, NPAD = 0, NTILE = 64, TG = 4, ngroups = 1, LKPAD = 0, adim = 0;
   int self_q = 8;
   bool cross_whole = false;
+  bool tm = false;  // token-major GEMMs (bound batch = one tile of <= 64 tokens)
   int wg = 4;  // weight atoms per ring slot
   int ba = 4;  // activation atoms per TMA box
   int split[M::NUM_MATS] = {1, 3, 3, 3, 1, 6};
@@ -145,12 +147,13 @@ fa_status ma2_create(const fa_config& c, int device, fa_handle* h) {
     }
   FA_CUDA(h, cudaMemcpy(s->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
   FA_CUDA(h, cudaMemcpy(s->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
-  if (cudaFuncSetAttribute(M::ma2_denoise_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmemDyn) != cudaSuccess)
-    return fail(h, FA_ERR_CUDA, "cannot reserve %d bytes of shared memory", fa::kSmemDyn);
-  int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, M::ma2_denoise_kernel, fa::kThreads, fa::kSmemDyn) != cudaSuccess ||
-      occ < 1)
-    return fail(h, FA_ERR_UNSUPPORTED, "megakernel does not fit on an SM (occupancy %d)", occ);
+  for (const void* k : {(const void*)M::ma2_denoise_kernel, (const void*)M::ma2_denoise_kernel_tm}) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmemDyn) != cudaSuccess)
+      return fail(h, FA_ERR_CUDA, "cannot reserve %d bytes of shared memory", fa::kSmemDyn);
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, fa::kThreads, fa::kSmemDyn) != cudaSuccess || occ < 1)
+      return fail(h, FA_ERR_UNSUPPORTED, "megakernel does not fit on an SM (occupancy %d)", occ);
+  }
   return FA_OK;
 }
 
@@ -316,6 +319,18 @@ static fa_status ma2_plan(fa_handle* h) {
   s->ba = s->NTILE == 64 ? 4 : 2;
   for (int m = 0; m < M::NUM_MATS; ++m)
     while ((kMatK[m] / 64 / s->split_eff[m]) % s->ba != 0) s->ba >>= 1;
+  // Token-major GEMMs (opt-in, FA_MA2_TM=1) while the bound batch is one tile of <= 64 tokens and
+  // every unit's K range is whole 256-K chunks: activation chunks in three 32 KB staging slots,
+  // 32 KB weight slots. Measured on B200 at C3 (bs=1): 33.5 ms per chunk against 29.3 ms for the
+  // weight-major GEMMs (gate/up 1.73 -> 1.56 ms, but the single-chunk self-out / cross-q /
+  // cross-out units and the down projection slower), so it is not the default here.
+  {
+    const char* e = getenv("FA_MA2_TM");
+    bool tm = e && atoi(e) != 0 && s->NTILE == 64 && s->ngroups == 1;
+    for (int m = 0; m < M::NUM_MATS; ++m) tm = tm && (kMatK[m] / 64 / s->split_eff[m]) % fa::kTmChunkAtoms == 0;
+    s->tm = tm;
+    if (tm) { s->wg = 2; s->ba = fa::kTmChunkAtoms; }
+  }
   for (int oi = 0; oi < M::NUM_MATS; ++oi) {
     const int m = order[oi];
     const int mtiles = kMatRows[m] / 128, katoms = kMatK[m] / 64, split = s->split_eff[m], per_split = katoms / split;
@@ -347,10 +362,12 @@ static fa_status ma2_plan(fa_handle* h) {
     bb = std::min(bb, std::min(fa::kMaxBBytes, fa::kMaxBAtoms * tile));
     bb = std::max(bb, tile * ntg * std::max(s->ba, s->wg));  // one activation box and weight slot per token tile
     if (plans[i].a_cnt > 0) bb = std::max(tile, std::min(bb, 64 * 1024));
+    if (s->tm) bb = 3 * (int)fa::kTmChunkBytes;  // K = 768: three chunks per unit at most load at once
     plans[i].b_bytes = bb;
     const int work = std::max(bb, M::kMinWork) + fa::kStageBytes;
     plans[i].ring_slots = std::min(fa::kMaxRing, (fa::kSmemUse - work) / (s->wg * fa::kAtomBytes));
-    if (plans[i].ring_slots < 1) return fail(h, FA_ERR_INVALID, "shared-memory plan leaves no weight ring");
+    if (plans[i].ring_slots < (s->tm ? 2 : 1))  // a token-major chunk of a 128-row unit takes 2 ring slots
+      return fail(h, FA_ERR_INVALID, "shared-memory plan leaves no weight ring");
     for (int m = 0; m < M::NUM_MATS; ++m) {
       plans[i].g_off[m] = (int)gu.size();
       plans[i].g_cnt[m] = (int)per[(size_t)i * M::NUM_MATS + m].size();
@@ -495,7 +512,8 @@ fa_status ma2_sample(fa_handle* h, int batch, const float* noise, float* out, cu
   if (h->timing) FA_CUDA(h, cudaMemsetAsync(h->stage_ns, 0, fa::kMaxStages * sizeof(unsigned long long), stream));
   FA_CUDA(h, cudaMemcpyAsync(s->x_t, noise, bytes, cudaMemcpyDefault, stream));
   void* args[] = {&p};
-  FA_CUDA(h, cudaLaunchCooperativeKernel((const void*)M::ma2_denoise_kernel, dim3(h->num_sms), dim3(fa::kThreads), args,
+  FA_CUDA(h, cudaLaunchCooperativeKernel(s->tm ? (const void*)M::ma2_denoise_kernel_tm : (const void*)M::ma2_denoise_kernel,
+                                         dim3(h->num_sms), dim3(fa::kThreads), args,
                                          fa::kSmemDyn, stream));
   FA_CUDA(h, cudaMemcpyAsync(out, s->x_t, bytes, cudaMemcpyDefault, stream));
   h->last_launches = 1;

@@ -963,6 +963,7 @@ struct Ma2Model {
   using Epi = Ma2Epi;
   static constexpr int kMats = NUM_MATS;  // QKV, self-out, cross-q, cross-out, gate/up, down
   static constexpr bool kF8 = false;       // bf16 weight stream only
+  static constexpr bool kTM = false;       // token-major GEMMs (one tile of <= 64 tokens)
   __device__ static float row_scale(const Params&, int, int, int, int) { return 1.0f; }
   __device__ static int rows(int m) { return mat_rows(m); }
   __device__ static int wmap(int m) { return MAP_W_QKV + m; }
@@ -1032,8 +1033,53 @@ struct Ma2Model {
   }
 };
 
+// Token-major traits (bound batch = one tile of <= 64 tokens): thread = token n, v = 32
+// consecutive accumulator columns c0.. = 32 consecutive rows of the unit's 128-row weight tile.
+// In the packed gate/up tile, rows 32 q + i (i < 16) are the gate and rows 32 q + 16 + i the up
+// projection of feature 64 mtile + 16 q + i (the same packing as the weight-major epilogue).
+struct Ma2ModelTM : Ma2Model {
+  static constexpr bool kTM = true;
+  __device__ static void epi_tm(const Epi& e, const GemmUnit& gu, int m, int n, int c0, const float* v) {
+    if (n >= e.NT) return;
+    const int r0 = gu.mtile * 128 + c0;
+    auto pack = [](float lo, float hi) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+      return *reinterpret_cast<uint32_t*>(&b2);
+    };
+    if (m == MAT_QKV) {  // + bias -> bf16 row n of qkv
+      const float* b = e.bias[MAT_QKV] + r0;
+      uint4* d = reinterpret_cast<uint4*>(e.qkv + (size_t)n * QKV_ROWS + r0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        d[k] = make_uint4(pack(v[8 * k] + b[8 * k], v[8 * k + 1] + b[8 * k + 1]), pack(v[8 * k + 2] + b[8 * k + 2], v[8 * k + 3] + b[8 * k + 3]),
+                          pack(v[8 * k + 4] + b[8 * k + 4], v[8 * k + 5] + b[8 * k + 5]), pack(v[8 * k + 6] + b[8 * k + 6], v[8 * k + 7] + b[8 * k + 7]));
+    } else if (m == MAT_GU) {  // silu(gate + b_gate) * (up + b_up) -> bf16 features f0 .. f0 + 15
+      const int f0 = 64 * gu.mtile + 16 * (c0 >> 5);
+      float h[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float g = v[i] + e.bias[MAT_GU][f0 + i], u = v[16 + i] + e.b_up[f0 + i];
+        h[i] = g / (1.f + __expf(-g)) * u;
+      }
+      uint4* d = reinterpret_cast<uint4*>(e.hbuf + (size_t)n * F + f0);
+      d[0] = make_uint4(pack(h[0], h[1]), pack(h[2], h[3]), pack(h[4], h[5]), pack(h[6], h[7]));
+      d[1] = make_uint4(pack(h[8], h[9]), pack(h[10], h[11]), pack(h[12], h[13]), pack(h[14], h[15]));
+    } else {  // fp32 K-split partial, bias carried by split 0
+      const float* b = e.bias[m] + r0;
+      float4* d = reinterpret_cast<float4*>(e.part + ((size_t)gu.split * e.NPAD + n) * D + r0);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float4 o = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        if (gu.split == 0) { o.x += b[4 * k]; o.y += b[4 * k + 1]; o.z += b[4 * k + 2]; o.w += b[4 * k + 3]; }
+        d[k] = o;
+      }
+    }
+  }
+};
+
 // ------------------------------------------------------------------ kernel
-__global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_constant__ Params p) {
+template <class Model>
+__device__ __forceinline__ void ma2_denoise_body(const Params& p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Bars bars;
   __shared__ uint32_t s_tmem;
@@ -1049,7 +1095,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
   if (threadIdx.x == 0) {
     s_plan = p.plans[blockIdx.x];
     g_trp = nullptr;
-    s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = s_st.xu = s_st.xc = 0;
+    s_st.wit = s_st.bload = s_st.bfree = s_st.acc = s_st.nq = s_st.nu = s_st.xu = s_st.xc = s_st.qtm = 0;
     s_st.last_q = -1;
     s_st.k_pre = 0;
   }
@@ -1073,10 +1119,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     c.ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     c.work = c.ring + (size_t)c.ring_slots * p.wg * kAtomBytes;
     c.stage = c.work + max(s_plan.b_bytes, kMinWork);
+    c.tm_slots = min(4, s_plan.b_bytes / (int)kTmChunkBytes);
     c.bars = &bars;
     for (int i = 0; i < kMaxRing; ++i) { mbar_init(&bars.wfull[i], 1); mbar_init(&bars.wempty[i], 1); }
     mbar_init(&bars.bfull, 1);
     mbar_init(&bars.bempty, 1);
+    for (int i = 0; i < 4; ++i) { mbar_init(&bars.sfull[i], 1); mbar_init(&bars.sempty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&bars.acc_full[i], 1); mbar_init(&bars.acc_empty[i], 128); }
     mbar_init(&bars.drain, 1);
     // tcgen05 cross-attention: Q built / K / S / S done / V / P written / O, once per unit
@@ -1101,7 +1149,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
   __syncthreads();
 
   if (warp == 0) {
-    run_producer<Ma2Model>(p, c);
+    run_producer<Model>(p, c);
     __syncwarp();
   } else {
     const bool is_mma = (warp == 1);
@@ -1153,8 +1201,13 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
         for (int s = 0; s < 12; ++s) {
           const int m = gemm_of(s);
           if (m >= 0) {
-            if (is_mma) mma_gemm<Ma2Model>(p, c, st, m);
-            if (is_epi) ecnt = epi_gemm<Ma2Model>(p, c, ecnt, m, l, cs);
+            if constexpr (Model::kTM) {
+              if (is_mma) mma_gemm_tm<Model>(p, c, st, m);
+              if (is_epi) ecnt = epi_gemm_tm<Model>(p, c, ecnt, m, l);
+            } else {
+              if (is_mma) mma_gemm<Model>(p, c, st, m);
+              if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l, cs);
+            }
           } else if (s == 1) {
             if (p.self_tc) {
               if (is_mma) mma_self(p, c, st);
@@ -1202,6 +1255,13 @@ __global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_c
     tc_fence_after();
     tmem_dealloc(s_tmem, 512);
   }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel(const __grid_constant__ Params p) {
+  ma2_denoise_body<Ma2Model>(p);
+}
+__global__ void __launch_bounds__(kThreads, 1) ma2_denoise_kernel_tm(const __grid_constant__ Params p) {
+  ma2_denoise_body<Ma2ModelTM>(p);
 }
 
 }  // namespace ma2

@@ -1086,7 +1086,7 @@ __device__ __forceinline__ void denoise_body(const Params& p) {
           if (m >= 0) {
             if constexpr (Model::kTM) {
               if (is_mma) mma_gemm_tm<Model>(p, c, st, m);
-              if (is_epi) ecnt = epi_gemm_tm<Model>(p, c, ecnt, m);
+              if (is_epi) ecnt = epi_gemm_tm<Model>(p, c, ecnt, m, l);
             } else {
               if (is_mma) mma_gemm<Model>(p, c, st, m);
               if (is_epi) ecnt = epi_gemm<Model>(p, c, ecnt, m, l, cs);

@@ -28,7 +28,11 @@ def oracle_bf16(c):
     return M.flow(c2)
 
 
-def test_ma2_small(require_gpu):
+@pytest.mark.parametrize("tm", ["0", "1"])
+def test_ma2_small(require_gpu, monkeypatch, tm):
+    """One observation against the fp32 oracle, with the weight-major GEMMs ("0", the default) and
+    the opt-in token-major GEMMs ("1": activation tile as the M=64 A operand)."""
+    monkeypatch.setenv("FA_MA2_TM", tm)
     c = M.make_case(seed=51, L=2, T=30, Lk=300, B=1, num_steps=2)
     out, _ = run(c)
     ref = oracle_bf16(c)
