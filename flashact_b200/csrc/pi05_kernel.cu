@@ -305,30 +305,20 @@ __device__ __forceinline__ void epi_tile(const EpiCtx& p, const GemmUnit& gu, in
         const float o = hi ? fmaf(v[k], cs[k], partner[k] * sn[k]) : fmaf(v[k], cs[k], -partner[k] * sn[k]);
         st[k * 128] = __float2bfloat16(o);
       }
-    } else {  // V: natural order, stored transposed [dim][token]: 8 tokens per 16-byte store
-      const int dim = (mt - 18) * 128 + row;
+    } else {  // V: staged transposed, one 128-byte row of 64 tokens per dim (16-byte chunks
+              // swizzled by the row: 4-way bank conflicts instead of 32-way); epi_copy_out writes
+              // the rows along the token axis
+      uint8_t* srow = p.stage + row * 128;
+      const int c = (nb - nb0) >> 3;  // 16 tokens = chunks c, c + 1
 #pragma unroll
-      for (int g8 = 0; g8 < 16; g8 += 8) {
-        const int n0 = nb + g8;
-        const int b0 = tok_bi(p.invT, n0), t0 = n0 - b0 * p.T;
-        if (n0 + 7 < p.NT && t0 + 7 < p.T && (t0 & 7) == 0) {
-          uint32_t w[4];
+      for (int h = 0; h < 2; ++h) {
+        uint32_t w[4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            __nv_bfloat162 b2 = __floats2bfloat162_rn(v[g8 + 2 * k], v[g8 + 2 * k + 1]);
-            w[k] = *reinterpret_cast<uint32_t*>(&b2);
-          }
-          *reinterpret_cast<uint4*>(p.svt + ((size_t)b0 * HD + dim) * TPAD + t0) = make_uint4(w[0], w[1], w[2], w[3]);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int n = n0 + k;
-            if (n < p.NT) {
-              const int b = tok_bi(p.invT, n), t = n - b * p.T;
-              p.svt[((size_t)b * HD + dim) * TPAD + t] = __float2bfloat16(v[g8 + k]);
-            }
-          }
+        for (int k = 0; k < 4; ++k) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * h + 2 * k], v[8 * h + 2 * k + 1]);
+          w[k] = *reinterpret_cast<uint32_t*>(&b2);
         }
+        *reinterpret_cast<uint4*>(srow + (((c + h) ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
   } else if (m == MAT_GU) {  // GeGLU: lanes 0-15 gate rows, 16-31 up rows of one feature
@@ -360,6 +350,24 @@ __device__ __forceinline__ void epi_copy_out(const EpiCtx& p, const GemmUnit& gu
       if (n >= p.NT || (gu.half && (seg >> 2) != gu.half - 1)) continue;
       const uint4 val = *reinterpret_cast<const uint4*>(p.stage + t * 128 + seg * 16);
       *reinterpret_cast<uint4*>(p.hbuf + (size_t)n * F + 64 * gu.mtile + seg * 8) = val;
+    }
+  } else if (gu.mtile >= 18) {  // V: staged dim rows of 64 tokens -> svt [b][dim][t], two tokens per store
+    const int d0 = gu.half ? 64 * (gu.half - 1) : 0, nd = gu.half ? 64 : 128;
+    for (int it = e; it < nd * 32; it += 128) {
+      const int row = d0 + (it >> 5), tk = r0 + 2 * (it & 31), n = nb0 + tk;
+      if (tk >= r1 || n >= p.NT) continue;
+      const uint32_t pair = *reinterpret_cast<const uint32_t*>(p.stage + row * 128 + (((tk >> 3) ^ (row & 7)) << 4) + (tk & 7) * 2);
+      const int b = tok_bi(p.invT, n), t = n - b * p.T, dim = (gu.mtile - 18) * 128 + row;
+      __nv_bfloat16* dst = p.svt + ((size_t)b * HD + dim) * TPAD + t;
+      if ((t & 1) == 0 && t + 1 < p.T && n + 1 < p.NT && tk + 1 < r1) {
+        *reinterpret_cast<uint32_t*>(dst) = pair;
+      } else {  // the pair straddles an observation (odd T) or ends the batch
+        dst[0] = __ushort_as_bfloat16((unsigned short)(pair & 0xFFFF));
+        if (tk + 1 < r1 && n + 1 < p.NT) {
+          const int b1 = tok_bi(p.invT, n + 1), t1 = n + 1 - b1 * p.T;
+          p.svt[((size_t)b1 * HD + dim) * TPAD + t1] = __ushort_as_bfloat16((unsigned short)(pair >> 16));
+        }
+      }
     }
   } else {  // Q / K: 64 rows x 256 B, dims [0, 64) -> 64 pb + ..., dims [64, 128) -> 128 + 64 pb + ...
     const int mt = gu.mtile;
@@ -455,7 +463,7 @@ struct Pi05Model {
     e.NT = p.NT; e.T = p.T; e.NPAD = p.NPAD; e.invT = p.invT; e.rope_cos = p.rope_cos; e.rope_sin = p.rope_sin;
     e.q = p.q; e.sk = p.sk; e.svt = p.svt; e.hbuf = p.hbuf; e.part = p.part; e.stage = c.stage;
   }
-  __device__ static bool staged(int m, const GemmUnit& gu) { return m == MAT_GU || (m == MAT_QKV && gu.mtile < 18); }
+  __device__ static bool staged(int m, const GemmUnit&) { return m == MAT_GU || m == MAT_QKV; }
   __device__ static void epi_tile(const Epi& e, const GemmUnit& gu, int m, int qd, int lane, int row, int nb, int nb0,
                                   const float* v) {
     pi05::epi_tile(e, gu, m, qd, lane, row, nb, nb0, v);
